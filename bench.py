@@ -1,0 +1,322 @@
+"""Benchmark: BF16 GB/s encoded per quant type on the single-tensor encoder
+sweep (4096 rows x 14336 columns of BF16, N(0, 0.02) with 0.1% outliers at
++-8 sigma, per-column log-normal imatrix with sigma 1.5), device-resident and
+end to end through the host-buffer C-ABI entry point.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step encodes the tensor once to every type of the sweep.  L2 (126 MB) is
+flushed before every timed encode (the 117 MB input fits in L2).  Under
+torchrun every rank encodes its own copy (weak scaling, no collective on the
+data path); the time is the max over ranks.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_ROWS, NE0 = 4096, 14336
+SEED = 20261201
+SWEEP = ["Q4_K", "Q5_K", "Q6_K", "Q8_0"]
+METRIC = "BF16 GB/s encoded per quant type"
+TYPE_IDS = {"Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "IQ2_XXS": 16, "IQ2_XS": 17, "IQ3_XXS": 18,
+            "IQ4_NL": 20, "IQ3_S": 21, "IQ2_S": 22, "IQ4_XS": 23}
+OUT_BYTES_PER_ELT = {"Q8_0": 34 / 32, "Q4_K": 144 / 256, "Q5_K": 176 / 256, "Q6_K": 210 / 256,
+                     "IQ2_XXS": 66 / 256, "IQ2_XS": 74 / 256, "IQ2_S": 82 / 256, "IQ3_XXS": 98 / 256,
+                     "IQ3_S": 110 / 256, "IQ4_NL": 18 / 32, "IQ4_XS": 136 / 256}
+# Algorithmic FP32 operations per element of the reference algorithm with its
+# loop invariants hoisted (each add/sub/mul/div/sqrt/round/min/max = 1):
+#  Q4_K/Q5_K: 37 grids x (9 sum-pass + 2 clamp + 6 error-pass) + initial grid
+#             (sum of one pass, 11) + weights (4) + folds/requantisation (~8)
+#  Q6_K: 19 grids x (2 clamp + 1 round + 6) + weights (4) + requant (4)
+#  Q8_0: abs/max, multiply, round (HBM-bound; bytes are the roofline)
+FLOPS_PER_ELT = {"Q4_K": 37 * 17 + 11 + 4 + 8, "Q5_K": 37 * 17 + 11 + 4 + 8, "Q6_K": 19 * 9 + 4 + 4, "Q8_0": 4}
+
+
+def make_workload(seed=SEED):
+    rng = np.random.default_rng(seed)
+    w = rng.standard_normal((N_ROWS, NE0), dtype=np.float32)
+    w *= np.float32(0.02)
+    k = int(round(w.size * 0.001))
+    idx = rng.choice(w.size, size=k, replace=False)
+    w.reshape(-1)[idx] = rng.choice(np.array([-0.16, 0.16], dtype=np.float32), size=k)
+    u = w.view(np.uint32)
+    bits = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)  # RNE to BF16
+    im = np.exp(rng.normal(0.0, 1.5, size=NE0)).astype(np.float32)
+    return bits, im
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    return int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")), ws
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            p = [x.strip() for x in ln.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                smax.append(float(p[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline(bits, im, types, budget_s=12.0):
+    """The reference algorithm (the C restatement in oracle/) on host cores:
+    a bounded sample of rows of the same tensor per type."""
+    from oracle import oracle as O
+    cores = os.cpu_count() or 1
+    per_type = {}
+    tot_bytes, tot_t = 0, 0.0
+    for name in types:
+        ty = TYPE_IDS[name]
+        rows = 16
+        t0 = time.perf_counter()
+        O.encode_tensor_bf16(ty, bits[:rows], im, n_threads=cores)
+        dt = time.perf_counter() - t0
+        # grow the sample to about budget_s / len(types) of work
+        target = budget_s / len(types)
+        rows = int(min(N_ROWS, max(rows, rows * target / max(dt, 1e-3) * 0.8)))
+        rows = max(cores, rows - rows % cores)
+        t0 = time.perf_counter()
+        O.encode_tensor_bf16(ty, bits[:rows], im, n_threads=cores)
+        dt = time.perf_counter() - t0
+        per_type[name] = {"gbs": rows * NE0 * 2 / dt / 1e9, "rows": rows}
+        tot_bytes += rows * NE0 * 2
+        tot_t += dt
+    return {"value": tot_bytes / tot_t / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
+            "per_type": {k: round(v["gbs"], 5) for k, v in per_type.items()},
+            "sample": "; ".join(f"{k}: first {v['rows']} rows x {NE0}" for k, v in per_type.items())}
+
+
+def run_reference(args):
+    rank, _, world = dist_env()
+    if rank != 0:
+        return 0
+    bits, im = make_workload()
+    types = args.types.split(",")
+    for _ in range(args.warmup):
+        cpu_baseline(bits, im, types, budget_s=2.0)
+    vals = []
+    samples = None
+    t_start = time.perf_counter()
+    for _ in range(args.steps):
+        cb = cpu_baseline(bits, im, types, budget_s=args.ref_budget)
+        vals.append(cb["value"])
+        samples = cb
+    wall = time.perf_counter() - t_start
+    value = statistics.median(vals)
+    line = {"metric": METRIC, "value": round(value, 5), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(wall / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": f"encoder sweep {N_ROWS}x{NE0} BF16 ({','.join(types)})", "types": types,
+                       "l2": "n/a (host CPU)"},
+            "cpu_baseline": {"value": round(value, 5), "unit": "GB/s", "cores": samples["cores"], "kind": "port",
+                             "sample": samples["sample"]},
+            "e2e": {"value": round(value, 5), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "per_type_gbs": samples["per_type"]}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    import shoehorn_b200 as sh
+
+    rank, local_rank, world = dist_env()
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    dev = torch.device("cuda", local_rank)
+    ctx = sh.Context(local_rank)
+    types = [t for t in args.types.split(",") if sh.type_supported(TYPE_IDS[t])]
+    bits, im = make_workload()
+    src = torch.from_numpy(bits.view(np.int16)).to(dev)
+    imt = torch.from_numpy(im).to(dev)
+    outs = {t: torch.empty((N_ROWS, sh.row_bytes(TYPE_IDS[t], NE0)), dtype=torch.uint8, device=dev) for t in types}
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def encode(t):
+        ctx.encode_rows(TYPE_IDS[t], src, imt, out=outs[t], stream=stream)
+
+    for _ in range(args.warmup):
+        for t in types:
+            flush.zero_()
+            encode(t)
+    ctx.sync(stream)
+    torch.cuda.synchronize()
+
+    ev = {t: [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+          for t in types}
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local_rank)).split(",")[0])
+                           if os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")[0].isdigit() else local_rank)
+    sampler.start()
+    launches0 = ctx.launch_count()
+    for k in range(args.steps):
+        for t in types:
+            flush.zero_()  # evict the input from L2 before every timed encode
+            s, e = ev[t][k]
+            s.record(stream)
+            encode(t)
+            e.record(stream)
+    torch.cuda.synchronize()
+    launches = ctx.launch_count() - launches0
+    ctx.sync(stream)
+    per_type_ms = {t: statistics.mean(s.elapsed_time(e) for s, e in ev[t]) for t in types}
+    step_ms = sum(per_type_ms.values())
+    # max over ranks
+    if world > 1:
+        tt = torch.tensor([step_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        step_ms = float(tt.item())
+
+    # end to end: host (pinned) buffers through the C-ABI host entry point
+    src_h = torch.from_numpy(bits.view(np.int16)).pin_memory()
+    outs_h = {t: torch.empty(tuple(outs[t].shape), dtype=torch.uint8).pin_memory() for t in types}
+    for t in types:
+        ctx.encode_tensor_host(TYPE_IDS[t], src_h, im, out=outs_h[t])
+    if world > 1:
+        dist.barrier()
+    e2e_t = {t: [] for t in types}
+    for _ in range(max(1, min(args.steps, 3))):
+        for t in types:
+            t0 = time.perf_counter()
+            ctx.encode_tensor_host(TYPE_IDS[t], src_h, im, out=outs_h[t])
+            e2e_t[t].append(time.perf_counter() - t0)
+    e2e_step = sum(statistics.median(v) for v in e2e_t.values())
+    if world > 1:
+        tt = torch.tensor([e2e_step], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_step = float(tt.item())
+    clocks = sampler.stop()
+
+    in_bytes = N_ROWS * NE0 * 2
+    value = world * len(types) * in_bytes / (step_ms * 1e-3) / 1e9
+    e2e_value = world * len(types) * in_bytes / e2e_step / 1e9
+    per_type = {t: round(in_bytes / (per_type_ms[t] * 1e-3) / 1e9, 3) for t in types}
+
+    # roofline of the dominant kernel (largest share of the step)
+    dom = max(types, key=lambda t: per_type_ms[t])
+    elts = N_ROWS * NE0
+    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peaks = json.load(open(peaks_path)) if os.path.exists(peaks_path) else {}
+    props = torch.cuda.get_device_properties(dev)
+    sm_mhz = clocks.get("sm_mhz") or peaks.get("sm_max_mhz", 1965.0)
+    if dom == "Q8_0":
+        alg = elts * (2 + OUT_BYTES_PER_ELT[dom])
+        hbm = peaks.get("hbm_gbs", 6650.0)
+        roof = {"bound": "hbm", "achieved": round(alg / (per_type_ms[dom] * 1e-3) / 1e9, 2),
+                "peak": hbm, "unit": "GB/s",
+                "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if "hbm_gbs" in peaks else "fallback"}
+    else:
+        alg = elts * FLOPS_PER_ELT[dom]
+        # FP32 pipe: 128 lanes per SM, one add/mul/min/max per lane per clock;
+        # FMA pairing is unavailable (no contraction, by the parity contract)
+        peak = props.multi_processor_count * 128 * sm_mhz * 1e6 / 1e12
+        roof = {"bound": "fp32", "achieved": round(alg / (per_type_ms[dom] * 1e-3) / 1e12, 3),
+                "peak": round(peak, 3), "unit": "TFLOP/s",
+                "peak_source": f"{props.multi_processor_count} SMs x 128 FP32 lanes x median SM clock "
+                               f"{sm_mhz:.0f} MHz under load (no FP32 figure in MEASURED_PEAKS.json)"}
+    roof["frac"] = round(roof["achieved"] / roof["peak"], 4)
+    roof["kernel"] = f"{dom} encoder"
+    roof["traffic"] = None
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(bits, im, types, budget_s=args.ref_budget)
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": f"encoder sweep {N_ROWS}x{NE0} BF16 ({','.join(types)}), imatrix-weighted",
+                           "types": types, "rows": N_ROWS, "ne0": NE0,
+                           "l2": "flushed (512 MB write) before every timed encode",
+                           "parallelism": f"weak: each of {world} ranks encodes its own copy"},
+                "per_type_gbs": per_type,
+                "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
+                        "h2d_bytes_per_step": len(types) * in_bytes,
+                        "d2h_bytes_per_step": sum(int(outs[t].numel()) for t in types)},
+                "roofline": roof, "clocks": clocks, "gpu_launches": launches,
+                "cpu_baseline": cpu}
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--types", default=",".join(SWEEP))
+    ap.add_argument("--ref-budget", type=float, default=12.0, help="seconds of CPU work per reference sample")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,581 @@
+// C ABI of the library (include/shoehorn_cuda.h): validation, stream-ordered
+// scratch, launches, bounded waits and the pipelined host-buffer entry points.
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <thread>
+#include <vector>
+
+#include "iq_host.h"
+#include "kernels.cuh"
+#include "shoehorn_cuda.h"
+
+using namespace shc;
+
+struct shc_ctx {
+    int device = 0;
+    int num_sms = 0;
+    int *d_status = nullptr;
+    int *h_status_pool = nullptr;  // pinned, kStatusSlots ints
+    std::atomic<unsigned> status_slot{0};
+    void *d_tables = nullptr;
+    IqTables iq{};
+    std::atomic<int64_t> launches{0};
+    // host-buffer pipeline resources (one host call at a time)
+    std::mutex host_mu;
+    cudaStream_t hs[3] = {nullptr, nullptr, nullptr};  // h2d, compute, d2h
+    void *pin[4] = {nullptr, nullptr, nullptr, nullptr};  // in0, in1, out0, out1 (pageable staging)
+    size_t pin_bytes[4] = {0, 0, 0, 0};
+};
+
+namespace {
+
+constexpr unsigned kStatusSlots = 64;
+
+struct DevGuard {
+    int prev = -1;
+    explicit DevGuard(int d) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != d) cudaSetDevice(d);
+    }
+    ~DevGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+int cuda_status(cudaError_t e) {
+    if (e == cudaSuccess) return SHC_OK;
+    if (e == cudaErrorMemoryAllocation) return SHC_ENOMEM;
+    return SHC_ECUDA;
+}
+
+#define SHC_TRY(expr)                                   \
+    do {                                                \
+        cudaError_t _e = (expr);                        \
+        if (_e != cudaSuccess) return cuda_status(_e);  \
+    } while (0)
+
+bool valid_src_type(uint32_t s) { return s == SHC_SRC_F32 || s == SHC_SRC_F16 || s == SHC_SRC_BF16; }
+size_t src_elem_bytes(uint32_t s) { return s == SHC_SRC_F32 ? 4 : 2; }
+
+bool encodable(uint32_t t) {
+    switch (t) {
+    case SHC_TYPE_F32: case SHC_TYPE_F16: case SHC_TYPE_BF16: case SHC_TYPE_Q8_0: case SHC_TYPE_Q4_K:
+    case SHC_TYPE_Q5_K: case SHC_TYPE_Q6_K:
+        return true;
+    default:
+        return is_iq(t) ? iq_supported(t) : false;
+    }
+}
+
+// Wait for an event with a deadline; never blocks past it.
+int wait_event(cudaEvent_t ev, std::chrono::steady_clock::time_point deadline, bool bounded) {
+    for (;;) {
+        cudaError_t e = cudaEventQuery(ev);
+        if (e == cudaSuccess) return SHC_OK;
+        if (e != cudaErrorNotReady) return cuda_status(e);
+        if (bounded && std::chrono::steady_clock::now() > deadline) return SHC_ETIMEOUT;
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+}
+
+int wait_stream(cudaStream_t st, int64_t timeout_ms) {
+    cudaEvent_t ev;
+    SHC_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    cudaError_t e = cudaEventRecord(ev, st);
+    if (e != cudaSuccess) {
+        cudaEventDestroy(ev);
+        return cuda_status(e);
+    }
+    auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms < 0 ? 0 : timeout_ms);
+    int rc = wait_event(ev, deadline, timeout_ms >= 0);
+    cudaEventDestroy(ev);
+    return rc;
+}
+
+EncArgs make_args(shc_ctx *ctx, uint32_t src_type, const void *src, int64_t n_rows, int64_t ne0, int64_t row_stride,
+                  const float *im, int64_t im_len, int64_t rows_per_mat, int64_t row0, int64_t row_step, uint8_t *dst,
+                  int64_t dst_row_bytes) {
+    EncArgs a{};
+    a.src.ptr = src;
+    a.src.src_type = (int)src_type;
+    a.src.ne0 = ne0;
+    a.src.row_stride = row_stride;
+    a.im.ptr = im;
+    a.im.len = im ? im_len : 0;
+    a.im.rows_per_mat = rows_per_mat;
+    a.n_rows = n_rows;
+    a.row0 = row0;
+    a.row_step = row_step;
+    a.sigma2 = nullptr;
+    a.dst = dst;
+    a.dst_row_bytes = dst_row_bytes;
+    a.status = ctx->d_status;
+    a.dst_aligned16 = (((uintptr_t)dst & 15) == 0 && (dst_row_bytes & 15) == 0) ? 1 : 0;
+    return a;
+}
+
+int check_common(shc_ctx *ctx, uint32_t src_type, const void *src, int64_t n_rows, int64_t ne0, const float *im) {
+    if (!ctx) return SHC_EINVAL;
+    if (!valid_src_type(src_type) || n_rows < 0 || ne0 <= 0) return SHC_EINVAL;
+    if (n_rows > 0 && !src) return SHC_EINVAL;
+    if (((uintptr_t)src & 15) != 0) return SHC_EINVAL;  // 128-bit row loads
+    if (im && ((uintptr_t)im & 15) != 0) return SHC_EINVAL;
+    if (ne0 % 8 != 0) return SHC_EINVAL;
+    return SHC_OK;
+}
+
+// Encode one view of rows on `st` (sigma^2 pre-pass into stream-ordered
+// scratch when the type needs it).
+int encode_view(shc_ctx *ctx, uint32_t type, EncArgs a, cudaStream_t st) {
+    if (a.n_rows == 0) return SHC_OK;
+    float *sig = nullptr;
+    if (needs_sigma2(type)) {
+        SHC_TRY(cudaMallocAsync((void **)&sig, sizeof(float) * (size_t)a.n_rows, st));
+        cudaError_t e = launch_row_sigma2(a.src, a.n_rows, sig, st);
+        ctx->launches++;
+        if (e != cudaSuccess) {
+            cudaFreeAsync(sig, st);
+            return cuda_status(e);
+        }
+        a.sigma2 = sig;
+    }
+    cudaError_t e;
+    if (block_elems(type) == 1) e = launch_plain(type, a, ctx->num_sms, st);
+    else if (is_iq(type)) e = launch_iq(type, a, ctx->iq, ctx->num_sms, st);
+    else e = launch_kquant(type, a, ctx->num_sms, st);
+    ctx->launches++;
+    if (sig) cudaFreeAsync(sig, st);
+    return cuda_status(e);
+}
+
+int upload_iq_tables(shc_ctx *ctx) {
+    IqHostTable t[5];
+    size_t total = 0;
+    for (int w = 0; w < 5; w++) {
+        build_iq_tables(w, t[w]);
+        total += (t[w].kmap.size() + t[w].neighbours.size() + t[w].grid_coords.size()) * 4 + 256;
+    }
+    SHC_TRY(cudaMalloc(&ctx->d_tables, total));
+    std::vector<uint8_t> host(total, 0);
+    size_t off = 0;
+    auto place = [&](const void *p, size_t bytes) {
+        std::memcpy(host.data() + off, p, bytes);
+        size_t at = off;
+        off += (bytes + 255) & ~(size_t)255;
+        return static_cast<uint8_t *>(ctx->d_tables) + at;
+    };
+    for (int w = 0; w < 5; w++) {
+        ctx->iq.kmap[w] = reinterpret_cast<const int32_t *>(place(t[w].kmap.data(), t[w].kmap.size() * 4));
+        ctx->iq.neighbours[w] = reinterpret_cast<const uint32_t *>(place(t[w].neighbours.data(), t[w].neighbours.size() * 4));
+        ctx->iq.grid_coords[w] = reinterpret_cast<const uint32_t *>(place(t[w].grid_coords.data(), t[w].grid_coords.size() * 4));
+    }
+    SHC_TRY(cudaMemcpy(ctx->d_tables, host.data(), total, cudaMemcpyHostToDevice));
+    return SHC_OK;
+}
+
+int ensure_pinned(shc_ctx *ctx, int slot, size_t bytes) {
+    if (ctx->pin_bytes[slot] >= bytes) return SHC_OK;
+    if (ctx->pin[slot]) cudaFreeHost(ctx->pin[slot]);
+    ctx->pin[slot] = nullptr;
+    ctx->pin_bytes[slot] = 0;
+    SHC_TRY(cudaHostAlloc(&ctx->pin[slot], bytes, cudaHostAllocDefault));
+    ctx->pin_bytes[slot] = bytes;
+    return SHC_OK;
+}
+
+bool is_pinned(const void *p) {
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return attr.type == cudaMemoryTypeHost;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *shc_status_string(int s) {
+    switch (s) {
+    case SHC_OK: return "ok";
+    case SHC_EINVAL: return "invalid argument";
+    case SHC_ECUDA: return "CUDA runtime error";
+    case SHC_EOFFGRID: return "IQ point off the lattice";
+    case SHC_ENONEIGHBOUR: return "IQ neighbour search found no finite candidate";
+    case SHC_ETIMEOUT: return "timed out";
+    case SHC_ENOMEM: return "out of memory";
+    case SHC_ENODEV: return "no usable sm_100 device";
+    default: return "unknown status";
+    }
+}
+
+int64_t shc_row_bytes(uint32_t type, int64_t ne0) {
+    const int64_t be = block_elems(type), bb = block_bytes(type);
+    if (be == 0 || ne0 < 0 || ne0 % be != 0) return -1;
+    return ne0 / be * bb;
+}
+
+int shc_type_supported(uint32_t type) { return encodable(type) ? 1 : 0; }
+
+int shc_init(int device, shc_ctx **out) {
+    if (!out) return SHC_EINVAL;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+        cudaGetLastError();
+        return SHC_ENODEV;
+    }
+    cudaDeviceProp prop;
+    SHC_TRY(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10) return SHC_ENODEV;  // built for sm_100a only
+    DevGuard g(device);
+    shc_ctx *ctx = new (std::nothrow) shc_ctx();
+    if (!ctx) return SHC_ENOMEM;
+    ctx->device = device;
+    ctx->num_sms = prop.multiProcessorCount;
+    int rc = SHC_OK;
+    if (cudaMalloc((void **)&ctx->d_status, sizeof(int)) != cudaSuccess ||
+        cudaMemset(ctx->d_status, 0, sizeof(int)) != cudaSuccess ||
+        cudaHostAlloc((void **)&ctx->h_status_pool, sizeof(int) * kStatusSlots, cudaHostAllocDefault) != cudaSuccess) {
+        rc = SHC_ENOMEM;
+    }
+    if (rc == SHC_OK) rc = upload_iq_tables(ctx);
+    for (int i = 0; rc == SHC_OK && i < 3; i++)
+        if (cudaStreamCreateWithFlags(&ctx->hs[i], cudaStreamNonBlocking) != cudaSuccess) rc = SHC_ECUDA;
+    if (rc != SHC_OK) {
+        shc_free(ctx);
+        return rc;
+    }
+    *out = ctx;
+    return SHC_OK;
+}
+
+int shc_free(shc_ctx *ctx) {
+    if (!ctx) return SHC_EINVAL;
+    {
+        DevGuard g(ctx->device);
+        cudaDeviceSynchronize();
+        for (int i = 0; i < 3; i++)
+            if (ctx->hs[i]) cudaStreamDestroy(ctx->hs[i]);
+        for (int i = 0; i < 4; i++)
+            if (ctx->pin[i]) cudaFreeHost(ctx->pin[i]);
+        if (ctx->d_tables) cudaFree(ctx->d_tables);
+        if (ctx->d_status) cudaFree(ctx->d_status);
+        if (ctx->h_status_pool) cudaFreeHost(ctx->h_status_pool);
+    }
+    delete ctx;
+    return SHC_OK;
+}
+
+int64_t shc_launch_count(const shc_ctx *ctx) { return ctx ? ctx->launches.load() : -1; }
+
+int shc_encode_rows(shc_ctx *ctx, uint32_t type, uint32_t src_type, const void *src, int64_t n_rows, int64_t ne0,
+                    const float *im, int64_t im_len, int64_t rows_per_mat, int64_t row0, uint8_t *dst, void *stream) {
+    int rc = check_common(ctx, src_type, src, n_rows, ne0, im);
+    if (rc != SHC_OK) return rc;
+    const int64_t rb = shc_row_bytes(type, ne0);
+    if (rb < 0 || !encodable(type) || (n_rows > 0 && !dst)) return SHC_EINVAL;
+    DevGuard g(ctx->device);
+    EncArgs a = make_args(ctx, src_type, src, n_rows, ne0, ne0, im, im_len, rows_per_mat, row0, 1, dst, rb);
+    return encode_view(ctx, type, a, (cudaStream_t)stream);
+}
+
+int shc_decode_rows(shc_ctx *ctx, uint32_t type, const uint8_t *src, int64_t n_rows, int64_t ne0, float *dst,
+                    void *stream) {
+    if (!ctx || n_rows < 0 || ne0 <= 0) return SHC_EINVAL;
+    const int64_t rb = shc_row_bytes(type, ne0);
+    if (rb < 0 || block_elems(type) == 0) return SHC_EINVAL;
+    if (n_rows == 0) return SHC_OK;
+    if (!src || !dst) return SHC_EINVAL;
+    if (type == SHC_TYPE_F32 && ((uintptr_t)src & 3)) return SHC_EINVAL;
+    DevGuard g(ctx->device);
+    cudaError_t e = launch_decode(type, src, n_rows, ne0, dst, ctx->num_sms, (cudaStream_t)stream);
+    ctx->launches++;
+    return cuda_status(e);
+}
+
+int shc_row_errors(shc_ctx *ctx, const uint32_t *types, int n_types, uint32_t src_type, const void *src,
+                   int64_t n_rows, int64_t ne0, const float *im, int64_t im_len, int64_t rows_per_mat, int64_t row0,
+                   int64_t row_step, double *err, void *stream) {
+    int rc = check_common(ctx, src_type, src, n_rows, ne0, im);
+    if (rc != SHC_OK) return rc;
+    if (!types || n_types < 1 || n_types > 32 || row_step < 1) return SHC_EINVAL;
+    for (int t = 0; t < n_types; t++)
+        if (!encodable(types[t]) || shc_row_bytes(types[t], ne0) < 0) return SHC_EINVAL;
+    const int64_t n_s = (n_rows + row_step - 1) / row_step;
+    if (n_s == 0) return SHC_OK;
+    if (!err) return SHC_EINVAL;
+    DevGuard g(ctx->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    EncArgs a = make_args(ctx, src_type, src, n_s, ne0, ne0 * row_step, im, im_len, rows_per_mat, row0, row_step,
+                          nullptr, 0);
+    bool any_sig = false;
+    for (int t = 0; t < n_types; t++) any_sig |= needs_sigma2(types[t]);
+    float *sig = nullptr;
+    std::vector<uint8_t *> codes((size_t)n_types, nullptr);
+    auto cleanup = [&]() {
+        for (auto p : codes)
+            if (p) cudaFreeAsync(p, st);
+        if (sig) cudaFreeAsync(sig, st);
+    };
+    if (any_sig) {
+        if (cudaMallocAsync((void **)&sig, sizeof(float) * (size_t)n_s, st) != cudaSuccess) return SHC_ENOMEM;
+        cudaError_t e = launch_row_sigma2(a.src, n_s, sig, st);
+        ctx->launches++;
+        if (e != cudaSuccess) {
+            cleanup();
+            return cuda_status(e);
+        }
+    }
+    for (int t = 0; t < n_types; t++) {
+        const uint32_t ty = types[t];
+        if (block_elems(ty) == 1) continue;  // elementwise types are round-tripped inside the error pass
+        const int64_t rb = shc_row_bytes(ty, ne0);
+        if (cudaMallocAsync((void **)&codes[(size_t)t], (size_t)(rb * n_s), st) != cudaSuccess) {
+            cleanup();
+            return SHC_ENOMEM;
+        }
+        EncArgs at = a;
+        at.dst = codes[(size_t)t];
+        at.dst_row_bytes = rb;
+        at.dst_aligned16 = ((rb & 15) == 0) ? 1 : 0;
+        at.sigma2 = sig;
+        cudaError_t e;
+        if (is_iq(ty)) e = launch_iq(ty, at, ctx->iq, ctx->num_sms, st);
+        else e = launch_kquant(ty, at, ctx->num_sms, st);
+        ctx->launches++;
+        if (e != cudaSuccess) {
+            cleanup();
+            return cuda_status(e);
+        }
+    }
+    cudaError_t e = launch_row_sse(types, n_types, codes.data(), a, err, st);
+    ctx->launches++;
+    cleanup();
+    return cuda_status(e);
+}
+
+int shc_sync(shc_ctx *ctx, void *stream, int64_t timeout_ms) {
+    if (!ctx) return SHC_EINVAL;
+    DevGuard g(ctx->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    int *slot = ctx->h_status_pool + (ctx->status_slot.fetch_add(1) % kStatusSlots);
+    *slot = 0;
+    SHC_TRY(cudaMemcpyAsync(slot, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost, st));
+    SHC_TRY(cudaMemsetAsync(ctx->d_status, 0, sizeof(int), st));
+    int rc = wait_stream(st, timeout_ms);
+    if (rc != SHC_OK) return rc;
+    return *slot;
+}
+
+int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const void *host_src, int64_t n_rows,
+                           int64_t ne0, const float *host_im, int64_t im_len, int64_t rows_per_mat, int64_t row0,
+                           uint8_t *host_dst, int64_t timeout_ms) {
+    if (!ctx || !valid_src_type(src_type) || n_rows < 0 || ne0 <= 0 || ne0 % 8 != 0) return SHC_EINVAL;
+    const int64_t rb = shc_row_bytes(type, ne0);
+    if (rb < 0 || !encodable(type)) return SHC_EINVAL;
+    if (n_rows == 0) return SHC_OK;
+    if (!host_src || !host_dst) return SHC_EINVAL;
+    std::lock_guard<std::mutex> lk(ctx->host_mu);
+    DevGuard g(ctx->device);
+    const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms < 0 ? 0 : timeout_ms);
+    const bool bounded = timeout_ms >= 0;
+    const size_t eb = src_elem_bytes(src_type);
+    const size_t in_row = (size_t)ne0 * eb;
+    // ~64 MiB of source per chunk keeps three chunks in flight per direction
+    int64_t chunk = std::max<int64_t>(1, (int64_t)((64u << 20) / in_row));
+    chunk = std::min(chunk, n_rows);
+    const int64_t n_chunks = (n_rows + chunk - 1) / chunk;
+    const bool pin_src = is_pinned(host_src), pin_dst = is_pinned(host_dst);
+    cudaStream_t s_in = ctx->hs[0], s_cmp = ctx->hs[1], s_out = ctx->hs[2];
+    int rc = SHC_OK;
+    void *d_in[2] = {nullptr, nullptr};
+    uint8_t *d_out[2] = {nullptr, nullptr};
+    float *d_im = nullptr;
+    cudaEvent_t ev_in[2], ev_cmp[2], ev_out[2];
+    for (int b = 0; b < 2; b++) {
+        cudaEventCreateWithFlags(&ev_in[b], cudaEventDisableTiming);
+        cudaEventCreateWithFlags(&ev_cmp[b], cudaEventDisableTiming);
+        cudaEventCreateWithFlags(&ev_out[b], cudaEventDisableTiming);
+    }
+    auto fail = [&](int code) {
+        if (rc == SHC_OK) rc = code;
+    };
+    for (int b = 0; b < 2 && rc == SHC_OK; b++) {
+        if (cudaMallocAsync(&d_in[b], in_row * (size_t)chunk, s_cmp) != cudaSuccess) fail(SHC_ENOMEM);
+        if (cudaMallocAsync((void **)&d_out[b], (size_t)rb * (size_t)chunk, s_cmp) != cudaSuccess) fail(SHC_ENOMEM);
+        if (!pin_src && rc == SHC_OK) fail(ensure_pinned(ctx, b, in_row * (size_t)chunk));
+        if (!pin_dst && rc == SHC_OK) fail(ensure_pinned(ctx, 2 + b, (size_t)rb * (size_t)chunk));
+    }
+    if (rc == SHC_OK && host_im && im_len > 0) {
+        if (cudaMallocAsync((void **)&d_im, sizeof(float) * (size_t)im_len, s_cmp) != cudaSuccess) fail(SHC_ENOMEM);
+        else if (cudaMemcpyAsync(d_im, host_im, sizeof(float) * (size_t)im_len, cudaMemcpyHostToDevice, s_cmp) != cudaSuccess)
+            fail(SHC_ECUDA);
+    }
+    if (rc == SHC_OK) {
+        // the allocations above are ordered on s_cmp; make the copy streams wait
+        cudaEventRecord(ev_cmp[0], s_cmp);
+        cudaStreamWaitEvent(s_in, ev_cmp[0], 0);
+        cudaStreamWaitEvent(s_out, ev_cmp[0], 0);
+        cudaEventRecord(ev_cmp[1], s_cmp);
+        for (int b = 0; b < 2; b++) {
+            cudaEventRecord(ev_out[b], s_out);
+            cudaEventRecord(ev_in[b], s_in);
+        }
+    }
+    std::vector<int64_t> pending_out(2, -1);  // chunk whose pageable output sits in pin[2+b]
+    auto drain_out = [&](int b) {
+        if (pending_out[b] < 0) return;
+        int w = wait_event(ev_out[b], deadline, bounded);
+        if (w != SHC_OK) {
+            fail(w);
+            return;
+        }
+        const int64_t k = pending_out[b];
+        const int64_t r0 = k * chunk, nr = std::min(chunk, n_rows - r0);
+        std::memcpy(host_dst + r0 * rb, ctx->pin[2 + b], (size_t)(nr * rb));
+        pending_out[b] = -1;
+    };
+    for (int64_t k = 0; k < n_chunks && rc == SHC_OK; k++) {
+        const int b = (int)(k & 1);
+        const int64_t r0 = k * chunk, nr = std::min(chunk, n_rows - r0);
+        const size_t in_bytes = in_row * (size_t)nr;
+        const uint8_t *src_k = static_cast<const uint8_t *>(host_src) + (size_t)r0 * in_row;
+        // H2D of chunk k into d_in[b] once the encode of chunk k-2 released it
+        cudaStreamWaitEvent(s_in, ev_cmp[b], 0);
+        if (pin_src) {
+            if (cudaMemcpyAsync(d_in[b], src_k, in_bytes, cudaMemcpyHostToDevice, s_in) != cudaSuccess) fail(SHC_ECUDA);
+        } else {
+            int w = wait_event(ev_in[b], deadline, bounded);  // staging slot free
+            if (w != SHC_OK) { fail(w); break; }
+            std::memcpy(ctx->pin[b], src_k, in_bytes);
+            if (cudaMemcpyAsync(d_in[b], ctx->pin[b], in_bytes, cudaMemcpyHostToDevice, s_in) != cudaSuccess) fail(SHC_ECUDA);
+        }
+        cudaEventRecord(ev_in[b], s_in);
+        // encode chunk k once its input landed and d_out[b] was drained
+        cudaStreamWaitEvent(s_cmp, ev_in[b], 0);
+        cudaStreamWaitEvent(s_cmp, ev_out[b], 0);
+        EncArgs a = make_args(ctx, src_type, d_in[b], nr, ne0, ne0, d_im, im_len, rows_per_mat, row0 + r0, 1, d_out[b], rb);
+        int e = encode_view(ctx, type, a, s_cmp);
+        if (e != SHC_OK) { fail(e); break; }
+        cudaEventRecord(ev_cmp[b], s_cmp);
+        // D2H of chunk k
+        cudaStreamWaitEvent(s_out, ev_cmp[b], 0);
+        if (pin_dst) {
+            if (cudaMemcpyAsync(host_dst + r0 * rb, d_out[b], (size_t)(nr * rb), cudaMemcpyDeviceToHost, s_out) != cudaSuccess)
+                fail(SHC_ECUDA);
+        } else {
+            drain_out(b);
+            if (cudaMemcpyAsync(ctx->pin[2 + b], d_out[b], (size_t)(nr * rb), cudaMemcpyDeviceToHost, s_out) != cudaSuccess)
+                fail(SHC_ECUDA);
+            pending_out[b] = k;
+        }
+        cudaEventRecord(ev_out[b], s_out);
+    }
+    for (int b = 0; b < 2; b++) drain_out(b);
+    // release buffers after all queued work; wait (bounded) for completion
+    cudaEvent_t done;
+    cudaEventCreateWithFlags(&done, cudaEventDisableTiming);
+    cudaEventRecord(done, s_in);
+    cudaStreamWaitEvent(s_cmp, done, 0);
+    cudaEventRecord(done, s_out);
+    cudaStreamWaitEvent(s_cmp, done, 0);
+    for (int b = 0; b < 2; b++) {
+        if (d_in[b]) cudaFreeAsync(d_in[b], s_cmp);
+        if (d_out[b]) cudaFreeAsync(d_out[b], s_cmp);
+    }
+    if (d_im) cudaFreeAsync(d_im, s_cmp);
+    cudaEventRecord(done, s_cmp);
+    int w = wait_event(done, deadline, bounded);
+    if (rc == SHC_OK) rc = w;
+    cudaEventDestroy(done);
+    for (int b = 0; b < 2; b++) {
+        cudaEventDestroy(ev_in[b]);
+        cudaEventDestroy(ev_cmp[b]);
+        cudaEventDestroy(ev_out[b]);
+    }
+    if (rc == SHC_OK) {
+        int st = shc_sync(ctx, s_cmp, timeout_ms);
+        if (st != SHC_OK) rc = st;
+    }
+    return rc;
+}
+
+int shc_row_errors_host(shc_ctx *ctx, const uint32_t *types, int n_types, uint32_t src_type, const void *host_src,
+                        int64_t n_rows, int64_t ne0, const float *host_im, int64_t im_len, int64_t rows_per_mat,
+                        int64_t row0, int64_t row_step, double *err, int64_t timeout_ms) {
+    if (!ctx || !valid_src_type(src_type) || n_rows < 0 || ne0 <= 0 || row_step < 1 || !types || n_types < 1 ||
+        n_types > 32)
+        return SHC_EINVAL;
+    const int64_t n_s = (n_rows + row_step - 1) / row_step;
+    if (n_s == 0) return SHC_OK;
+    if (!host_src || !err) return SHC_EINVAL;
+    std::lock_guard<std::mutex> lk(ctx->host_mu);
+    DevGuard g(ctx->device);
+    cudaStream_t st = ctx->hs[1];
+    const size_t eb = src_elem_bytes(src_type), in_row = (size_t)ne0 * eb;
+    // sampled rows in chunks of ~256 MiB of source
+    int64_t chunk = std::max<int64_t>(1, (int64_t)((256u << 20) / in_row));
+    chunk = std::min(chunk, n_s);
+    void *d_in = nullptr;
+    float *d_im = nullptr;
+    double *d_err = nullptr;
+    int rc = SHC_OK;
+    if (cudaMallocAsync(&d_in, in_row * (size_t)chunk, st) != cudaSuccess ||
+        cudaMallocAsync((void **)&d_err, sizeof(double) * (size_t)n_types * (size_t)chunk, st) != cudaSuccess)
+        rc = SHC_ENOMEM;
+    if (rc == SHC_OK && host_im && im_len > 0) {
+        if (cudaMallocAsync((void **)&d_im, sizeof(float) * (size_t)im_len, st) != cudaSuccess) rc = SHC_ENOMEM;
+        else if (cudaMemcpyAsync(d_im, host_im, sizeof(float) * (size_t)im_len, cudaMemcpyHostToDevice, st) != cudaSuccess)
+            rc = SHC_ECUDA;
+    }
+    std::vector<double> part((size_t)n_types * (size_t)chunk);
+    for (int64_t i0 = 0; i0 < n_s && rc == SHC_OK; i0 += chunk) {
+        const int64_t ni = std::min(chunk, n_s - i0);
+        const uint8_t *src0 = static_cast<const uint8_t *>(host_src) + (size_t)(i0 * row_step) * in_row;
+        // gather the sampled rows (pitch row_step rows) in one strided copy
+        if (cudaMemcpy2DAsync(d_in, in_row, src0, in_row * (size_t)row_step, in_row, (size_t)ni, cudaMemcpyHostToDevice,
+                              st) != cudaSuccess) {
+            rc = SHC_ECUDA;
+            break;
+        }
+        rc = shc_row_errors(ctx, types, n_types, src_type, d_in, ni, ne0, d_im, im_len, rows_per_mat,
+                            row0 + i0 * row_step, 1, d_err, st);
+        if (rc != SHC_OK) break;
+        if (cudaMemcpyAsync(part.data(), d_err, sizeof(double) * (size_t)n_types * (size_t)ni, cudaMemcpyDeviceToHost,
+                            st) != cudaSuccess) {
+            rc = SHC_ECUDA;
+            break;
+        }
+        rc = wait_stream(st, timeout_ms);
+        if (rc != SHC_OK) break;
+        for (int t = 0; t < n_types; t++)
+            std::memcpy(err + (size_t)t * (size_t)n_s + (size_t)i0, part.data() + (size_t)t * (size_t)ni,
+                        sizeof(double) * (size_t)ni);
+    }
+    if (d_in) cudaFreeAsync(d_in, st);
+    if (d_err) cudaFreeAsync(d_err, st);
+    if (d_im) cudaFreeAsync(d_im, st);
+    int s = shc_sync(ctx, st, timeout_ms);
+    return rc != SHC_OK ? rc : s;
+}
+
+int shc_grid_info(int which, int32_t *grid_size, int32_t *map_size, int64_t *n_neighbours, int32_t *map_out,
+                  uint32_t *neighbours_out) {
+    if (which < 0 || which > 4) return SHC_EINVAL;
+    IqHostTable t;
+    build_iq_tables(which, t);
+    if (grid_size) *grid_size = t.grid_size;
+    if (map_size) *map_size = (int32_t)t.kmap.size();
+    if (n_neighbours) *n_neighbours = (int64_t)t.neighbours.size();
+    if (map_out) std::memcpy(map_out, t.kmap.data(), t.kmap.size() * 4);
+    if (neighbours_out) std::memcpy(neighbours_out, t.neighbours.data(), t.neighbours.size() * 4);
+    return SHC_OK;
+}
+
+}  // extern "C"

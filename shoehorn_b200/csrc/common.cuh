@@ -1,0 +1,145 @@
+// Device-side scalar semantics shared by every encoder kernel.
+//
+// The encoders must reproduce the reference's Rust f32 arithmetic bit for bit
+// (src/quant.rs, src/quant_iq.rs).  The library is compiled with
+// -fmad=false -prec-div=true -prec-sqrt=true -ftz=false, so every a*b+c below
+// is a separately rounded multiply and add, `/` and sqrtf are IEEE-correct and
+// subnormals are kept.  The helpers here pin the remaining Rust semantics:
+//   nearest_int  f32::round (half away from zero) then a saturating `as i32`
+//   rmaxf/rminf  f32::max / f32::min: NaN-ignoring, with -0 < +0 (the aarch64
+//                FMAXNM/FMINNM result)
+//   f16 bits     half::f16::from_f32, IEEE round-to-nearest-even
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "shoehorn_cuda.h"
+
+namespace shc {
+
+constexpr float kGroupMaxEps = 1e-15f;
+constexpr float kGroupMaxEpsIq3Xxs = 1e-8f;
+constexpr float kGroupMaxEpsIq2S = 1e-8f;
+
+// quant.rs:16 nearest_int: `x.round() as i32` (saturating, NaN -> 0).
+__device__ __forceinline__ int nearest_int(float x) {
+    float r = roundf(x);
+    if (r != r) return 0;
+    if (r >= 2147483648.0f) return 2147483647;
+    if (r <= -2147483648.0f) return (-2147483647 - 1);
+    return (int)r;
+}
+
+// nearest_int(x).clamp(0, hi) kept in float.  For the small integer ranges of
+// the encoders this equals the integer result converted back: fmaxf returns
+// the non-NaN operand, so NaN -> 0 as in the integer path, and +-inf saturate
+// to the bounds.  A zero may come out as -0.0; every use of l is a product
+// folded into a sum that starts at +0, where the sign of a zero term never
+// changes the result.
+__device__ __forceinline__ float round_clamp0_f(float x, float hi) {
+    float r = roundf(x);
+    r = fmaxf(r, 0.0f);
+    r = fminf(r, hi);
+    return r;
+}
+// nearest_int(x).clamp(lo, hi) in float for a negative lower bound: NaN must
+// map to 0 (not lo) as the saturating cast does.
+__device__ __forceinline__ float round_clamp_f(float x, float lo, float hi) {
+    float r = roundf(x);
+    r = (r != r) ? 0.0f : r;
+    r = fmaxf(r, lo);
+    r = fminf(r, hi);
+    return r;
+}
+
+__device__ __forceinline__ int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
+
+__device__ __forceinline__ float rmaxf(float a, float b) {
+    if (a != a) return b;
+    if (b != b) return a;
+    if (a > b) return a;
+    if (b > a) return b;
+    return signbit(a) ? b : a;
+}
+__device__ __forceinline__ float rminf(float a, float b) {
+    if (a != a) return b;
+    if (b != b) return a;
+    if (a < b) return a;
+    if (b < a) return b;
+    return signbit(a) ? a : b;
+}
+
+__device__ __forceinline__ uint16_t f16_bits(float x) { return __half_as_ushort(__float2half_rn(x)); }
+__device__ __forceinline__ float f16_val(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) { return __uint_as_float(((uint32_t)b) << 16); }
+
+// Device status word: first nonzero code wins (atomicCAS from 0).
+__device__ __forceinline__ void set_status(int *status, int code) {
+    if (status) atomicCAS(status, 0, code);
+}
+
+// Row source: the reference feeds encoders f32 rows decoded from the model's
+// storage type (main.rs:397-406 via quant.rs:581 decode_row).
+struct RowSrc {
+    const void *ptr;
+    int src_type;  // SHC_SRC_F32 / SHC_SRC_F16 / SHC_SRC_BF16
+    int64_t ne0;
+    int64_t row_stride;  // elements between consecutive rows
+};
+
+// Load 8 consecutive source elements starting at (row, col) as f32.
+// col is a multiple of 8; the row base is 16-byte aligned for BF16/F16 and
+// 32-byte aligned for F32 (checked on the host before launch).
+__device__ __forceinline__ void load8(const RowSrc &s, int64_t row, int64_t col, float v[8]) {
+    if (s.src_type == SHC_SRC_BF16) {
+        const uint4 q = __ldg(reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(s.ptr) + row * s.row_stride + col));
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            v[2 * k] = __uint_as_float(w[k] << 16);
+            v[2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
+        }
+    } else if (s.src_type == SHC_SRC_F16) {
+        const uint4 q = __ldg(reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(s.ptr) + row * s.row_stride + col));
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            v[2 * k] = f16_val((uint16_t)(w[k] & 0xFFFF));
+            v[2 * k + 1] = f16_val((uint16_t)(w[k] >> 16));
+        }
+    } else {
+        const float4 *p = reinterpret_cast<const float4 *>(static_cast<const float *>(s.ptr) + row * s.row_stride + col);
+        const float4 a = __ldg(p), b = __ldg(p + 1);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    }
+}
+
+__device__ __forceinline__ float load1(const RowSrc &s, int64_t row, int64_t col) {
+    if (s.src_type == SHC_SRC_BF16) return bf16_bits_to_f32(static_cast<const uint16_t *>(s.ptr)[row * s.row_stride + col]);
+    if (s.src_type == SHC_SRC_F16) return f16_val(static_cast<const uint16_t *>(s.ptr)[row * s.row_stride + col]);
+    return static_cast<const float *>(s.ptr)[row * s.row_stride + col];
+}
+
+// imatrix.rs:124-141 row_slice, as a column-weight pointer for a global row
+// index (nullptr means "no imatrix": the per-type fallback weights apply).
+struct ImSrc {
+    const float *ptr;
+    int64_t len;
+    int64_t rows_per_mat;
+};
+__device__ __forceinline__ const float *im_row(const ImSrc &im, int64_t ne0, int64_t grow) {
+    if (!im.ptr) return nullptr;
+    if (im.len == ne0) return im.ptr;
+    if (im.rows_per_mat > 0 && im.len % ne0 == 0) {
+        int64_t mat = grow / im.rows_per_mat;
+        int64_t n_mats = im.len / ne0;
+        int64_t m = mat < n_mats - 1 ? mat : n_mats - 1;
+        return im.ptr + m * ne0;
+    }
+    return nullptr;
+}
+
+}  // namespace shc

@@ -1,0 +1,568 @@
+// K-quant and Q8_0 encoders for sm_100a.
+//
+// Parity contract: every kernel reproduces src/quant.rs bit for bit.  The
+// scale searches evaluate all candidate grids in parallel (one lane owns one
+// (sub-block, candidate) pair and folds its sums serially over the elements,
+// in the reference's order) and then reproduce the reference's sequential
+// selection: a strict `err < best_err` chain is an argmin with first-index
+// tie-break, computed with warp shuffles; the cross-multiplied
+// `sumlx^2 > best*suml2` chain of make_qx_quants is replayed serially.
+//
+// Work decomposition: one warp per 256-element super-block (grid-stride over
+// all super-blocks of the tensor), 128-bit loads of the source row into
+// registers/shared memory, the imatrix slice read through the read-only path.
+#include "kernels.cuh"
+
+namespace shc {
+
+// ---------------------------------------------------------------------------
+// Row sigma^2 (quant.rs:153-155): sequential f32 fold of x^2 over the whole
+// row, then / ne0.  One thread per row (the fold is order-dependent), rows
+// staged 32 x 64 per warp through shared memory so the global loads stay
+// coalesced; the next tile is loaded while the current one is summed.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) row_sigma2_kernel(RowSrc src, int64_t n_rows, float *out) {
+    __shared__ float tile[4][32][65];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int64_t rbase = ((int64_t)blockIdx.x * 4 + wid) * 32;
+    if (rbase >= n_rows) return;
+    const int64_t ne0 = src.ne0;
+    float v[8][8];
+    auto load_tile = [&](int64_t c0) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int r = i * 4 + (lane >> 3), c = (lane & 7) * 8;
+            if (rbase + r < n_rows && c0 + c < ne0) load8(src, rbase + r, c0 + c, v[i]);
+        }
+    };
+    auto store_tile = [&](int64_t c0) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int r = i * 4 + (lane >> 3), c = (lane & 7) * 8;
+            if (rbase + r < n_rows && c0 + c < ne0) {
+#pragma unroll
+                for (int k = 0; k < 8; k++) tile[wid][r][c + k] = v[i][k];
+            }
+        }
+    };
+    float s = 0.0f;
+    load_tile(0);
+    store_tile(0);
+    for (int64_t c0 = 0; c0 < ne0; c0 += 64) {
+        __syncwarp();
+        const bool more = c0 + 64 < ne0;
+        if (more) load_tile(c0 + 64);
+        const int nc = (int)(ne0 - c0 < 64 ? ne0 - c0 : 64);
+        const float *t = tile[wid][lane];
+        if (rbase + lane < n_rows) {
+            if (nc == 64) {
+#pragma unroll 16
+                for (int c = 0; c < 64; c++) s += t[c] * t[c];
+            } else {
+                for (int c = 0; c < nc; c++) s += t[c] * t[c];
+            }
+        }
+        __syncwarp();
+        if (more) store_tile(c0 + 64);
+    }
+    if (rbase + lane < n_rows) out[rbase + lane] = s / (float)ne0;
+}
+
+cudaError_t launch_row_sigma2(const RowSrc &src, int64_t n_rows, float *out, cudaStream_t st) {
+    if (n_rows <= 0) return cudaSuccess;
+    const int64_t blocks = (n_rows + 127) / 128;
+    row_sigma2_kernel<<<(unsigned)blocks, 128, 0, st>>>(src, n_rows, out);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void load_im8(const float *imr, int64_t col, float b[8]) {
+    if (imr) {
+        const float4 *p = reinterpret_cast<const float4 *>(imr + col);
+        const float4 a0 = __ldg(p), a1 = __ldg(p + 1);
+        b[0] = a0.x; b[1] = a0.y; b[2] = a0.z; b[3] = a0.w;
+        b[4] = a1.x; b[5] = a1.y; b[6] = a1.z; b[7] = a1.w;
+    } else {
+#pragma unroll
+        for (int k = 0; k < 8; k++) b[k] = 1.0f;
+    }
+}
+
+// Store nbytes of a shared-memory staged block to global memory, 16 B per
+// lane when both ends are 16-byte aligned, else 2 B or 1 B per lane.
+__device__ __forceinline__ void store_block(uint8_t *dstp, const uint8_t *sp, int nbytes, bool aligned16, int lane) {
+    if (aligned16 && (nbytes & 15) == 0 && ((uintptr_t)dstp & 15) == 0) {
+        for (int i = lane; i < nbytes / 16; i += 32)
+            reinterpret_cast<uint4 *>(dstp)[i] = reinterpret_cast<const uint4 *>(sp)[i];
+    } else if ((nbytes & 1) == 0 && ((uintptr_t)dstp & 1) == 0) {
+        for (int i = lane; i < nbytes / 2; i += 32)
+            reinterpret_cast<uint16_t *>(dstp)[i] = reinterpret_cast<const uint16_t *>(sp)[i];
+    } else {
+        for (int i = lane; i < nbytes; i += 32) dstp[i] = sp[i];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Q8_0 (quant.rs:159-169): per 32-block amax, d = amax/127, q = round(x/d).
+// HBM-bound.  A warp handles 8 blocks (256 elements) per group, 4 lanes per
+// block, 8 elements per lane; groups are flat over the tensor's blocks.
+// ---------------------------------------------------------------------------
+constexpr int kQ80Unroll = 4;
+
+__global__ void __launch_bounds__(256) enc_q8_0_kernel(EncArgs a) {
+    __shared__ __align__(16) uint8_t s_out[8][kQ80Unroll][272];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int64_t bpr = a.src.ne0 >> 5;
+    const int64_t nblk = a.n_rows * bpr;
+    const int64_t ngrp = (nblk + 7) >> 3;
+    const int64_t stride = (int64_t)gridDim.x * 8 * kQ80Unroll;
+    for (int64_t g0 = ((int64_t)blockIdx.x * 8 + wid) * kQ80Unroll; g0 < ngrp; g0 += stride) {
+        float v[kQ80Unroll][8];
+#pragma unroll
+        for (int u = 0; u < kQ80Unroll; u++) {
+            const int64_t blk = (g0 + u) * 8 + (lane >> 2);
+            if (g0 + u < ngrp && blk < nblk) {
+                const int64_t row = blk / bpr;
+                const int64_t col = (blk - row * bpr) * 32 + (lane & 3) * 8;
+                load8(a.src, row, col, v[u]);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 8; k++) v[u][k] = 0.0f;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kQ80Unroll; u++) {
+            float amax = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 8; k++) amax = rmaxf(amax, fabsf(v[u][k]));
+            amax = rmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+            amax = rmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+            const float d = amax / 127.0f;
+            const float id = d > 0.0f ? 1.0f / d : 0.0f;
+            uint8_t *o = &s_out[wid][u][(lane >> 2) * 34];
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                o[2 + (lane & 3) * 8 + k] = (uint8_t)(int8_t)clampi(nearest_int(v[u][k] * id), -127, 127);
+            if ((lane & 3) == 0) {
+                const uint16_t h = f16_bits(d);
+                o[0] = (uint8_t)(h & 0xFF);
+                o[1] = (uint8_t)(h >> 8);
+            }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int u = 0; u < kQ80Unroll; u++) {
+            const int64_t blk0 = (g0 + u) * 8;
+            if (g0 + u < ngrp) {
+                const int nb = (int)(nblk - blk0 < 8 ? nblk - blk0 : 8);
+                store_block(a.dst + blk0 * 34, s_out[wid][u], nb * 34, a.dst_aligned16 && nb == 8, lane);
+            }
+        }
+        __syncwarp();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Q6_K (quant.rs:231-291) with make_qx_quants(nmax=32) (quant.rs:34-73) per
+// 16-element sub-block.  Two lanes per sub-block split the 19 candidate
+// grids; the selection chain is replayed serially from shared memory.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) enc_q6_k_kernel(EncArgs a) {
+    __shared__ float s_x[8][16 * 17];
+    __shared__ float s_w[8][16 * 17];
+    __shared__ float2 s_cand[8][16][20];
+    __shared__ float s_scale[8][16];
+    __shared__ __align__(16) uint8_t s_out[8][224];
+    __shared__ uint8_t s_l[8][256];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int s = lane >> 1, q = lane & 1;
+    const int64_t ne0 = a.src.ne0, nsb = ne0 >> 8, total = a.n_rows * nsb;
+    for (int64_t g = (int64_t)blockIdx.x * 8 + wid; g < total; g += (int64_t)gridDim.x * 8) {
+        const int64_t row = g / nsb;
+        const int64_t sbi = g - row * nsb;
+        const int64_t col0 = sbi << 8;
+        const float sig = a.sigma2[row];
+        const float *imr = im_row(a.im, ne0, a.row0 + row * a.row_step);
+        float v[8], base[8];
+        load8(a.src, row, col0 + lane * 8, v);
+        load_im8(imr, col0 + lane * 8, base);
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            s_x[wid][s * 17 + q * 8 + k] = v[k];
+            s_w[wid][s * 17 + q * 8 + k] = base[k] * sqrtf(sig + v[k] * v[k]);
+        }
+        __syncwarp();
+        float x[16], w[16], wx[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            x[i] = s_x[wid][s * 17 + i];
+            w[i] = s_w[wid][s * 17 + i];
+            wx[i] = w[i] * x[i];
+        }
+        // make_qx_quants: max |x| (first strict maximum wins)
+        float amax = 0.0f, mx = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            const float av = fabsf(x[i]);
+            if (av > amax) { amax = av; mx = x[i]; }
+        }
+        const bool live = !(amax < kGroupMaxEps);
+        if (live) {
+            const int is0 = q == 0 ? -9 : 1;
+            const int ncand = q == 0 ? 10 : 9;
+            for (int t = 0; t < ncand; t++) {
+                const int is = is0 + t;
+                const float iscale = -(32.0f + 0.1f * (float)is) / mx;
+                float sumlx = 0.0f, suml2 = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    const float l = round_clamp_f(iscale * x[i], -32.0f, 31.0f);
+                    sumlx += wx[i] * l;
+                    suml2 += w[i] * (l * l);
+                }
+                s_cand[wid][s][is + 9] = make_float2(sumlx, suml2);
+            }
+        }
+        __syncwarp();
+        float best_scale = 0.0f;
+        if (live && q == 0) {
+            float best = 0.0f;
+            bool first = true;
+            for (int c = 0; c < 19; c++) {
+                const float2 cs = s_cand[wid][s][c];
+                if (cs.y > 0.0f && (first || cs.x * cs.x > best * cs.y)) {
+                    const float sc = cs.x / cs.y;
+                    best_scale = sc;
+                    best = sc * cs.x;
+                    first = false;
+                }
+            }
+            s_scale[wid][s] = best_scale;
+        } else if (!live && q == 0) {
+            s_scale[wid][s] = 0.0f;
+        }
+        __syncwarp();
+        best_scale = s_scale[wid][s];
+        float max_abs = 0.0f, max_scale = 0.0f;
+#pragma unroll
+        for (int sb = 0; sb < 16; sb++) {
+            const float sv = s_scale[wid][sb];
+            if (fabsf(sv) > max_abs) { max_abs = fabsf(sv); max_scale = sv; }
+        }
+        uint8_t *o = s_out[wid];
+        if (max_abs < kGroupMaxEps) {
+            for (int i = lane; i < 210; i += 32) o[i] = 0;
+        } else {
+            const float iscale = -128.0f / max_scale;
+            const float d = 1.0f / iscale;
+            const int8_t qsc = (int8_t)(uint8_t)(min(nearest_int(iscale * best_scale), 127) & 0xFF);
+            const float dd = d * (float)qsc;
+            // lane owns elements lane*8..lane*8+7 = sub-block s, offset q*8
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const int l = dd == 0.0f ? 32 : clampi(nearest_int(v[k] / dd), -32, 31) + 32;
+                s_l[wid][lane * 8 + k] = (uint8_t)l;
+            }
+            if (q == 0) o[192 + s] = (uint8_t)qsc;
+            if (lane == 0) {
+                const uint16_t h = f16_bits(d);
+                o[208] = (uint8_t)(h & 0xFF);
+                o[209] = (uint8_t)(h >> 8);
+            }
+            __syncwarp();
+            const uint8_t *L = s_l[wid];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const uint8_t *lo = L + h * 128;
+                const int l = lane;
+                o[h * 64 + l] = (uint8_t)((lo[l] & 0xF) | ((lo[l + 64] & 0xF) << 4));
+                o[h * 64 + 32 + l] = (uint8_t)((lo[l + 32] & 0xF) | ((lo[l + 96] & 0xF) << 4));
+                o[128 + h * 32 + l] = (uint8_t)((lo[l] >> 4) | ((lo[l + 32] >> 4) << 2) | ((lo[l + 64] >> 4) << 4) |
+                                                ((lo[l + 96] >> 4) << 6));
+            }
+        }
+        __syncwarp();
+        store_block(a.dst + row * a.dst_row_bytes + sbi * 210, o, 210, false, lane);
+        __syncwarp();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Q4_K / Q5_K (quant.rs:294-379) with make_qkx3_quants (quant.rs:77-141,
+// rmin -0.9, rdelta 0.05, 37 grids) per 32-element sub-block.  Four lanes per
+// sub-block: lane q evaluates jobs j = q, q+4, ..., j < 38, where j < 37 is
+// grid `is = j` and j == 37 is the initial nmax/(vmax-vmin) grid.
+// ---------------------------------------------------------------------------
+template <int NMAX>
+__global__ void __launch_bounds__(256) enc_qk45_kernel(EncArgs a) {
+    constexpr int BB = NMAX == 31 ? 176 : 144;
+    constexpr float FN = (float)NMAX;
+    __shared__ float s_x[8][8 * 33];
+    __shared__ float s_w[8][8 * 33];
+    __shared__ __align__(16) uint8_t s_out[8][BB];
+    __shared__ uint8_t s_l[8][256];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int s = lane >> 2, q = lane & 3;
+    const int64_t ne0 = a.src.ne0, nsb = ne0 >> 8, total = a.n_rows * nsb;
+    for (int64_t g = (int64_t)blockIdx.x * 8 + wid; g < total; g += (int64_t)gridDim.x * 8) {
+        const int64_t row = g / nsb;
+        const int64_t sbi = g - row * nsb;
+        const int64_t col0 = sbi << 8;
+        const float sig = a.sigma2[row];
+        const float *imr = im_row(a.im, ne0, a.row0 + row * a.row_step);
+        float v[8], base[8];
+        load8(a.src, row, col0 + lane * 8, v);
+        load_im8(imr, col0 + lane * 8, base);
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            s_x[wid][s * 33 + q * 8 + k] = v[k];
+            s_w[wid][s * 33 + q * 8 + k] = base[k] * sqrtf(sig + v[k] * v[k]);
+        }
+        __syncwarp();
+        float x[32], w[32];
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+            x[i] = s_x[wid][s * 33 + i];
+            w[i] = s_w[wid][s * 33 + i];
+        }
+        // make_qkx3_quants
+        float vmin = INFINITY, vmax = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 32; i++) vmin = rminf(vmin, x[i]);
+        vmin = rminf(vmin, 0.0f);
+#pragma unroll
+        for (int i = 0; i < 32; i++) vmax = rmaxf(vmax, x[i]);
+        // Shuffles below run on every lane, so the per-lane candidate loop
+        // is the only code inside the data-dependent branch.
+        const bool degen = vmax <= vmin;
+        const float range = vmax - vmin;
+        const float iscale0 = FN / range;
+        const float scale0 = 1.0f / iscale0;
+        float init_err = 0.0f, best_e = 0.0f, best_s = 0.0f, best_m = 0.0f;
+        int best_j = -1;
+        if (!degen) {
+            float sum_w = 0.0f, sum_x = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+                sum_w += w[i];
+                sum_x += w[i] * x[i];
+            }
+            for (int j = q; j < 38; j += 4) {
+                const float iscale = j == 37 ? iscale0 : (-0.9f + 0.05f * (float)j + FN) / range;
+                float sl = 0.0f, sl2 = 0.0f, sxl = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 32; i++) {
+                    const float l = round_clamp0_f(iscale * (x[i] - vmin), FN);
+                    const float wl = w[i] * l;
+                    sl += wl;
+                    sl2 += w[i] * (l * l);
+                    sxl += wl * x[i];
+                }
+                float ts, tm;
+                bool valid;
+                if (j == 37) {
+                    ts = scale0;
+                    tm = vmin;
+                    valid = true;
+                } else {
+                    const float D = sum_w * sl2 - sl * sl;
+                    valid = D > 0.0f;
+                    ts = (sum_w * sxl - sum_x * sl) / D;
+                    tm = (sl2 * sum_x - sl * sxl) / D;
+                    if (tm > 0.0f) {
+                        tm = 0.0f;
+                        ts = sl2 > 0.0f ? sxl / sl2 : 0.0f;
+                    }
+                }
+                if (valid) {
+                    float err = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < 32; i++) {
+                        const float l = round_clamp0_f(iscale * (x[i] - vmin), FN);
+                        const float diff = ts * l + tm - x[i];
+                        err += w[i] * diff * diff;
+                    }
+                    if (j == 37) {
+                        init_err = err;
+                    } else if (err == err && (best_j < 0 || err < best_e)) {
+                        best_e = err;
+                        best_j = j;
+                        best_s = ts;
+                        best_m = tm;
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        // argmin (err, j) over the four lanes of this sub-block
+#pragma unroll
+        for (int off = 1; off <= 2; off <<= 1) {
+            const float oe = __shfl_xor_sync(0xffffffffu, best_e, off);
+            const int oj = __shfl_xor_sync(0xffffffffu, best_j, off);
+            const float os = __shfl_xor_sync(0xffffffffu, best_s, off);
+            const float om = __shfl_xor_sync(0xffffffffu, best_m, off);
+            if (oj >= 0 && (best_j < 0 || oe < best_e || (oe == best_e && oj < best_j))) {
+                best_e = oe;
+                best_j = oj;
+                best_s = os;
+                best_m = om;
+            }
+        }
+        init_err = __shfl_sync(0xffffffffu, init_err, (lane & ~3) | 1);
+        float scale, mn;
+        if (degen) {
+            scale = 0.0f;
+            mn = vmin;
+        } else if (best_j >= 0 && best_e < init_err) {
+            scale = best_s;
+            mn = best_m;
+        } else {
+            scale = scale0;
+            mn = vmin;
+        }
+        const float mins_s = -mn;
+        float max_scale = scale, max_min = mins_s;
+#pragma unroll
+        for (int off = 4; off <= 16; off <<= 1) {
+            max_scale = rmaxf(max_scale, __shfl_xor_sync(0xffffffffu, max_scale, off));
+            max_min = rmaxf(max_min, __shfl_xor_sync(0xffffffffu, max_min, off));
+        }
+        max_scale = rmaxf(0.0f, max_scale);
+        max_min = rmaxf(0.0f, max_min);
+        const float inv_scale = max_scale > 0.0f ? 63.0f / max_scale : 0.0f;
+        const float inv_min = max_min > 0.0f ? 63.0f / max_min : 0.0f;
+        const int lsq = clampi(nearest_int(inv_scale * scale), 0, 63);
+        const int lmq = clampi(nearest_int(inv_min * mins_s), 0, 63);
+        const float d = max_scale / 63.0f;
+        const float dmin = max_min / 63.0f;
+        const float dsub = d * (float)lsq;
+        const float msub = dmin * (float)lmq;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int l = dsub == 0.0f ? 0 : clampi(nearest_int((v[k] + msub) / dsub), 0, NMAX);
+            s_l[wid][lane * 8 + k] = (uint8_t)l;
+        }
+        int lsq_all[8], lmq_all[8];
+#pragma unroll
+        for (int t = 0; t < 8; t++) {
+            lsq_all[t] = __shfl_sync(0xffffffffu, lsq, t * 4);
+            lmq_all[t] = __shfl_sync(0xffffffffu, lmq, t * 4);
+        }
+        uint8_t *o = s_out[wid];
+        if (lane < 4) {
+            const int t = lane;
+            o[4 + t] = (uint8_t)(lsq_all[t] | ((lsq_all[t + 4] >> 4) << 6));
+            o[8 + t] = (uint8_t)(lmq_all[t] | ((lmq_all[t + 4] >> 4) << 6));
+            o[12 + t] = (uint8_t)((lsq_all[t + 4] & 0xF) | ((lmq_all[t + 4] & 0xF) << 4));
+        }
+        if (lane == 0) {
+            const uint16_t hd = f16_bits(d), hm = f16_bits(dmin);
+            o[0] = (uint8_t)(hd & 0xFF);
+            o[1] = (uint8_t)(hd >> 8);
+            o[2] = (uint8_t)(hm & 0xFF);
+            o[3] = (uint8_t)(hm >> 8);
+        }
+        __syncwarp();
+        const uint8_t *L = s_l[wid];
+        if (NMAX == 31) {
+            uint8_t qh = 0;
+#pragma unroll
+            for (int chunk = 0; chunk < 4; chunk++) {
+                if (L[chunk * 64 + lane] >= 16) qh |= (uint8_t)(1u << (chunk * 2));
+                if (L[chunk * 64 + 32 + lane] >= 16) qh |= (uint8_t)(2u << (chunk * 2));
+            }
+            o[16 + lane] = qh;
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                const int b = lane * 4 + t, chunk = b >> 5, l = b & 31;
+                o[48 + b] = (uint8_t)((L[chunk * 64 + l] & 0xF) | ((L[chunk * 64 + 32 + l] & 0xF) << 4));
+            }
+        } else {
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                const int b = lane * 4 + t, chunk = b >> 5, l = b & 31;
+                o[16 + b] = (uint8_t)((L[chunk * 64 + l] & 0xF) | (L[chunk * 64 + 32 + l] << 4));
+            }
+        }
+        __syncwarp();
+        store_block(a.dst + row * a.dst_row_bytes + sbi * BB, o, BB, a.dst_aligned16 != 0, lane);
+        __syncwarp();
+    }
+}
+
+template __global__ void enc_qk45_kernel<15>(EncArgs);
+template __global__ void enc_qk45_kernel<31>(EncArgs);
+
+// ---------------------------------------------------------------------------
+// Elementwise encodings (quant.rs:546-560): F32 copy, F16 round-to-nearest-
+// even, BF16 by truncating the low 16 bits (`(v.to_bits() >> 16) as u16`).
+// ---------------------------------------------------------------------------
+__global__ void enc_plain_kernel(uint32_t type, EncArgs a) {
+    const int64_t ne0 = a.src.ne0, n = a.n_rows * ne0;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = e / ne0, col = e - row * ne0;
+        const float x = load1(a.src, row, col);
+        if (type == SHC_TYPE_F32) {
+            reinterpret_cast<float *>(a.dst)[e] = x;
+        } else {
+            const uint16_t h = type == SHC_TYPE_F16 ? f16_bits(x) : (uint16_t)(__float_as_uint(x) >> 16);
+            reinterpret_cast<uint16_t *>(a.dst)[e] = h;
+        }
+    }
+}
+
+cudaError_t launch_plain(uint32_t type, const EncArgs &a, int num_sms, cudaStream_t st) {
+    const int64_t n = a.n_rows * a.src.ne0;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > (int64_t)num_sms * 16) blocks = (int64_t)num_sms * 16;
+    if (blocks < 1) blocks = 1;
+    enc_plain_kernel<<<(unsigned)blocks, 256, 0, st>>>(type, a);
+    return cudaGetLastError();
+}
+
+// Grid for the persistent warp-per-super-block kernels: enough CTAs to fill
+// every SM at the occupancy the kernel reaches, never more than the work.
+static unsigned persistent_grid(const void *fn, int threads, int num_sms, int64_t work_warps) {
+    int per_sm = 1;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, 0);
+    if (per_sm < 1) per_sm = 1;
+    int64_t want = (work_warps + threads / 32 - 1) / (threads / 32);
+    int64_t cap = (int64_t)num_sms * per_sm;
+    if (want > cap) want = cap;
+    if (want < 1) want = 1;
+    return (unsigned)want;
+}
+
+cudaError_t launch_kquant(uint32_t type, const EncArgs &a, int num_sms, cudaStream_t st) {
+    const int64_t nsb = a.src.ne0 / 256;
+    switch (type) {
+    case SHC_TYPE_Q8_0: {
+        const int64_t ngrp = (a.n_rows * (a.src.ne0 / 32) + 7) / 8;
+        unsigned grid = persistent_grid((const void *)enc_q8_0_kernel, 256, num_sms, (ngrp + kQ80Unroll - 1) / kQ80Unroll);
+        enc_q8_0_kernel<<<grid, 256, 0, st>>>(a);
+        break;
+    }
+    case SHC_TYPE_Q6_K: {
+        unsigned grid = persistent_grid((const void *)enc_q6_k_kernel, 256, num_sms, a.n_rows * nsb);
+        enc_q6_k_kernel<<<grid, 256, 0, st>>>(a);
+        break;
+    }
+    case SHC_TYPE_Q4_K: {
+        unsigned grid = persistent_grid((const void *)enc_qk45_kernel<15>, 256, num_sms, a.n_rows * nsb);
+        enc_qk45_kernel<15><<<grid, 256, 0, st>>>(a);
+        break;
+    }
+    case SHC_TYPE_Q5_K: {
+        unsigned grid = persistent_grid((const void *)enc_qk45_kernel<31>, 256, num_sms, a.n_rows * nsb);
+        enc_qk45_kernel<31><<<grid, 256, 0, st>>>(a);
+        break;
+    }
+    default:
+        return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace shc

@@ -1,0 +1,208 @@
+"""GPU parity: the CUDA encoders, decoders and fused error pass against the
+CPU oracle, byte for byte (codes), bit for bit (decoded f32, f64 errors).
+
+All calls go through the C ABI (libshoehorn_cuda.so via shoehorn_b200)."""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests.helpers import (BF16, F16, F32, IQ, KQUANT, NAMES, PLAIN, bf16_bits_to_f32, edge_rows, f32_to_bf16_bits,
+                           student_rows, sweep_rows)
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+import shoehorn_b200 as sh  # noqa: E402
+
+
+def supported(types):
+    return [t for t in types if sh.type_supported(t)]
+
+
+ENC_TYPES = supported(KQUANT + IQ) + PLAIN
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def gpu_encode(ctx, ty, bits, im=None, rows_per_mat=0, row0=0):
+    src = dev(bits.view(np.int16))
+    imt = None if im is None else dev(im)
+    out = ctx.encode_rows(ty, src, imt, rows_per_mat=rows_per_mat, row0=row0, sync=True)
+    return out.cpu().numpy()
+
+
+def oracle_encode(ty, bits, im=None, rows_per_mat=0, row0=0):
+    if row0 == 0:
+        return O.encode_tensor_bf16(ty, bits, im, rows_per_mat=rows_per_mat)
+    # shift the imatrix matrix selection by row0 (imatrix.rs:124 with global rows)
+    x = bf16_bits_to_f32(bits)
+    ne0 = bits.shape[1]
+    rows = []
+    for r in range(bits.shape[0]):
+        g = row0 + r
+        ims = None
+        if im is not None:
+            if im.size == ne0:
+                ims = im
+            elif rows_per_mat > 0 and im.size % ne0 == 0:
+                m = min(g // rows_per_mat, im.size // ne0 - 1)
+                ims = im[m * ne0:(m + 1) * ne0]
+        rows.append(O.encode_row(ty, x[r], ims))
+    return np.stack(rows)
+
+
+def assert_bytes_equal(got, want, ty):
+    if not np.array_equal(got, want):
+        bad = np.argwhere(got != want)
+        r, c = bad[0]
+        raise AssertionError(f"{NAMES[ty]}: {len(bad)} bytes differ; first at row {r} byte {c}: "
+                             f"gpu {got[r, c]} oracle {want[r, c]}")
+
+
+@pytest.mark.parametrize("ty", ENC_TYPES, ids=lambda t: NAMES[t])
+def test_encode_matches_oracle_sweep_rows(ctx, ty):
+    bits, im = sweep_rows(48, 2048, seed=100 + ty)
+    assert_bytes_equal(gpu_encode(ctx, ty, bits, im), oracle_encode(ty, bits, im), ty)
+
+
+@pytest.mark.parametrize("ty", ENC_TYPES, ids=lambda t: NAMES[t])
+def test_encode_matches_oracle_student_rows_no_imatrix(ctx, ty):
+    bits, _ = student_rows(32, 4096, seed=200 + ty)
+    assert_bytes_equal(gpu_encode(ctx, ty, bits, None), oracle_encode(ty, bits, None), ty)
+
+
+@pytest.mark.parametrize("ty", ENC_TYPES, ids=lambda t: NAMES[t])
+def test_encode_matches_oracle_edge_rows(ctx, ty):
+    x = edge_rows(1024)
+    bits = f32_to_bf16_bits(x)
+    im = np.ones(1024, np.float32)
+    assert_bytes_equal(gpu_encode(ctx, ty, bits, im), oracle_encode(ty, bits, im), ty)
+    assert_bytes_equal(gpu_encode(ctx, ty, bits, None), oracle_encode(ty, bits, None), ty)
+
+
+@pytest.mark.parametrize("ty", supported(KQUANT + IQ), ids=lambda t: NAMES[t])
+def test_expert_imatrix_slicing_and_row0(ctx, ty):
+    """imatrix.rs:124-141: an imatrix of n_mats*ne0 selects matrix row/rows_per_mat."""
+    bits, _ = sweep_rows(24, 512, seed=300 + ty)
+    rng = np.random.default_rng(ty)
+    im3 = np.exp(rng.normal(0, 1, 3 * 512)).astype(np.float32)
+    got = gpu_encode(ctx, ty, bits, im3, rows_per_mat=8, row0=5)
+    want = oracle_encode(ty, bits, im3, rows_per_mat=8, row0=5)
+    assert_bytes_equal(got, want, ty)
+    # an imatrix whose length is not a multiple of ne0 means "no imatrix"
+    got = gpu_encode(ctx, ty, bits, im3[:700], rows_per_mat=8)
+    assert_bytes_equal(got, oracle_encode(ty, bits, None), ty)
+
+
+@pytest.mark.parametrize("src_dtype", ["f32", "f16"])
+def test_f32_and_f16_sources(ctx, src_dtype):
+    bits, im = sweep_rows(16, 1024, seed=7)
+    x = bf16_bits_to_f32(bits)
+    if src_dtype == "f16":
+        x = x.astype(np.float16).astype(np.float32)
+    src = dev(x if src_dtype == "f32" else x.astype(np.float16))
+    for ty in supported(KQUANT + IQ):
+        got = ctx.encode_rows(ty, src, dev(im), sync=True).cpu().numpy()
+        want = np.stack([O.encode_row(ty, r, im) for r in x])
+        assert_bytes_equal(got, want, ty)
+
+
+@pytest.mark.parametrize("ty", supported(KQUANT + IQ) + [F16, BF16, F32], ids=lambda t: NAMES[t])
+def test_decode_matches_oracle(ctx, ty):
+    bits, im = student_rows(8, 1024, seed=400 + ty)
+    x = bf16_bits_to_f32(bits)
+    codes = np.stack([O.encode_row(ty, r, im) for r in x])
+    got = ctx.decode_rows(ty, dev(codes), 1024, sync=True).cpu().numpy()
+    want = np.stack([O.decode_row(ty, c, 1024) for c in codes])
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("row_step", [1, 3])
+def test_row_errors_match_oracle(ctx, row_step):
+    bits, im = sweep_rows(20, 1024, seed=500)
+    types = supported(KQUANT + IQ) + [F16]
+    got = ctx.row_errors(types, dev(bits.view(np.int16)), dev(im), row_step=row_step).cpu().numpy()
+    for t, ty in enumerate(types):
+        want = O.row_errors_bf16(ty, bits, im, row_step=row_step)
+        assert np.array_equal(got[t].view(np.uint64), want.view(np.uint64)), NAMES[ty]
+
+
+def test_row_errors_without_imatrix_and_edges(ctx):
+    x = edge_rows(512)
+    bits = f32_to_bf16_bits(x)
+    types = supported(KQUANT + IQ) + [F16, BF16]
+    got = ctx.row_errors(types, dev(bits.view(np.int16)), None).cpu().numpy()
+    for t, ty in enumerate(types):
+        want = O.row_errors_bf16(ty, bits, None)
+        assert np.array_equal(got[t].view(np.uint64), want.view(np.uint64)), NAMES[ty]
+
+
+def test_row_api_mirrors_reference(ctx):
+    x = bf16_bits_to_f32(sweep_rows(1, 512, seed=9)[0])[0]
+    for ty in supported(KQUANT):
+        enc = sh.encode_row(ty, x)
+        assert np.array_equal(enc, O.encode_row(ty, x))
+        assert np.array_equal(sh.decode_row(ty, enc, 512).view(np.uint32), O.decode_row(ty, enc, 512).view(np.uint32))
+        assert sh.row_error(ty, x) == O.row_error(ty, x)
+    with pytest.raises(ValueError):
+        sh.encode_row(sh.GgmlType.Q4_K, np.zeros(100, np.float32))  # ragged row, like the reference's assert
+
+
+@pytest.mark.parametrize("pinned", [False, True])
+def test_host_entry_point_matches_device(ctx, pinned):
+    bits, im = sweep_rows(300, 1024, seed=21)
+    for ty in supported(KQUANT + IQ):
+        want = oracle_encode(ty, bits, im)
+        if pinned:
+            src = torch.from_numpy(bits.view(np.int16)).pin_memory()
+            out = torch.empty(want.shape, dtype=torch.uint8).pin_memory()
+            ctx.encode_tensor_host(ty, src, im, out=out)
+            got = out.numpy()
+        else:
+            got = ctx.encode_tensor_host(ty, bits, im)
+        assert_bytes_equal(got, want, ty)
+
+
+def test_host_row_errors_match_oracle(ctx):
+    bits, im = sweep_rows(37, 1024, seed=31)
+    types = supported(KQUANT + IQ) + [F16]
+    got = ctx.row_errors_host(types, bits, im, row_step=4)
+    for t, ty in enumerate(types):
+        want = O.row_errors_bf16(ty, bits, im, row_step=4)
+        assert np.array_equal(got[t].view(np.uint64), want.view(np.uint64)), NAMES[ty]
+
+
+def test_sync_reports_clean_status(ctx):
+    ctx.sync()
+    assert ctx.launch_count() > 0
+
+
+# ---- full encoder-sweep size (4096 x 14336): sampled rows vs the oracle, plus
+# size-independent properties over every row ----
+@pytest.fixture(scope="module")
+def big_tensor():
+    bits, im = sweep_rows(4096, 14336, seed=20261201)
+    return bits, im
+
+
+@pytest.mark.parametrize("ty", supported(KQUANT + IQ), ids=lambda t: NAMES[t])
+def test_full_size_encode(ctx, big_tensor, ty):
+    bits, im = big_tensor
+    src = dev(bits.view(np.int16))
+    imt = dev(im)
+    a = ctx.encode_rows(ty, src, imt, sync=True)
+    b = ctx.encode_rows(ty, src, imt, sync=True)
+    assert torch.equal(a, b)  # deterministic
+    codes = a.cpu().numpy()
+    rng = np.random.default_rng(ty)
+    rows = np.sort(rng.choice(4096, size=6, replace=False))
+    rows[0], rows[-1] = 0, 4095
+    want = O.encode_tensor_bf16(ty, bits[rows], im)
+    assert_bytes_equal(codes[rows], want, ty)
+    # decode of every row stays within the reference's round-trip tolerance band
+    dec = ctx.decode_rows(ty, a, 14336, sync=True)
+    x = src.view(torch.bfloat16).float()
+    rel = ((dec - x).pow(2).mean() / x.pow(2).mean()).sqrt().item()
+    assert np.isfinite(rel) and rel < 0.8
