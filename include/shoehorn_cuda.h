@@ -137,6 +137,38 @@ int shc_row_errors_host(shc_ctx *ctx, const uint32_t *types, int n_types, uint32
                         int64_t n_rows, int64_t ne0, const float *host_imatrix, int64_t imatrix_len,
                         int64_t rows_per_mat, int64_t row0, int64_t row_step, double *err, int64_t timeout_ms);
 
+/* Allocation-free encode for Q4_K, Q5_K and Q6_K.  No counterpart in the
+ * reference (its CPU encoders allocate freely).
+ *
+ * shc_encode_rows draws its per-row sigma^2 scratch from CUDA's
+ * stream-ordered allocator.  Some callers cannot allocate device memory at
+ * the point where they encode: a host program whose own allocator reserved
+ * the GPU's memory up front (a cudaMalloc from the library would then fail
+ * or fragment that pool), or one that must not risk the device-wide
+ * synchronisation cudaMalloc/cudaFree can cause in the middle of its work.
+ * This entry point makes no allocation at all; its scratch is a fixed buffer
+ * of SHC_NOALLOC_MAX_ROWS floats (256 KiB) compiled into the library, held
+ * on every GPU that loads the library until the process exits.
+ *
+ *  - Runs on the calling thread's current CUDA device, asynchronously on
+ *    `stream`; src, imatrix and dst are caller-owned device pointers with the
+ *    same meaning and the same output bytes as shc_encode_rows.
+ *  - The first call on each device looks up the buffer's device address;
+ *    make that first call before any stream capture on that device.
+ *  - n_rows > SHC_NOALLOC_MAX_ROWS returns SHC_ETOOLARGE and launches
+ *    nothing; split larger tensors into row ranges (row0 keeps the imatrix
+ *    selection right).
+ *  - One buffer is shared by every call on a device and keeps the last
+ *    call's contents.  Each call writes every entry it reads before reading
+ *    it, so nothing needs clearing; but calls whose work overlaps on the GPU
+ *    (different streams or host threads) race on it: issue them on one
+ *    stream. */
+#define SHC_ETOOLARGE -8
+#define SHC_NOALLOC_MAX_ROWS 65536
+int shc_encode_rows_noalloc(uint32_t ggml_type, uint32_t src_type, const void *src, int64_t n_rows, int64_t ne0,
+                            const float *imatrix, int64_t imatrix_len, int64_t rows_per_mat, int64_t row0,
+                            uint8_t *dst, void *stream);
+
 /* Number of kernel launches issued by this context so far (instrumentation
  * for benchmarks). */
 int64_t shc_launch_count(const shc_ctx *ctx);

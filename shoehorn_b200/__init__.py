@@ -20,7 +20,7 @@ SHC_OK = 0
 _STATUS = {
     0: "ok", -1: "invalid argument", -2: "CUDA runtime error", -3: "IQ point off the lattice",
     -4: "IQ neighbour search found no finite candidate", -5: "timed out", -6: "out of memory",
-    -7: "no usable sm_100 device",
+    -7: "no usable sm_100 device", -8: "request exceeds the fixed scratch of shc_encode_rows_noalloc",
 }
 
 SRC_F32, SRC_F16, SRC_BF16 = 0, 1, 30

@@ -14,7 +14,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libshoehorn_cuda.so")
 BUILD_DIR = os.path.join(HERE, "_build")
-SOURCES = ["api.cu", "kquant.cu", "decode.cu", "iq.cu", "iq_host.cpp"]
+SOURCES = ["api.cu", "kquant.cu", "decode.cu", "iq.cu", "iq_host.cpp", "noalloc.cu"]
 HEADERS = ["common.cuh", "kernels.cuh", "iq_host.h", "iq_tables.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FP = ["-fmad=false", "-prec-div=true", "-prec-sqrt=true", "-ftz=false"]

@@ -210,6 +210,7 @@ const char *shc_status_string(int s) {
     case SHC_ETIMEOUT: return "timed out";
     case SHC_ENOMEM: return "out of memory";
     case SHC_ENODEV: return "no usable sm_100 device";
+    case SHC_ETOOLARGE: return "request exceeds the fixed scratch of shc_encode_rows_noalloc";
     default: return "unknown status";
     }
 }
