@@ -1,16 +1,790 @@
 // IQ codebook encoders (src/quant_iq.rs) for sm_100a.
+//
+// One warp per 256-element super-block.  The per-block scale trials of the
+// reference are independent given the block's weights, so every
+// (block, trial) pair is a lane job; the trials' (sumqx, sumq2) go to shared
+// memory and the reference's sequential `sumqx^2 > best*sumq2` chain is then
+// replayed by one lane per block, which also re-runs the winning trial to
+// recover its lattice points (cheaper than keeping every trial's points).
+// Lattice lookups use the compact kmap staged in shared memory; neighbour
+// lists are read through the read-only cache.
+#include <cfloat>
+
+#include "iq_tables.h"
 #include "kernels.cuh"
 
 namespace shc {
 
+// ---------------------------------------------------------------------------
+// IQ4_NL / IQ4_XS (quant_iq.rs:1002-1157)
+// ---------------------------------------------------------------------------
+__device__ const float d_kv_f[16] = {-127.f, -104.f, -83.f, -65.f, -49.f, -35.f, -22.f, -10.f,
+                                     1.f,    13.f,   25.f,  38.f,  53.f,  69.f,  89.f,  113.f};
+
+// best_index_int8 (quant_iq.rs:1002-1024).  For x strictly inside
+// (v0, v15) the binary search ends at the unique mu with v[mu-1] <= x < v[mu];
+// the codebook values are integers, so v[k] <= x <=> v[k] <= floor(x) and
+// mu = 1 + cnt[floor(x)], with cnt[f] = #{k in 1..14 : v[k] <= f}.
+struct Iq4Lut {
+    float v[16];
+    uint8_t cnt[256];  // indexed by floor(x) + 128
+};
+
+__device__ __forceinline__ int best_index_iq4(const Iq4Lut &L, float x) {
+    if (x <= -127.0f) return 0;
+    if (x >= 113.0f) return 15;
+    if (x != x) return 15;  // the reference's search walks to the top for NaN
+    const int f = (int)floorf(x);
+    const int mu = 1 + L.cnt[f + 128];
+    return (x - L.v[mu - 1] < L.v[mu] - x) ? mu - 1 : mu;
+}
+
+__device__ void init_iq4_lut(Iq4Lut &L) {
+    for (int i = threadIdx.x; i < 16; i += blockDim.x) L.v[i] = d_kv_f[i];
+    for (int f = threadIdx.x; f < 256; f += blockDim.x) {
+        int c = 0;
+        for (int k = 1; k <= 14; k++) c += (d_kv_f[k] <= (float)(f - 128)) ? 1 : 0;
+        L.cnt[f] = (uint8_t)c;
+    }
+}
+
+// XS: a warp encodes one 256-element super-block (8 blocks of 32).
+// NL: a warp encodes 8 consecutive 32-element blocks (each its own super-block).
+template <bool XS>
+__global__ void __launch_bounds__(256) enc_iq4_kernel(EncArgs a) {
+    __shared__ Iq4Lut lut;
+    __shared__ float s_x[8][8 * 33];
+    __shared__ float s_w[8][8 * 33];
+    __shared__ float2 s_res[8][8][16];
+    __shared__ float s_scale[8][8];
+    __shared__ __align__(16) uint8_t s_out[8][144];
+    __shared__ uint8_t s_l[8][256];
+    init_iq4_lut(lut);
+    __syncthreads();
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int b = lane >> 2, q = lane & 3;
+    const int64_t ne0 = a.src.ne0;
+    const int64_t nunits = XS ? a.n_rows * (ne0 >> 8) : (a.n_rows * (ne0 >> 5) + 7) >> 3;
+    const int64_t bpr = ne0 >> 5;
+    const int64_t nblk = a.n_rows * bpr;
+    for (int64_t g = (int64_t)blockIdx.x * 8 + wid; g < nunits; g += (int64_t)gridDim.x * 8) {
+        // this lane group's 32-block: row and column
+        int64_t row, col;
+        bool valid = true;
+        if (XS) {
+            const int64_t nsb = ne0 >> 8;
+            row = g / nsb;
+            col = (g - row * nsb) * 256 + b * 32;
+        } else {
+            const int64_t blk = g * 8 + b;
+            valid = blk < nblk;
+            row = valid ? blk / bpr : 0;
+            col = valid ? (blk - row * bpr) * 32 : 0;
+        }
+        const float *imr = valid ? im_row(a.im, ne0, a.row0 + row * a.row_step) : nullptr;
+        float v[8], base[8];
+        if (valid) {
+            load8(a.src, row, col + q * 8, v);
+            if (imr) {
+#pragma unroll
+                for (int k = 0; k < 8; k++) base[k] = __ldg(imr + col + q * 8 + k);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; k++) v[k] = 0.0f;
+        }
+        float *xs = &s_x[wid][b * 33];
+#pragma unroll
+        for (int k = 0; k < 8; k++) xs[q * 8 + k] = v[k];
+        __syncwarp();
+        // sigma2 = 2 * (sequential sum of x^2 over the super-block) / size
+        float sig;
+        {
+            float s = 0.0f;
+            if (XS) {
+                for (int bb = 0; bb < 8; bb++)
+                    for (int i = 0; i < 32; i++) s += s_x[wid][bb * 33 + i] * s_x[wid][bb * 33 + i];
+                sig = 2.0f * s / 256.0f;
+            } else {
+                for (int i = 0; i < 32; i++) s += xs[i] * xs[i];
+                sig = 2.0f * s / 32.0f;
+            }
+        }
+        float *ws = &s_w[wid][b * 33];
+#pragma unroll
+        for (int k = 0; k < 8; k++) ws[q * 8 + k] = imr ? base[k] * sqrtf(sig + v[k] * v[k]) : v[k] * v[k];
+        __syncwarp();
+        float x[32], w[32];
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+            x[i] = xs[i];
+            w[i] = ws[i];
+        }
+        float amax = 0.0f, mx = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+            const float av = fabsf(x[i]);
+            if (av > amax) { amax = av; mx = x[i]; }
+        }
+        const bool live = !(amax < kGroupMaxEps);
+        if (live) {
+            // job 0: the initial grid d = -max/v0; jobs 1..15: itry = job - 8
+            for (int j = q; j < 16; j += 4) {
+                const float id = j == 0 ? 1.0f / (-mx / -127.0f) : ((float)(j - 8) + -127.0f) / mx;
+                float sumqx = 0.0f, sumq2 = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 32; i++) {
+                    const float qv = lut.v[best_index_iq4(lut, id * x[i])];
+                    const float wq = w[i] * qv;
+                    sumqx += wq * x[i];
+                    sumq2 += wq * qv;
+                }
+                s_res[wid][b][j] = make_float2(sumqx, sumq2);
+            }
+        }
+        __syncwarp();
+        if (q == 0) {
+            float d = 0.0f;
+            if (live) {
+                const float2 r0 = s_res[wid][b][0];
+                d = r0.y > 0.0f ? r0.x / r0.y : 0.0f;
+                float best = d * r0.x;
+                for (int j = 1; j < 16; j++) {
+                    const float2 r = s_res[wid][b][j];
+                    if (r.y > 0.0f && r.x * r.x > best * r.y) {
+                        d = r.x / r.y;
+                        best = d * r.x;
+                    }
+                }
+            }
+            s_scale[wid][b] = d;
+        }
+        __syncwarp();
+        uint8_t *o = s_out[wid];
+        float idl;
+        if (XS) {
+            float amax_s = 0.0f, max_s = 0.0f;
+#pragma unroll
+            for (int bb = 0; bb < 8; bb++) {
+                const float dv = s_scale[wid][bb];
+                if (fabsf(dv) > amax_s) { amax_s = fabsf(dv); max_s = dv; }
+            }
+            const float d = -max_s / 32.0f;
+            const float id = d != 0.0f ? 1.0f / d : 0.0f;
+            const int l = clampi(nearest_int(id * s_scale[wid][b]), -32, 31);
+            const float dl = d * (float)l;
+            idl = dl != 0.0f ? 1.0f / dl : 0.0f;
+            if (lane == 0) {
+                const uint16_t h = f16_bits(d);
+                o[0] = (uint8_t)(h & 0xFF);
+                o[1] = (uint8_t)(h >> 8);
+            }
+            // scales_h (2 B) and scales_l (4 B) from the eight 6-bit scales
+            const int lu = l + 32;
+            int lus[8];
+#pragma unroll
+            for (int bb = 0; bb < 8; bb++) lus[bb] = __shfl_sync(0xffffffffu, lu, bb * 4);
+            if (lane == 0) {
+                uint16_t h16 = 0;
+#pragma unroll
+                for (int bb = 0; bb < 8; bb++) h16 |= (uint16_t)(((lus[bb] >> 4) & 3) << (2 * bb));
+                o[2] = (uint8_t)(h16 & 0xFF);
+                o[3] = (uint8_t)(h16 >> 8);
+#pragma unroll
+                for (int t = 0; t < 4; t++) o[4 + t] = (uint8_t)((lus[2 * t] & 0xF) | ((lus[2 * t + 1] & 0xF) << 4));
+            }
+        } else {
+            const float sc = s_scale[wid][b];
+            idl = sc != 0.0f ? 1.0f / sc : 0.0f;
+            if (q == 0) {
+                const uint16_t h = f16_bits(sc);
+                o[b * 18] = (uint8_t)(h & 0xFF);
+                o[b * 18 + 1] = (uint8_t)(h >> 8);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; k++) s_l[wid][lane * 8 + k] = (uint8_t)best_index_iq4(lut, idl * v[k]);
+        __syncwarp();
+        // q4[16*i + j] = L[32i + j] | L[32i + 16 + j] << 4; lane packs 4 bytes of its block
+        {
+            const uint8_t *L = s_l[wid] + b * 32;
+            uint8_t *qo = XS ? o + 8 + b * 16 : o + b * 18 + 2;
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                const int jj = q * 4 + t;
+                qo[jj] = (uint8_t)(L[jj] | (L[16 + jj] << 4));
+            }
+        }
+        __syncwarp();
+        if (XS) {
+            const int64_t nsb = ne0 >> 8;
+            const int64_t sbi = g - (g / nsb) * nsb;
+            store_block(a.dst + (g / nsb) * a.dst_row_bytes + sbi * 136, o, 136, a.dst_aligned16 != 0, lane);
+        } else {
+            const int64_t blk0 = g * 8;
+            const int nb = (int)(nblk - blk0 < 8 ? nblk - blk0 : 8);
+            store_block(a.dst + blk0 * 18, o, nb * 18, a.dst_aligned16 && nb == 8, lane);
+        }
+        __syncwarp();
+    }
+}
+
+}  // namespace shc
+
+namespace shc {
+
+// ---------------------------------------------------------------------------
+// IQ2_XXS / IQ2_XS / IQ2_S / IQ3_XXS / IQ3_S (quant_iq.rs:275-935)
+// ---------------------------------------------------------------------------
+// V: 0 IQ2_XXS, 1 IQ2_XS, 2 IQ2_S, 3 IQ3_XXS, 4 IQ3_S (also the table slot).
+template <int V>
+struct IqCfg {
+    static constexpr bool IQ2 = V < 3;
+    static constexpr int BS = (V == 1 || V == 2) ? 16 : 32;  // block size
+    static constexpr int NB = 256 / BS;                      // blocks per super-block
+    static constexpr int G = IQ2 ? 8 : 4;                    // lattice dimension
+    static constexpr int NG = BS / G;                        // lattice groups per block
+    static constexpr int NSG = BS / 8;                       // sign groups per block
+    static constexpr int KM = IQ2 ? 3 : 8;                   // k_max_q
+    static constexpr int BITS = IQ2 ? 2 : 3;
+    static constexpr int NT = V == 0 ? 13 : (V == 3 ? 31 : 19);
+    static constexpr int IS_LO = V == 0 ? -6 : (V == 3 ? -15 : -9);
+    static constexpr float STEP = IQ2 ? 0.1f : 0.2f;
+    static constexpr bool PARITY = (V == 0 || V == 1 || V == 3);  // 7 stored sign bits + parity
+    static constexpr bool QP = V == 0;                            // make_qp_quants seed
+    static constexpr bool SIG2X = (V >= 2);                       // sigma2 = 2 * mean(x^2)
+    static constexpr int OUT = V == 0 ? 66 : V == 1 ? 74 : V == 2 ? 82 : V == 3 ? 98 : 110;
+    static constexpr int KMAP = IQ2 ? 6561 : 4096;
+};
+
+// Compact lattice index of G levels l[0..G).
+template <int V>
+__device__ __forceinline__ int lattice_index(const int *l) {
+    using C = IqCfg<V>;
+    int u = 0;
+    if (C::IQ2) {
+#pragma unroll
+        for (int i = C::G - 1; i >= 0; i--) u = u * 3 + l[i];
+    } else {
+#pragma unroll
+        for (int i = 0; i < C::G; i++) u |= l[i] << (3 * i);
+    }
+    return u;
+}
+
+// find_best_neighbour (quant_iq.rs:137-167): first strict minimum of
+// sum_i waux_i * (scale*g_i - x_i)^2 over the neighbour list; writes the
+// winner's levels (g-1)/2.  Returns false if no candidate was finite.
+template <int V>
+__device__ __forceinline__ bool best_neighbour(const uint32_t *__restrict__ nb, int m, const float *xv, const float *wa,
+                                               float scale, int *l) {
+    using C = IqCfg<V>;
+    constexpr uint32_t MASK = (1u << C::BITS) - 1;
+    const uint32_t *p = nb + (-m - 1);
+    const int n = (int)__ldg(p);
+    float best = FLT_MAX;
+    uint32_t bc = 0;
+    bool found = false;
+    for (int t = 0; t < n; t++) {
+        const uint32_t c = __ldg(p + 1 + t) >> 16;
+        float d2 = 0.0f;
+#pragma unroll
+        for (int i = 0; i < C::G; i++) {
+            const float pg = (float)(2 * (int)((c >> (C::BITS * i)) & MASK) + 1);
+            const float diff = scale * pg - xv[i];
+            d2 += wa[i] * diff * diff;
+        }
+        if (d2 < best) {
+            best = d2;
+            bc = c;
+            found = true;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < C::G; i++) l[i] = (int)((bc >> (C::BITS * i)) & MASK);
+    return found;
+}
+
+// One scale trial over one block: rounds every group to the lattice at id,
+// snaps off-grid groups to the best neighbour at this_scale, and returns the
+// weighted sums.  la receives the levels, on[k] whether group k was on-grid.
+template <int V>
+__device__ __forceinline__ void iq_trial(const float *xv, const float *w, const float *wa, float id, float this_scale,
+                                         const int *kmap, const uint32_t *nb, int *la, bool *on, float &sumqx,
+                                         float &sumq2, int *status) {
+    using C = IqCfg<V>;
+#pragma unroll
+    for (int k = 0; k < C::NG; k++) {
+        int l[C::G];
+#pragma unroll
+        for (int i = 0; i < C::G; i++)
+            l[i] = clampi(nearest_int(0.5f * (id * xv[k * C::G + i] - 1.0f)), 0, C::KM - 1);
+        const int m = kmap[lattice_index<V>(l)];
+        on[k] = m >= 0;
+        if (m < 0) {
+            float xg[C::G], wg[C::G];
+#pragma unroll
+            for (int i = 0; i < C::G; i++) {
+                xg[i] = xv[k * C::G + i];
+                wg[i] = wa[k * C::G + i];
+            }
+            if (!best_neighbour<V>(nb, m, xg, wg, this_scale, l)) set_status(status, SHC_ENONEIGHBOUR);
+        }
+#pragma unroll
+        for (int i = 0; i < C::G; i++) la[k * C::G + i] = l[i];
+    }
+    float sx = 0.0f, s2 = 0.0f;
+#pragma unroll
+    for (int i = 0; i < C::BS; i++) {
+        const float q = (float)(2 * la[i] + 1);
+        sx += w[i] * xv[i] * q;
+        s2 += w[i] * q * q;
+    }
+    sumqx = sx;
+    sumq2 = s2;
+}
+
+// make_qp_quants (quant_iq.rs:170-241), n = 32, nmax = 4: the IQ2_XXS seed.
+__device__ float make_qp_quants32(const float *x, const float *w) {
+    constexpr int n = 32, nmax = 4;
+    float max = 0.0f;
+    for (int i = 0; i < n; i++) max = rmaxf(max, x[i]);
+    if (max < kGroupMaxEps) return 0.0f;
+    float iscale = (float)nmax / max;
+    uint8_t ls[32];
+    for (int i = 0; i < n; i++) ls[i] = (uint8_t)nearest_int(iscale * x[i]);
+    const float scale = 1.0f / iscale;
+    float best_mse = 0.0f;
+    for (int i = 0; i < n; i++) {
+        const float diff = x[i] - scale * (float)ls[i];
+        best_mse += w[i] * diff * diff;
+    }
+    for (int is = -4; is <= 4; is++) {
+        if (is == 0) continue;
+        const float iscale_is = (0.1f * (float)is + (float)nmax) / max;
+        const float scale_is = 1.0f / iscale_is;
+        float mse = 0.0f;
+        for (int i = 0; i < n; i++) {
+            const int l = min(nearest_int(iscale_is * x[i]), nmax);
+            const float diff = x[i] - scale_is * (float)l;
+            mse += w[i] * diff * diff;
+        }
+        if (mse < best_mse) {
+            best_mse = mse;
+            iscale = iscale_is;
+        }
+    }
+    float sumlx = 0.0f, suml2 = 0.0f;
+    for (int i = 0; i < n; i++) {
+        const int l = min(nearest_int(iscale * x[i]), nmax);
+        ls[i] = (uint8_t)l;
+        sumlx += w[i] * x[i] * (float)l;
+        suml2 += w[i] * (float)(l * l);
+    }
+    for (int it = 0; it < 5; it++) {
+        int n_changed = 0;
+        for (int i = 0; i < n; i++) {
+            const float wi = w[i];
+            const float li = (float)ls[i];
+            const float slx = sumlx - wi * x[i] * li;
+            const float sl2 = suml2 - wi * li * li;
+            if (slx > 0.0f && sl2 > 0.0f) {
+                const int new_l = min(nearest_int(x[i] * sl2 / slx), nmax);
+                if ((uint8_t)new_l != ls[i]) {
+                    const float slx2 = slx + wi * x[i] * (float)new_l;
+                    const float sl22 = sl2 + wi * (float)(new_l * new_l);
+                    if (slx2 * slx2 * suml2 > sumlx * sumlx * sl22) {
+                        ls[i] = (uint8_t)new_l;
+                        sumlx = slx2;
+                        suml2 = sl22;
+                        n_changed++;
+                    }
+                }
+            }
+        }
+        if (n_changed == 0) break;
+    }
+    return suml2 > 0.0f ? sumlx / suml2 : 0.0f;
+}
+
+template <int V>
+struct IqWarpSmem {
+    float x[256];
+    float xv[256];
+    float w[256];
+    float wa[256];
+    float2 res[IqCfg<V>::NB * IqCfg<V>::NT];
+    float bscale0[IqCfg<V>::NB];  // chain start scale per block (qp seed or max/(2k-1))
+    float bmax[IqCfg<V>::NB];     // max |x| (or the qp effective max) per block
+    float bscale[IqCfg<V>::NB];   // final block scale
+    uint8_t live[IqCfg<V>::NB];
+    uint8_t signs[32];            // per 8-element sign group
+    uint16_t gidx[64];            // grid index per lattice group
+    __align__(16) uint8_t out[112];
+};
+
+template <int V>
+__global__ void __launch_bounds__(256) enc_iq_lattice_kernel(EncArgs a, const int32_t *__restrict__ g_kmap,
+                                                             const uint32_t *__restrict__ g_nb) {
+    using C = IqCfg<V>;
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    int *kmap = reinterpret_cast<int *>(smem_raw);
+    IqWarpSmem<V> *wsm_all = reinterpret_cast<IqWarpSmem<V> *>(smem_raw + ((C::KMAP * 4 + 15) & ~15));
+    for (int i = threadIdx.x; i < C::KMAP; i += blockDim.x) kmap[i] = g_kmap[i];
+    __syncthreads();
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    IqWarpSmem<V> &S = wsm_all[wid];
+    const int64_t ne0 = a.src.ne0, nsb = ne0 >> 8, total = a.n_rows * nsb;
+    for (int64_t g = (int64_t)blockIdx.x * 8 + wid; g < total; g += (int64_t)gridDim.x * 8) {
+        const int64_t row = g / nsb;
+        const int64_t sbi = g - row * nsb;
+        const int64_t col0 = sbi << 8;
+        const float *imr = im_row(a.im, ne0, a.row0 + row * a.row_step);
+        // ---- P0: load, super-block sigma^2, weights, signs ----
+        float v[8];
+        load8(a.src, row, col0 + lane * 8, v);
+#pragma unroll
+        for (int k = 0; k < 8; k++) S.x[lane * 8 + k] = v[k];
+        __syncwarp();
+        float ssum = 0.0f;
+        for (int i = 0; i < 256; i++) ssum += S.x[i] * S.x[i];
+        const float sig = C::SIG2X ? 2.0f * ssum / 256.0f : ssum / 256.0f;
+        float base[8];
+        load_im8(imr, col0 + lane * 8, base);
+        float wv[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            float wt;
+            if (V == 2) wt = imr ? base[k] * sqrtf(sig + v[k] * v[k]) : 0.25f * sig + v[k] * v[k];
+            else if (V >= 3) wt = imr ? base[k] * sqrtf(sig + v[k] * v[k]) : v[k] * v[k];
+            else wt = base[k] * sqrtf(sig + v[k] * v[k]);
+            wv[k] = wt;
+            S.w[lane * 8 + k] = wt;
+            S.wa[lane * 8 + k] = sqrtf(wt);
+        }
+        // sign group `lane` = elements lane*8 .. lane*8+7
+        {
+            float xv8[8];
+            int nflip = 0;
+            uint32_t s = 0;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                if (v[i] >= 0.0f) {
+                    xv8[i] = v[i];
+                } else {
+                    xv8[i] = -v[i];
+                    nflip++;
+                    s |= 1u << i;
+                }
+            }
+            if (C::PARITY && (nflip % 2) != 0) {
+                int imin = 0;
+                float mn = wv[0] * v[0] * v[0];
+#pragma unroll
+                for (int i = 1; i < 8; i++) {
+                    const float ax = wv[i] * v[i] * v[i];
+                    if (ax < mn) { mn = ax; imin = i; }
+                }
+#pragma unroll
+                for (int i = 0; i < 8; i++)
+                    if (i == imin) xv8[i] = -xv8[i];
+                s ^= 1u << imin;
+            }
+#pragma unroll
+            for (int i = 0; i < 8; i++) S.xv[lane * 8 + i] = xv8[i];
+            S.signs[lane] = (uint8_t)(C::PARITY ? (s & 127u) : s);
+        }
+        __syncwarp();
+        // ---- P1: per-block max and starting scale ----
+        if (lane < C::NB) {
+            const int b = lane;
+            const float *xb = S.xv + b * C::BS;
+            float mx = xb[0];
+            for (int i = 0; i < C::BS; i++) mx = rmaxf(mx, xb[i]);
+            bool live;
+            if (V == 0 || V == 1) live = !(mx < kGroupMaxEps);
+            else if (V == 2) live = !(mx < kGroupMaxEpsIq2S);
+            else if (V == 3) live = !(mx <= kGroupMaxEpsIq3Xxs);
+            else live = !(mx <= 0.0f);
+            float s0 = 0.0f, ref = mx;
+            if (live) {
+                if (C::QP) {
+                    s0 = make_qp_quants32(xb, S.w + b * C::BS);
+                    ref = s0 * (float)C::KM;  // eff_max
+                    if (ref <= 0.0f) live = false;
+                } else {
+                    s0 = mx / (float)(2 * C::KM - 1);
+                }
+            }
+            S.live[b] = live ? 1 : 0;
+            S.bscale0[b] = s0;
+            S.bmax[b] = ref;
+        }
+        __syncwarp();
+        // ---- P2: every (block, trial) pair ----
+        for (int j = lane; j < C::NB * C::NT; j += 32) {
+            const int b = j / C::NT, t = j - b * C::NT;
+            if (!S.live[b]) continue;
+            const int is = C::IS_LO + t;
+            float id;
+            if (C::QP) id = ((float)(2 * C::KM - 1) + (float)is * C::STEP) / S.bmax[b];
+            else id = ((float)(2 * C::KM - 1) + (float)is * C::STEP) / S.bmax[b];
+            const float this_scale = 1.0f / id;
+            int la[C::BS];
+            bool on[C::NG];
+            float sx, s2;
+            iq_trial<V>(S.xv + b * C::BS, S.w + b * C::BS, S.wa + b * C::BS, id, this_scale, kmap,
+                        g_nb, la, on, sx, s2, a.status);
+            S.res[j] = make_float2(sx, s2);
+        }
+        __syncwarp();
+        // ---- P3: per block: replay the chain, re-run the winner, re-project ----
+        if (lane < C::NB) {
+            const int b = lane;
+            const float *xb = S.xv + b * C::BS, *wb = S.w + b * C::BS, *ab = S.wa + b * C::BS;
+            float scale = 0.0f;
+            if (S.live[b]) {
+                scale = S.bscale0[b];
+                float best = 0.0f;
+                int win = -1;
+                for (int t = 0; t < C::NT; t++) {
+                    const float2 r = S.res[b * C::NT + t];
+                    if (r.y > 0.0f && r.x * r.x > best * r.y) {
+                        scale = r.x / r.y;
+                        best = scale * r.x;
+                        win = t;
+                    }
+                }
+                int ls[C::BS];
+                bool on[C::NG];
+#pragma unroll
+                for (int i = 0; i < C::BS; i++) ls[i] = 0;
+#pragma unroll
+                for (int k = 0; k < C::NG; k++) on[k] = (V != 4);
+                if (win >= 0) {
+                    const int is = C::IS_LO + win;
+                    const float id = ((float)(2 * C::KM - 1) + (float)is * C::STEP) / S.bmax[b];
+                    float sx, s2;
+                    iq_trial<V>(xb, wb, ab, id, 1.0f / id, kmap, g_nb, ls, on, sx, s2, a.status);
+                }
+                int n_not = 0;
+#pragma unroll
+                for (int k = 0; k < C::NG; k++) n_not += on[k] ? 0 : 1;
+                const bool reproject = (V == 0) ? (scale > 0.0f) : (n_not > 0 && scale > 0.0f);
+                if (reproject) {
+                    const float id = 1.0f / scale;
+#pragma unroll
+                    for (int k = 0; k < C::NG; k++) {
+                        const bool redo = (V == 0 || V == 4) ? true : !on[k];
+                        if (!redo) continue;
+                        int l[C::G];
+#pragma unroll
+                        for (int i = 0; i < C::G; i++)
+                            l[i] = clampi(nearest_int(0.5f * (id * xb[k * C::G + i] - 1.0f)), 0, C::KM - 1);
+                        const int m = kmap[lattice_index<V>(l)];
+                        if (m < 0) {
+                            float xg[C::G], wg[C::G];
+#pragma unroll
+                            for (int i = 0; i < C::G; i++) {
+                                xg[i] = xb[k * C::G + i];
+                                wg[i] = ab[k * C::G + i];
+                            }
+                            if (!best_neighbour<V>(g_nb, m, xg, wg, scale, l)) set_status(a.status, SHC_ENONEIGHBOUR);
+                        }
+#pragma unroll
+                        for (int i = 0; i < C::G; i++) ls[k * C::G + i] = l[i];
+                    }
+                    float sx = 0.0f, s2 = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < C::BS; i++) {
+                        const float q = (float)(2 * ls[i] + 1);
+                        sx += wb[i] * xb[i] * q;
+                        s2 += wb[i] * q * q;
+                    }
+                    if (s2 > 0.0f) scale = sx / s2;
+                }
+                if (scale < 0.0f) {
+                    scale = -scale;
+                    for (int k = 0; k < C::NSG; k++) {
+                        const uint8_t s = S.signs[b * C::NSG + k];
+                        S.signs[b * C::NSG + k] = C::PARITY ? (uint8_t)((~s) & 127) : (uint8_t)(~s);
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < C::NG; k++) {
+                    const int m = kmap[lattice_index<V>(ls + k * C::G)];
+                    if (m < 0) set_status(a.status, SHC_EOFFGRID);
+                    S.gidx[b * C::NG + k] = (uint16_t)(m < 0 ? 0 : m);
+                }
+            } else {
+#pragma unroll
+                for (int k = 0; k < C::NG; k++) S.gidx[b * C::NG + k] = 0;
+                for (int k = 0; k < C::NSG; k++) S.signs[b * C::NSG + k] = 0;
+            }
+            S.bscale[b] = scale;
+        }
+        __syncwarp();
+        // ---- P4: super-block scale and packing (lane 0) ----
+        if (lane == 0) {
+            uint8_t *o = S.out;
+            for (int i = 0; i < C::OUT; i++) o[i] = 0;
+            float max_scale = 0.0f;
+            for (int b = 0; b < C::NB; b++) max_scale = rmaxf(max_scale, S.bscale[b]);
+            const bool has = max_scale != 0.0f;
+            const float d = max_scale / 31.0f;
+            const float id = 1.0f / d;
+            auto nib = [&](int b) { return clampi(nearest_int(0.5f * (id * S.bscale[b] - 1.0f)), 0, 15); };
+            auto put16 = [&](int at, uint16_t h) {
+                o[at] = (uint8_t)(h & 0xFF);
+                o[at + 1] = (uint8_t)(h >> 8);
+            };
+            auto put32 = [&](int at, uint32_t u) {
+                o[at] = (uint8_t)u;
+                o[at + 1] = (uint8_t)(u >> 8);
+                o[at + 2] = (uint8_t)(u >> 16);
+                o[at + 3] = (uint8_t)(u >> 24);
+            };
+            if (V == 0) {  // IQ2_XXS: the q2 words only reach the output with a nonzero scale
+                if (has) {
+                    put16(0, f16_bits(d));
+                    for (int b = 0; b < 8; b++) {
+                        uint32_t q0 = 0, q1 = 0;
+                        for (int k = 0; k < 4; k++) {
+                            q0 |= (uint32_t)S.gidx[b * 4 + k] << (8 * k);
+                            q1 |= (uint32_t)S.signs[b * 4 + k] << (7 * k);
+                        }
+                        q1 |= (uint32_t)nib(b) << 28;
+                        put32(2 + 8 * b, q0);
+                        put32(6 + 8 * b, q1);
+                    }
+                }
+            } else if (V == 1) {  // IQ2_XS
+                if (has) {
+                    put16(0, f16_bits(d));
+                    for (int b = 0; b < 16; b++)
+                        for (int k = 0; k < 2; k++)
+                            put16(2 + 2 * (2 * b + k), (uint16_t)(S.gidx[b * 2 + k] | (S.signs[b * 2 + k] << 9)));
+                    for (int b = 0; b < 16; b++) {
+                        const uint8_t l = (uint8_t)nib(b);
+                        if (b % 2 == 0) o[66 + b / 2] = l;
+                        else o[66 + b / 2] |= (uint8_t)(l << 4);
+                    }
+                }
+            } else if (V == 2) {  // IQ2_S: grid and sign bytes are written per block
+                for (int b = 0; b < 16; b++) {
+                    if (!S.live[b]) continue;
+                    for (int k = 0; k < 2; k++) {
+                        const int i8v = 2 * b + k, gi = S.gidx[b * 2 + k];
+                        o[2 + i8v] = (uint8_t)(gi & 255);
+                        o[2 + 64 + i8v / 4] |= (uint8_t)((gi >> 8) << (2 * (i8v % 4)));
+                        o[2 + 32 + i8v] = S.signs[b * 2 + k];
+                    }
+                }
+                if (has) {
+                    put16(0, f16_bits(d * 0.9875f));
+                    for (int b = 0; b < 16; b++) {
+                        const uint8_t l = (uint8_t)nib(b);
+                        const int so = 2 + 64 + 8 + b / 2;
+                        if (b % 2 == 0) o[so] = l;
+                        else o[so] |= (uint8_t)(l << 4);
+                    }
+                }
+            } else if (V == 3) {  // IQ3_XXS
+                for (int b = 0; b < 8; b++) {
+                    if (!S.live[b]) continue;
+                    for (int k = 0; k < 8; k++) o[2 + 8 * b + k] = (uint8_t)S.gidx[b * 8 + k];
+                }
+                if (has) {
+                    put16(0, f16_bits(d * 1.0125f));
+                    for (int b = 0; b < 8; b++) {
+                        uint32_t sas = 0;
+                        if (S.live[b])
+                            sas = (uint32_t)S.signs[b * 4] | ((uint32_t)S.signs[b * 4 + 1] << 7) |
+                                  ((uint32_t)S.signs[b * 4 + 2] << 14) | ((uint32_t)S.signs[b * 4 + 3] << 21);
+                        sas |= (uint32_t)nib(b) << 28;
+                        put32(2 + 64 + 4 * b, sas);
+                    }
+                }
+            } else {  // IQ3_S
+                for (int b = 0; b < 8; b++) {
+                    if (!S.live[b]) continue;
+                    for (int k = 0; k < 8; k++) {
+                        const int gi = S.gidx[b * 8 + k];
+                        o[2 + 8 * b + k] = (uint8_t)(gi & 255);
+                        o[2 + 64 + b] |= (uint8_t)((gi >> 8) << k);
+                    }
+                    for (int k = 0; k < 4; k++) o[2 + 64 + 8 + 4 * b + k] = S.signs[b * 4 + k];
+                }
+                if (has) {
+                    put16(0, f16_bits(d * 1.033f));
+                    for (int b = 0; b < 8; b += 2) {
+                        const uint8_t l1 = (uint8_t)nib(b), l2 = (uint8_t)nib(b + 1);
+                        o[2 + 64 + 8 + 32 + b / 2] = (uint8_t)(l1 | (l2 << 4));
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        store_block(a.dst + row * a.dst_row_bytes + sbi * C::OUT, S.out, C::OUT, a.dst_aligned16 != 0, lane);
+        __syncwarp();
+    }
+}
+
+template <int V>
+static cudaError_t launch_lattice(const EncArgs &a, const IqTables &iq, int num_sms, cudaStream_t st) {
+    using C = IqCfg<V>;
+    const size_t smem = ((C::KMAP * 4 + 15) & ~(size_t)15) + 8 * sizeof(IqWarpSmem<V>);
+    auto fn = enc_iq_lattice_kernel<V>;
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 1;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, smem);
+    if (per_sm < 1) per_sm = 1;
+    const int64_t work = a.n_rows * (a.src.ne0 / 256);
+    int64_t grid = (work + 7) / 8;
+    const int64_t cap = (int64_t)num_sms * per_sm;
+    if (grid > cap) grid = cap;
+    if (grid < 1) grid = 1;
+    fn<<<(unsigned)grid, 256, smem, st>>>(a, iq.kmap[V], iq.neighbours[V]);
+    return cudaGetLastError();
+}
+
+template <bool XS>
+static cudaError_t launch_iq4(const EncArgs &a, int num_sms, cudaStream_t st) {
+    auto fn = enc_iq4_kernel<XS>;
+    int per_sm = 1;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, 0);
+    if (per_sm < 1) per_sm = 1;
+    const int64_t units = XS ? a.n_rows * (a.src.ne0 / 256) : (a.n_rows * (a.src.ne0 / 32) + 7) / 8;
+    int64_t grid = (units + 7) / 8;
+    const int64_t cap = (int64_t)num_sms * per_sm;
+    if (grid > cap) grid = cap;
+    if (grid < 1) grid = 1;
+    fn<<<(unsigned)grid, 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
 bool iq_supported(uint32_t type) {
-    (void)type;
-    return false;
+    switch (type) {
+    case SHC_TYPE_IQ4_NL: case SHC_TYPE_IQ4_XS: case SHC_TYPE_IQ2_XXS: case SHC_TYPE_IQ2_XS: case SHC_TYPE_IQ2_S:
+    case SHC_TYPE_IQ3_XXS: case SHC_TYPE_IQ3_S:
+        return true;
+    default:
+        return false;
+    }
 }
 
 cudaError_t launch_iq(uint32_t type, const EncArgs &a, const IqTables &iq, int num_sms, cudaStream_t st) {
-    (void)type; (void)a; (void)iq; (void)num_sms; (void)st;
-    return cudaErrorNotSupported;
+    switch (type) {
+    case SHC_TYPE_IQ4_NL: return launch_iq4<false>(a, num_sms, st);
+    case SHC_TYPE_IQ4_XS: return launch_iq4<true>(a, num_sms, st);
+    case SHC_TYPE_IQ2_XXS: return launch_lattice<0>(a, iq, num_sms, st);
+    case SHC_TYPE_IQ2_XS: return launch_lattice<1>(a, iq, num_sms, st);
+    case SHC_TYPE_IQ2_S: return launch_lattice<2>(a, iq, num_sms, st);
+    case SHC_TYPE_IQ3_XXS: return launch_lattice<3>(a, iq, num_sms, st);
+    case SHC_TYPE_IQ3_S: return launch_lattice<4>(a, iq, num_sms, st);
+    default: return cudaErrorNotSupported;
+    }
 }
 
 }  // namespace shc

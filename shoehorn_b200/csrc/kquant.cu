@@ -76,35 +76,6 @@ cudaError_t launch_row_sigma2(const RowSrc &src, int64_t n_rows, float *out, cud
 }
 
 // ---------------------------------------------------------------------------
-// helpers
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ void load_im8(const float *imr, int64_t col, float b[8]) {
-    if (imr) {
-        const float4 *p = reinterpret_cast<const float4 *>(imr + col);
-        const float4 a0 = __ldg(p), a1 = __ldg(p + 1);
-        b[0] = a0.x; b[1] = a0.y; b[2] = a0.z; b[3] = a0.w;
-        b[4] = a1.x; b[5] = a1.y; b[6] = a1.z; b[7] = a1.w;
-    } else {
-#pragma unroll
-        for (int k = 0; k < 8; k++) b[k] = 1.0f;
-    }
-}
-
-// Store nbytes of a shared-memory staged block to global memory, 16 B per
-// lane when both ends are 16-byte aligned, else 2 B or 1 B per lane.
-__device__ __forceinline__ void store_block(uint8_t *dstp, const uint8_t *sp, int nbytes, bool aligned16, int lane) {
-    if (aligned16 && (nbytes & 15) == 0 && ((uintptr_t)dstp & 15) == 0) {
-        for (int i = lane; i < nbytes / 16; i += 32)
-            reinterpret_cast<uint4 *>(dstp)[i] = reinterpret_cast<const uint4 *>(sp)[i];
-    } else if ((nbytes & 1) == 0 && ((uintptr_t)dstp & 1) == 0) {
-        for (int i = lane; i < nbytes / 2; i += 32)
-            reinterpret_cast<uint16_t *>(dstp)[i] = reinterpret_cast<const uint16_t *>(sp)[i];
-    } else {
-        for (int i = lane; i < nbytes; i += 32) dstp[i] = sp[i];
-    }
-}
-
-// ---------------------------------------------------------------------------
 // Q8_0 (quant.rs:159-169): per 32-block amax, d = amax/127, q = round(x/d).
 // HBM-bound.  A warp handles 8 blocks (256 elements) per group, 4 lanes per
 // block, 8 elements per lane; groups are flat over the tensor's blocks.
