@@ -1,14 +1,18 @@
-"""Benchmark: BF16 GB/s encoded per quant type on the single-tensor encoder
-sweep (4096 rows x 14336 columns of BF16, N(0, 0.02) with 0.1% outliers at
-+-8 sigma, per-column log-normal imatrix with sigma 1.5), device-resident and
-end to end through the host-buffer C-ABI entry point.
+"""Benchmark: BF16 GB/s encoded per quant type.
+
+Default workload (--workload kquant): the single-tensor encoder sweep, 4096
+rows x 14336 columns of BF16 (N(0, 0.02) with 0.1% outliers at +-8 sigma,
+per-column log-normal imatrix with sigma 1.5) to Q4_K, Q5_K, Q6_K and Q8_0.
+--workload iq: the IQ codebook configuration, [4096 x 4096] and
+[14336 x 4096] Student-t tensors to every IQ type.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-A step encodes the tensor once to every type of the sweep.  L2 (126 MB) is
-flushed before every timed encode (the 117 MB input fits in L2).  Under
-torchrun every rank encodes its own copy (weak scaling, no collective on the
-data path); the time is the max over ranks.
+A step encodes every tensor once to every type.  `value` is device-resident
+(inputs in HBM); `e2e` goes through the host-buffer C-ABI entry point with
+pinned host input and output.  L2 (126 MB) is flushed before every timed
+encode.  Under torchrun every rank encodes its own copy (weak scaling, no
+collective on the data path); the time is the max over ranks.
 """
 import argparse
 import json
@@ -39,20 +43,53 @@ OUT_BYTES_PER_ELT = {"Q8_0": 34 / 32, "Q4_K": 144 / 256, "Q5_K": 176 / 256, "Q6_
 #             (sum of one pass, 11) + weights (4) + folds/requantisation (~8)
 #  Q6_K: 19 grids x (2 clamp + 1 round + 6) + weights (4) + requant (4)
 #  Q8_0: abs/max, multiply, round (HBM-bound; bytes are the roofline)
-FLOPS_PER_ELT = {"Q4_K": 37 * 17 + 11 + 4 + 8, "Q5_K": 37 * 17 + 11 + 4 + 8, "Q6_K": 19 * 9 + 4 + 4, "Q8_0": 4}
+#  IQ*: trials x (4 rounding + 6 weighted sums) + weights/signs/re-projection
+#        (~20); IQ2_XXS adds its make_qp_quants seed (~60).  The data-dependent
+#        neighbour searches are not counted, so IQ fractions are lower bounds.
+#  IQ4_*: 16 grids x (index lookup ~6 + 5 sums) + final pass (~8)
+FLOPS_PER_ELT = {"Q4_K": 37 * 17 + 11 + 4 + 8, "Q5_K": 37 * 17 + 11 + 4 + 8, "Q6_K": 19 * 9 + 4 + 4, "Q8_0": 4,
+                 "IQ2_XXS": 13 * 10 + 20 + 60, "IQ2_XS": 19 * 10 + 20, "IQ2_S": 19 * 10 + 20,
+                 "IQ3_XXS": 31 * 10 + 20, "IQ3_S": 19 * 10 + 20, "IQ4_NL": 16 * 11 + 8, "IQ4_XS": 16 * 11 + 8}
+
+
+IQ_TYPES = ["IQ2_XXS", "IQ2_XS", "IQ2_S", "IQ3_XXS", "IQ3_S", "IQ4_NL", "IQ4_XS"]
+
+
+def _to_bf16(w):
+    u = w.view(np.uint32)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)  # RNE to BF16
 
 
 def make_workload(seed=SEED):
+    """Encoder sweep: 4096 rows x 14336, N(0, 0.02) + 0.1% outliers at +-8 sigma,
+    imatrix log-normal (sigma 1.5)."""
     rng = np.random.default_rng(seed)
     w = rng.standard_normal((N_ROWS, NE0), dtype=np.float32)
     w *= np.float32(0.02)
     k = int(round(w.size * 0.001))
     idx = rng.choice(w.size, size=k, replace=False)
     w.reshape(-1)[idx] = rng.choice(np.array([-0.16, 0.16], dtype=np.float32), size=k)
-    u = w.view(np.uint32)
-    bits = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)  # RNE to BF16
     im = np.exp(rng.normal(0.0, 1.5, size=NE0)).astype(np.float32)
-    return bits, im
+    return _to_bf16(w), im
+
+
+def make_iq_workload(seed=SEED):
+    """IQ codebook config: [4096 rows x 4096] and [14336 rows x 4096] Student-t
+    (nu=5) scaled to std 0.02, imatrix log-normal (sigma 1)."""
+    out = []
+    for i, rows in enumerate((4096, 14336)):
+        rng = np.random.default_rng(seed + 1 + i)
+        w = (rng.standard_t(5.0, size=(rows, 4096)) * (0.02 / np.sqrt(5.0 / 3.0))).astype(np.float32)
+        im = np.exp(rng.normal(0.0, 1.0, size=4096)).astype(np.float32)
+        out.append((f"{rows}x4096", _to_bf16(w), im))
+    return out
+
+
+def workload_tensors(name):
+    if name == "iq":
+        return make_iq_workload()
+    bits, im = make_workload()
+    return [(f"{N_ROWS}x{NE0}", bits, im)]
 
 
 def dist_env():
@@ -111,60 +148,68 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_baseline(bits, im, types, budget_s=12.0):
+def cpu_baseline(tensors, types, budget_s=12.0):
     """The reference algorithm (the C restatement in oracle/) on host cores:
-    a bounded sample of rows of the same tensor per type."""
+    a bounded sample of rows of the same tensors per type."""
     from oracle import oracle as O
     cores = os.cpu_count() or 1
     per_type = {}
     tot_bytes, tot_t = 0, 0.0
+    samples = []
     for name in types:
         ty = TYPE_IDS[name]
-        rows = 16
-        t0 = time.perf_counter()
-        O.encode_tensor_bf16(ty, bits[:rows], im, n_threads=cores)
-        dt = time.perf_counter() - t0
-        # grow the sample to about budget_s / len(types) of work
-        target = budget_s / len(types)
-        rows = int(min(N_ROWS, max(rows, rows * target / max(dt, 1e-3) * 0.8)))
-        rows = max(cores, rows - rows % cores)
-        t0 = time.perf_counter()
-        O.encode_tensor_bf16(ty, bits[:rows], im, n_threads=cores)
-        dt = time.perf_counter() - t0
-        per_type[name] = {"gbs": rows * NE0 * 2 / dt / 1e9, "rows": rows}
-        tot_bytes += rows * NE0 * 2
-        tot_t += dt
+        b_bytes, b_t = 0, 0.0
+        for tname, bits, im in tensors:
+            ne0 = bits.shape[1]
+            rows = 16
+            t0 = time.perf_counter()
+            O.encode_tensor_bf16(ty, bits[:rows], im, n_threads=cores)
+            dt = time.perf_counter() - t0
+            target = budget_s / len(types) / len(tensors)
+            rows = int(min(bits.shape[0], max(rows, rows * target / max(dt, 1e-3) * 0.8)))
+            rows = max(min(cores, bits.shape[0]), rows - rows % cores)
+            t0 = time.perf_counter()
+            O.encode_tensor_bf16(ty, bits[:rows], im, n_threads=cores)
+            dt = time.perf_counter() - t0
+            b_bytes += rows * ne0 * 2
+            b_t += dt
+            samples.append(f"{name} {tname}: first {rows} rows")
+        per_type[name] = b_bytes / b_t / 1e9
+        tot_bytes += b_bytes
+        tot_t += b_t
     return {"value": tot_bytes / tot_t / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
-            "per_type": {k: round(v["gbs"], 5) for k, v in per_type.items()},
-            "sample": "; ".join(f"{k}: first {v['rows']} rows x {NE0}" for k, v in per_type.items())}
+            "per_type": {k: round(v, 5) for k, v in per_type.items()}, "sample": "; ".join(samples)}
+
+
+def workload_label(args, tensors, types):
+    shapes = " + ".join(t[0] for t in tensors)
+    return f"{'IQ codebook' if args.workload == 'iq' else 'encoder sweep'} {shapes} BF16 ({','.join(types)}), imatrix-weighted"
 
 
 def run_reference(args):
     rank, _, world = dist_env()
     if rank != 0:
         return 0
-    bits, im = make_workload()
+    tensors = workload_tensors(args.workload)
     types = args.types.split(",")
     for _ in range(args.warmup):
-        cpu_baseline(bits, im, types, budget_s=2.0)
+        cpu_baseline(tensors, types, budget_s=2.0)
     vals = []
-    samples = None
+    cb = None
     t_start = time.perf_counter()
     for _ in range(args.steps):
-        cb = cpu_baseline(bits, im, types, budget_s=args.ref_budget)
+        cb = cpu_baseline(tensors, types, budget_s=args.ref_budget)
         vals.append(cb["value"])
-        samples = cb
     wall = time.perf_counter() - t_start
     value = statistics.median(vals)
     line = {"metric": METRIC, "value": round(value, 5), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(wall / args.steps * 1e3, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": f"encoder sweep {N_ROWS}x{NE0} BF16 ({','.join(types)})", "types": types,
-                       "l2": "n/a (host CPU)"},
-            "cpu_baseline": {"value": round(value, 5), "unit": "GB/s", "cores": samples["cores"], "kind": "port",
-                             "sample": samples["sample"]},
+            "config": {"workload": workload_label(args, tensors, types), "types": types, "l2": "n/a (host CPU)"},
+            "cpu_baseline": {"value": round(value, 5), "unit": "GB/s", "cores": cb["cores"], "kind": "port",
+                             "sample": cb["sample"]},
             "e2e": {"value": round(value, 5), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "per_type_gbs": samples["per_type"]}
+            "per_type_gbs": cb["per_type"]}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -182,62 +227,79 @@ def run_ours(args):
     dev = torch.device("cuda", local_rank)
     ctx = sh.Context(local_rank)
     types = [t for t in args.types.split(",") if sh.type_supported(TYPE_IDS[t])]
-    bits, im = make_workload()
-    src = torch.from_numpy(bits.view(np.int16)).to(dev)
-    imt = torch.from_numpy(im).to(dev)
-    outs = {t: torch.empty((N_ROWS, sh.row_bytes(TYPE_IDS[t], NE0)), dtype=torch.uint8, device=dev) for t in types}
+    tensors = workload_tensors(args.workload)
+    dtens = []
+    for tname, bits, im in tensors:
+        src = torch.from_numpy(bits.view(np.int16)).to(dev)
+        imt = torch.from_numpy(im).to(dev)
+        outs = {t: torch.empty((bits.shape[0], sh.row_bytes(TYPE_IDS[t], bits.shape[1])), dtype=torch.uint8,
+                               device=dev) for t in types}
+        dtens.append((tname, src, imt, outs))
     flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    def encode(t):
-        ctx.encode_rows(TYPE_IDS[t], src, imt, out=outs[t], stream=stream)
+    def encode(t, d):
+        ctx.encode_rows(TYPE_IDS[t], d[1], d[2], out=d[3][t], stream=stream)
 
     for _ in range(args.warmup):
         for t in types:
-            flush.zero_()
-            encode(t)
+            for d in dtens:
+                flush.zero_()
+                encode(t, d)
     ctx.sync(stream)
     torch.cuda.synchronize()
 
-    ev = {t: [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-          for t in types}
+    ev = {(t, i): [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(args.steps)] for t in types for i in range(len(dtens))}
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    sampler = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local_rank)).split(",")[0])
-                           if os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")[0].isdigit() else local_rank)
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
+    smi_index = int(vis[local_rank]) if len(vis) > local_rank and vis[local_rank].isdigit() else local_rank
+    sampler = ClockSampler(smi_index)
     sampler.start()
     launches0 = ctx.launch_count()
     for k in range(args.steps):
         for t in types:
-            flush.zero_()  # evict the input from L2 before every timed encode
-            s, e = ev[t][k]
-            s.record(stream)
-            encode(t)
-            e.record(stream)
+            for i, d in enumerate(dtens):
+                flush.zero_()  # evict the input from L2 before every timed encode
+                s, e = ev[(t, i)][k]
+                s.record(stream)
+                encode(t, d)
+                e.record(stream)
     torch.cuda.synchronize()
     launches = ctx.launch_count() - launches0
     ctx.sync(stream)
-    per_type_ms = {t: statistics.mean(s.elapsed_time(e) for s, e in ev[t]) for t in types}
+    # per type: median over steps of the summed tensor times
+    per_type_ms, per_type_min = {}, {}
+    for t in types:
+        steps_ms = [sum(ev[(t, i)][k][0].elapsed_time(ev[(t, i)][k][1]) for i in range(len(dtens)))
+                    for k in range(args.steps)]
+        per_type_ms[t] = statistics.median(steps_ms)
+        per_type_min[t] = min(steps_ms)
     step_ms = sum(per_type_ms.values())
-    # max over ranks
     if world > 1:
         tt = torch.tensor([step_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         step_ms = float(tt.item())
 
     # end to end: host (pinned) buffers through the C-ABI host entry point
-    src_h = torch.from_numpy(bits.view(np.int16)).pin_memory()
-    outs_h = {t: torch.empty(tuple(outs[t].shape), dtype=torch.uint8).pin_memory() for t in types}
+    htens = []
+    for (tname, bits, im), d in zip(tensors, dtens):
+        src_h = torch.from_numpy(bits.view(np.int16)).pin_memory()
+        outs_h = {t: torch.empty(tuple(d[3][t].shape), dtype=torch.uint8).pin_memory() for t in types}
+        htens.append((src_h, im, outs_h))
     for t in types:
-        ctx.encode_tensor_host(TYPE_IDS[t], src_h, im, out=outs_h[t])
+        for src_h, im, outs_h in htens:
+            ctx.encode_tensor_host(TYPE_IDS[t], src_h, im, out=outs_h[t])
     if world > 1:
         dist.barrier()
     e2e_t = {t: [] for t in types}
     for _ in range(max(1, min(args.steps, 3))):
         for t in types:
             t0 = time.perf_counter()
-            ctx.encode_tensor_host(TYPE_IDS[t], src_h, im, out=outs_h[t])
+            for src_h, im, outs_h in htens:
+                ctx.encode_tensor_host(TYPE_IDS[t], src_h, im, out=outs_h[t])
             e2e_t[t].append(time.perf_counter() - t0)
     e2e_step = sum(statistics.median(v) for v in e2e_t.values())
     if world > 1:
@@ -246,14 +308,14 @@ def run_ours(args):
         e2e_step = float(tt.item())
     clocks = sampler.stop()
 
-    in_bytes = N_ROWS * NE0 * 2
+    in_bytes = sum(int(d[1].numel()) * 2 for d in dtens)
+    elts = in_bytes // 2
     value = world * len(types) * in_bytes / (step_ms * 1e-3) / 1e9
     e2e_value = world * len(types) * in_bytes / e2e_step / 1e9
     per_type = {t: round(in_bytes / (per_type_ms[t] * 1e-3) / 1e9, 3) for t in types}
 
     # roofline of the dominant kernel (largest share of the step)
     dom = max(types, key=lambda t: per_type_ms[t])
-    elts = N_ROWS * NE0
     peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     peaks = json.load(open(peaks_path)) if os.path.exists(peaks_path) else {}
     props = torch.cuda.get_device_properties(dev)
@@ -261,8 +323,8 @@ def run_ours(args):
     if dom == "Q8_0":
         alg = elts * (2 + OUT_BYTES_PER_ELT[dom])
         hbm = peaks.get("hbm_gbs", 6650.0)
-        roof = {"bound": "hbm", "achieved": round(alg / (per_type_ms[dom] * 1e-3) / 1e9, 2),
-                "peak": hbm, "unit": "GB/s",
+        roof = {"bound": "hbm", "achieved": round(alg / (per_type_ms[dom] * 1e-3) / 1e9, 2), "peak": hbm,
+                "unit": "GB/s",
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if "hbm_gbs" in peaks else "fallback"}
     else:
         alg = elts * FLOPS_PER_ELT[dom]
@@ -279,20 +341,22 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_baseline(bits, im, types, budget_s=args.ref_budget)
+        cpu = cpu_baseline(tensors, types, budget_s=args.ref_budget)
 
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                "config": {"workload": f"encoder sweep {N_ROWS}x{NE0} BF16 ({','.join(types)}), imatrix-weighted",
-                           "types": types, "rows": N_ROWS, "ne0": NE0,
+                "config": {"workload": workload_label(args, tensors, types), "types": types,
+                           "tensors": [t[0] for t in tensors],
                            "l2": "flushed (512 MB write) before every timed encode",
                            "parallelism": f"weak: each of {world} ranks encodes its own copy"},
                 "per_type_gbs": per_type,
+                "per_type_ms": {t: round(v, 4) for t, v in per_type_ms.items()},
+                "per_type_ms_min": {t: round(v, 4) for t, v in per_type_min.items()},
                 "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
                         "h2d_bytes_per_step": len(types) * in_bytes,
-                        "d2h_bytes_per_step": sum(int(outs[t].numel()) for t in types)},
+                        "d2h_bytes_per_step": sum(int(d[3][t].numel()) for d in dtens for t in types)},
                 "roofline": roof, "clocks": clocks, "gpu_launches": launches,
                 "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)
@@ -309,10 +373,13 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--types", default=",".join(SWEEP))
+    ap.add_argument("--workload", default="kquant", choices=["kquant", "iq"])
+    ap.add_argument("--types", default=None, help="comma-separated types (default: the workload's)")
     ap.add_argument("--ref-budget", type=float, default=12.0, help="seconds of CPU work per reference sample")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     args = ap.parse_args()
+    if args.types is None:
+        args.types = ",".join(IQ_TYPES if args.workload == "iq" else SWEEP)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -326,7 +326,9 @@ static void enc_q8_0(const float *x, int64_t n, uint8_t *out) {
 
 /* quant.rs:171-181 */
 static void enc_q4_0(const float *x, int64_t n, const float *im, float sigma2, uint8_t *out) {
-    uint8_t ls[32];
+    /* one level vector for the whole row, as the reference's `ls` outlives the
+       block loop: a block where no grid is accepted keeps the previous levels */
+    uint8_t ls[32] = {0};
     float w[32];
     for (int64_t b = 0; b < n / 32; b++) {
         const float *blk = x + 32 * b;
@@ -340,7 +342,7 @@ static void enc_q4_0(const float *x, int64_t n, const float *im, float sigma2, u
 
 /* quant.rs:183-198 */
 static void enc_q5_0(const float *x, int64_t n, const float *im, float sigma2, uint8_t *out) {
-    uint8_t ls[32];
+    uint8_t ls[32] = {0};
     float w[32];
     for (int64_t b = 0; b < n / 32; b++) {
         const float *blk = x + 32 * b;
@@ -357,7 +359,7 @@ static void enc_q5_0(const float *x, int64_t n, const float *im, float sigma2, u
 
 /* quant.rs:200-211 */
 static void enc_q4_1(const float *x, int64_t n, const float *im, float sigma2, uint8_t *out) {
-    uint8_t ls[32];
+    uint8_t ls[32] = {0};
     float w[32];
     for (int64_t b = 0; b < n / 32; b++) {
         const float *blk = x + 32 * b;
@@ -373,7 +375,7 @@ static void enc_q4_1(const float *x, int64_t n, const float *im, float sigma2, u
 
 /* quant.rs:213-229 */
 static void enc_q5_1(const float *x, int64_t n, const float *im, float sigma2, uint8_t *out) {
-    uint8_t ls[32];
+    uint8_t ls[32] = {0};
     float w[32];
     for (int64_t b = 0; b < n / 32; b++) {
         const float *blk = x + 32 * b;

@@ -16,6 +16,12 @@ OUT = os.path.join(HERE, "libshoehorn_cuda.so")
 BUILD_DIR = os.path.join(HERE, "_build")
 SOURCES = ["api.cu", "kquant.cu", "decode.cu", "iq.cu", "iq_host.cpp", "noalloc.cu"]
 HEADERS = ["common.cuh", "kernels.cuh", "iq_host.h", "iq_tables.h"]
+HOST = os.path.join(HERE, "host")
+HOST_SOURCES = ["gguf.cpp", "imatrix.cpp", "solver.cpp", "pipeline.cpp", "synthetic.cpp", "host_api.cpp"]
+HOST_HEADERS = ["gguf.hpp", "imatrix.hpp", "solver.hpp", "pipeline.hpp"]
+HOST_LIB = os.path.join(HERE, "libshoehorn_host.so")
+CLI = os.path.join(HERE, "shoehorn-gpu")
+CUDA_INC = "/usr/local/cuda/include"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FP = ["-fmad=false", "-prec-div=true", "-prec-sqrt=true", "-ftz=false"]
 
@@ -61,6 +67,25 @@ def build(verbose=False, extra=()):
         list(ex.map(run, jobs))
     if jobs or _stale(OUT, objs):
         run([nvcc(), *ARCH, "-shared", "-o", OUT, *objs])
+    # host pipeline (C++): libshoehorn_host.so and the shoehorn-gpu CLI
+    hh = [os.path.join(HOST, h) for h in HOST_HEADERS] + [os.path.join(ROOT, "include", "shoehorn_cuda.h")]
+    hobjs, hjobs = [], []
+    gxx = ["g++", "-std=c++17", "-O2", "-fPIC", "-Wall", "-Wextra", "-I", os.path.join(ROOT, "include"), "-I", HOST,
+           "-I", CUDA_INC]
+    for src in HOST_SOURCES + ["cli.cpp"]:
+        sp = os.path.join(HOST, src)
+        o = os.path.join(BUILD_DIR, "host_" + src + ".o")
+        hobjs.append(o)
+        if _stale(o, [sp, *hh, __file__]):
+            hjobs.append([*gxx, "-c", sp, "-o", o])
+    with concurrent.futures.ThreadPoolExecutor(max_workers=min(8, max(1, len(hjobs)))) as ex:
+        list(ex.map(run, hjobs))
+    lib_objs = hobjs[:-1]
+    link_common = ["-L" + HERE, "-lshoehorn_cuda", "-Xlinker", "-rpath=$ORIGIN", "-lpthread"]
+    if hjobs or _stale(HOST_LIB, lib_objs + [OUT]):
+        run([nvcc(), *ARCH, "-shared", "-o", HOST_LIB, *lib_objs, *link_common])
+    if hjobs or _stale(CLI, hobjs + [OUT]):
+        run([nvcc(), *ARCH, "-o", CLI, *hobjs, *link_common])
     return OUT
 
 

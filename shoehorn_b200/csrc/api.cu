@@ -1,6 +1,8 @@
 // C ABI of the library (include/shoehorn_cuda.h): validation, stream-ordered
 // scratch, launches, bounded waits and the pipelined host-buffer entry points.
 #include <algorithm>
+#include <cstdio>
+#include <cstdlib>
 #include <atomic>
 #include <chrono>
 #include <cstring>
@@ -23,6 +25,7 @@ struct shc_ctx {
     std::atomic<unsigned> status_slot{0};
     void *d_tables = nullptr;
     IqTables iq{};
+    cudaMemPool_t pool = nullptr;  // per-call scratch; keeps its memory between calls
     std::atomic<int64_t> launches{0};
     // host-buffer pipeline resources (one host call at a time)
     std::mutex host_mu;
@@ -48,6 +51,7 @@ struct DevGuard {
 
 int cuda_status(cudaError_t e) {
     if (e == cudaSuccess) return SHC_OK;
+    if (getenv("SHC_DEBUG")) fprintf(stderr, "shoehorn_cuda: %s\n", cudaGetErrorString(e));
     if (e == cudaErrorMemoryAllocation) return SHC_ENOMEM;
     return SHC_ECUDA;
 }
@@ -64,7 +68,8 @@ size_t src_elem_bytes(uint32_t s) { return s == SHC_SRC_F32 ? 4 : 2; }
 bool encodable(uint32_t t) {
     switch (t) {
     case SHC_TYPE_F32: case SHC_TYPE_F16: case SHC_TYPE_BF16: case SHC_TYPE_Q8_0: case SHC_TYPE_Q4_K:
-    case SHC_TYPE_Q5_K: case SHC_TYPE_Q6_K:
+    case SHC_TYPE_Q5_K: case SHC_TYPE_Q6_K: case SHC_TYPE_Q4_0: case SHC_TYPE_Q4_1: case SHC_TYPE_Q5_0:
+    case SHC_TYPE_Q5_1:
         return true;
     default:
         return is_iq(t) ? iq_supported(t) : false;
@@ -124,8 +129,12 @@ int check_common(shc_ctx *ctx, uint32_t src_type, const void *src, int64_t n_row
     if (n_rows > 0 && !src) return SHC_EINVAL;
     if (((uintptr_t)src & 15) != 0) return SHC_EINVAL;  // 128-bit row loads
     if (im && ((uintptr_t)im & 15) != 0) return SHC_EINVAL;
-    if (ne0 % 8 != 0) return SHC_EINVAL;
     return SHC_OK;
+}
+
+// Stream-ordered per-call scratch from the context's pool.
+cudaError_t scratch_alloc(shc_ctx *ctx, void **p, size_t bytes, cudaStream_t st) {
+    return cudaMallocFromPoolAsync(p, bytes, ctx->pool, st);
 }
 
 // Encode one view of rows on `st` (sigma^2 pre-pass into stream-ordered
@@ -134,7 +143,7 @@ int encode_view(shc_ctx *ctx, uint32_t type, EncArgs a, cudaStream_t st) {
     if (a.n_rows == 0) return SHC_OK;
     float *sig = nullptr;
     if (needs_sigma2(type)) {
-        SHC_TRY(cudaMallocAsync((void **)&sig, sizeof(float) * (size_t)a.n_rows, st));
+        SHC_TRY(scratch_alloc(ctx, (void **)&sig, sizeof(float) * (size_t)a.n_rows, st));
         cudaError_t e = launch_row_sigma2(a.src, a.n_rows, sig, st);
         ctx->launches++;
         if (e != cudaSuccess) {
@@ -152,12 +161,49 @@ int encode_view(shc_ctx *ctx, uint32_t type, EncArgs a, cudaStream_t st) {
     return cuda_status(e);
 }
 
+// Re-encode the host lists (quant_iq.rs neighbour order kept) into the layout
+// the device encoder of variant w reads, with kmap offsets remapped.
+void device_lists(int w, const IqHostTable &t, std::vector<int32_t> &kmap, std::vector<uint8_t> &bytes) {
+    kmap = t.kmap;
+    bytes.clear();
+    for (size_t c = 0; c < t.kmap.size(); c++) {
+        const int32_t m = t.kmap[c];
+        if (m >= 0) continue;
+        const size_t off = (size_t)(-m - 1);
+        const uint32_t n = t.neighbours[off];
+        if (w == 0) {  // 8-bit grid indices (256-point grid, lists of at most 255)
+            kmap[c] = -(int32_t)(bytes.size() + 1);
+            bytes.push_back((uint8_t)n);
+            for (uint32_t k = 1; k <= n; k++) bytes.push_back((uint8_t)(t.neighbours[off + k] & 0xFFFF));
+        } else if (w == 1) {  // 16-bit coords, entries 16-byte aligned
+            size_t slot = bytes.size() / 2;
+            while ((slot + 1) % 8 != 0) slot++;
+            bytes.resize((slot + 1 + ((n + 7) / 8) * 8) * 2, 0);
+            uint16_t *p16 = reinterpret_cast<uint16_t *>(bytes.data());
+            p16[slot] = (uint16_t)n;
+            for (uint32_t k = 1; k <= n; k++) p16[slot + k] = (uint16_t)(t.neighbours[off + k] >> 16);
+            kmap[c] = -(int32_t)(slot + 1);
+        } else {  // 16-bit coords, packed
+            const size_t slot = bytes.size() / 2;
+            bytes.resize((slot + 1 + n) * 2);
+            uint16_t *p16 = reinterpret_cast<uint16_t *>(bytes.data());
+            p16[slot] = (uint16_t)n;
+            for (uint32_t k = 1; k <= n; k++) p16[slot + k] = (uint16_t)(t.neighbours[off + k] >> 16);
+            kmap[c] = -(int32_t)(slot + 1);
+        }
+    }
+    while (bytes.size() % 16) bytes.push_back(0);
+}
+
 int upload_iq_tables(shc_ctx *ctx) {
     IqHostTable t[5];
+    std::vector<int32_t> dk[5];
+    std::vector<uint8_t> lists[5];
     size_t total = 0;
     for (int w = 0; w < 5; w++) {
         build_iq_tables(w, t[w]);
-        total += (t[w].kmap.size() + t[w].neighbours.size() + t[w].grid_coords.size()) * 4 + 256;
+        device_lists(w, t[w], dk[w], lists[w]);
+        total += (t[w].kmap.size() * 2 + t[w].neighbours.size() + t[w].grid_coords.size()) * 4 + lists[w].size() + 1024;
     }
     SHC_TRY(cudaMalloc(&ctx->d_tables, total));
     std::vector<uint8_t> host(total, 0);
@@ -172,6 +218,9 @@ int upload_iq_tables(shc_ctx *ctx) {
         ctx->iq.kmap[w] = reinterpret_cast<const int32_t *>(place(t[w].kmap.data(), t[w].kmap.size() * 4));
         ctx->iq.neighbours[w] = reinterpret_cast<const uint32_t *>(place(t[w].neighbours.data(), t[w].neighbours.size() * 4));
         ctx->iq.grid_coords[w] = reinterpret_cast<const uint32_t *>(place(t[w].grid_coords.data(), t[w].grid_coords.size() * 4));
+        ctx->iq.dkmap[w] = reinterpret_cast<const int32_t *>(place(dk[w].data(), dk[w].size() * 4));
+        ctx->iq.lists[w] = place(lists[w].data(), lists[w].size());
+        ctx->iq.lists_bytes[w] = (int)lists[w].size();
     }
     SHC_TRY(cudaMemcpy(ctx->d_tables, host.data(), total, cudaMemcpyHostToDevice));
     return SHC_OK;
@@ -245,6 +294,17 @@ int shc_init(int device, shc_ctx **out) {
         cudaHostAlloc((void **)&ctx->h_status_pool, sizeof(int) * kStatusSlots, cudaHostAllocDefault) != cudaSuccess) {
         rc = SHC_ENOMEM;
     }
+    if (rc == SHC_OK) {
+        cudaMemPoolProps pp{};
+        pp.allocType = cudaMemAllocationTypePinned;
+        pp.handleTypes = cudaMemHandleTypeNone;
+        pp.location.type = cudaMemLocationTypeDevice;
+        pp.location.id = device;
+        uint64_t keep = UINT64_MAX;  // never hand memory back at a synchronisation
+        if (cudaMemPoolCreate(&ctx->pool, &pp) != cudaSuccess ||
+            cudaMemPoolSetAttribute(ctx->pool, cudaMemPoolAttrReleaseThreshold, &keep) != cudaSuccess)
+            rc = SHC_ECUDA;
+    }
     if (rc == SHC_OK) rc = upload_iq_tables(ctx);
     for (int i = 0; rc == SHC_OK && i < 3; i++)
         if (cudaStreamCreateWithFlags(&ctx->hs[i], cudaStreamNonBlocking) != cudaSuccess) rc = SHC_ECUDA;
@@ -266,6 +326,7 @@ int shc_free(shc_ctx *ctx) {
         for (int i = 0; i < 4; i++)
             if (ctx->pin[i]) cudaFreeHost(ctx->pin[i]);
         if (ctx->d_tables) cudaFree(ctx->d_tables);
+        if (ctx->pool) cudaMemPoolDestroy(ctx->pool);
         if (ctx->d_status) cudaFree(ctx->d_status);
         if (ctx->h_status_pool) cudaFreeHost(ctx->h_status_pool);
     }
@@ -281,6 +342,7 @@ int shc_encode_rows(shc_ctx *ctx, uint32_t type, uint32_t src_type, const void *
     if (rc != SHC_OK) return rc;
     const int64_t rb = shc_row_bytes(type, ne0);
     if (rb < 0 || !encodable(type) || (n_rows > 0 && !dst)) return SHC_EINVAL;
+    if (block_elems(type) > 1 && ne0 % 8 != 0) return SHC_EINVAL;  // 128-bit row loads
     DevGuard g(ctx->device);
     EncArgs a = make_args(ctx, src_type, src, n_rows, ne0, ne0, im, im_len, rows_per_mat, row0, 1, dst, rb);
     return encode_view(ctx, type, a, (cudaStream_t)stream);
@@ -325,7 +387,7 @@ int shc_row_errors(shc_ctx *ctx, const uint32_t *types, int n_types, uint32_t sr
         if (sig) cudaFreeAsync(sig, st);
     };
     if (any_sig) {
-        if (cudaMallocAsync((void **)&sig, sizeof(float) * (size_t)n_s, st) != cudaSuccess) return SHC_ENOMEM;
+        if (scratch_alloc(ctx, (void **)&sig, sizeof(float) * (size_t)n_s, st) != cudaSuccess) return SHC_ENOMEM;
         cudaError_t e = launch_row_sigma2(a.src, n_s, sig, st);
         ctx->launches++;
         if (e != cudaSuccess) {
@@ -337,7 +399,7 @@ int shc_row_errors(shc_ctx *ctx, const uint32_t *types, int n_types, uint32_t sr
         const uint32_t ty = types[t];
         if (block_elems(ty) == 1) continue;  // elementwise types are round-tripped inside the error pass
         const int64_t rb = shc_row_bytes(ty, ne0);
-        if (cudaMallocAsync((void **)&codes[(size_t)t], (size_t)(rb * n_s), st) != cudaSuccess) {
+        if (scratch_alloc(ctx, (void **)&codes[(size_t)t], (size_t)(rb * n_s), st) != cudaSuccess) {
             cleanup();
             return SHC_ENOMEM;
         }
@@ -408,13 +470,13 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
         if (rc == SHC_OK) rc = code;
     };
     for (int b = 0; b < 2 && rc == SHC_OK; b++) {
-        if (cudaMallocAsync(&d_in[b], in_row * (size_t)chunk, s_cmp) != cudaSuccess) fail(SHC_ENOMEM);
-        if (cudaMallocAsync((void **)&d_out[b], (size_t)rb * (size_t)chunk, s_cmp) != cudaSuccess) fail(SHC_ENOMEM);
+        if (scratch_alloc(ctx, &d_in[b], in_row * (size_t)chunk, s_cmp) != cudaSuccess) fail(SHC_ENOMEM);
+        if (scratch_alloc(ctx, (void **)&d_out[b], (size_t)rb * (size_t)chunk, s_cmp) != cudaSuccess) fail(SHC_ENOMEM);
         if (!pin_src && rc == SHC_OK) fail(ensure_pinned(ctx, b, in_row * (size_t)chunk));
         if (!pin_dst && rc == SHC_OK) fail(ensure_pinned(ctx, 2 + b, (size_t)rb * (size_t)chunk));
     }
     if (rc == SHC_OK && host_im && im_len > 0) {
-        if (cudaMallocAsync((void **)&d_im, sizeof(float) * (size_t)im_len, s_cmp) != cudaSuccess) fail(SHC_ENOMEM);
+        if (scratch_alloc(ctx, (void **)&d_im, sizeof(float) * (size_t)im_len, s_cmp) != cudaSuccess) fail(SHC_ENOMEM);
         else if (cudaMemcpyAsync(d_im, host_im, sizeof(float) * (size_t)im_len, cudaMemcpyHostToDevice, s_cmp) != cudaSuccess)
             fail(SHC_ECUDA);
     }
@@ -527,11 +589,11 @@ int shc_row_errors_host(shc_ctx *ctx, const uint32_t *types, int n_types, uint32
     float *d_im = nullptr;
     double *d_err = nullptr;
     int rc = SHC_OK;
-    if (cudaMallocAsync(&d_in, in_row * (size_t)chunk, st) != cudaSuccess ||
-        cudaMallocAsync((void **)&d_err, sizeof(double) * (size_t)n_types * (size_t)chunk, st) != cudaSuccess)
+    if (scratch_alloc(ctx, &d_in, in_row * (size_t)chunk, st) != cudaSuccess ||
+        scratch_alloc(ctx, (void **)&d_err, sizeof(double) * (size_t)n_types * (size_t)chunk, st) != cudaSuccess)
         rc = SHC_ENOMEM;
     if (rc == SHC_OK && host_im && im_len > 0) {
-        if (cudaMallocAsync((void **)&d_im, sizeof(float) * (size_t)im_len, st) != cudaSuccess) rc = SHC_ENOMEM;
+        if (scratch_alloc(ctx, (void **)&d_im, sizeof(float) * (size_t)im_len, st) != cudaSuccess) rc = SHC_ENOMEM;
         else if (cudaMemcpyAsync(d_im, host_im, sizeof(float) * (size_t)im_len, cudaMemcpyHostToDevice, st) != cudaSuccess)
             rc = SHC_ECUDA;
     }

@@ -276,29 +276,52 @@ __device__ __forceinline__ int lattice_index(const int *l) {
 // sum_i waux_i * (scale*g_i - x_i)^2 over the neighbour list; writes the
 // winner's levels (g-1)/2.  Returns false if no candidate was finite.
 template <int V>
-__device__ __forceinline__ bool best_neighbour(const uint32_t *__restrict__ nb, int m, const float *xv, const float *wa,
-                                               float scale, int *l) {
+__device__ __forceinline__ void nb_eval(uint32_t c, const float *xv, const float *wa, float scale, float &best,
+                                        uint32_t &bc, bool &found) {
     using C = IqCfg<V>;
     constexpr uint32_t MASK = (1u << C::BITS) - 1;
-    const uint32_t *p = nb + (-m - 1);
-    const int n = (int)__ldg(p);
+    float d2 = 0.0f;
+#pragma unroll
+    for (int i = 0; i < C::G; i++) {
+        const float pg = (float)(2 * (int)((c >> (C::BITS * i)) & MASK) + 1);
+        const float diff = scale * pg - xv[i];
+        d2 += wa[i] * diff * diff;
+    }
+    if (d2 < best) {
+        best = d2;
+        bc = c;
+        found = true;
+    }
+}
+
+template <int V>
+__device__ __forceinline__ bool best_neighbour(const void *lists, const uint16_t *gco, int m, const float *xv,
+                                               const float *wa, float scale, int *l) {
+    using C = IqCfg<V>;
+    constexpr uint32_t MASK = (1u << C::BITS) - 1;
     float best = FLT_MAX;
     uint32_t bc = 0;
     bool found = false;
-    for (int t = 0; t < n; t++) {
-        const uint32_t c = __ldg(p + 1 + t) >> 16;
-        float d2 = 0.0f;
+    if (V == 0) {  // shared memory, 8-bit grid indices
+        const uint8_t *p = static_cast<const uint8_t *>(lists) + (-m - 1);
+        const int n = p[0];
+        for (int t = 0; t < n; t++) nb_eval<V>(gco[p[1 + t]], xv, wa, scale, best, bc, found);
+    } else if (V == 1) {  // global memory, 16-byte aligned runs of 8 entries
+        const uint16_t *p = static_cast<const uint16_t *>(lists) + (-m - 1);
+        const int n = (int)__ldg(p);
+        const uint4 *q = reinterpret_cast<const uint4 *>(p + 1);
+        for (int ch = 0; ch * 8 < n; ch++) {
+            const uint4 v = __ldg(q + ch);
+            const uint32_t e[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int i = 0; i < C::G; i++) {
-            const float pg = (float)(2 * (int)((c >> (C::BITS * i)) & MASK) + 1);
-            const float diff = scale * pg - xv[i];
-            d2 += wa[i] * diff * diff;
+            for (int k = 0; k < 8; k++) {
+                if (ch * 8 + k < n) nb_eval<V>((e[k >> 1] >> (16 * (k & 1))) & 0xFFFFu, xv, wa, scale, best, bc, found);
+            }
         }
-        if (d2 < best) {
-            best = d2;
-            bc = c;
-            found = true;
-        }
+    } else {  // shared memory, 16-bit coordinates
+        const uint16_t *p = static_cast<const uint16_t *>(lists) + (-m - 1);
+        const int n = p[0];
+        for (int t = 0; t < n; t++) nb_eval<V>(p[1 + t], xv, wa, scale, best, bc, found);
     }
 #pragma unroll
     for (int i = 0; i < C::G; i++) l[i] = (int)((bc >> (C::BITS * i)) & MASK);
@@ -310,7 +333,7 @@ __device__ __forceinline__ bool best_neighbour(const uint32_t *__restrict__ nb, 
 // weighted sums.  la receives the levels, on[k] whether group k was on-grid.
 template <int V>
 __device__ __forceinline__ void iq_trial(const float *xv, const float *w, const float *wa, float id, float this_scale,
-                                         const int *kmap, const uint32_t *nb, int *la, bool *on, float &sumqx,
+                                         const int *kmap, const void *nb, const uint16_t *gco, int *la, bool *on, float &sumqx,
                                          float &sumq2, int *status) {
     using C = IqCfg<V>;
 #pragma unroll
@@ -328,7 +351,7 @@ __device__ __forceinline__ void iq_trial(const float *xv, const float *w, const 
                 xg[i] = xv[k * C::G + i];
                 wg[i] = wa[k * C::G + i];
             }
-            if (!best_neighbour<V>(nb, m, xg, wg, this_scale, l)) set_status(status, SHC_ENONEIGHBOUR);
+            if (!best_neighbour<V>(nb, gco, m, xg, wg, this_scale, l)) set_status(status, SHC_ENONEIGHBOUR);
         }
 #pragma unroll
         for (int i = 0; i < C::G; i++) la[k * C::G + i] = l[i];
@@ -423,15 +446,32 @@ struct IqWarpSmem {
     __align__(16) uint8_t out[112];
 };
 
+// Lists that live in shared memory for variant V (all but IQ2_XS, whose
+// 375 KB of lists stay in global memory).
+template <int V>
+__host__ __device__ constexpr bool lists_in_smem() { return V != 1; }
+
 template <int V>
 __global__ void __launch_bounds__(256) enc_iq_lattice_kernel(EncArgs a, const int32_t *__restrict__ g_kmap,
-                                                             const uint32_t *__restrict__ g_nb) {
+                                                             const uint8_t *__restrict__ g_lists, int lists_bytes,
+                                                             const uint32_t *__restrict__ g_coords) {
     using C = IqCfg<V>;
     extern __shared__ __align__(16) uint8_t smem_raw[];
+    // shared memory: compact kmap | per-warp state | grid coords | lists
     int *kmap = reinterpret_cast<int *>(smem_raw);
     IqWarpSmem<V> *wsm_all = reinterpret_cast<IqWarpSmem<V> *>(smem_raw + ((C::KMAP * 4 + 15) & ~15));
+    uint16_t *gco = reinterpret_cast<uint16_t *>(reinterpret_cast<uint8_t *>(wsm_all + 8));
+    uint8_t *s_lists = reinterpret_cast<uint8_t *>(gco + 256);
     for (int i = threadIdx.x; i < C::KMAP; i += blockDim.x) kmap[i] = g_kmap[i];
+    if (V == 0)
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) gco[i] = (uint16_t)g_coords[i];
+    if (lists_in_smem<V>()) {
+        const uint4 *src4 = reinterpret_cast<const uint4 *>(g_lists);
+        uint4 *dst4 = reinterpret_cast<uint4 *>(s_lists);
+        for (int i = threadIdx.x; i < lists_bytes / 16; i += blockDim.x) dst4[i] = src4[i];
+    }
     __syncthreads();
+    const void *nbs = lists_in_smem<V>() ? (const void *)s_lists : (const void *)g_lists;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     IqWarpSmem<V> &S = wsm_all[wid];
     const int64_t ne0 = a.src.ne0, nsb = ne0 >> 8, total = a.n_rows * nsb;
@@ -534,7 +574,7 @@ __global__ void __launch_bounds__(256) enc_iq_lattice_kernel(EncArgs a, const in
             bool on[C::NG];
             float sx, s2;
             iq_trial<V>(S.xv + b * C::BS, S.w + b * C::BS, S.wa + b * C::BS, id, this_scale, kmap,
-                        g_nb, la, on, sx, s2, a.status);
+                        nbs, gco, la, on, sx, s2, a.status);
             S.res[j] = make_float2(sx, s2);
         }
         __syncwarp();
@@ -565,7 +605,7 @@ __global__ void __launch_bounds__(256) enc_iq_lattice_kernel(EncArgs a, const in
                     const int is = C::IS_LO + win;
                     const float id = ((float)(2 * C::KM - 1) + (float)is * C::STEP) / S.bmax[b];
                     float sx, s2;
-                    iq_trial<V>(xb, wb, ab, id, 1.0f / id, kmap, g_nb, ls, on, sx, s2, a.status);
+                    iq_trial<V>(xb, wb, ab, id, 1.0f / id, kmap, nbs, gco, ls, on, sx, s2, a.status);
                 }
                 int n_not = 0;
 #pragma unroll
@@ -589,7 +629,7 @@ __global__ void __launch_bounds__(256) enc_iq_lattice_kernel(EncArgs a, const in
                                 xg[i] = xb[k * C::G + i];
                                 wg[i] = ab[k * C::G + i];
                             }
-                            if (!best_neighbour<V>(g_nb, m, xg, wg, scale, l)) set_status(a.status, SHC_ENONEIGHBOUR);
+                            if (!best_neighbour<V>(nbs, gco, m, xg, wg, scale, l)) set_status(a.status, SHC_ENONEIGHBOUR);
                         }
 #pragma unroll
                         for (int i = 0; i < C::G; i++) ls[k * C::G + i] = l[i];
@@ -733,7 +773,8 @@ __global__ void __launch_bounds__(256) enc_iq_lattice_kernel(EncArgs a, const in
 template <int V>
 static cudaError_t launch_lattice(const EncArgs &a, const IqTables &iq, int num_sms, cudaStream_t st) {
     using C = IqCfg<V>;
-    const size_t smem = ((C::KMAP * 4 + 15) & ~(size_t)15) + 8 * sizeof(IqWarpSmem<V>);
+    const size_t smem = ((C::KMAP * 4 + 15) & ~(size_t)15) + 8 * sizeof(IqWarpSmem<V>) + 512 +
+                        (lists_in_smem<V>() ? (size_t)iq.lists_bytes[V] : 0);
     auto fn = enc_iq_lattice_kernel<V>;
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -745,7 +786,8 @@ static cudaError_t launch_lattice(const EncArgs &a, const IqTables &iq, int num_
     const int64_t cap = (int64_t)num_sms * per_sm;
     if (grid > cap) grid = cap;
     if (grid < 1) grid = 1;
-    fn<<<(unsigned)grid, 256, smem, st>>>(a, iq.kmap[V], iq.neighbours[V]);
+    fn<<<(unsigned)grid, 256, smem, st>>>(a, iq.dkmap[V], static_cast<const uint8_t *>(iq.lists[V]),
+                                          iq.lists_bytes[V], iq.grid_coords[V]);
     return cudaGetLastError();
 }
 

@@ -17,61 +17,94 @@ namespace shc {
 
 // ---------------------------------------------------------------------------
 // Row sigma^2 (quant.rs:153-155): sequential f32 fold of x^2 over the whole
-// row, then / ne0.  One thread per row (the fold is order-dependent), rows
-// staged 32 x 64 per warp through shared memory so the global loads stay
-// coalesced; the next tile is loaded while the current one is summed.
+// row, then / ne0.  The fold is order-dependent, so one thread owns one row;
+// a warp owns 32 rows.  Tiles of 32 rows x 128 bytes stream into an 8-deep
+// shared-memory ring with cp.async (16-byte chunks, 4 rows x 128 B per
+// instruction, coalesced); chunk (row r, j) sits in slot j*32 + r so that
+// lane r reads its row 16 bytes at a time without bank conflicts.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(128) row_sigma2_kernel(RowSrc src, int64_t n_rows, float *out) {
-    __shared__ float tile[4][32][65];
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    const int64_t rbase = ((int64_t)blockIdx.x * 4 + wid) * 32;
-    if (rbase >= n_rows) return;
+constexpr int kSigStages = 8;
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+__global__ void __launch_bounds__(32) row_sigma2_kernel(RowSrc src, int64_t n_rows, float *out) {
+    __shared__ __align__(16) uint4 ring[kSigStages][256];
+    const int lane = threadIdx.x;
+    const int64_t rbase = (int64_t)blockIdx.x * 32;
     const int64_t ne0 = src.ne0;
-    float v[8][8];
-    auto load_tile = [&](int64_t c0) {
+    const int esz = src.src_type == SHC_SRC_F32 ? 4 : 2;
+    const int per_chunk = 16 / esz;            // elements per 16-byte chunk
+    const int64_t tile_cols = 8 * per_chunk;   // 128 bytes of every row per tile
+    const int64_t ntiles = (ne0 + tile_cols - 1) / tile_cols;
+    const char *base = static_cast<const char *>(src.ptr);
+    const int64_t row_bytes = src.row_stride * esz;
+    auto issue = [&](int64_t t) {
+        if (t < ntiles) {
+            uint4 *slot = ring[t % kSigStages];
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const int r = i * 4 + (lane >> 3), c = (lane & 7) * 8;
-            if (rbase + r < n_rows && c0 + c < ne0) load8(src, rbase + r, c0 + c, v[i]);
-        }
-    };
-    auto store_tile = [&](int64_t c0) {
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const int r = i * 4 + (lane >> 3), c = (lane & 7) * 8;
-            if (rbase + r < n_rows && c0 + c < ne0) {
-#pragma unroll
-                for (int k = 0; k < 8; k++) tile[wid][r][c + k] = v[i][k];
+            for (int i = 0; i < 8; i++) {
+                const int r = i * 4 + (lane >> 3), j = lane & 7;
+                const int64_t col = t * tile_cols + (int64_t)j * per_chunk;
+                if (rbase + r < n_rows && col < ne0)
+                    cp_async16(&slot[j * 32 + r], base + (rbase + r) * row_bytes + col * esz);
             }
         }
+        cp_async_commit();  // always commit so the group count stays fixed
     };
+#pragma unroll
+    for (int t = 0; t < kSigStages - 1; t++) issue(t);
     float s = 0.0f;
-    load_tile(0);
-    store_tile(0);
-    for (int64_t c0 = 0; c0 < ne0; c0 += 64) {
+    const bool mine = rbase + lane < n_rows;
+    for (int64_t t = 0; t < ntiles; t++) {
+        issue(t + kSigStages - 1);
+        cp_async_wait<kSigStages - 1>();
         __syncwarp();
-        const bool more = c0 + 64 < ne0;
-        if (more) load_tile(c0 + 64);
-        const int nc = (int)(ne0 - c0 < 64 ? ne0 - c0 : 64);
-        const float *t = tile[wid][lane];
-        if (rbase + lane < n_rows) {
-            if (nc == 64) {
-#pragma unroll 16
-                for (int c = 0; c < 64; c++) s += t[c] * t[c];
-            } else {
-                for (int c = 0; c < nc; c++) s += t[c] * t[c];
+        const uint4 *slot = ring[t % kSigStages];
+        const int64_t c0 = t * tile_cols;
+        const int nchunks = (int)((ne0 - c0 >= tile_cols) ? 8 : (ne0 - c0 + per_chunk - 1) / per_chunk);
+        if (mine) {
+            for (int j = 0; j < nchunks; j++) {
+                const uint4 q = slot[j * 32 + lane];
+                const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
+                if (src.src_type == SHC_SRC_F32) {
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const float x = __uint_as_float(wv[k]);
+                        s += x * x;
+                    }
+                } else if (src.src_type == SHC_SRC_BF16) {
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const float x0 = __uint_as_float(wv[k] << 16), x1 = __uint_as_float(wv[k] & 0xFFFF0000u);
+                        s += x0 * x0;
+                        s += x1 * x1;
+                    }
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const float x0 = f16_val((uint16_t)(wv[k] & 0xFFFF)), x1 = f16_val((uint16_t)(wv[k] >> 16));
+                        s += x0 * x0;
+                        s += x1 * x1;
+                    }
+                }
             }
         }
         __syncwarp();
-        if (more) store_tile(c0 + 64);
     }
-    if (rbase + lane < n_rows) out[rbase + lane] = s / (float)ne0;
+    cp_async_wait<0>();
+    if (mine) out[rbase + lane] = s / (float)ne0;
 }
 
 cudaError_t launch_row_sigma2(const RowSrc &src, int64_t n_rows, float *out, cudaStream_t st) {
     if (n_rows <= 0) return cudaSuccess;
-    const int64_t blocks = (n_rows + 127) / 128;
-    row_sigma2_kernel<<<(unsigned)blocks, 128, 0, st>>>(src, n_rows, out);
+    const int64_t blocks = (n_rows + 31) / 32;
+    row_sigma2_kernel<<<(unsigned)blocks, 32, 0, st>>>(src, n_rows, out);
     return cudaGetLastError();
 }
 
@@ -89,15 +122,20 @@ __global__ void __launch_bounds__(256) enc_q8_0_kernel(EncArgs a) {
     const int64_t nblk = a.n_rows * bpr;
     const int64_t ngrp = (nblk + 7) >> 3;
     const int64_t stride = (int64_t)gridDim.x * 8 * kQ80Unroll;
+    const bool contiguous = a.src.row_stride == a.src.ne0;
     for (int64_t g0 = ((int64_t)blockIdx.x * 8 + wid) * kQ80Unroll; g0 < ngrp; g0 += stride) {
         float v[kQ80Unroll][8];
 #pragma unroll
         for (int u = 0; u < kQ80Unroll; u++) {
             const int64_t blk = (g0 + u) * 8 + (lane >> 2);
             if (g0 + u < ngrp && blk < nblk) {
-                const int64_t row = blk / bpr;
-                const int64_t col = (blk - row * bpr) * 32 + (lane & 3) * 8;
-                load8(a.src, row, col, v[u]);
+                if (contiguous) {  // rows back to back: the block index is the element offset / 32
+                    load8(a.src, 0, blk * 32 + (lane & 3) * 8, v[u]);
+                } else {
+                    const int64_t row = blk / bpr;
+                    const int64_t col = (blk - row * bpr) * 32 + (lane & 3) * 8;
+                    load8(a.src, row, col, v[u]);
+                }
             } else {
 #pragma unroll
                 for (int k = 0; k < 8; k++) v[u][k] = 0.0f;
@@ -267,7 +305,7 @@ __global__ void __launch_bounds__(256) enc_q6_k_kernel(EncArgs a) {
 // grid `is = j` and j == 37 is the initial nmax/(vmax-vmin) grid.
 // ---------------------------------------------------------------------------
 template <int NMAX>
-__global__ void __launch_bounds__(256) enc_qk45_kernel(EncArgs a) {
+__global__ void __launch_bounds__(256, 1) enc_qk45_kernel(EncArgs a) {
     constexpr int BB = NMAX == 31 ? 176 : 144;
     constexpr float FN = (float)NMAX;
     __shared__ float s_x[8][8 * 33];
@@ -292,7 +330,7 @@ __global__ void __launch_bounds__(256) enc_qk45_kernel(EncArgs a) {
             s_w[wid][s * 33 + q * 8 + k] = base[k] * sqrtf(sig + v[k] * v[k]);
         }
         __syncwarp();
-        float x[32], w[32];
+        float x[32], w[32], xm[32];
 #pragma unroll
         for (int i = 0; i < 32; i++) {
             x[i] = s_x[wid][s * 33 + i];
@@ -305,6 +343,9 @@ __global__ void __launch_bounds__(256) enc_qk45_kernel(EncArgs a) {
         vmin = rminf(vmin, 0.0f);
 #pragma unroll
         for (int i = 0; i < 32; i++) vmax = rmaxf(vmax, x[i]);
+        // x[i] - vmin is the same rounded value for every grid: hoisted
+#pragma unroll
+        for (int i = 0; i < 32; i++) xm[i] = x[i] - vmin;
         // Shuffles below run on every lane, so the per-lane candidate loop
         // is the only code inside the data-dependent branch.
         const bool degen = vmax <= vmin;
@@ -323,12 +364,13 @@ __global__ void __launch_bounds__(256) enc_qk45_kernel(EncArgs a) {
             for (int j = q; j < 38; j += 4) {
                 const float iscale = j == 37 ? iscale0 : (-0.9f + 0.05f * (float)j + FN) / range;
                 float sl = 0.0f, sl2 = 0.0f, sxl = 0.0f;
+                float l[32];
 #pragma unroll
                 for (int i = 0; i < 32; i++) {
-                    const float l = round_clamp0_f(iscale * (x[i] - vmin), FN);
-                    const float wl = w[i] * l;
+                    l[i] = round_clamp0_f(iscale * xm[i], FN);
+                    const float wl = w[i] * l[i];
                     sl += wl;
-                    sl2 += w[i] * (l * l);
+                    sl2 += w[i] * (l[i] * l[i]);
                     sxl += wl * x[i];
                 }
                 float ts, tm;
@@ -351,8 +393,7 @@ __global__ void __launch_bounds__(256) enc_qk45_kernel(EncArgs a) {
                     float err = 0.0f;
 #pragma unroll
                     for (int i = 0; i < 32; i++) {
-                        const float l = round_clamp0_f(iscale * (x[i] - vmin), FN);
-                        const float diff = ts * l + tm - x[i];
+                        const float diff = ts * l[i] + tm - x[i];
                         err += w[i] * diff * diff;
                     }
                     if (j == 37) {
@@ -467,6 +508,250 @@ template __global__ void enc_qk45_kernel<15>(EncArgs);
 template __global__ void enc_qk45_kernel<31>(EncArgs);
 
 // ---------------------------------------------------------------------------
+// Legacy 32-blocks (quant.rs:171-229): Q4_0/Q5_0 with make_qx_quants (nmax 8
+// or 16), Q4_1/Q5_1 with make_qkx3_quants (nmax 15 or 31); these keep the
+// search's level vector, so the winner's levels are recomputed from its
+// grid.  A warp encodes 8 consecutive blocks (flat over the tensor's blocks,
+// rows may change inside a group), 4 lanes per block.
+// KIND: 0 Q4_0, 1 Q5_0, 2 Q4_1, 3 Q5_1
+// ---------------------------------------------------------------------------
+template <int KIND>
+__global__ void __launch_bounds__(256) enc_legacy_kernel(EncArgs a) {
+    constexpr bool SYM = KIND < 2;
+    constexpr int NMAX = KIND == 0 ? 8 : KIND == 1 ? 16 : KIND == 2 ? 15 : 31;
+    constexpr int BB = KIND == 0 ? 18 : KIND == 1 ? 22 : KIND == 2 ? 20 : 24;
+    constexpr float FN = (float)NMAX;
+    __shared__ float s_x[8][8 * 33];
+    __shared__ float s_w[8][8 * 33];
+    __shared__ float2 s_cand[8][8][20];
+    __shared__ __align__(16) uint8_t s_out[8][8 * BB];
+    __shared__ uint8_t s_l[8][256];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int b = lane >> 2, q = lane & 3;
+    const int64_t ne0 = a.src.ne0, bpr = ne0 >> 5, nblk = a.n_rows * bpr;
+    const int64_t ngrp = (nblk + 7) >> 3;
+    for (int64_t g = (int64_t)blockIdx.x * 8 + wid; g < ngrp; g += (int64_t)gridDim.x * 8) {
+        const int64_t blk = g * 8 + b;
+        const bool valid = blk < nblk;
+        const int64_t row = valid ? blk / bpr : 0;
+        const int64_t col = valid ? (blk - row * bpr) * 32 : 0;
+        float v[8], base[8];
+        float sig = 0.0f;
+        if (valid) {
+            load8(a.src, row, col + q * 8, v);
+            load_im8(im_row(a.im, ne0, a.row0 + row * a.row_step), col + q * 8, base);
+            sig = a.sigma2[row];
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; k++) { v[k] = 0.0f; base[k] = 1.0f; }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            s_x[wid][b * 33 + q * 8 + k] = v[k];
+            s_w[wid][b * 33 + q * 8 + k] = base[k] * sqrtf(sig + v[k] * v[k]);
+        }
+        __syncwarp();
+        float x[32], w[32];
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+            x[i] = s_x[wid][b * 33 + i];
+            w[i] = s_w[wid][b * 33 + i];
+        }
+        float d_out = 0.0f, m_out = 0.0f, win_iscale = 0.0f, win_vmin = 0.0f;
+        int mode = 0;  // SYM: 0 all nmax (tiny block), 1 levels from win_iscale
+                       // ASYM: 0 all zero (degenerate), 1 levels from win_iscale over x - vmin
+        if (SYM) {
+            // make_qx_quants (quant.rs:34-73)
+            float amax = 0.0f, mx = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+                const float av = fabsf(x[i]);
+                if (av > amax) { amax = av; mx = x[i]; }
+            }
+            const bool live = !(amax < kGroupMaxEps);
+            if (live) {
+                for (int t = q; t < 19; t += 4) {
+                    const float iscale = -(FN + 0.1f * (float)(t - 9)) / mx;
+                    float sumlx = 0.0f, suml2 = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < 32; i++) {
+                        const float l = round_clamp_f(iscale * x[i], -FN, FN - 1.0f);
+                        sumlx += w[i] * x[i] * l;
+                        suml2 += w[i] * (l * l);
+                    }
+                    s_cand[wid][b][t] = make_float2(sumlx, suml2);
+                }
+            }
+            __syncwarp();
+            if (live) {
+                float best = 0.0f, best_scale = 0.0f;
+                bool first = true;
+                int win = -1;
+                for (int t = 0; t < 19; t++) {
+                    const float2 c = s_cand[wid][b][t];
+                    if (c.y > 0.0f && (first || c.x * c.x > best * c.y)) {
+                        const float sc = c.x / c.y;
+                        best_scale = sc;
+                        best = sc * c.x;
+                        first = false;
+                        win = t;
+                    }
+                }
+                d_out = best_scale;
+                if (win >= 0) {
+                    mode = 1;
+                    win_iscale = -(FN + 0.1f * (float)(win - 9)) / mx;
+                } else {
+                    mode = 2;  // no grid accepted: the level vector stays all zero
+                }
+            }
+        } else {
+            // make_qkx3_quants (quant.rs:77-141), rmin -0.9, rdelta 0.05, 36 steps
+            float vmin = INFINITY, vmax = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < 32; i++) vmin = rminf(vmin, x[i]);
+            vmin = rminf(vmin, 0.0f);
+#pragma unroll
+            for (int i = 0; i < 32; i++) vmax = rmaxf(vmax, x[i]);
+            const bool degen = vmax <= vmin;
+            const float range = vmax - vmin;
+            const float iscale0 = FN / range;
+            const float scale0 = 1.0f / iscale0;
+            float init_err = 0.0f, best_e = 0.0f, best_s = 0.0f, best_m = 0.0f;
+            int best_j = -1;
+            if (!degen) {
+                float sum_w = 0.0f, sum_x = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 32; i++) {
+                    sum_w += w[i];
+                    sum_x += w[i] * x[i];
+                }
+                for (int j = q; j < 38; j += 4) {
+                    const float iscale = j == 37 ? iscale0 : (-0.9f + 0.05f * (float)j + FN) / range;
+                    float sl = 0.0f, sl2 = 0.0f, sxl = 0.0f;
+                    float l[32];
+#pragma unroll
+                    for (int i = 0; i < 32; i++) {
+                        l[i] = round_clamp0_f(iscale * (x[i] - vmin), FN);
+                        const float wl = w[i] * l[i];
+                        sl += wl;
+                        sl2 += w[i] * (l[i] * l[i]);
+                        sxl += wl * x[i];
+                    }
+                    float ts, tm;
+                    bool ok;
+                    if (j == 37) {
+                        ts = scale0;
+                        tm = vmin;
+                        ok = true;
+                    } else {
+                        const float D = sum_w * sl2 - sl * sl;
+                        ok = D > 0.0f;
+                        ts = (sum_w * sxl - sum_x * sl) / D;
+                        tm = (sl2 * sum_x - sl * sxl) / D;
+                        if (tm > 0.0f) {
+                            tm = 0.0f;
+                            ts = sl2 > 0.0f ? sxl / sl2 : 0.0f;
+                        }
+                    }
+                    if (ok) {
+                        float err = 0.0f;
+#pragma unroll
+                        for (int i = 0; i < 32; i++) {
+                            const float diff = ts * l[i] + tm - x[i];
+                            err += w[i] * diff * diff;
+                        }
+                        if (j == 37) {
+                            init_err = err;
+                        } else if (err == err && (best_j < 0 || err < best_e)) {
+                            best_e = err;
+                            best_j = j;
+                            best_s = ts;
+                            best_m = tm;
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+#pragma unroll
+            for (int off = 1; off <= 2; off <<= 1) {
+                const float oe = __shfl_xor_sync(0xffffffffu, best_e, off);
+                const int oj = __shfl_xor_sync(0xffffffffu, best_j, off);
+                const float os = __shfl_xor_sync(0xffffffffu, best_s, off);
+                const float om = __shfl_xor_sync(0xffffffffu, best_m, off);
+                if (oj >= 0 && (best_j < 0 || oe < best_e || (oe == best_e && oj < best_j))) {
+                    best_e = oe;
+                    best_j = oj;
+                    best_s = os;
+                    best_m = om;
+                }
+            }
+            init_err = __shfl_sync(0xffffffffu, init_err, (lane & ~3) | 1);
+            if (degen) {
+                d_out = 0.0f;
+                m_out = vmin;
+                mode = 0;
+            } else if (best_j >= 0 && best_e < init_err) {
+                d_out = best_s;
+                m_out = best_m;
+                mode = 1;
+                win_iscale = (-0.9f + 0.05f * (float)best_j + FN) / range;
+            } else {
+                d_out = scale0;
+                m_out = vmin;
+                mode = 1;
+                win_iscale = iscale0;
+            }
+            win_vmin = vmin;
+        }
+        // levels of this lane's 8 elements
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            int l;
+            if (SYM) l = mode == 1 ? clampi(nearest_int(win_iscale * v[k]), -NMAX, NMAX - 1) + NMAX : (mode == 0 ? NMAX : 0);
+            else l = mode == 1 ? clampi(nearest_int(win_iscale * (v[k] - win_vmin)), 0, NMAX) : 0;
+            s_l[wid][lane * 8 + k] = (uint8_t)l;
+        }
+        __syncwarp();
+        {
+            uint8_t *o = s_out[wid] + b * BB;
+            const uint8_t *L = s_l[wid] + b * 32;
+            if (q == 0) {
+                const uint16_t hd = f16_bits(d_out);
+                o[0] = (uint8_t)(hd & 0xFF);
+                o[1] = (uint8_t)(hd >> 8);
+                if (!SYM) {
+                    const uint16_t hm = f16_bits(m_out);
+                    o[2] = (uint8_t)(hm & 0xFF);
+                    o[3] = (uint8_t)(hm >> 8);
+                }
+                if (KIND == 1 || KIND == 3) {
+                    uint32_t qh = 0;
+                    for (int j = 0; j < 32; j++) qh |= ((uint32_t)((L[j] >> 4) & 1)) << j;
+                    const int at = KIND == 1 ? 2 : 4;
+                    o[at] = (uint8_t)qh;
+                    o[at + 1] = (uint8_t)(qh >> 8);
+                    o[at + 2] = (uint8_t)(qh >> 16);
+                    o[at + 3] = (uint8_t)(qh >> 24);
+                }
+            }
+            const int qs = KIND == 0 ? 2 : KIND == 1 ? 6 : KIND == 2 ? 4 : 8;
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                const int j = q * 4 + t;
+                o[qs + j] = (KIND == 2 || KIND == 0) ? (uint8_t)((L[j] & 0xF) | (L[j + 16] << 4))
+                                                     : (uint8_t)((L[j] & 0xF) | ((L[j + 16] & 0xF) << 4));
+            }
+        }
+        __syncwarp();
+        const int64_t blk0 = g * 8;
+        const int nb = (int)(nblk - blk0 < 8 ? nblk - blk0 : 8);
+        store_block(a.dst + blk0 * BB, s_out[wid], nb * BB, a.dst_aligned16 && nb == 8, lane);
+        __syncwarp();
+    }
+}
+
+// ---------------------------------------------------------------------------
 // Elementwise encodings (quant.rs:546-560): F32 copy, F16 round-to-nearest-
 // even, BF16 by truncating the low 16 bits (`(v.to_bits() >> 16) as u16`).
 // ---------------------------------------------------------------------------
@@ -528,6 +813,19 @@ cudaError_t launch_kquant(uint32_t type, const EncArgs &a, int num_sms, cudaStre
     case SHC_TYPE_Q5_K: {
         unsigned grid = persistent_grid((const void *)enc_qk45_kernel<31>, 256, num_sms, a.n_rows * nsb);
         enc_qk45_kernel<31><<<grid, 256, 0, st>>>(a);
+        break;
+    }
+    case SHC_TYPE_Q4_0: case SHC_TYPE_Q5_0: case SHC_TYPE_Q4_1: case SHC_TYPE_Q5_1: {
+        const int64_t ngrp = (a.n_rows * (a.src.ne0 / 32) + 7) / 8;
+        const void *fn = type == SHC_TYPE_Q4_0 ? (const void *)enc_legacy_kernel<0>
+                         : type == SHC_TYPE_Q5_0 ? (const void *)enc_legacy_kernel<1>
+                         : type == SHC_TYPE_Q4_1 ? (const void *)enc_legacy_kernel<2>
+                                                 : (const void *)enc_legacy_kernel<3>;
+        unsigned grid = persistent_grid(fn, 256, num_sms, ngrp);
+        if (type == SHC_TYPE_Q4_0) enc_legacy_kernel<0><<<grid, 256, 0, st>>>(a);
+        else if (type == SHC_TYPE_Q5_0) enc_legacy_kernel<1><<<grid, 256, 0, st>>>(a);
+        else if (type == SHC_TYPE_Q4_1) enc_legacy_kernel<2><<<grid, 256, 0, st>>>(a);
+        else enc_legacy_kernel<3><<<grid, 256, 0, st>>>(a);
         break;
     }
     default:

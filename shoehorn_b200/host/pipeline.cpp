@@ -1,0 +1,684 @@
+// plan / quantize over the CUDA library (reference src/main.rs:209-751).
+#include "pipeline.hpp"
+
+#include <cuda_runtime.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cmath>
+#include <condition_variable>
+#include <cstdio>
+#include <cstring>
+#include <exception>
+#include <map>
+#include <mutex>
+#include <thread>
+
+#include "shoehorn_cuda.h"
+
+namespace shh {
+
+using Clock = std::chrono::steady_clock;
+static double secs_since(Clock::time_point t0) {
+    return std::chrono::duration<double>(Clock::now() - t0).count();
+}
+
+// ---------------------------------------------------------------------------
+// sizes and the budget model (main.rs:209-337)
+// ---------------------------------------------------------------------------
+uint64_t parse_size(const std::string &s0) {
+    std::string s = s0;
+    while (!s.empty() && isspace((unsigned char)s.back())) s.pop_back();
+    size_t b = 0;
+    while (b < s.size() && isspace((unsigned char)s[b])) b++;
+    s = s.substr(b);
+    std::string lower = s;
+    for (auto &c : lower) c = (char)tolower((unsigned char)c);
+    auto ends = [&](const char *suf) {
+        const size_t n = strlen(suf);
+        return lower.size() >= n && lower.compare(lower.size() - n, n, suf) == 0;
+    };
+    std::string num;
+    uint64_t mult = 1;
+    if (ends("gib")) { num = lower.substr(0, lower.size() - 3); mult = 1ull << 30; }
+    else if (ends("mib")) { num = lower.substr(0, lower.size() - 3); mult = 1ull << 20; }
+    else if (ends("gb")) { num = lower.substr(0, lower.size() - 2); mult = 1000000000ull; }
+    else if (ends("mb")) { num = lower.substr(0, lower.size() - 2); mult = 1000000ull; }
+    else if (ends("g")) { num = lower.substr(0, lower.size() - 1); mult = 1ull << 30; }
+    else if (ends("m")) { num = lower.substr(0, lower.size() - 1); mult = 1ull << 20; }
+    else num = lower;
+    while (!num.empty() && isspace((unsigned char)num.back())) num.pop_back();
+    size_t nb = 0;
+    while (nb < num.size() && isspace((unsigned char)num[nb])) nb++;
+    num = num.substr(nb);
+    char *end = nullptr;
+    const double v = num.empty() ? NAN : strtod(num.c_str(), &end);
+    if (num.empty() || end != num.c_str() + num.size() || std::isnan(v)) throw Error("bad size \"" + s0 + "\"");
+    // a bare number up to 4096 means GiB (main.rs:228-230)
+    if (mult == 1 && v != 0.0 && v <= 4096.0) mult = 1ull << 30;
+    const double r = v * (double)mult;
+    if (r <= 0) return 0;
+    if (r >= 18446744073709551615.0) return UINT64_MAX;
+    return (uint64_t)r;
+}
+
+std::string fmt_size(uint64_t b) {
+    char buf[64];
+    if (b >= (1ull << 30)) snprintf(buf, sizeof buf, "%.2f GiB", (double)b / (double)(1ull << 30));
+    else if (b >= (1ull << 20)) snprintf(buf, sizeof buf, "%.1f MiB", (double)b / (double)(1ull << 20));
+    else snprintf(buf, sizeof buf, "%llu B", (unsigned long long)b);
+    return buf;
+}
+
+double kv_bytes_per_element(const std::string &kv) {
+    if (kv == "f16") return 2.0;
+    if (kv == "q8_0") return 34.0 / 32.0;
+    if (kv == "q4_0") return 18.0 / 32.0;
+    throw Error("unsupported --kv " + kv + " (use f16, q8_0, or q4_0)");
+}
+
+static const Value *find_kv(const std::vector<KV> &kvs, const std::string &key) {
+    for (auto &p : kvs)
+        if (p.first == key) return &p.second;
+    return nullptr;
+}
+
+Hyper hyperparams(const std::vector<KV> &kvs) {
+    Hyper h;
+    const Value *a = find_kv(kvs, "general.architecture");
+    if (!a || !a->as_str()) throw Error("missing general.architecture");
+    h.arch = *a->as_str();
+    auto get = [&](const std::string &key, uint64_t &out) {
+        const Value *v = find_kv(kvs, h.arch + "." + key);
+        return v && v->as_u64(out);
+    };
+    if (!get("block_count", h.n_layer)) throw Error("missing block_count");
+    if (!get("embedding_length", h.n_embd)) h.n_embd = 0;
+    uint64_t n_head = 1;
+    if (!get("attention.head_count", n_head)) n_head = 1;
+    n_head = std::max<uint64_t>(n_head, 1);
+    if (!get("attention.head_count_kv", h.n_kv_head)) h.n_kv_head = n_head;
+    if (!get("attention.key_length", h.key_len)) h.key_len = h.n_embd / n_head;
+    if (!get("attention.value_length", h.val_len)) h.val_len = h.key_len;
+    if (!get("vocab_size", h.n_vocab)) {
+        const Value *t = find_kv(kvs, "tokenizer.ggml.tokens");
+        h.n_vocab = (t && t->type == 9) ? t->arr.size() : 32000;
+    }
+    return h;
+}
+
+Budget compute_budget(const FitArgs &args, const Hyper &h) {
+    Budget b;
+    if (!args.budget.empty()) {
+        b.usable_vram = parse_size(args.budget);
+        b.source = "--budget " + args.budget;
+    } else if (!args.target.empty()) {
+        b.usable_vram = parse_size(args.target) * 74 / 100;
+        b.source = "--target " + args.target + " (74% of RAM, macOS working-set approximation)";
+    } else {
+        // The reference probes Metal/NVML free memory (vram.rs); here the
+        // first GPU's free memory stands in for it.
+        size_t free_b = 0, total_b = 0;
+        if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess)
+            throw Error("no probeable GPU found; pass --budget");
+        b.usable_vram = free_b;
+        b.source = "CUDA free memory";
+    }
+    const double kv_elem = kv_bytes_per_element(args.kv);
+    b.kv_bytes = (uint64_t)((double)h.n_layer * (double)args.ctx * (double)h.n_kv_head * (double)(h.key_len + h.val_len) *
+                            kv_elem);
+    const uint64_t ubatch = std::min<uint64_t>(512, args.ctx);
+    b.compute_bytes = ubatch * h.n_vocab * 4 + ubatch * h.n_embd * 4 * 8;
+    b.reserve = !args.reserve.empty() ? parse_size(args.reserve) : (args.calibrate ? (160ull << 20) : (512ull << 20));
+    const uint64_t overhead = b.kv_bytes + b.compute_bytes + b.reserve;
+    if (overhead >= b.usable_vram)
+        throw Error("no room for weights: VRAM " + fmt_size(b.usable_vram) + " - KV " + fmt_size(b.kv_bytes) +
+                    " - compute " + fmt_size(b.compute_bytes) + " - reserve " + fmt_size(b.reserve) +
+                    " <= 0 (try smaller --ctx)");
+    b.model_budget = b.usable_vram - overhead;
+    return b;
+}
+
+static bool ends_with(const std::string &s, const char *suf) {
+    const size_t n = strlen(suf);
+    return s.size() >= n && s.compare(s.size() - n, n, suf) == 0;
+}
+
+Disposition dispose(const TensorInfo &t) {
+    Disposition d;
+    const bool quantizable = t.dims.size() >= 2 && ends_with(t.name, ".weight") && t.ne0() % 32 == 0;
+    if (!quantizable) {
+        d.fixed = true;
+        d.ty = (t.ty == T_F16 || t.ty == T_BF16 || t.ty == T_F32) ? T_F32 : t.ty;
+        return d;
+    }
+    d.fixed = false;
+    const bool sensitive = t.name == "token_embd.weight" || t.name == "output.weight";
+    if (t.ne0() % 256 == 0) {
+        d.cands = {T_IQ4_XS, T_Q4_K, T_Q5_K, T_Q6_K, T_Q8_0};
+        if (!sensitive) d.cands.insert(d.cands.end(), {T_IQ2_XXS, T_IQ2_XS, T_IQ2_S, T_IQ3_XXS, T_IQ3_S});
+    } else {
+        d.cands = {T_IQ4_NL, T_Q4_0, T_Q4_1, T_Q5_0, T_Q5_1, T_Q8_0};
+    }
+    d.cands.push_back(T_F16);
+    std::stable_sort(d.cands.begin(), d.cands.end(),
+                     [&](uint32_t a, uint32_t b) { return row_bytes(a, t.ne0()) < row_bytes(b, t.ne0()); });
+    return d;
+}
+
+ModelView view_of(const Model &m) {
+    ModelView v;
+    v.kvs = m.kvs;
+    v.tensors = m.tensors;
+    v.alignment = m.alignment;
+    v.total_bytes = m.total_bytes();
+    const Model *mp = &m;
+    v.data = [mp](size_t i) { return mp->tensor_data(mp->tensors[i]); };
+    return v;
+}
+
+// ---------------------------------------------------------------------------
+// GPU workers
+// ---------------------------------------------------------------------------
+struct GpuPool::Worker {
+    int dev = 0;
+    shc_ctx *ctx = nullptr;
+    cudaStream_t st = nullptr;
+    std::vector<void *> dbuf = std::vector<void *>(8, nullptr);
+    std::vector<size_t> dsz = std::vector<size_t>(8, 0);
+    std::vector<void *> hbuf = std::vector<void *>(4, nullptr);
+    std::vector<size_t> hsz = std::vector<size_t>(4, 0);
+    void *d(int slot, size_t bytes) {
+        if (dsz[(size_t)slot] < bytes) {
+            if (dbuf[(size_t)slot]) cudaFree(dbuf[(size_t)slot]);
+            dbuf[(size_t)slot] = nullptr;
+            dsz[(size_t)slot] = 0;
+            if (cudaMalloc(&dbuf[(size_t)slot], bytes) != cudaSuccess) throw Error("device allocation failed");
+            dsz[(size_t)slot] = bytes;
+        }
+        return dbuf[(size_t)slot];
+    }
+    void *h(int slot, size_t bytes) {
+        if (hsz[(size_t)slot] < bytes) {
+            if (hbuf[(size_t)slot]) cudaFreeHost(hbuf[(size_t)slot]);
+            hbuf[(size_t)slot] = nullptr;
+            hsz[(size_t)slot] = 0;
+            if (cudaMallocHost(&hbuf[(size_t)slot], bytes) != cudaSuccess) throw Error("pinned allocation failed");
+            hsz[(size_t)slot] = bytes;
+        }
+        return hbuf[(size_t)slot];
+    }
+};
+
+static void cuda_check(cudaError_t e, const char *what) {
+    if (e != cudaSuccess) throw Error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+static void shc_check(int rc, const char *what) {
+    if (rc != SHC_OK) throw Error(std::string(what) + ": " + shc_status_string(rc));
+}
+
+GpuPool::GpuPool(int n_gpus, int64_t timeout_ms) : timeout_ms_(timeout_ms) {
+    int avail = 0;
+    if (cudaGetDeviceCount(&avail) != cudaSuccess || avail < 1) throw Error("no CUDA device");
+    if (n_gpus < 1 || n_gpus > avail) n_gpus = n_gpus < 1 ? 1 : avail;
+    for (int w = 0; w < n_gpus; w++) {
+        auto wk = std::make_unique<Worker>();
+        wk->dev = w;
+        cuda_check(cudaSetDevice(w), "cudaSetDevice");
+        shc_check(shc_init(w, &wk->ctx), "shc_init");
+        cuda_check(cudaStreamCreateWithFlags(&wk->st, cudaStreamNonBlocking), "cudaStreamCreate");
+        workers_.push_back(std::move(wk));
+    }
+    cudaSetDevice(0);
+}
+
+GpuPool::~GpuPool() {
+    for (auto &w : workers_) {
+        cudaSetDevice(w->dev);
+        cudaStreamSynchronize(w->st);
+        for (auto p : w->dbuf)
+            if (p) cudaFree(p);
+        for (auto p : w->hbuf)
+            if (p) cudaFreeHost(p);
+        cudaStreamDestroy(w->st);
+        shc_free(w->ctx);
+    }
+}
+
+void GpuPool::run(size_t n_jobs, const std::function<void(int, size_t)> &fn) {
+    std::atomic<size_t> next{0};
+    std::exception_ptr err;
+    std::mutex mu;
+    std::vector<std::thread> th;
+    for (int w = 0; w < size(); w++) {
+        th.emplace_back([&, w]() {
+            cudaSetDevice(workers_[(size_t)w]->dev);
+            for (;;) {
+                const size_t j = next.fetch_add(1);
+                if (j >= n_jobs) break;
+                {
+                    std::lock_guard<std::mutex> lk(mu);
+                    if (err) break;
+                }
+                try {
+                    fn(w, j);
+                } catch (...) {
+                    std::lock_guard<std::mutex> lk(mu);
+                    if (!err) err = std::current_exception();
+                    break;
+                }
+            }
+        });
+    }
+    for (auto &t : th) t.join();
+    if (err) std::rethrow_exception(err);
+}
+
+// Bring rows of one tensor to the device as an f32/f16/bf16 view: a strided
+// host->device gather, then a device decode for block-quantized storage
+// (the reference decodes with quant.rs:581 decode_row before measuring).
+struct DevRows {
+    const void *ptr;
+    uint32_t src_type;
+};
+static DevRows rows_to_device(GpuPool::Worker &wk, const TensorInfo &t, const uint8_t *data, uint64_t r0, uint64_t n,
+                              uint64_t step) {
+    const uint64_t ne0 = t.ne0(), srb = row_bytes(t.ty, ne0);
+    void *raw = wk.d(0, (size_t)(n * srb + 16));
+    cuda_check(cudaMemcpy2DAsync(raw, srb, data + r0 * srb, srb * step, srb, n, cudaMemcpyHostToDevice, wk.st),
+               "row upload");
+    if (t.ty == T_F32 || t.ty == T_F16 || t.ty == T_BF16) return {raw, t.ty};
+    void *f = wk.d(1, (size_t)(n * ne0 * 4 + 16));
+    shc_check(shc_decode_rows(wk.ctx, t.ty, static_cast<const uint8_t *>(raw), (int64_t)n, (int64_t)ne0,
+                              static_cast<float *>(f), wk.st),
+              "decode source rows");
+    return {f, SHC_SRC_F32};
+}
+
+// ---------------------------------------------------------------------------
+// build_plan (main.rs:454-589)
+// ---------------------------------------------------------------------------
+static uint64_t rows_per_mat_of(const TensorInfo &t) { return t.dims.size() >= 3 ? t.dims[1] : t.n_rows(); }
+
+// Parse "TYPE[,name=TYPE...]" for the uniform harness mode.
+static void parse_uniform(const std::string &spec, uint32_t &def, std::map<std::string, uint32_t> &over) {
+    size_t p = 0;
+    bool first = true;
+    while (p <= spec.size()) {
+        const size_t c = spec.find(',', p);
+        const std::string item = spec.substr(p, c == std::string::npos ? std::string::npos : c - p);
+        const size_t eq = item.find('=');
+        uint32_t ty;
+        if (eq == std::string::npos) {
+            if (!type_from_name(item, ty)) throw Error("unknown type in --uniform: " + item);
+            if (!first) throw Error("--uniform: the default type must come first");
+            def = ty;
+        } else {
+            if (!type_from_name(item.substr(eq + 1), ty)) throw Error("unknown type in --uniform: " + item);
+            over[item.substr(0, eq)] = ty;
+        }
+        first = false;
+        if (c == std::string::npos) break;
+        p = c + 1;
+    }
+}
+
+static std::pair<std::vector<PlanEntry>, uint64_t> assemble_entries(const ModelView &m,
+                                                                    const std::vector<std::pair<size_t, uint32_t>> &fixed,
+                                                                    const std::vector<TensorChoices> &choices,
+                                                                    const std::vector<size_t> &sel) {
+    std::vector<PlanEntry> entries;
+    for (auto &f : fixed) {
+        const auto &t = m.tensors[f.first];
+        entries.push_back({f.first, f.second, row_bytes(f.second, t.ne0()) * t.n_rows(), false});
+    }
+    uint64_t solved = 0;
+    for (size_t i = 0; i < choices.size(); i++) {
+        const auto &c = choices[i].cands[sel[i]];
+        solved += c.bytes;
+        entries.push_back({choices[i].tensor_idx, c.ty, c.bytes, true});
+    }
+    std::stable_sort(entries.begin(), entries.end(),
+                     [](const PlanEntry &a, const PlanEntry &b) { return a.tensor_idx < b.tensor_idx; });
+    return {entries, solved};
+}
+
+Plan build_plan(const FitArgs &args, const ModelView &m, const Imatrix &im, GpuPool &pool, Timing &tm) {
+    Plan plan;
+    const Hyper h = hyperparams(m.kvs);
+    const bool uniform = !args.uniform.empty();
+    if (!uniform) plan.budget = compute_budget(args, h);
+    if (args.imatrix.empty() && im.empty())
+        fprintf(stderr, "warning: no imatrix given; quantizing with activation-agnostic weights\n");
+    fprintf(stderr, "model: %s | %zu tensors | arch %s | ctx %llu\n", fmt_size(m.total_bytes).c_str(),
+            m.tensors.size(), h.arch.c_str(), (unsigned long long)args.ctx);
+    size_t already = 0;
+    for (auto &t : m.tensors)
+        if (!(t.ty == T_F16 || t.ty == T_BF16 || t.ty == T_F32)) already++;
+    if (already * 2 > m.tensors.size())
+        fprintf(stderr, "warning: source is already quantized; re-quantizing compounds the loss - start from the "
+                        "BF16/F16 GGUF if one exists\n");
+    {
+        uint64_t train_ctx;
+        const Value *v = find_kv(m.kvs, h.arch + ".context_length");
+        if (v && v->as_u64(train_ctx) && args.ctx > train_ctx)
+            fprintf(stderr, "warning: --ctx %llu exceeds the model's training context %llu; budgeting for it anyway\n",
+                    (unsigned long long)args.ctx, (unsigned long long)train_ctx);
+    }
+    if (!uniform)
+        fprintf(stderr, "budget: %s usable (%s) - %s KV - %s compute est - %s reserve = %s for weights\n",
+                fmt_size(plan.budget.usable_vram).c_str(), plan.budget.source.c_str(),
+                fmt_size(plan.budget.kv_bytes).c_str(), fmt_size(plan.budget.compute_bytes).c_str(),
+                fmt_size(plan.budget.reserve).c_str(), fmt_size(plan.budget.model_budget).c_str());
+
+    std::vector<std::pair<size_t, std::vector<uint32_t>>> to_solve;
+    size_t n_with_im = 0;
+    for (size_t i = 0; i < m.tensors.size(); i++) {
+        const auto &t = m.tensors[i];
+        const Disposition d = dispose(t);
+        if (d.fixed) {
+            plan.fixed_bytes += row_bytes(d.ty, t.ne0()) * t.n_rows();
+            plan.fixed.emplace_back(i, d.ty);
+        } else {
+            if (lookup(im, t.name)) n_with_im++;
+            to_solve.emplace_back(i, d.cands);
+        }
+    }
+    fprintf(stderr, "tensors: %zu to solve (%zu with imatrix data), %zu fixed (%s)\n", to_solve.size(), n_with_im,
+            plan.fixed.size(), fmt_size(plan.fixed_bytes).c_str());
+
+    if (uniform) {
+        uint32_t def = T_Q4_K;
+        std::map<std::string, uint32_t> over;
+        parse_uniform(args.uniform, def, over);
+        std::vector<size_t> sel;
+        for (auto &ts : to_solve) {
+            const auto &t = m.tensors[ts.first];
+            auto it = over.find(t.name);
+            const uint32_t ty = it != over.end() ? it->second : def;
+            TensorChoices tc;
+            tc.tensor_idx = ts.first;
+            tc.cands.push_back({ty, row_bytes(ty, t.ne0()) * t.n_rows(), 0.0});
+            plan.choices.push_back(tc);
+            sel.push_back(0);
+        }
+        auto [entries, solved] = assemble_entries(m, plan.fixed, plan.choices, sel);
+        plan.entries = entries;
+        plan.total_bytes = plan.fixed_bytes + solved;
+        plan.budget.model_budget = plan.total_bytes;
+        plan.budget.usable_vram = plan.total_bytes;
+        plan.budget.source = "--uniform " + args.uniform;
+        return plan;
+    }
+    if (plan.fixed_bytes >= plan.budget.model_budget) throw Error("fixed tensors alone exceed the weight budget");
+
+    // ---- measure weighted error for every (tensor, candidate) on the GPUs ----
+    const auto t0 = Clock::now();
+    const uint64_t sample_rows = args.exact_errors ? UINT64_MAX : 128;
+    struct Meas {
+        uint64_t step, sampled;
+        std::vector<std::vector<double>> err;  // [cand][sampled row]
+    };
+    std::vector<Meas> meas(to_solve.size());
+    struct Job {
+        size_t k;        // index into to_solve
+        uint64_t i0, i1; // sampled-row range
+        double cost;
+    };
+    std::vector<Job> jobs;
+    double total_cost = 0;
+    for (size_t k = 0; k < to_solve.size(); k++) {
+        const auto &t = m.tensors[to_solve[k].first];
+        const uint64_t n_rows = t.n_rows();
+        const uint64_t step = std::max<uint64_t>(n_rows / std::min(sample_rows, std::max<uint64_t>(n_rows, 1)), 1);
+        const uint64_t sampled = (n_rows + step - 1) / step;
+        meas[k].step = step;
+        meas[k].sampled = sampled;
+        meas[k].err.assign(to_solve[k].second.size(), std::vector<double>((size_t)sampled, 0.0));
+        total_cost += (double)sampled * (double)t.ne0() * (double)to_solve[k].second.size();
+    }
+    const double max_job_cost = std::max(total_cost / (8.0 * pool.size()), 1.0);
+    for (size_t k = 0; k < to_solve.size(); k++) {
+        const auto &t = m.tensors[to_solve[k].first];
+        const uint64_t step = meas[k].step, sampled = meas[k].sampled, rpm = rows_per_mat_of(t);
+        const double per_row = (double)t.ne0() * (double)to_solve[k].second.size();
+        // rows per job: bounded by cost and by ~256 MiB of f32 rows; never across a matrix
+        uint64_t cap = std::max<uint64_t>(1, (uint64_t)(max_job_cost / per_row));
+        cap = std::min<uint64_t>(cap, std::max<uint64_t>(1, (256ull << 20) / (t.ne0() * 4)));
+        uint64_t i = 0;
+        while (i < sampled) {
+            uint64_t end = std::min(sampled, i + cap);
+            const uint64_t mat = (i * step) / rpm;
+            while (end > i + 1 && ((end - 1) * step) / rpm != mat) end--;
+            jobs.push_back({k, i, end, per_row * (double)(end - i)});
+            i = end;
+        }
+    }
+    std::stable_sort(jobs.begin(), jobs.end(), [](const Job &a, const Job &b) { return a.cost > b.cost; });
+    pool.run(jobs.size(), [&](int w, size_t j) {
+        auto &wk = pool.worker(w);
+        const Job &jb = jobs[j];
+        const size_t ti = to_solve[jb.k].first;
+        const auto &t = m.tensors[ti];
+        const auto &types = to_solve[jb.k].second;
+        const uint64_t ne0 = t.ne0(), step = meas[jb.k].step, ni = jb.i1 - jb.i0;
+        const DevRows src = rows_to_device(wk, t, m.data(ti), jb.i0 * step, ni, step);
+        const std::vector<float> *tim = lookup(im, t.name);
+        const float *ims = row_slice(tim, ne0, rows_per_mat_of(t), jb.i0 * step);
+        float *dim = nullptr;
+        if (ims) {
+            dim = static_cast<float *>(wk.d(2, ne0 * 4));
+            cuda_check(cudaMemcpyAsync(dim, ims, ne0 * 4, cudaMemcpyHostToDevice, wk.st), "imatrix upload");
+        }
+        double *derr = static_cast<double *>(wk.d(3, types.size() * ni * 8));
+        shc_check(shc_row_errors(wk.ctx, types.data(), (int)types.size(), src.src_type, src.ptr, (int64_t)ni,
+                                 (int64_t)ne0, dim, ims ? (int64_t)ne0 : 0, 0, 0, 1, derr, wk.st),
+                  "row errors");
+        double *herr = static_cast<double *>(wk.h(0, types.size() * ni * 8));
+        cuda_check(cudaMemcpyAsync(herr, derr, types.size() * ni * 8, cudaMemcpyDeviceToHost, wk.st), "error download");
+        shc_check(shc_sync(wk.ctx, wk.st, args.timeout_ms), "row errors");
+        for (size_t c = 0; c < types.size(); c++)
+            std::memcpy(meas[jb.k].err[c].data() + jb.i0, herr + c * ni, ni * 8);
+    });
+    for (size_t k = 0; k < to_solve.size(); k++) {
+        const auto &t = m.tensors[to_solve[k].first];
+        const double scale = (double)t.n_rows() / (double)meas[k].sampled;
+        TensorChoices tc;
+        tc.tensor_idx = to_solve[k].first;
+        for (size_t c = 0; c < to_solve[k].second.size(); c++) {
+            double err = 0.0;  // rows in row order, as the reference's closure folds them
+            for (double e : meas[k].err[c]) err += e;
+            const uint32_t ty = to_solve[k].second[c];
+            tc.cands.push_back({ty, row_bytes(ty, t.ne0()) * t.n_rows(), err * scale});
+        }
+        plan.choices.push_back(std::move(tc));
+    }
+    tm.measure_s = secs_since(t0);
+
+    const auto t1 = Clock::now();
+    const uint64_t weight_budget = plan.budget.model_budget - plan.fixed_bytes;
+    auto sel = solve(plan.choices, weight_budget);
+    tm.solve_s = secs_since(t1);
+    if (!sel) {
+        uint64_t mn = 0;
+        for (auto &tc : plan.choices) mn += tc.cands[0].bytes;
+        throw Error("even the smallest mix (" + fmt_size(mn) + " + " + fmt_size(plan.fixed_bytes) +
+                    " fixed) exceeds the weight budget " + fmt_size(plan.budget.model_budget) +
+                    "; lower --ctx / --reserve or use a smaller model");
+    }
+    auto [entries, solved] = assemble_entries(m, plan.fixed, plan.choices, *sel);
+    plan.entries = entries;
+    plan.total_bytes = plan.fixed_bytes + solved;
+    return plan;
+}
+
+void print_plan(const Plan &plan, const ModelView &m) {
+    printf("\n%-42s %16s %7s %12s %6s\n", "tensor", "shape", "type", "size", "bpw");
+    std::map<std::string, std::pair<size_t, uint64_t>> by_type;
+    uint64_t total_elems = 0;
+    for (auto &t : m.tensors) total_elems += t.n_elements();
+    for (auto &e : plan.entries) {
+        const auto &t = m.tensors[e.tensor_idx];
+        std::string shape;
+        for (size_t i = 0; i < t.dims.size(); i++) shape += (i ? "x" : "") + std::to_string(t.dims[i]);
+        const double bpw = (double)e.bytes * 8.0 / (double)t.n_elements();
+        auto &bt = by_type[type_name(e.ty)];
+        bt.first++;
+        bt.second += e.bytes;
+        printf("%-42s %16s %7s %12s %6.2f\n", t.name.c_str(), shape.c_str(), type_name(e.ty).c_str(),
+               fmt_size(e.bytes).c_str(), bpw);
+    }
+    printf("\nby type:\n");
+    for (auto &kv : by_type) printf("  %6s: %3zu tensors, %s\n", kv.first.c_str(), kv.second.first, fmt_size(kv.second.second).c_str());
+    const Budget &b = plan.budget;
+    printf("\nweights: %s of %s budget (%.3f%% used, %s slack) | overall %.3f bpw\n", fmt_size(plan.total_bytes).c_str(),
+           fmt_size(b.model_budget).c_str(), 100.0 * (double)plan.total_bytes / (double)std::max<uint64_t>(b.model_budget, 1),
+           fmt_size(b.model_budget - std::min(b.model_budget, plan.total_bytes)).c_str(),
+           (double)plan.total_bytes * 8.0 / (double)std::max<uint64_t>(total_elems, 1));
+    printf("projected VRAM at ctx: %s weights + %s KV + %s compute + %s reserve = %s of %s available\n",
+           fmt_size(plan.total_bytes).c_str(), fmt_size(b.kv_bytes).c_str(), fmt_size(b.compute_bytes).c_str(),
+           fmt_size(b.reserve).c_str(), fmt_size(plan.total_bytes + b.kv_bytes + b.compute_bytes + b.reserve).c_str(),
+           fmt_size(b.usable_vram).c_str());
+}
+
+uint32_t file_type_code(const std::vector<PlanEntry> &entries) {
+    uint64_t best_bytes = 0;
+    uint32_t best = 1;
+    for (auto &e : entries) {
+        if (!e.solved) continue;
+        uint32_t code;
+        switch (e.ty) {
+        case T_F16: code = 1; break;
+        case T_Q4_0: code = 2; break;
+        case T_Q4_1: code = 3; break;
+        case T_Q5_0: code = 8; break;
+        case T_Q5_1: code = 9; break;
+        case T_Q8_0: code = 7; break;
+        case T_Q4_K: code = 15; break;
+        case T_Q5_K: code = 17; break;
+        case T_Q6_K: code = 18; break;
+        case T_IQ2_XXS: code = 19; break;
+        case T_IQ2_XS: code = 20; break;
+        case T_IQ3_XXS: code = 23; break;
+        case T_IQ4_NL: code = 25; break;
+        case T_IQ3_S: code = 26; break;
+        case T_IQ2_S: code = 28; break;
+        case T_IQ4_XS: code = 30; break;
+        default: code = 1;
+        }
+        if (e.bytes > best_bytes) {
+            best_bytes = e.bytes;
+            best = code;
+        }
+    }
+    return best;
+}
+
+// ---------------------------------------------------------------------------
+// write_quantized (main.rs:691-751): output laid out up front, tensors encoded
+// by the GPUs in row ranges straight into a memory map of the temporary file
+// ---------------------------------------------------------------------------
+void write_quantized(const std::string &out_path, const Plan &plan, const ModelView &m, const Imatrix &im,
+                     GpuPool &pool, Timing &tm) {
+    const auto t0 = Clock::now();
+    std::vector<TensorInfo> infos;
+    for (auto &e : plan.entries) {
+        const auto &t = m.tensors[e.tensor_idx];
+        TensorInfo ti;
+        ti.name = t.name;
+        ti.dims = t.dims;
+        ti.ty = e.ty;
+        infos.push_back(ti);
+    }
+    std::vector<KV> kvs;
+    for (auto &kv : m.kvs)
+        if (kv.first != "general.file_type" && kv.first != "general.quantization_version" && kv.first.rfind("split.", 0) != 0)
+            kvs.push_back(kv);
+    kvs.emplace_back("general.file_type", Value::U32(file_type_code(plan.entries)));
+    kvs.emplace_back("general.quantization_version", Value::U32(2));
+    const Layout L = layout_for(kvs, infos, m.alignment);
+    // An empty out_path encodes into anonymous memory (benchmarks without a disk
+    // write); otherwise *.tmp next to the output, renamed when complete.
+    const bool to_file = !out_path.empty();
+    const std::string tmp = out_path + ".tmp";
+    uint8_t *map = nullptr;
+    if (to_file) {
+        const int fd = ::open(tmp.c_str(), O_RDWR | O_CREAT | O_TRUNC, 0644);
+        if (fd < 0) throw Error("creating " + tmp);
+        if (ftruncate(fd, (off_t)L.total) != 0) {
+            ::close(fd);
+            throw Error("sizing " + tmp);
+        }
+        map = L.total ? static_cast<uint8_t *>(mmap(nullptr, L.total, PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0)) : nullptr;
+        ::close(fd);
+    } else {
+        map = static_cast<uint8_t *>(mmap(nullptr, L.total, PROT_READ | PROT_WRITE, MAP_PRIVATE | MAP_ANONYMOUS, -1, 0));
+    }
+    if (L.total && map == MAP_FAILED) throw Error("mmap " + tmp);
+    const auto hdr = header_bytes(kvs, infos, m.alignment, L);
+    std::memcpy(map, hdr.data(), hdr.size());
+
+    struct Job {
+        size_t e;
+        uint64_t r0, r1;
+        double cost;
+    };
+    std::vector<Job> jobs;
+    uint64_t total_elems = 0;
+    for (auto &e : plan.entries) total_elems += m.tensors[e.tensor_idx].n_elements();
+    const uint64_t cap_elems = std::max<uint64_t>(1ull << 20, std::min<uint64_t>(64ull << 20, total_elems / (8 * pool.size())));
+    for (size_t ei = 0; ei < plan.entries.size(); ei++) {
+        const auto &e = plan.entries[ei];
+        const auto &t = m.tensors[e.tensor_idx];
+        const uint64_t n_rows = t.n_rows(), ne0 = t.ne0(), rpm = rows_per_mat_of(t);
+        if (e.ty == t.ty) {  // copied untouched (main.rs:735-737)
+            std::memcpy(map + L.data_start + L.offsets[ei], m.data(e.tensor_idx), t.byte_size());
+            continue;
+        }
+        const uint64_t rows_cap = std::max<uint64_t>(1, cap_elems / std::max<uint64_t>(ne0, 1));
+        for (uint64_t r = 0; r < n_rows;) {
+            uint64_t end = std::min(n_rows, r + rows_cap);
+            const uint64_t mat = r / rpm;
+            end = std::min(end, (mat + 1) * rpm);
+            jobs.push_back({ei, r, end, (double)(end - r) * (double)ne0});
+            r = end;
+        }
+    }
+    std::stable_sort(jobs.begin(), jobs.end(), [](const Job &a, const Job &b) { return a.cost > b.cost; });
+    pool.run(jobs.size(), [&](int w, size_t j) {
+        auto &wk = pool.worker(w);
+        const Job &jb = jobs[j];
+        const auto &e = plan.entries[jb.e];
+        const auto &t = m.tensors[e.tensor_idx];
+        const uint64_t ne0 = t.ne0(), n = jb.r1 - jb.r0, drb = row_bytes(e.ty, ne0);
+        const DevRows src = rows_to_device(wk, t, m.data(e.tensor_idx), jb.r0, n, 1);
+        const std::vector<float> *tim = lookup(im, t.name);
+        const float *ims = row_slice(tim, ne0, rows_per_mat_of(t), jb.r0);
+        float *dim = nullptr;
+        if (ims) {
+            dim = static_cast<float *>(wk.d(2, ne0 * 4));
+            cuda_check(cudaMemcpyAsync(dim, ims, ne0 * 4, cudaMemcpyHostToDevice, wk.st), "imatrix upload");
+        }
+        uint8_t *dout = static_cast<uint8_t *>(wk.d(4, n * drb + 16));
+        shc_check(shc_encode_rows(wk.ctx, e.ty, src.src_type, src.ptr, (int64_t)n, (int64_t)ne0, dim,
+                                  ims ? (int64_t)ne0 : 0, 0, 0, dout, wk.st),
+                  "encode rows");
+        uint8_t *hout = static_cast<uint8_t *>(wk.h(1, n * drb));
+        cuda_check(cudaMemcpyAsync(hout, dout, n * drb, cudaMemcpyDeviceToHost, wk.st), "encoded download");
+        shc_check(shc_sync(wk.ctx, wk.st, 3600 * 1000), "encode rows");
+        std::memcpy(map + L.data_start + L.offsets[jb.e] + jb.r0 * drb, hout, n * drb);
+    });
+    if (L.total) {
+        if (to_file) msync(map, L.total, MS_SYNC);
+        munmap(map, L.total);
+    }
+    if (to_file && rename(tmp.c_str(), out_path.c_str()) != 0) throw Error("renaming " + tmp + " -> " + out_path);
+    tm.encode_s = secs_since(t0);
+    fprintf(stderr, "wrote %s (%s)\n", to_file ? out_path.c_str() : "(memory)", fmt_size(L.total).c_str());
+}
+
+}  // namespace shh

@@ -1,0 +1,132 @@
+// The plan / quantize flow of the reference (src/main.rs:272-751) over the
+// CUDA library: budget model, candidate ladder, the fused error table on the
+// GPUs, the knapsack solve, and the streaming GGUF v3 writer.  Tensors, and
+// row ranges of large tensors, are spread over the GPUs of one box; there is
+// no collective on this path, only a host-side gather of per-row errors
+// (summed in row order) and of encoded byte ranges at precomputed offsets.
+#pragma once
+#include <cstdint>
+#include <functional>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "gguf.hpp"
+#include "imatrix.hpp"
+#include "solver.hpp"
+
+struct shc_ctx;
+
+namespace shh {
+
+struct FitArgs {  // main.rs:43-85, plus the GPU harness options
+    std::string model, imatrix;
+    uint64_t ctx = 8192;
+    std::string budget, target, kv = "f16", reserve;
+    bool calibrate = false;
+    bool exact_errors = false;
+    int gpus = 1;
+    std::string uniform;  // "TYPE[,tensor=TYPE...]": fixed mix instead of a solve
+    int64_t timeout_ms = 3600 * 1000;
+};
+
+uint64_t parse_size(const std::string &s);  // main.rs:209-232
+std::string fmt_size(uint64_t b);           // main.rs:252-260
+double kv_bytes_per_element(const std::string &kv);
+
+struct Hyper {  // main.rs:262-292
+    std::string arch;
+    uint64_t n_layer = 0, n_kv_head = 0, key_len = 0, val_len = 0, n_embd = 0, n_vocab = 0;
+};
+Hyper hyperparams(const std::vector<KV> &kvs);
+
+struct Budget {  // main.rs:294-337
+    uint64_t usable_vram = 0, kv_bytes = 0, compute_bytes = 0, reserve = 0, model_budget = 0;
+    std::string source;
+};
+Budget compute_budget(const FitArgs &args, const Hyper &h);
+
+struct Disposition {  // main.rs:339-380
+    bool fixed = true;
+    uint32_t ty = T_F32;
+    std::vector<uint32_t> cands;  // sorted by row bytes (stable)
+};
+Disposition dispose(const TensorInfo &t);
+
+struct PlanEntry {
+    size_t tensor_idx = 0;
+    uint32_t ty = 0;
+    uint64_t bytes = 0;
+    bool solved = false;
+};
+
+struct Timing {
+    double measure_s = 0, solve_s = 0, encode_s = 0;
+};
+
+struct Plan {
+    std::vector<PlanEntry> entries;
+    Budget budget;
+    uint64_t total_bytes = 0;
+    std::vector<TensorChoices> choices;
+    std::vector<std::pair<size_t, uint32_t>> fixed;
+    uint64_t fixed_bytes = 0;
+};
+
+// Tensor storage seen by the pipeline: infos plus a host pointer to each
+// tensor's raw bytes (an mmap'd GGUF, or synthetic data in host memory).
+struct ModelView {
+    std::vector<KV> kvs;
+    std::vector<TensorInfo> tensors;
+    uint64_t alignment = 32;
+    std::function<const uint8_t *(size_t)> data;
+    uint64_t total_bytes = 0;
+};
+ModelView view_of(const Model &m);
+
+// One worker thread and library context per GPU.
+class GpuPool {
+  public:
+    explicit GpuPool(int n_gpus, int64_t timeout_ms);
+    ~GpuPool();
+    int size() const { return (int)workers_.size(); }
+    // Runs fn(worker, job) for jobs 0..n_jobs-1, pulled dynamically by the
+    // workers in index order; rethrows the first failure.
+    void run(size_t n_jobs, const std::function<void(int, size_t)> &fn);
+    struct Worker;
+    Worker &worker(int w) { return *workers_[(size_t)w]; }
+
+  private:
+    std::vector<std::unique_ptr<Worker>> workers_;
+    int64_t timeout_ms_;
+};
+
+// main.rs:454-589 build_plan: measures every (tensor, candidate) error on
+// the GPUs and solves for the budget (or applies the uniform mix).
+Plan build_plan(const FitArgs &args, const ModelView &m, const Imatrix &im, GpuPool &pool, Timing &tm);
+void print_plan(const Plan &plan, const ModelView &m);
+uint32_t file_type_code(const std::vector<PlanEntry> &entries);  // main.rs:628-659
+// main.rs:691-751 write_quantized (without the calibration reuse path):
+// writes out_path via a temporary file and a rename.
+void write_quantized(const std::string &out_path, const Plan &plan, const ModelView &m, const Imatrix &im,
+                     GpuPool &pool, Timing &tm);
+
+// Synthetic models of the benchmark configurations (weights generated from
+// a seed straight into host memory).
+struct HostBuffer {
+    uint8_t *ptr = nullptr;
+    size_t n = 0;
+    bool pinned = false;
+    explicit HostBuffer(size_t bytes);
+    ~HostBuffer();
+    HostBuffer(const HostBuffer &) = delete;
+    HostBuffer &operator=(const HostBuffer &) = delete;
+};
+struct SyntheticModel {
+    ModelView view;
+    std::vector<std::unique_ptr<HostBuffer>> storage;
+    Imatrix imatrix;
+};
+std::unique_ptr<SyntheticModel> synthetic_model(const std::string &name, uint64_t seed, int threads);
+
+}  // namespace shh

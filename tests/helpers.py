@@ -9,7 +9,7 @@ IQ2_XXS, IQ2_XS, IQ3_XXS, IQ4_NL, IQ3_S, IQ2_S, IQ4_XS, BF16 = 16, 17, 18, 20, 2
 NAMES = {F32: "F32", F16: "F16", Q4_0: "Q4_0", Q4_1: "Q4_1", Q5_0: "Q5_0", Q5_1: "Q5_1", Q8_0: "Q8_0",
          Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K", IQ2_XXS: "IQ2_XXS", IQ2_XS: "IQ2_XS", IQ3_XXS: "IQ3_XXS",
          IQ4_NL: "IQ4_NL", IQ3_S: "IQ3_S", IQ2_S: "IQ2_S", IQ4_XS: "IQ4_XS", BF16: "BF16"}
-KQUANT = [Q8_0, Q6_K, Q4_K, Q5_K]
+KQUANT = [Q8_0, Q6_K, Q4_K, Q5_K, Q4_0, Q4_1, Q5_0, Q5_1]
 LEGACY = [Q4_0, Q4_1, Q5_0, Q5_1]
 IQ = [IQ2_XXS, IQ2_XS, IQ2_S, IQ3_XXS, IQ3_S, IQ4_NL, IQ4_XS]
 PLAIN = [F32, F16, BF16]
