@@ -257,55 +257,81 @@ struct IqCfg {
     static constexpr int KMAP = IQ2 ? 6561 : 4096;
 };
 
-// Compact lattice index of G levels l[0..G).
+// Levels of one block packed BITS per element, group k (G levels, the
+// lattice index's own bit layout) at bit k*G*BITS; groups never straddle
+// the two words (IQ2: 4 groups of 16 bits per word, IQ3: 5 of 12).
 template <int V>
-__device__ __forceinline__ int lattice_index(const int *l) {
+struct Levels {
     using C = IqCfg<V>;
-    int u = 0;
-    if (C::IQ2) {
-#pragma unroll
-        for (int i = C::G - 1; i >= 0; i--) u = u * 3 + l[i];
-    } else {
-#pragma unroll
-        for (int i = 0; i < C::G; i++) u |= l[i] << (3 * i);
+    static constexpr int GB = C::G * C::BITS;
+    static constexpr int GPW = 64 / GB;
+    uint64_t p0 = 0, p1 = 0;
+    __device__ __forceinline__ void set_group(int k, uint32_t g) {
+        const uint64_t mask = (1ull << GB) - 1;
+        if (k < GPW) {
+            const int sh = k * GB;
+            p0 = (p0 & ~(mask << sh)) | ((uint64_t)g << sh);
+        } else {
+            const int sh = (k - GPW) * GB;
+            p1 = (p1 & ~(mask << sh)) | ((uint64_t)g << sh);
+        }
     }
+    __device__ __forceinline__ uint32_t group(int k) const {
+        const uint64_t mask = (1ull << GB) - 1;
+        return k < GPW ? (uint32_t)((p0 >> (k * GB)) & mask) : (uint32_t)((p1 >> ((k - GPW) * GB)) & mask);
+    }
+    __device__ __forceinline__ int level(int i) const {  // i compile-time after unrolling
+        const int k = i / C::G, w = i % C::G;
+        const int sh = (k % GPW) * GB + w * C::BITS;
+        return (int)(((k < GPW ? p0 : p1) >> sh) & ((1u << C::BITS) - 1));
+    }
+};
+
+// Compact kmap index of a group given in the lattice bit layout.
+template <int V>
+__device__ __forceinline__ int kmap_index(uint32_t g) {
+    using C = IqCfg<V>;
+    if (!C::IQ2) return (int)g;  // IQ3: sum l_i << 3i is already the index
+    int u = 0;
+#pragma unroll
+    for (int i = C::G - 1; i >= 0; i--) u = u * 3 + (int)((g >> (2 * i)) & 3u);
     return u;
 }
 
 // find_best_neighbour (quant_iq.rs:137-167): first strict minimum of
-// sum_i waux_i * (scale*g_i - x_i)^2 over the neighbour list; writes the
-// winner's levels (g-1)/2.  Returns false if no candidate was finite.
+// sum_i waux_i * (scale*g_i - x_i)^2 over the neighbour list of kmap entry m;
+// returns the winner's packed levels ((g-1)/2), or ~0u if no candidate was
+// finite.  Kept out of line: the encoders call it from several places.
 template <int V>
-__device__ __forceinline__ void nb_eval(uint32_t c, const float *xv, const float *wa, float scale, float &best,
-                                        uint32_t &bc, bool &found) {
+__device__ __noinline__ uint32_t best_neighbour(const void *lists, const uint16_t *gco, int m, const float *xg_s,
+                                                const float *wg_s, float scale) {
     using C = IqCfg<V>;
     constexpr uint32_t MASK = (1u << C::BITS) - 1;
-    float d2 = 0.0f;
+    float xg[C::G], wg[C::G];
 #pragma unroll
     for (int i = 0; i < C::G; i++) {
-        const float pg = (float)(2 * (int)((c >> (C::BITS * i)) & MASK) + 1);
-        const float diff = scale * pg - xv[i];
-        d2 += wa[i] * diff * diff;
+        xg[i] = xg_s[i];
+        wg[i] = wg_s[i];
     }
-    if (d2 < best) {
-        best = d2;
-        bc = c;
-        found = true;
-    }
-}
-
-template <int V>
-__device__ __forceinline__ bool best_neighbour(const void *lists, const uint16_t *gco, int m, const float *xv,
-                                               const float *wa, float scale, int *l) {
-    using C = IqCfg<V>;
-    constexpr uint32_t MASK = (1u << C::BITS) - 1;
     float best = FLT_MAX;
-    uint32_t bc = 0;
-    bool found = false;
+    uint32_t bc = ~0u;
+    auto eval = [&](uint32_t c) {
+        float d2 = 0.0f;
+#pragma unroll
+        for (int i = 0; i < C::G; i++) {
+            const float pg = (float)(2 * (int)((c >> (C::BITS * i)) & MASK) + 1);
+            const float diff = scale * pg - xg[i];
+            d2 += wg[i] * diff * diff;
+        }
+        if (d2 < best) {
+            best = d2;
+            bc = c;
+        }
+    };
     if (V == 0) {  // shared memory, 8-bit grid indices
         const uint8_t *p = static_cast<const uint8_t *>(lists) + (-m - 1);
         const int n = p[0];
-        for (int t = 0; t < n; t++) nb_eval<V>(gco[p[1 + t]], xv, wa, scale, best, bc, found);
+        for (int t = 0; t < n; t++) eval(gco[p[1 + t]]);
     } else if (V == 1) {  // global memory, 16-byte aligned runs of 8 entries
         const uint16_t *p = static_cast<const uint16_t *>(lists) + (-m - 1);
         const int n = (int)__ldg(p);
@@ -314,57 +340,72 @@ __device__ __forceinline__ bool best_neighbour(const void *lists, const uint16_t
             const uint4 v = __ldg(q + ch);
             const uint32_t e[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-            for (int k = 0; k < 8; k++) {
-                if (ch * 8 + k < n) nb_eval<V>((e[k >> 1] >> (16 * (k & 1))) & 0xFFFFu, xv, wa, scale, best, bc, found);
-            }
+            for (int k = 0; k < 8; k++)
+                if (ch * 8 + k < n) eval((e[k >> 1] >> (16 * (k & 1))) & 0xFFFFu);
         }
     } else {  // shared memory, 16-bit coordinates
         const uint16_t *p = static_cast<const uint16_t *>(lists) + (-m - 1);
         const int n = p[0];
-        for (int t = 0; t < n; t++) nb_eval<V>(p[1 + t], xv, wa, scale, best, bc, found);
+        for (int t = 0; t < n; t++) eval(p[1 + t]);
     }
-#pragma unroll
-    for (int i = 0; i < C::G; i++) l[i] = (int)((bc >> (C::BITS * i)) & MASK);
-    return found;
+    return bc;
 }
 
-// One scale trial over one block: rounds every group to the lattice at id,
-// snaps off-grid groups to the best neighbour at this_scale, and returns the
-// weighted sums.  la receives the levels, on[k] whether group k was on-grid.
+// Round one group to the lattice at `id` (quant_iq.rs: l = clamp(round(
+// 0.5*(id*x - 1)), 0, kmax-1)); returns the group's packed levels.
 template <int V>
-__device__ __forceinline__ void iq_trial(const float *xv, const float *w, const float *wa, float id, float this_scale,
-                                         const int *kmap, const void *nb, const uint16_t *gco, int *la, bool *on, float &sumqx,
-                                         float &sumq2, int *status) {
+__device__ __forceinline__ uint32_t round_group(const float *xg, float id) {
     using C = IqCfg<V>;
+    uint32_t g = 0;
 #pragma unroll
-    for (int k = 0; k < C::NG; k++) {
-        int l[C::G];
-#pragma unroll
-        for (int i = 0; i < C::G; i++)
-            l[i] = clampi(nearest_int(0.5f * (id * xv[k * C::G + i] - 1.0f)), 0, C::KM - 1);
-        const int m = kmap[lattice_index<V>(l)];
-        on[k] = m >= 0;
-        if (m < 0) {
-            float xg[C::G], wg[C::G];
-#pragma unroll
-            for (int i = 0; i < C::G; i++) {
-                xg[i] = xv[k * C::G + i];
-                wg[i] = wa[k * C::G + i];
-            }
-            if (!best_neighbour<V>(nb, gco, m, xg, wg, this_scale, l)) set_status(status, SHC_ENONEIGHBOUR);
-        }
-#pragma unroll
-        for (int i = 0; i < C::G; i++) la[k * C::G + i] = l[i];
+    for (int i = 0; i < C::G; i++) {
+        const int l = (int)round_clamp0_f(0.5f * (id * xg[i] - 1.0f), (float)(C::KM - 1));
+        g |= (uint32_t)l << (C::BITS * i);
     }
-    float sx = 0.0f, s2 = 0.0f;
+    return g;
+}
+
+// Weighted sums of a block for packed levels: sumqx += w*x*q, sumq2 += w*q*q.
+template <int V>
+__device__ __forceinline__ void block_sums(const float *xv, const float *w, const Levels<V> &lv, float &sx, float &s2) {
+    using C = IqCfg<V>;
+    float a = 0.0f, c = 0.0f;
 #pragma unroll
     for (int i = 0; i < C::BS; i++) {
-        const float q = (float)(2 * la[i] + 1);
-        sx += w[i] * xv[i] * q;
-        s2 += w[i] * q * q;
+        const float q = (float)(2 * lv.level(i) + 1);
+        a += w[i] * xv[i] * q;
+        c += w[i] * q * q;
     }
-    sumqx = sx;
-    sumq2 = s2;
+    sx = a;
+    s2 = c;
+}
+
+// One scale trial over one block: every group rounded to the lattice at id,
+// off-grid groups snapped to the best neighbour at this_scale.  offmask gets
+// bit k for each group that was off the grid.
+template <int V>
+__device__ __forceinline__ void iq_trial(const float *xv, const float *w, const float *wa, float id, float this_scale,
+                                         const int *kmap, const void *nb, const uint16_t *gco, Levels<V> &lv,
+                                         uint32_t &offmask, float &sumqx, float &sumq2, int *status) {
+    using C = IqCfg<V>;
+    lv.p0 = lv.p1 = 0;
+    offmask = 0;
+#pragma unroll 1
+    for (int k = 0; k < C::NG; k++) {
+        uint32_t g = round_group<V>(xv + k * C::G, id);
+        const int m = kmap[kmap_index<V>(g)];
+        if (m < 0) {
+            offmask |= 1u << k;
+            uint32_t c = best_neighbour<V>(nb, gco, m, xv + k * C::G, wa + k * C::G, this_scale);
+            if (c == ~0u) {
+                set_status(status, SHC_ENONEIGHBOUR);
+                c = 0;
+            }
+            g = c;
+        }
+        lv.set_group(k, g);
+    }
+    block_sums<V>(xv, w, lv, sumqx, sumq2);
 }
 
 // make_qp_quants (quant_iq.rs:170-241), n = 32, nmax = 4: the IQ2_XXS seed.
@@ -430,12 +471,15 @@ __device__ float make_qp_quants32(const float *x, const float *w) {
     return suml2 > 0.0f ? sumlx / suml2 : 0.0f;
 }
 
+// Per-warp shared state; block arrays padded to BS+1 so lanes working on
+// different blocks hit different banks.
 template <int V>
 struct IqWarpSmem {
+    static constexpr int BP = IqCfg<V>::BS + 1;
     float x[256];
-    float xv[256];
-    float w[256];
-    float wa[256];
+    float xv[IqCfg<V>::NB * BP];
+    float w[IqCfg<V>::NB * BP];
+    float wa[IqCfg<V>::NB * BP];
     float2 res[IqCfg<V>::NB * IqCfg<V>::NT];
     float bscale0[IqCfg<V>::NB];  // chain start scale per block (qp seed or max/(2k-1))
     float bmax[IqCfg<V>::NB];     // max |x| (or the qp effective max) per block
@@ -456,6 +500,7 @@ __global__ void __launch_bounds__(256) enc_iq_lattice_kernel(EncArgs a, const in
                                                              const uint8_t *__restrict__ g_lists, int lists_bytes,
                                                              const uint32_t *__restrict__ g_coords) {
     using C = IqCfg<V>;
+    constexpr int BP = C::BS + 1;
     extern __shared__ __align__(16) uint8_t smem_raw[];
     // shared memory: compact kmap | per-warp state | grid coords | lists
     int *kmap = reinterpret_cast<int *>(smem_raw);
@@ -492,6 +537,8 @@ __global__ void __launch_bounds__(256) enc_iq_lattice_kernel(EncArgs a, const in
         float base[8];
         load_im8(imr, col0 + lane * 8, base);
         float wv[8];
+        // this lane's 8 elements lie in one block: element lane*8+k
+        const int eb = (lane * 8) / C::BS, ei = (lane * 8) % C::BS;
 #pragma unroll
         for (int k = 0; k < 8; k++) {
             float wt;
@@ -499,14 +546,14 @@ __global__ void __launch_bounds__(256) enc_iq_lattice_kernel(EncArgs a, const in
             else if (V >= 3) wt = imr ? base[k] * sqrtf(sig + v[k] * v[k]) : v[k] * v[k];
             else wt = base[k] * sqrtf(sig + v[k] * v[k]);
             wv[k] = wt;
-            S.w[lane * 8 + k] = wt;
-            S.wa[lane * 8 + k] = sqrtf(wt);
+            S.w[eb * BP + ei + k] = wt;
+            S.wa[eb * BP + ei + k] = sqrtf(wt);
         }
         // sign group `lane` = elements lane*8 .. lane*8+7
         {
             float xv8[8];
             int nflip = 0;
-            uint32_t s = 0;
+            uint32_t sgn = 0;
 #pragma unroll
             for (int i = 0; i < 8; i++) {
                 if (v[i] >= 0.0f) {
@@ -514,7 +561,7 @@ __global__ void __launch_bounds__(256) enc_iq_lattice_kernel(EncArgs a, const in
                 } else {
                     xv8[i] = -v[i];
                     nflip++;
-                    s |= 1u << i;
+                    sgn |= 1u << i;
                 }
             }
             if (C::PARITY && (nflip % 2) != 0) {
@@ -528,17 +575,17 @@ __global__ void __launch_bounds__(256) enc_iq_lattice_kernel(EncArgs a, const in
 #pragma unroll
                 for (int i = 0; i < 8; i++)
                     if (i == imin) xv8[i] = -xv8[i];
-                s ^= 1u << imin;
+                sgn ^= 1u << imin;
             }
 #pragma unroll
-            for (int i = 0; i < 8; i++) S.xv[lane * 8 + i] = xv8[i];
-            S.signs[lane] = (uint8_t)(C::PARITY ? (s & 127u) : s);
+            for (int i = 0; i < 8; i++) S.xv[eb * BP + ei + i] = xv8[i];
+            S.signs[lane] = (uint8_t)(C::PARITY ? (sgn & 127u) : sgn);
         }
         __syncwarp();
         // ---- P1: per-block max and starting scale ----
         if (lane < C::NB) {
             const int b = lane;
-            const float *xb = S.xv + b * C::BS;
+            const float *xb = S.xv + b * BP;
             float mx = xb[0];
             for (int i = 0; i < C::BS; i++) mx = rmaxf(mx, xb[i]);
             bool live;
@@ -549,7 +596,7 @@ __global__ void __launch_bounds__(256) enc_iq_lattice_kernel(EncArgs a, const in
             float s0 = 0.0f, ref = mx;
             if (live) {
                 if (C::QP) {
-                    s0 = make_qp_quants32(xb, S.w + b * C::BS);
+                    s0 = make_qp_quants32(xb, S.w + b * BP);
                     ref = s0 * (float)C::KM;  // eff_max
                     if (ref <= 0.0f) live = false;
                 } else {
@@ -565,23 +612,19 @@ __global__ void __launch_bounds__(256) enc_iq_lattice_kernel(EncArgs a, const in
         for (int j = lane; j < C::NB * C::NT; j += 32) {
             const int b = j / C::NT, t = j - b * C::NT;
             if (!S.live[b]) continue;
-            const int is = C::IS_LO + t;
-            float id;
-            if (C::QP) id = ((float)(2 * C::KM - 1) + (float)is * C::STEP) / S.bmax[b];
-            else id = ((float)(2 * C::KM - 1) + (float)is * C::STEP) / S.bmax[b];
-            const float this_scale = 1.0f / id;
-            int la[C::BS];
-            bool on[C::NG];
+            const float id = ((float)(2 * C::KM - 1) + (float)(C::IS_LO + t) * C::STEP) / S.bmax[b];
+            Levels<V> lv;
+            uint32_t off;
             float sx, s2;
-            iq_trial<V>(S.xv + b * C::BS, S.w + b * C::BS, S.wa + b * C::BS, id, this_scale, kmap,
-                        nbs, gco, la, on, sx, s2, a.status);
+            iq_trial<V>(S.xv + b * BP, S.w + b * BP, S.wa + b * BP, id, 1.0f / id, kmap, nbs, gco, lv, off, sx, s2,
+                        a.status);
             S.res[j] = make_float2(sx, s2);
         }
         __syncwarp();
         // ---- P3: per block: replay the chain, re-run the winner, re-project ----
         if (lane < C::NB) {
             const int b = lane;
-            const float *xb = S.xv + b * C::BS, *wb = S.w + b * C::BS, *ab = S.wa + b * C::BS;
+            const float *xb = S.xv + b * BP, *wb = S.w + b * BP, *ab = S.wa + b * BP;
             float scale = 0.0f;
             if (S.live[b]) {
                 scale = S.bscale0[b];
@@ -595,69 +638,51 @@ __global__ void __launch_bounds__(256) enc_iq_lattice_kernel(EncArgs a, const in
                         win = t;
                     }
                 }
-                int ls[C::BS];
-                bool on[C::NG];
-#pragma unroll
-                for (int i = 0; i < C::BS; i++) ls[i] = 0;
-#pragma unroll
-                for (int k = 0; k < C::NG; k++) on[k] = (V != 4);
+                Levels<V> ls;
+                // on-grid flags start true (IQ3_S: false) and follow the winning trial
+                uint32_t off = (V == 4) ? ((1u << C::NG) - 1) : 0u;
                 if (win >= 0) {
-                    const int is = C::IS_LO + win;
-                    const float id = ((float)(2 * C::KM - 1) + (float)is * C::STEP) / S.bmax[b];
+                    const float id = ((float)(2 * C::KM - 1) + (float)(C::IS_LO + win) * C::STEP) / S.bmax[b];
                     float sx, s2;
-                    iq_trial<V>(xb, wb, ab, id, 1.0f / id, kmap, nbs, gco, ls, on, sx, s2, a.status);
+                    iq_trial<V>(xb, wb, ab, id, 1.0f / id, kmap, nbs, gco, ls, off, sx, s2, a.status);
                 }
-                int n_not = 0;
-#pragma unroll
-                for (int k = 0; k < C::NG; k++) n_not += on[k] ? 0 : 1;
-                const bool reproject = (V == 0) ? (scale > 0.0f) : (n_not > 0 && scale > 0.0f);
+                const bool reproject = (V == 0) ? (scale > 0.0f) : (off != 0 && scale > 0.0f);
                 if (reproject) {
                     const float id = 1.0f / scale;
-#pragma unroll
+#pragma unroll 1
                     for (int k = 0; k < C::NG; k++) {
-                        const bool redo = (V == 0 || V == 4) ? true : !on[k];
+                        const bool redo = (V == 0 || V == 4) ? true : ((off >> k) & 1u);
                         if (!redo) continue;
-                        int l[C::G];
-#pragma unroll
-                        for (int i = 0; i < C::G; i++)
-                            l[i] = clampi(nearest_int(0.5f * (id * xb[k * C::G + i] - 1.0f)), 0, C::KM - 1);
-                        const int m = kmap[lattice_index<V>(l)];
+                        uint32_t gq = round_group<V>(xb + k * C::G, id);
+                        const int m = kmap[kmap_index<V>(gq)];
                         if (m < 0) {
-                            float xg[C::G], wg[C::G];
-#pragma unroll
-                            for (int i = 0; i < C::G; i++) {
-                                xg[i] = xb[k * C::G + i];
-                                wg[i] = ab[k * C::G + i];
+                            uint32_t c = best_neighbour<V>(nbs, gco, m, xb + k * C::G, ab + k * C::G, scale);
+                            if (c == ~0u) {
+                                set_status(a.status, SHC_ENONEIGHBOUR);
+                                c = 0;
                             }
-                            if (!best_neighbour<V>(nbs, gco, m, xg, wg, scale, l)) set_status(a.status, SHC_ENONEIGHBOUR);
+                            gq = c;
                         }
-#pragma unroll
-                        for (int i = 0; i < C::G; i++) ls[k * C::G + i] = l[i];
+                        ls.set_group(k, gq);
                     }
-                    float sx = 0.0f, s2 = 0.0f;
-#pragma unroll
-                    for (int i = 0; i < C::BS; i++) {
-                        const float q = (float)(2 * ls[i] + 1);
-                        sx += wb[i] * xb[i] * q;
-                        s2 += wb[i] * q * q;
-                    }
+                    float sx, s2;
+                    block_sums<V>(xb, wb, ls, sx, s2);
                     if (s2 > 0.0f) scale = sx / s2;
                 }
                 if (scale < 0.0f) {
                     scale = -scale;
                     for (int k = 0; k < C::NSG; k++) {
-                        const uint8_t s = S.signs[b * C::NSG + k];
-                        S.signs[b * C::NSG + k] = C::PARITY ? (uint8_t)((~s) & 127) : (uint8_t)(~s);
+                        const uint8_t sg = S.signs[b * C::NSG + k];
+                        S.signs[b * C::NSG + k] = C::PARITY ? (uint8_t)((~sg) & 127) : (uint8_t)(~sg);
                     }
                 }
-#pragma unroll
+#pragma unroll 1
                 for (int k = 0; k < C::NG; k++) {
-                    const int m = kmap[lattice_index<V>(ls + k * C::G)];
+                    const int m = kmap[kmap_index<V>(ls.group(k))];
                     if (m < 0) set_status(a.status, SHC_EOFFGRID);
                     S.gidx[b * C::NG + k] = (uint16_t)(m < 0 ? 0 : m);
                 }
             } else {
-#pragma unroll
                 for (int k = 0; k < C::NG; k++) S.gidx[b * C::NG + k] = 0;
                 for (int k = 0; k < C::NSG; k++) S.signs[b * C::NSG + k] = 0;
             }

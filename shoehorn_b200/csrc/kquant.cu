@@ -218,6 +218,12 @@ __global__ void __launch_bounds__(256) enc_q6_k_kernel(EncArgs a) {
             if (av > amax) { amax = av; mx = x[i]; }
         }
         const bool live = !(amax < kGroupMaxEps);
+        // with finite inputs iscale*x is finite, so the NaN -> 0 rule of the
+        // saturating cast cannot trigger and the plain clamp is exact
+        float xsum = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 16; i++) xsum += x[i] * 0.0f;
+        const bool finite = xsum == 0.0f;
         if (live) {
             const int is0 = q == 0 ? -9 : 1;
             const int ncand = q == 0 ? 10 : 9;
@@ -225,11 +231,20 @@ __global__ void __launch_bounds__(256) enc_q6_k_kernel(EncArgs a) {
                 const int is = is0 + t;
                 const float iscale = -(32.0f + 0.1f * (float)is) / mx;
                 float sumlx = 0.0f, suml2 = 0.0f;
+                if (finite) {
 #pragma unroll
-                for (int i = 0; i < 16; i++) {
-                    const float l = round_clamp_f(iscale * x[i], -32.0f, 31.0f);
-                    sumlx += wx[i] * l;
-                    suml2 += w[i] * (l * l);
+                    for (int i = 0; i < 16; i++) {
+                        const float l = fminf(fmaxf(roundf(iscale * x[i]), -32.0f), 31.0f);
+                        sumlx += wx[i] * l;
+                        suml2 += w[i] * (l * l);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; i++) {
+                        const float l = round_clamp_f(iscale * x[i], -32.0f, 31.0f);
+                        sumlx += wx[i] * l;
+                        suml2 += w[i] * (l * l);
+                    }
                 }
                 s_cand[wid][s][is + 9] = make_float2(sumlx, suml2);
             }
@@ -336,13 +351,28 @@ __global__ void __launch_bounds__(256, 1) enc_qk45_kernel(EncArgs a) {
             x[i] = s_x[wid][s * 33 + i];
             w[i] = s_w[wid][s * 33 + i];
         }
-        // make_qkx3_quants
-        float vmin = INFINITY, vmax = -INFINITY;
+        // make_qkx3_quants.  min/max folds are order-independent (NaN is
+        // skipped), so they run as trees on the hardware min/max; the sign
+        // of a zero vmin/vmax never reaches Q4_K/Q5_K bytes (it only enters
+        // x - vmin, scale*l + vmin, and -vmin folded with +0 by max).
+        float vmin, vmax;
+        {
+            float mn[16], mxv[16];
 #pragma unroll
-        for (int i = 0; i < 32; i++) vmin = rminf(vmin, x[i]);
-        vmin = rminf(vmin, 0.0f);
+            for (int i = 0; i < 16; i++) {
+                mn[i] = fminf(x[2 * i], x[2 * i + 1]);
+                mxv[i] = fmaxf(x[2 * i], x[2 * i + 1]);
+            }
 #pragma unroll
-        for (int i = 0; i < 32; i++) vmax = rmaxf(vmax, x[i]);
+            for (int s2 = 8; s2 >= 1; s2 >>= 1)
+#pragma unroll
+                for (int i = 0; i < s2; i++) {
+                    mn[i] = fminf(mn[i], mn[i + s2]);
+                    mxv[i] = fmaxf(mxv[i], mxv[i + s2]);
+                }
+            vmin = fminf(fminf(INFINITY, mn[0]), 0.0f);
+            vmax = fmaxf(-INFINITY, mxv[0]);
+        }
         // x[i] - vmin is the same rounded value for every grid: hoisted
 #pragma unroll
         for (int i = 0; i < 32; i++) xm[i] = x[i] - vmin;
@@ -445,15 +475,15 @@ __global__ void __launch_bounds__(256, 1) enc_qk45_kernel(EncArgs a) {
         max_min = rmaxf(0.0f, max_min);
         const float inv_scale = max_scale > 0.0f ? 63.0f / max_scale : 0.0f;
         const float inv_min = max_min > 0.0f ? 63.0f / max_min : 0.0f;
-        const int lsq = clampi(nearest_int(inv_scale * scale), 0, 63);
-        const int lmq = clampi(nearest_int(inv_min * mins_s), 0, 63);
+        const int lsq = (int)round_clamp0_f(inv_scale * scale, 63.0f);
+        const int lmq = (int)round_clamp0_f(inv_min * mins_s, 63.0f);
         const float d = max_scale / 63.0f;
         const float dmin = max_min / 63.0f;
         const float dsub = d * (float)lsq;
         const float msub = dmin * (float)lmq;
 #pragma unroll
         for (int k = 0; k < 8; k++) {
-            const int l = dsub == 0.0f ? 0 : clampi(nearest_int((v[k] + msub) / dsub), 0, NMAX);
+            const int l = dsub == 0.0f ? 0 : (int)round_clamp0_f((v[k] + msub) / dsub, FN);
             s_l[wid][lane * 8 + k] = (uint8_t)l;
         }
         int lsq_all[8], lmq_all[8];

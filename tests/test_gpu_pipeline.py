@@ -147,8 +147,8 @@ def test_sampled_errors_and_imatrix_plan_match_the_oracle(tmp_path):
 
 
 def test_uniform_mix_harness(tmp_path):
-    src = str(tmp_path / "tiny.gguf")
-    run("synth", "tiny", src)
+    src = str(tmp_path / "e2e.gguf")
+    run("synth", "e2e", src)
     out = str(tmp_path / "u.gguf")
     run("quantize", "-m", src, "-o", out, "--uniform", "Q4_K,token_embd.weight=Q6_K")
     fit = gguf.GGUFReader(out)
