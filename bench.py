@@ -92,6 +92,19 @@ def workload_tensors(name):
     return [(f"{N_ROWS}x{NE0}", bits, im)]
 
 
+def captured_traffic(type_name, in_bytes):
+    """DRAM bytes per launch of a type's encoder from the committed ncu capture
+    (profiles/traffic_encoder_sweep.txt), for the 4096 x 14336 tensor only."""
+    path = os.path.join(ROOT, "profiles", "traffic_encoder_sweep.txt")
+    if in_bytes != N_ROWS * NE0 * 2 or not os.path.exists(path):
+        return None
+    for line in open(path):
+        f = line.split()
+        if len(f) >= 4 and not line.startswith("#") and f[1] == type_name:
+            return int(f[2]) + int(f[3])
+    return None
+
+
 def dist_env():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     return int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")), ws
@@ -337,7 +350,7 @@ def run_ours(args):
                                f"{sm_mhz:.0f} MHz under load (no FP32 figure in MEASURED_PEAKS.json)"}
     roof["frac"] = round(roof["achieved"] / roof["peak"], 4)
     roof["kernel"] = f"{dom} encoder"
-    roof["traffic"] = None
+    roof["traffic"] = captured_traffic(dom, in_bytes)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

@@ -450,8 +450,9 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
     const bool bounded = timeout_ms >= 0;
     const size_t eb = src_elem_bytes(src_type);
     const size_t in_row = (size_t)ne0 * eb;
-    // ~64 MiB of source per chunk keeps three chunks in flight per direction
-    int64_t chunk = std::max<int64_t>(1, (int64_t)((64u << 20) / in_row));
+    // ~16 MiB of source per chunk: copies of one chunk overlap the encode of
+    // the previous one, and the first and last chunks (not overlapped) stay short
+    int64_t chunk = std::max<int64_t>(1, (int64_t)((16u << 20) / in_row));
     chunk = std::min(chunk, n_rows);
     const int64_t n_chunks = (n_rows + chunk - 1) / chunk;
     const bool pin_src = is_pinned(host_src), pin_dst = is_pinned(host_dst);

@@ -67,6 +67,7 @@ int main(int argc, char **argv) {
             else if (s == "--calibrate") a.calibrate = true;
             else if (s == "--exact-errors") a.exact_errors = true;
             else if (s == "--gpus") a.gpus = std::stoi(val());
+            else if (s == "--streams") a.workers_per_gpu = std::stoi(val());
             else if (s == "--uniform") a.uniform = val();
             else if (s == "--seed") seed = std::stoull(val());
             else if (!s.empty() && s[0] != '-') {
@@ -113,13 +114,13 @@ int main(int argc, char **argv) {
             const ModelView mv = view_of(*model);
             Imatrix im;
             if (!a.imatrix.empty()) im = load_imatrix(a.imatrix);
-            GpuPool pool(a.gpus, a.timeout_ms);
+            GpuPool pool(a.gpus, a.timeout_ms, a.workers_per_gpu);
             Timing tm;
             const Plan plan = build_plan(a, mv, im, pool, tm);
             print_plan(plan, mv);
             if (cmd == "quantize") write_quantized(out, plan, mv, im, pool, tm);
             fprintf(stderr, "timing: measure %.3f s, solve %.3f s, encode %.3f s on %d GPU(s)\n", tm.measure_s,
-                    tm.solve_s, tm.encode_s, pool.size());
+                    tm.solve_s, tm.encode_s, pool.gpus());
             return 0;
         }
         if (cmd == "bench-model") {
@@ -127,7 +128,7 @@ int main(int argc, char **argv) {
             const auto g0 = std::chrono::steady_clock::now();
             auto sm = synthetic_model(synth_name, seed, threads);
             const double gen_s = std::chrono::duration<double>(std::chrono::steady_clock::now() - g0).count();
-            GpuPool pool(a.gpus, a.timeout_ms);
+            GpuPool pool(a.gpus, a.timeout_ms, a.workers_per_gpu);
             Timing tm;
             const auto t0 = std::chrono::steady_clock::now();
             const Plan plan = build_plan(a, sm->view, sm->imatrix, pool, tm);
@@ -138,7 +139,7 @@ int main(int argc, char **argv) {
             printf("{\"model\": \"%s\", \"gpus\": %d, \"exact_errors\": %s, \"uniform\": \"%s\", \"elements\": %llu, "
                    "\"generate_s\": %.3f, \"measure_s\": %.3f, \"solve_s\": %.4f, \"encode_s\": %.3f, \"wall_s\": %.3f, "
                    "\"plan_bytes\": %llu, \"budget_bytes\": %llu}\n",
-                   synth_name.c_str(), pool.size(), a.exact_errors ? "true" : "false", a.uniform.c_str(),
+                   synth_name.c_str(), pool.gpus(), a.exact_errors ? "true" : "false", a.uniform.c_str(),
                    (unsigned long long)elems, gen_s, tm.measure_s, tm.solve_s, tm.encode_s, wall,
                    (unsigned long long)plan.total_bytes, (unsigned long long)plan.budget.model_budget);
             return 0;

@@ -221,15 +221,18 @@ static void shc_check(int rc, const char *what) {
     if (rc != SHC_OK) throw Error(std::string(what) + ": " + shc_status_string(rc));
 }
 
-GpuPool::GpuPool(int n_gpus, int64_t timeout_ms) : timeout_ms_(timeout_ms) {
+GpuPool::GpuPool(int n_gpus, int64_t timeout_ms, int per_gpu) : timeout_ms_(timeout_ms) {
     int avail = 0;
     if (cudaGetDeviceCount(&avail) != cudaSuccess || avail < 1) throw Error("no CUDA device");
     if (n_gpus < 1 || n_gpus > avail) n_gpus = n_gpus < 1 ? 1 : avail;
-    for (int w = 0; w < n_gpus; w++) {
+    n_gpus_ = n_gpus;
+    if (per_gpu < 1) per_gpu = 1;
+    // workers interleave the devices so the first jobs (the largest) spread
+    for (int w = 0; w < n_gpus * per_gpu; w++) {
         auto wk = std::make_unique<Worker>();
-        wk->dev = w;
-        cuda_check(cudaSetDevice(w), "cudaSetDevice");
-        shc_check(shc_init(w, &wk->ctx), "shc_init");
+        wk->dev = w % n_gpus;
+        cuda_check(cudaSetDevice(wk->dev), "cudaSetDevice");
+        shc_check(shc_init(wk->dev, &wk->ctx), "shc_init");
         cuda_check(cudaStreamCreateWithFlags(&wk->st, cudaStreamNonBlocking), "cudaStreamCreate");
         workers_.push_back(std::move(wk));
     }
@@ -602,25 +605,41 @@ void write_quantized(const std::string &out_path, const Plan &plan, const ModelV
     kvs.emplace_back("general.quantization_version", Value::U32(2));
     const Layout L = layout_for(kvs, infos, m.alignment);
     // An empty out_path encodes into anonymous memory (benchmarks without a disk
-    // write); otherwise *.tmp next to the output, renamed when complete.
+    // write); otherwise *.tmp next to the output, renamed when complete.  File
+    // output uses positional writes from the workers' pinned buffers, so no
+    // page of the output is faulted in through a mapping.
     const bool to_file = !out_path.empty();
     const std::string tmp = out_path + ".tmp";
     uint8_t *map = nullptr;
+    int fd = -1;
     if (to_file) {
-        const int fd = ::open(tmp.c_str(), O_RDWR | O_CREAT | O_TRUNC, 0644);
+        fd = ::open(tmp.c_str(), O_RDWR | O_CREAT | O_TRUNC, 0644);
         if (fd < 0) throw Error("creating " + tmp);
         if (ftruncate(fd, (off_t)L.total) != 0) {
             ::close(fd);
             throw Error("sizing " + tmp);
         }
-        map = L.total ? static_cast<uint8_t *>(mmap(nullptr, L.total, PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0)) : nullptr;
-        ::close(fd);
-    } else {
+    } else if (L.total) {
         map = static_cast<uint8_t *>(mmap(nullptr, L.total, PROT_READ | PROT_WRITE, MAP_PRIVATE | MAP_ANONYMOUS, -1, 0));
+        if (map == MAP_FAILED) throw Error("mapping the output");
+        madvise(map, L.total, MADV_HUGEPAGE);
     }
-    if (L.total && map == MAP_FAILED) throw Error("mmap " + tmp);
+    auto put = [&](uint64_t off, const void *p, size_t n) {
+        if (!to_file) {
+            std::memcpy(map + off, p, n);
+            return;
+        }
+        const uint8_t *b = static_cast<const uint8_t *>(p);
+        while (n) {
+            const ssize_t w = pwrite(fd, b, n, (off_t)off);
+            if (w <= 0) throw Error("writing " + tmp);
+            b += w;
+            off += (uint64_t)w;
+            n -= (size_t)w;
+        }
+    };
     const auto hdr = header_bytes(kvs, infos, m.alignment, L);
-    std::memcpy(map, hdr.data(), hdr.size());
+    put(0, hdr.data(), hdr.size());
 
     struct Job {
         size_t e;
@@ -636,7 +655,7 @@ void write_quantized(const std::string &out_path, const Plan &plan, const ModelV
         const auto &t = m.tensors[e.tensor_idx];
         const uint64_t n_rows = t.n_rows(), ne0 = t.ne0(), rpm = rows_per_mat_of(t);
         if (e.ty == t.ty) {  // copied untouched (main.rs:735-737)
-            std::memcpy(map + L.data_start + L.offsets[ei], m.data(e.tensor_idx), t.byte_size());
+            put(L.data_start + L.offsets[ei], m.data(e.tensor_idx), t.byte_size());
             continue;
         }
         const uint64_t rows_cap = std::max<uint64_t>(1, cap_elems / std::max<uint64_t>(ne0, 1));
@@ -670,12 +689,10 @@ void write_quantized(const std::string &out_path, const Plan &plan, const ModelV
         uint8_t *hout = static_cast<uint8_t *>(wk.h(1, n * drb));
         cuda_check(cudaMemcpyAsync(hout, dout, n * drb, cudaMemcpyDeviceToHost, wk.st), "encoded download");
         shc_check(shc_sync(wk.ctx, wk.st, 3600 * 1000), "encode rows");
-        std::memcpy(map + L.data_start + L.offsets[jb.e] + jb.r0 * drb, hout, n * drb);
+        put(L.data_start + L.offsets[jb.e] + jb.r0 * drb, hout, n * drb);
     });
-    if (L.total) {
-        if (to_file) msync(map, L.total, MS_SYNC);
-        munmap(map, L.total);
-    }
+    if (map) munmap(map, L.total);
+    if (fd >= 0 && ::close(fd) != 0) throw Error("closing " + tmp);
     if (to_file && rename(tmp.c_str(), out_path.c_str()) != 0) throw Error("renaming " + tmp + " -> " + out_path);
     tm.encode_s = secs_since(t0);
     fprintf(stderr, "wrote %s (%s)\n", to_file ? out_path.c_str() : "(memory)", fmt_size(L.total).c_str());

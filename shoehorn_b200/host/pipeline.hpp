@@ -26,6 +26,7 @@ struct FitArgs {  // main.rs:43-85, plus the GPU harness options
     bool calibrate = false;
     bool exact_errors = false;
     int gpus = 1;
+    int workers_per_gpu = 3;  // concurrent jobs (own stream and context) per GPU
     std::string uniform;  // "TYPE[,tensor=TYPE...]": fixed mix instead of a solve
     int64_t timeout_ms = 3600 * 1000;
 };
@@ -84,12 +85,14 @@ struct ModelView {
 };
 ModelView view_of(const Model &m);
 
-// One worker thread and library context per GPU.
+// Worker threads, each with its own library context and stream, several per
+// GPU so that one job's copies overlap another's kernels.
 class GpuPool {
   public:
-    explicit GpuPool(int n_gpus, int64_t timeout_ms);
+    GpuPool(int n_gpus, int64_t timeout_ms, int per_gpu = 3);
     ~GpuPool();
     int size() const { return (int)workers_.size(); }
+    int gpus() const { return n_gpus_; }
     // Runs fn(worker, job) for jobs 0..n_jobs-1, pulled dynamically by the
     // workers in index order; rethrows the first failure.
     void run(size_t n_jobs, const std::function<void(int, size_t)> &fn);
@@ -99,6 +102,7 @@ class GpuPool {
   private:
     std::vector<std::unique_ptr<Worker>> workers_;
     int64_t timeout_ms_;
+    int n_gpus_ = 1;
 };
 
 // main.rs:454-589 build_plan: measures every (tensor, candidate) error on
