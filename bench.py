@@ -37,19 +37,21 @@ TYPE_IDS = {"Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "IQ2_XXS": 16, "IQ2_X
 OUT_BYTES_PER_ELT = {"Q8_0": 34 / 32, "Q4_K": 144 / 256, "Q5_K": 176 / 256, "Q6_K": 210 / 256,
                      "IQ2_XXS": 66 / 256, "IQ2_XS": 74 / 256, "IQ2_S": 82 / 256, "IQ3_XXS": 98 / 256,
                      "IQ3_S": 110 / 256, "IQ4_NL": 18 / 32, "IQ4_XS": 136 / 256}
-# Algorithmic FP32 operations per element of the reference algorithm with its
-# loop invariants hoisted (each add/sub/mul/div/sqrt/round/min/max = 1):
-#  Q4_K/Q5_K: 37 grids x (9 sum-pass + 2 clamp + 6 error-pass) + initial grid
-#             (sum of one pass, 11) + weights (4) + folds/requantisation (~8)
-#  Q6_K: 19 grids x (2 clamp + 1 round + 6) + weights (4) + requant (4)
-#  Q8_0: abs/max, multiply, round (HBM-bound; bytes are the roofline)
-#  IQ*: trials x (4 rounding + 6 weighted sums) + weights/signs/re-projection
-#        (~20); IQ2_XXS adds its make_qp_quants seed (~60).  The data-dependent
-#        neighbour searches are not counted, so IQ fractions are lower bounds.
-#  IQ4_*: 16 grids x (index lookup ~6 + 5 sums) + final pass (~8)
-FLOPS_PER_ELT = {"Q4_K": 37 * 17 + 11 + 4 + 8, "Q5_K": 37 * 17 + 11 + 4 + 8, "Q6_K": 19 * 9 + 4 + 4, "Q8_0": 4,
-                 "IQ2_XXS": 13 * 10 + 20 + 60, "IQ2_XS": 19 * 10 + 20, "IQ2_S": 19 * 10 + 20,
-                 "IQ3_XXS": 31 * 10 + 20, "IQ3_S": 19 * 10 + 20, "IQ4_NL": 16 * 11 + 8, "IQ4_XS": 16 * 11 + 8}
+# Algorithmic f32 operations per input element of the reference encoders,
+# counted by executing the oracle's op-counting build (oracle/opcount) on 32
+# evenly spaced rows of each benchmark tensor: every f32 add, sub, mul, div,
+# sqrt, compare, min/max and round-to-integer executed by the algorithm as
+# written (no CSE or hoisting credited), data-dependent neighbour searches
+# included.  The kernels execute fewer operations than this (loop invariants
+# hoisted, products shared), so the figure is the work done, not the
+# instructions issued.
+FLOPS_PER_ELT = {"Q4_K": 745.4, "Q5_K": 745.4, "Q6_K": 151.0, "Q8_0": 5.1,
+                 "IQ2_XXS": 1839.0, "IQ2_XS": 3738.2, "IQ2_S": 713.8, "IQ3_XXS": 1498.4, "IQ3_S": 963.8,
+                 "IQ4_NL": 274.7, "IQ4_XS": 274.7}
+# FP32 issue ceiling for separately rounded adds and multiplies on sm_100:
+# packed f32x2 add/mul retire 2 operations per lane per clock, 256 per SM
+# (shoehorn_b200/fp32-rate measures 251/clk/SM; scalar FADD/FMUL reach 122).
+FP32_OPS_PER_CLK_PER_SM = 256
 
 
 IQ_TYPES = ["IQ2_XXS", "IQ2_XS", "IQ2_S", "IQ3_XXS", "IQ3_S", "IQ4_NL", "IQ4_XS"]
@@ -341,13 +343,15 @@ def run_ours(args):
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if "hbm_gbs" in peaks else "fallback"}
     else:
         alg = elts * FLOPS_PER_ELT[dom]
-        # FP32 pipe: 128 lanes per SM, one add/mul/min/max per lane per clock;
-        # FMA pairing is unavailable (no contraction, by the parity contract)
-        peak = props.multi_processor_count * 128 * sm_mhz * 1e6 / 1e12
+        # no multiply-add contraction is allowed (parity), so the ceiling is
+        # separate f32 adds/multiplies at the packed f32x2 rate
+        peak = props.multi_processor_count * FP32_OPS_PER_CLK_PER_SM * sm_mhz * 1e6 / 1e12
         roof = {"bound": "fp32", "achieved": round(alg / (per_type_ms[dom] * 1e-3) / 1e12, 3),
                 "peak": round(peak, 3), "unit": "TFLOP/s",
-                "peak_source": f"{props.multi_processor_count} SMs x 128 FP32 lanes x median SM clock "
-                               f"{sm_mhz:.0f} MHz under load (no FP32 figure in MEASURED_PEAKS.json)"}
+                "peak_source": f"{props.multi_processor_count} SMs x {FP32_OPS_PER_CLK_PER_SM} f32 add/mul per clock "
+                               f"(packed f32x2; 251 measured by fp32-rate) x median SM clock {sm_mhz:.0f} MHz "
+                               "(MEASURED_PEAKS.json has no FP32 figure)",
+                "flops_per_elt": FLOPS_PER_ELT[dom], "flops_source": "oracle op-count build, as-written algorithm"}
     roof["frac"] = round(roof["achieved"] / roof["peak"], 4)
     roof["kernel"] = f"{dom} encoder"
     roof["traffic"] = captured_traffic(dom, in_bytes)

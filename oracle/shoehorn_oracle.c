@@ -35,7 +35,9 @@
 
 #include <math.h>
 #include <pthread.h>
+#ifndef SH_OPCOUNT
 #include <stdatomic.h>
+#endif
 #include <stdlib.h>
 #include <string.h>
 
@@ -94,6 +96,9 @@ int64_t oq_row_bytes(uint32_t type, int64_t n) {
 
 /* ---------------- scalar semantics ---------------- */
 
+/* The op-counting build (opcount/) supplies counted copies of nearest_int,
+ * rmaxf and rminf with the same semantics. */
+#ifndef SH_OPCOUNT
 /* quant.rs:16 nearest_int: f32::round (half away from zero), `as i32`. */
 int32_t oq_nearest_int(float x) {
     float r = roundf(x);
@@ -102,11 +107,13 @@ int32_t oq_nearest_int(float x) {
     if (r <= -2147483648.0f) return INT32_MIN;
     return (int32_t)r;
 }
+#endif
 #define nearest_int oq_nearest_int
 
 static inline int32_t clampi(int32_t v, int32_t lo, int32_t hi) { return v < lo ? lo : (v > hi ? hi : v); }
 static inline int32_t mini(int32_t a, int32_t b) { return a < b ? a : b; }
 
+#ifndef SH_OPCOUNT
 /* f32::max / f32::min: NaN-ignoring; -0 < +0. */
 static inline float rmaxf(float a, float b) {
     if (a != a) return b;
@@ -122,6 +129,7 @@ static inline float rminf(float a, float b) {
     if (b < a) return b;
     return signbit(a) ? a : b;
 }
+#endif
 
 /* IEEE binary16, round to nearest even (half::f16::from_f32). */
 uint16_t oq_f32_to_f16(float f) {
@@ -1699,6 +1707,7 @@ int oq_row_error(uint32_t type, const float *x, int64_t n, const float *im, doub
     return rc;
 }
 
+#ifndef SH_OPCOUNT
 /* ---------------- tensor drivers (main.rs:663-686, 549-563) ---------------- */
 
 /* imatrix.rs:124-141 row_slice */
@@ -1785,3 +1794,4 @@ int oq_row_errors_bf16(uint32_t type, const uint16_t *src, int64_t n_rows, int64
                .rows_per_mat = rows_per_mat, .row_step = row_step, .n_items = n_items, .dst = NULL, .err = err};
     return run_job(&j, n_threads);
 }
+#endif /* SH_OPCOUNT */

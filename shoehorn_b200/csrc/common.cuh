@@ -31,26 +31,54 @@ __device__ __forceinline__ int nearest_int(float x) {
     return (int)r;
 }
 
-// nearest_int(x).clamp(0, hi) kept in float.  For the small integer ranges of
-// the encoders this equals the integer result converted back: fmaxf returns
-// the non-NaN operand, so NaN -> 0 as in the integer path, and +-inf saturate
-// to the bounds.  A zero may come out as -0.0; every use of l is a product
-// folded into a sum that starts at +0, where the sign of a zero term never
-// changes the result.
-__device__ __forceinline__ float round_clamp0_f(float x, float hi) {
-    float r = roundf(x);
-    r = fmaxf(r, 0.0f);
-    r = fminf(r, hi);
-    return r;
+// Rounding without the conversion pipe.  roundf/floorf/rintf and float<->int
+// conversions issue at a quarter of the FP32 add rate per SM sub-partition on
+// sm_100; the helpers below round with three full-rate adds.  They rest on two
+// exact identities of IEEE binary32 arithmetic:
+//   (a) for 0 <= z < 2^23, RD(z + 2^23) = 2^23 + floor(z) (the floats of
+//       [2^23, 2^24) are the integers) and subtracting 2^23 again is exact;
+//   (b) for t >= 0, floor(RZ(t + 1/2)) = floor(t + 1/2): the exact sum s is
+//       >= 1/2, RZ never crosses the integer below s, and stays below s.
+// Hence floor_half_up(t) = floor(t + 1/2) = round-half-away-from-zero(t) for
+// 0 <= t < 2^23 - 1/2.  For t >= 2^23 - 1/2 the result is >= 2^23 - 1 (callers
+// clamp to bounds far below that); for t < 0 it is <= 0 (callers clamp at 0
+// or use the magnitude); NaN and +-inf pass through.
+__device__ __forceinline__ float floor_half_up(float t) {
+    return __fadd_rn(__fadd_rd(__fadd_rz(t, 0.5f), 8388608.0f), -8388608.0f);
 }
-// nearest_int(x).clamp(lo, hi) in float for a negative lower bound: NaN must
-// map to 0 (not lo) as the saturating cast does.
+__device__ __forceinline__ float2 floor_half_up2(float2 t) {
+    return __fadd2_rn(__fadd2_rd(__fadd2_rz(t, make_float2(0.5f, 0.5f)), make_float2(8388608.0f, 8388608.0f)),
+                      make_float2(-8388608.0f, -8388608.0f));
+}
+// Packed f32x2 arithmetic (two IEEE-rounded f32 operations per instruction).
+// Code generation for sm_100 contracts a packed multiply that feeds a packed
+// round-to-nearest add into a fused multiply-add in some operand patterns,
+// even under -fmad=false, which changes the rounding of the sum.  The
+// encoders therefore use packed multiplies only where their results feed
+// multiplies or scalar adds, and packed round-to-nearest adds only on
+// operands that are not products; scalar multiply/add pairs and
+// directed-rounding adds are not contracted.  The byte-parity tests over
+// thousands of super-blocks guard this rule.
+
+// f32::round for |x| < 2^23 - 1/2 (half away from zero, sign of x kept, so
+// -0.3 -> -0); larger magnitudes come out >= 2^23 - 1 with the sign of x.
+__device__ __forceinline__ float round_away_small(float x) { return copysignf(floor_half_up(fabsf(x)), x); }
+
+// nearest_int(x).clamp(0, hi) kept in float, for integer hi < 2^22.  Every x
+// is covered: x >= 0 rounds half away (floor_half_up), x in [-1/2, 0) gives 0
+// like the clamped -0/-1 of f32::round, x < -1/2 gives <= 0 -> 0, NaN -> 0
+// (fmaxf returns the non-NaN operand, as the saturating cast maps NaN to 0),
+// +inf -> hi.  A zero result is +0 (the last add of floor_half_up rounds
+// 2^23 - 2^23 to +0).
+__device__ __forceinline__ float round_clamp0_f(float x, float hi) {
+    return fminf(fmaxf(floor_half_up(x), 0.0f), hi);
+}
+// nearest_int(x).clamp(lo, hi) in float for lo < 0 < hi, |lo|, hi < 2^22:
+// NaN must map to 0 (not lo) as the saturating cast does.
 __device__ __forceinline__ float round_clamp_f(float x, float lo, float hi) {
-    float r = roundf(x);
+    float r = round_away_small(x);
     r = (r != r) ? 0.0f : r;
-    r = fmaxf(r, lo);
-    r = fminf(r, hi);
-    return r;
+    return fminf(fmaxf(r, lo), hi);
 }
 
 __device__ __forceinline__ int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }

@@ -145,7 +145,8 @@ __global__ void __launch_bounds__(256) enc_q8_0_kernel(EncArgs a) {
         for (int u = 0; u < kQ80Unroll; u++) {
             float amax = 0.0f;
 #pragma unroll
-            for (int k = 0; k < 8; k++) amax = rmaxf(amax, fabsf(v[u][k]));
+            // rmaxf(a, |x|) from a = +0: the operand is never -0, so fmaxf agrees
+            for (int k = 0; k < 8; k++) amax = fmaxf(amax, fabsf(v[u][k]));
             amax = rmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
             amax = rmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
             const float d = amax / 127.0f;
@@ -153,7 +154,9 @@ __global__ void __launch_bounds__(256) enc_q8_0_kernel(EncArgs a) {
             uint8_t *o = &s_out[wid][u][(lane >> 2) * 34];
 #pragma unroll
             for (int k = 0; k < 8; k++)
-                o[2 + (lane & 3) * 8 + k] = (uint8_t)(int8_t)clampi(nearest_int(v[u][k] * id), -127, 127);
+                // the int8 code is the low byte of r + 1.5 * 2^23 (exact for |r| <= 127)
+                o[2 + (lane & 3) * 8 + k] =
+                    (uint8_t)__float_as_uint(__fadd_rn(round_clamp_f(v[u][k] * id, -127.0f, 127.0f), 12582912.0f));
             if ((lane & 3) == 0) {
                 const uint16_t h = f16_bits(d);
                 o[0] = (uint8_t)(h & 0xFF);
@@ -234,7 +237,7 @@ __global__ void __launch_bounds__(256) enc_q6_k_kernel(EncArgs a) {
                 if (finite) {
 #pragma unroll
                     for (int i = 0; i < 16; i++) {
-                        const float l = fminf(fmaxf(roundf(iscale * x[i]), -32.0f), 31.0f);
+                        const float l = fminf(fmaxf(round_away_small(iscale * x[i]), -32.0f), 31.0f);
                         sumlx += wx[i] * l;
                         suml2 += w[i] * (l * l);
                     }
@@ -286,7 +289,7 @@ __global__ void __launch_bounds__(256) enc_q6_k_kernel(EncArgs a) {
             // lane owns elements lane*8..lane*8+7 = sub-block s, offset q*8
 #pragma unroll
             for (int k = 0; k < 8; k++) {
-                const int l = dd == 0.0f ? 32 : clampi(nearest_int(v[k] / dd), -32, 31) + 32;
+                const int l = dd == 0.0f ? 32 : (int)round_clamp_f(v[k] / dd, -32.0f, 31.0f) + 32;
                 s_l[wid][lane * 8 + k] = (uint8_t)l;
             }
             if (q == 0) o[192 + s] = (uint8_t)qsc;
@@ -318,18 +321,106 @@ __global__ void __launch_bounds__(256) enc_q6_k_kernel(EncArgs a) {
 // rmin -0.9, rdelta 0.05, 37 grids) per 32-element sub-block.  Four lanes per
 // sub-block: lane q evaluates jobs j = q, q+4, ..., j < 38, where j < 37 is
 // grid `is = j` and j == 37 is the initial nmax/(vmax-vmin) grid.
+//
+// Each lane holds its sub-block as 16 float2 pairs and runs the element-wise
+// products of a grid with packed f32x2 multiplies and adds (two IEEE-rounded
+// f32 operations per instruction, the same results as scalar code); the
+// reference's running sums stay scalar and in element order.  x is kept
+// negated (nx = -x): x - vmin = -(nx + vmin), w*l*x = -((w*l)*nx) and
+// diff - x = diff + nx are exact identities of round-to-nearest, so every
+// rounded value equals the reference's.
 // ---------------------------------------------------------------------------
+// NG grids of make_qkx3_quants over the lane's 32 elements (quant.rs:109-118),
+// interleaved element by element so that their serial sums form independent
+// dependency chains: l = nearest_int(iscale * (x - vmin)).clamp(0, nmax) and
+// the three weighted sums per grid.  CLEAN: every iscale and (x - vmin) is
+// finite, so y = iscale*(x - vmin) is >= 0 or +inf and the clamp at 0 is not
+// needed.
+template <bool CLEAN, int NG>
+__device__ __forceinline__ void qkx3_grids(const float *snx, const float *sw, float vmin, const float (&iscale)[NG],
+                                           float fn, float2 (&l)[NG][16], float (&sl)[NG], float (&sl2)[NG],
+                                           float (&sxl)[NG]) {
+    float2 nis[NG];
+#pragma unroll
+    for (int g = 0; g < NG; g++) {
+        nis[g] = make_float2(-iscale[g], -iscale[g]);
+        sl[g] = 0.0f;
+        sl2[g] = 0.0f;
+        sxl[g] = 0.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+        const float4 n4 = reinterpret_cast<const float4 *>(snx)[i >> 1];
+        const float4 w4 = reinterpret_cast<const float4 *>(sw)[i >> 1];
+        const float2 nxi = (i & 1) ? make_float2(n4.z, n4.w) : make_float2(n4.x, n4.y);
+        const float2 wi = (i & 1) ? make_float2(w4.z, w4.w) : make_float2(w4.x, w4.y);
+        const float2 ui = __fadd2_rn(nxi, make_float2(vmin, vmin));  // -(x - vmin)
+#pragma unroll
+        for (int g = 0; g < NG; g++) {
+            const float2 r = floor_half_up2(__fmul2_rn(nis[g], ui));  // the first add is RZ
+            float2 li;
+            if (CLEAN) {
+                li = make_float2(fminf(r.x, fn), fminf(r.y, fn));
+            } else {
+                li = make_float2(fminf(fmaxf(r.x, 0.0f), fn), fminf(fmaxf(r.y, 0.0f), fn));
+            }
+            l[g][i] = li;
+            const float2 wl = __fmul2_rn(wi, li);
+            const float2 wll = __fmul2_rn(wi, __fmul2_rn(li, li));  // (l*l) is exact, as the integer product
+            const float2 nwlx = __fmul2_rn(wl, nxi);                // -(w*l*x)
+            sl[g] = __fadd_rn(sl[g], wl.x);
+            sl2[g] = __fadd_rn(sl2[g], wll.x);
+            sxl[g] = __fsub_rn(sxl[g], nwlx.x);
+            sl[g] = __fadd_rn(sl[g], wl.y);
+            sl2[g] = __fadd_rn(sl2[g], wll.y);
+            sxl[g] = __fsub_rn(sxl[g], nwlx.y);
+        }
+    }
+}
+
+// Weighted squared error of NG candidate (scale, min) fits, interleaved
+// (quant.rs:125-128 and 100-101): diff = scale*l + min - x, err += w*diff*diff.
+template <int NG>
+__device__ __forceinline__ void qkx3_errors(const float *snx, const float *sw, const float2 (&l)[NG][16],
+                                            const float (&ts)[NG], const float (&tm)[NG], float (&err)[NG]) {
+#pragma unroll
+    for (int g = 0; g < NG; g++) err[g] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+        const float4 n4 = reinterpret_cast<const float4 *>(snx)[i >> 1];
+        const float4 w4 = reinterpret_cast<const float4 *>(sw)[i >> 1];
+        const float2 nxi = (i & 1) ? make_float2(n4.z, n4.w) : make_float2(n4.x, n4.y);
+        const float2 wi = (i & 1) ? make_float2(w4.z, w4.w) : make_float2(w4.x, w4.y);
+#pragma unroll
+        for (int g = 0; g < NG; g++) {
+            const float2 p = __fmul2_rn(make_float2(ts[g], ts[g]), l[g][i]);
+            const float2 d = __fadd2_rn(make_float2(__fadd_rn(p.x, tm[g]), __fadd_rn(p.y, tm[g])), nxi);
+            const float2 e = __fmul2_rn(__fmul2_rn(wi, d), d);
+            err[g] = __fadd_rn(err[g], e.x);
+            err[g] = __fadd_rn(err[g], e.y);
+        }
+    }
+}
+
+// One grid per round and two blocks (16 warps) per SM: the lane's sub-block
+// is read from shared memory in each pass instead of being held in
+// registers, which keeps the kernel within 128 registers per thread.
+constexpr int kQk45GridsPerRound = 1;
 template <int NMAX>
-__global__ void __launch_bounds__(256, 1) enc_qk45_kernel(EncArgs a) {
+__global__ void __launch_bounds__(256, 2) enc_qk45_kernel(EncArgs a) {
     constexpr int BB = NMAX == 31 ? 176 : 144;
     constexpr float FN = (float)NMAX;
-    __shared__ float s_x[8][8 * 33];
-    __shared__ float s_w[8][8 * 33];
+    // per warp: 8 sub-blocks of 32, padded to 36 floats so that the eight
+    // 16-byte reads of one instruction fall in distinct bank groups
+    __shared__ __align__(16) float s_nx[8][8 * 36];
+    __shared__ __align__(16) float s_w[8][8 * 36];
     __shared__ __align__(16) uint8_t s_out[8][BB];
     __shared__ uint8_t s_l[8][256];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int s = lane >> 2, q = lane & 3;
     const int64_t ne0 = a.src.ne0, nsb = ne0 >> 8, total = a.n_rows * nsb;
+    float *snx = &s_nx[wid][s * 36];
+    float *sw = &s_w[wid][s * 36];
     for (int64_t g = (int64_t)blockIdx.x * 8 + wid; g < total; g += (int64_t)gridDim.x * 8) {
         const int64_t row = g / nsb;
         const int64_t sbi = g - row * nsb;
@@ -339,43 +430,41 @@ __global__ void __launch_bounds__(256, 1) enc_qk45_kernel(EncArgs a) {
         float v[8], base[8];
         load8(a.src, row, col0 + lane * 8, v);
         load_im8(imr, col0 + lane * 8, base);
+        // element weights (quant.rs:144-151): base * sqrt(sigma2 + x*x)
+        {
+            float wk[8];
 #pragma unroll
-        for (int k = 0; k < 8; k++) {
-            s_x[wid][s * 33 + q * 8 + k] = v[k];
-            s_w[wid][s * 33 + q * 8 + k] = base[k] * sqrtf(sig + v[k] * v[k]);
+            for (int k = 0; k < 8; k += 2) {
+                const float2 vv = make_float2(v[k], v[k + 1]);
+                const float2 vv2 = __fmul2_rn(vv, vv);
+                const float2 sq = make_float2(sqrtf(__fadd_rn(sig, vv2.x)), sqrtf(__fadd_rn(sig, vv2.y)));
+                const float2 ww = __fmul2_rn(make_float2(base[k], base[k + 1]), sq);
+                wk[k] = ww.x;
+                wk[k + 1] = ww.y;
+            }
+            float4 *pn = reinterpret_cast<float4 *>(snx + q * 8);
+            float4 *pw = reinterpret_cast<float4 *>(sw + q * 8);
+            pn[0] = make_float4(-v[0], -v[1], -v[2], -v[3]);
+            pn[1] = make_float4(-v[4], -v[5], -v[6], -v[7]);
+            pw[0] = make_float4(wk[0], wk[1], wk[2], wk[3]);
+            pw[1] = make_float4(wk[4], wk[5], wk[6], wk[7]);
         }
-        __syncwarp();
-        float x[32], w[32], xm[32];
-#pragma unroll
-        for (int i = 0; i < 32; i++) {
-            x[i] = s_x[wid][s * 33 + i];
-            w[i] = s_w[wid][s * 33 + i];
-        }
-        // make_qkx3_quants.  min/max folds are order-independent (NaN is
-        // skipped), so they run as trees on the hardware min/max; the sign
-        // of a zero vmin/vmax never reaches Q4_K/Q5_K bytes (it only enters
-        // x - vmin, scale*l + vmin, and -vmin folded with +0 by max).
+        // vmin/vmax folds (quant.rs:87-88) are order-independent (NaN is
+        // skipped): this lane's 8 values, then the 4 lanes of the sub-block.
+        // The sign of a zero vmin/vmax never reaches Q4_K/Q5_K bytes (it
+        // only enters x - vmin, scale*l + vmin, and -vmin folded with +0 by max).
         float vmin, vmax;
         {
-            float mn[16], mxv[16];
-#pragma unroll
-            for (int i = 0; i < 16; i++) {
-                mn[i] = fminf(x[2 * i], x[2 * i + 1]);
-                mxv[i] = fmaxf(x[2 * i], x[2 * i + 1]);
-            }
-#pragma unroll
-            for (int s2 = 8; s2 >= 1; s2 >>= 1)
-#pragma unroll
-                for (int i = 0; i < s2; i++) {
-                    mn[i] = fminf(mn[i], mn[i + s2]);
-                    mxv[i] = fmaxf(mxv[i], mxv[i + s2]);
-                }
-            vmin = fminf(fminf(INFINITY, mn[0]), 0.0f);
-            vmax = fmaxf(-INFINITY, mxv[0]);
+            float mn = fminf(fminf(fminf(v[0], v[1]), fminf(v[2], v[3])), fminf(fminf(v[4], v[5]), fminf(v[6], v[7])));
+            float mx = fmaxf(fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3])), fmaxf(fmaxf(v[4], v[5]), fmaxf(v[6], v[7])));
+            mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, 2));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            vmin = fminf(fminf(INFINITY, mn), 0.0f);
+            vmax = fmaxf(-INFINITY, mx);
         }
-        // x[i] - vmin is the same rounded value for every grid: hoisted
-#pragma unroll
-        for (int i = 0; i < 32; i++) xm[i] = x[i] - vmin;
+        __syncwarp();
         // Shuffles below run on every lane, so the per-lane candidate loop
         // is the only code inside the data-dependent branch.
         const bool degen = vmax <= vmin;
@@ -387,52 +476,73 @@ __global__ void __launch_bounds__(256, 1) enc_qk45_kernel(EncArgs a) {
         if (!degen) {
             float sum_w = 0.0f, sum_x = 0.0f;
 #pragma unroll
-            for (int i = 0; i < 32; i++) {
-                sum_w += w[i];
-                sum_x += w[i] * x[i];
+            for (int c = 0; c < 8; c++) {
+                const float4 n4 = reinterpret_cast<const float4 *>(snx)[c];
+                const float4 w4 = reinterpret_cast<const float4 *>(sw)[c];
+                const float2 a = __fmul2_rn(make_float2(w4.x, w4.y), make_float2(n4.x, n4.y));
+                const float2 b = __fmul2_rn(make_float2(w4.z, w4.w), make_float2(n4.z, n4.w));
+                sum_w = __fadd_rn(sum_w, w4.x);
+                sum_x = __fsub_rn(sum_x, a.x);
+                sum_w = __fadd_rn(sum_w, w4.y);
+                sum_x = __fsub_rn(sum_x, a.y);
+                sum_w = __fadd_rn(sum_w, w4.z);
+                sum_x = __fsub_rn(sum_x, b.x);
+                sum_w = __fadd_rn(sum_w, w4.w);
+                sum_x = __fsub_rn(sum_x, b.y);
             }
-            for (int j = q; j < 38; j += 4) {
-                const float iscale = j == 37 ? iscale0 : (-0.9f + 0.05f * (float)j + FN) / range;
-                float sl = 0.0f, sl2 = 0.0f, sxl = 0.0f;
-                float l[32];
+            const bool range_finite = range < INFINITY;
+            // lane q takes jobs q, q+4, ..., two per round in increasing order,
+            // so the strict `<` below keeps the first minimum as the reference's
+            // chain does; jobs 38 and 39 (lanes 2 and 3, last round) are padding
+            constexpr int NG = kQk45GridsPerRound;
+#pragma unroll 1
+            for (int r = 0; r < 10 / NG; r++) {
+                const int j0 = q + 4 * NG * r;
+                float isc[NG];
 #pragma unroll
-                for (int i = 0; i < 32; i++) {
-                    l[i] = round_clamp0_f(iscale * xm[i], FN);
-                    const float wl = w[i] * l[i];
-                    sl += wl;
-                    sl2 += w[i] * (l[i] * l[i]);
-                    sxl += wl * x[i];
+                for (int g = 0; g < NG; g++) {
+                    const int j = j0 + 4 * g;
+                    isc[g] = j == 37 ? iscale0 : (-0.9f + 0.05f * (float)j + FN) / range;
                 }
-                float ts, tm;
-                bool valid;
-                if (j == 37) {
-                    ts = scale0;
-                    tm = vmin;
-                    valid = true;
-                } else {
-                    const float D = sum_w * sl2 - sl * sl;
-                    valid = D > 0.0f;
-                    ts = (sum_w * sxl - sum_x * sl) / D;
-                    tm = (sl2 * sum_x - sl * sxl) / D;
-                    if (tm > 0.0f) {
-                        tm = 0.0f;
-                        ts = sl2 > 0.0f ? sxl / sl2 : 0.0f;
+                float sl[NG], sl2[NG], sxl[NG];
+                float2 l[NG][16];
+                bool clean = range_finite;
+#pragma unroll
+                for (int g = 0; g < NG; g++) clean = clean && isc[g] < INFINITY;
+                if (clean) qkx3_grids<true, NG>(snx, sw, vmin, isc, FN, l, sl, sl2, sxl);
+                else qkx3_grids<false, NG>(snx, sw, vmin, isc, FN, l, sl, sl2, sxl);
+                float ts[NG], tm[NG];
+                bool valid[NG];
+#pragma unroll
+                for (int g = 0; g < NG; g++) {
+                    if (j0 + 4 * g == 37) {
+                        ts[g] = scale0;
+                        tm[g] = vmin;
+                        valid[g] = true;
+                    } else {
+                        const float D = __fsub_rn(__fmul_rn(sum_w, sl2[g]), __fmul_rn(sl[g], sl[g]));
+                        valid[g] = D > 0.0f;
+                        ts[g] = __fsub_rn(__fmul_rn(sum_w, sxl[g]), __fmul_rn(sum_x, sl[g])) / D;
+                        tm[g] = __fsub_rn(__fmul_rn(sl2[g], sum_x), __fmul_rn(sl[g], sxl[g])) / D;
+                        if (tm[g] > 0.0f) {
+                            tm[g] = 0.0f;
+                            ts[g] = sl2[g] > 0.0f ? sxl[g] / sl2[g] : 0.0f;
+                        }
                     }
                 }
-                if (valid) {
-                    float err = 0.0f;
+                float err[NG];
+                qkx3_errors<NG>(snx, sw, l, ts, tm, err);
 #pragma unroll
-                    for (int i = 0; i < 32; i++) {
-                        const float diff = ts * l[i] + tm - x[i];
-                        err += w[i] * diff * diff;
-                    }
+                for (int g = 0; g < NG; g++) {
+                    const int j = j0 + 4 * g;
+                    if (j >= 38 || !valid[g]) continue;
                     if (j == 37) {
-                        init_err = err;
-                    } else if (err == err && (best_j < 0 || err < best_e)) {
-                        best_e = err;
+                        init_err = err[g];
+                    } else if (err[g] == err[g] && (best_j < 0 || err[g] < best_e)) {
+                        best_e = err[g];
                         best_j = j;
-                        best_s = ts;
-                        best_m = tm;
+                        best_s = ts[g];
+                        best_m = tm[g];
                     }
                 }
             }
@@ -483,21 +593,22 @@ __global__ void __launch_bounds__(256, 1) enc_qk45_kernel(EncArgs a) {
         const float msub = dmin * (float)lmq;
 #pragma unroll
         for (int k = 0; k < 8; k++) {
-            const int l = dsub == 0.0f ? 0 : (int)round_clamp0_f((v[k] + msub) / dsub, FN);
+            // (x + msub) = (msub - nx); x re-read from shared memory
+            const int l = dsub == 0.0f ? 0 : (int)round_clamp0_f(__fsub_rn(msub, snx[q * 8 + k]) / dsub, FN);
             s_l[wid][lane * 8 + k] = (uint8_t)l;
         }
-        int lsq_all[8], lmq_all[8];
-#pragma unroll
-        for (int t = 0; t < 8; t++) {
-            lsq_all[t] = __shfl_sync(0xffffffffu, lsq, t * 4);
-            lmq_all[t] = __shfl_sync(0xffffffffu, lmq, t * 4);
-        }
+        // 6-bit scale/min packing (quant.rs:316-327): lane t < 4 writes bytes
+        // t, t+4, t+8 of the 12 from sub-blocks t and t+4
         uint8_t *o = s_out[wid];
-        if (lane < 4) {
-            const int t = lane;
-            o[4 + t] = (uint8_t)(lsq_all[t] | ((lsq_all[t + 4] >> 4) << 6));
-            o[8 + t] = (uint8_t)(lmq_all[t] | ((lmq_all[t + 4] >> 4) << 6));
-            o[12 + t] = (uint8_t)((lsq_all[t + 4] & 0xF) | ((lmq_all[t + 4] & 0xF) << 4));
+        {
+            const int t = lane & 3;
+            const int ls_a = __shfl_sync(0xffffffffu, lsq, t * 4), ls_b = __shfl_sync(0xffffffffu, lsq, t * 4 + 16);
+            const int lm_a = __shfl_sync(0xffffffffu, lmq, t * 4), lm_b = __shfl_sync(0xffffffffu, lmq, t * 4 + 16);
+            if (lane < 4) {
+                o[4 + t] = (uint8_t)(ls_a | ((ls_b >> 4) << 6));
+                o[8 + t] = (uint8_t)(lm_a | ((lm_b >> 4) << 6));
+                o[12 + t] = (uint8_t)((ls_b & 0xF) | ((lm_b & 0xF) << 4));
+            }
         }
         if (lane == 0) {
             const uint16_t hd = f16_bits(d), hm = f16_bits(dmin);

@@ -67,6 +67,14 @@ def test_encode_matches_oracle_sweep_rows(ctx, ty):
     assert_bytes_equal(gpu_encode(ctx, ty, bits, im), oracle_encode(ty, bits, im), ty)
 
 
+@pytest.mark.parametrize("ty", supported(KQUANT) + supported([20, 23]), ids=lambda t: NAMES[t])
+def test_encode_matches_oracle_many_rows(ctx, ty):
+    """4096 rows x 1024 (16384 super-blocks): enough near-ties between grid
+    errors that a single contracted multiply-add in a search shows up."""
+    bits, im = sweep_rows(4096, 1024, seed=5)
+    assert_bytes_equal(gpu_encode(ctx, ty, bits, im), oracle_encode(ty, bits, im), ty)
+
+
 @pytest.mark.parametrize("ty", ENC_TYPES, ids=lambda t: NAMES[t])
 def test_encode_matches_oracle_student_rows_no_imatrix(ctx, ty):
     bits, _ = student_rows(32, 4096, seed=200 + ty)
