@@ -73,6 +73,21 @@ __device__ __forceinline__ float round_away_small(float x) { return copysignf(fl
 __device__ __forceinline__ float round_clamp0_f(float x, float hi) {
     return fminf(fmaxf(floor_half_up(x), 0.0f), hi);
 }
+// nearest_int(x).clamp(0, hi) as an integer, for integer 0 < hi < 256,
+// without a conversion instruction: RD(RZ(x + 1/2) + 2^23) is 2^23 + the
+// rounded value (identities (a), (b) above), clamped in that biased form to
+// [2^23, 2^23 + hi] (NaN and everything below 2^23 go to the lower bound),
+// whose low mantissa bits are the result.
+__device__ __forceinline__ int round_clamp0_i(float x, float hi) {
+    const float b = __fadd_rd(__fadd_rz(x, 0.5f), 8388608.0f);
+    return (int)(__float_as_uint(fminf(fmaxf(b, 8388608.0f), 8388608.0f + hi)) & 0xFFu);
+}
+// (2l+1) as a float for a small non-negative integer l, without a conversion
+// instruction: the integer in the low mantissa bits of 2^23, minus 2^23.
+__device__ __forceinline__ float odd_level(uint32_t l) {
+    return __uint_as_float(0x4B000001u | (l << 1)) - 8388608.0f;
+}
+
 // nearest_int(x).clamp(lo, hi) in float for lo < 0 < hi, |lo|, hi < 2^22:
 // NaN must map to 0 (not lo) as the saturating cast does.
 __device__ __forceinline__ float round_clamp_f(float x, float lo, float hi) {

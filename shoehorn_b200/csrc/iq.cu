@@ -2,12 +2,14 @@
 //
 // One warp per 256-element super-block.  The per-block scale trials of the
 // reference are independent given the block's weights, so every
-// (block, trial) pair is a lane job; the trials' (sumqx, sumq2) go to shared
-// memory and the reference's sequential `sumqx^2 > best*sumq2` chain is then
-// replayed by one lane per block, which also re-runs the winning trial to
-// recover its lattice points (cheaper than keeping every trial's points).
-// Lattice lookups use the compact kmap staged in shared memory; neighbour
-// lists are read through the read-only cache.
+// (block, trial) pair is a lane job.  A job rounds its groups to the lattice;
+// the groups that land off the grid become search tasks, and each task's
+// neighbour list is scanned by a group of lanes together (the lists' lengths
+// vary, so one lane per list would serialise the warp on the longest).  The
+// reference's sequential `sumqx^2 > best*sumq2` chain over the trials is then
+// replayed by one lane per block.  Lattice lookups use the compact kmap
+// staged in shared memory; neighbour lists are read through the read-only
+// cache.
 #include <cfloat>
 
 #include "iq_tables.h"
@@ -298,59 +300,6 @@ __device__ __forceinline__ int kmap_index(uint32_t g) {
     return u;
 }
 
-// find_best_neighbour (quant_iq.rs:137-167): first strict minimum of
-// sum_i waux_i * (scale*g_i - x_i)^2 over the neighbour list of kmap entry m;
-// returns the winner's packed levels ((g-1)/2), or ~0u if no candidate was
-// finite.  Kept out of line: the encoders call it from several places.
-template <int V>
-__device__ __noinline__ uint32_t best_neighbour(const void *lists, const uint16_t *gco, int m, const float *xg_s,
-                                                const float *wg_s, float scale) {
-    using C = IqCfg<V>;
-    constexpr uint32_t MASK = (1u << C::BITS) - 1;
-    float xg[C::G], wg[C::G];
-#pragma unroll
-    for (int i = 0; i < C::G; i++) {
-        xg[i] = xg_s[i];
-        wg[i] = wg_s[i];
-    }
-    float best = FLT_MAX;
-    uint32_t bc = ~0u;
-    auto eval = [&](uint32_t c) {
-        float d2 = 0.0f;
-#pragma unroll
-        for (int i = 0; i < C::G; i++) {
-            const float pg = (float)(2 * (int)((c >> (C::BITS * i)) & MASK) + 1);
-            const float diff = scale * pg - xg[i];
-            d2 += wg[i] * diff * diff;
-        }
-        if (d2 < best) {
-            best = d2;
-            bc = c;
-        }
-    };
-    if (V == 0) {  // shared memory, 8-bit grid indices
-        const uint8_t *p = static_cast<const uint8_t *>(lists) + (-m - 1);
-        const int n = p[0];
-        for (int t = 0; t < n; t++) eval(gco[p[1 + t]]);
-    } else if (V == 1) {  // global memory, 16-byte aligned runs of 8 entries
-        const uint16_t *p = static_cast<const uint16_t *>(lists) + (-m - 1);
-        const int n = (int)__ldg(p);
-        const uint4 *q = reinterpret_cast<const uint4 *>(p + 1);
-        for (int ch = 0; ch * 8 < n; ch++) {
-            const uint4 v = __ldg(q + ch);
-            const uint32_t e[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int k = 0; k < 8; k++)
-                if (ch * 8 + k < n) eval((e[k >> 1] >> (16 * (k & 1))) & 0xFFFFu);
-        }
-    } else {  // shared memory, 16-bit coordinates
-        const uint16_t *p = static_cast<const uint16_t *>(lists) + (-m - 1);
-        const int n = p[0];
-        for (int t = 0; t < n; t++) eval(p[1 + t]);
-    }
-    return bc;
-}
-
 // Round one group to the lattice at `id` (quant_iq.rs: l = clamp(round(
 // 0.5*(id*x - 1)), 0, kmax-1)); returns the group's packed levels.
 template <int V>
@@ -359,7 +308,7 @@ __device__ __forceinline__ uint32_t round_group(const float *xg, float id) {
     uint32_t g = 0;
 #pragma unroll
     for (int i = 0; i < C::G; i++) {
-        const int l = (int)round_clamp0_f(0.5f * (id * xg[i] - 1.0f), (float)(C::KM - 1));
+        const int l = round_clamp0_i(0.5f * (id * xg[i] - 1.0f), (float)(C::KM - 1));
         g |= (uint32_t)l << (C::BITS * i);
     }
     return g;
@@ -372,40 +321,12 @@ __device__ __forceinline__ void block_sums(const float *xv, const float *w, cons
     float a = 0.0f, c = 0.0f;
 #pragma unroll
     for (int i = 0; i < C::BS; i++) {
-        const float q = (float)(2 * lv.level(i) + 1);
+        const float q = odd_level((uint32_t)lv.level(i));
         a += w[i] * xv[i] * q;
         c += w[i] * q * q;
     }
     sx = a;
     s2 = c;
-}
-
-// One scale trial over one block: every group rounded to the lattice at id,
-// off-grid groups snapped to the best neighbour at this_scale.  offmask gets
-// bit k for each group that was off the grid.
-template <int V>
-__device__ __forceinline__ void iq_trial(const float *xv, const float *w, const float *wa, float id, float this_scale,
-                                         const int *kmap, const void *nb, const uint16_t *gco, Levels<V> &lv,
-                                         uint32_t &offmask, float &sumqx, float &sumq2, int *status) {
-    using C = IqCfg<V>;
-    lv.p0 = lv.p1 = 0;
-    offmask = 0;
-#pragma unroll 1
-    for (int k = 0; k < C::NG; k++) {
-        uint32_t g = round_group<V>(xv + k * C::G, id);
-        const int m = kmap[kmap_index<V>(g)];
-        if (m < 0) {
-            offmask |= 1u << k;
-            uint32_t c = best_neighbour<V>(nb, gco, m, xv + k * C::G, wa + k * C::G, this_scale);
-            if (c == ~0u) {
-                set_status(status, SHC_ENONEIGHBOUR);
-                c = 0;
-            }
-            g = c;
-        }
-        lv.set_group(k, g);
-    }
-    block_sums<V>(xv, w, lv, sumqx, sumq2);
 }
 
 // make_qp_quants (quant_iq.rs:170-241), n = 32, nmax = 4: the IQ2_XXS seed.
@@ -471,56 +392,296 @@ __device__ float make_qp_quants32(const float *x, const float *w) {
     return suml2 > 0.0f ? sumlx / suml2 : 0.0f;
 }
 
+// Search layout per variant: jobs per chunk (each chunk's off-grid groups
+// are searched in one pass) and whether candidates are scored from a per-task
+// term table (IQ2: 8 dimensions x 3 levels, lists of ~10-60 entries) or
+// directly (IQ3: 4 dimensions x 8 levels, lists of ~10).
+// Neighbour search layout per variant.  IQ2 lists (8 dimensions, ~10-60
+// entries) are scanned cooperatively: a chunk of CJ jobs queues its off-grid
+// groups as tasks, and rounds of 32 tasks share the warp (term tables, equal
+// candidate ranges per lane).  IQ3 lists (4 dimensions, ~10 entries) are
+// scanned by the lane that owns the job, from lists staged in shared memory,
+// with 16 warps per block to hide the scans' latency.
+template <int V>
+struct IqSearch {
+    static constexpr bool COOP = V < 3;
+    static constexpr int CJ = 32;                  // jobs per chunk (COOP)
+    static constexpr bool LISTS_SMEM = !COOP;      // IQ3: 46-57 KB of lists
+    static constexpr int WARPS = COOP ? 8 : 16;    // warps per block
+};
+
 // Per-warp shared state; block arrays padded to BS+1 so lanes working on
 // different blocks hit different banks.
 template <int V>
 struct IqWarpSmem {
-    static constexpr int BP = IqCfg<V>::BS + 1;
-    float x[256];
-    float xv[IqCfg<V>::NB * BP];
-    float w[IqCfg<V>::NB * BP];
-    float wa[IqCfg<V>::NB * BP];
-    float2 res[IqCfg<V>::NB * IqCfg<V>::NT];
-    float bscale0[IqCfg<V>::NB];  // chain start scale per block (qp seed or max/(2k-1))
-    float bmax[IqCfg<V>::NB];     // max |x| (or the qp effective max) per block
-    float bscale[IqCfg<V>::NB];   // final block scale
-    uint8_t live[IqCfg<V>::NB];
-    uint8_t signs[32];            // per 8-element sign group
-    uint16_t gidx[64];            // grid index per lattice group
+    using C = IqCfg<V>;
+    static constexpr bool COOP = IqSearch<V>::COOP;
+    static constexpr int BP = C::BS + 1;
+    static constexpr int MAXT = COOP ? IqSearch<V>::CJ * C::NG : 1;  // search tasks per chunk of jobs
+    static constexpr int TS = C::G * C::KM + 1;  // term table row (padded: the lanes' rows fall in distinct banks)
+    unsigned long long key[MAXT];                // task: winning packed levels, or ~0u
+    unsigned long long rkey[COOP ? 32 : 1];      // round slot: best (d2 bits, list position)
+    union {
+        float x[256];                            // the super-block (weights and sigma^2 only)
+        float tab[COOP ? 32 * TS : 1];           // round slot: waux_i*diff*diff per (dimension, level)
+    };
+    float xv[C::NB * BP];
+    float w[C::NB * BP];
+    float wa[C::NB * BP];
+    float2 jres[C::NB * C::NT];                  // (sumqx, sumq2) of every (block, trial) job
+    int pre[COOP ? 33 : 1];                      // round slot: first candidate in the flattened lists
+    int rbase[COOP ? 32 : 1];                    // round slot: list offset
+    int tq_m[MAXT];                              // task: kmap entry (< 0: neighbour list offset)
+    float tq_s[MAXT];                            // task: scale the candidates are scored at
+    uint16_t tq_x[MAXT];                         // task: offset of the group in xv / wa
+    float bscale0[C::NB];                        // chain start scale per block (qp seed or max/(2k-1))
+    float bmax[C::NB];                           // max |x| (or the qp effective max) per block
+    float bscale[C::NB];                         // final block scale
+    uint8_t live[C::NB];
+    uint8_t signs[32];                           // per 8-element sign group
+    uint16_t gidx[64];                           // grid index per lattice group
     __align__(16) uint8_t out[112];
 };
 
-// Lists that live in shared memory for variant V (all but IQ2_XS, whose
-// 375 KB of lists stay in global memory).
+// Exclusive prefix of `cnt` over the warp; returns the lane's offset and
+// the total in `total`.
+__device__ __forceinline__ int warp_exclusive_scan(int cnt, int lane, int &total) {
+    int pos = cnt;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, pos, d);
+        if (lane >= d) pos += o;
+    }
+    total = __shfl_sync(0xffffffffu, pos, 31);
+    return pos - cnt;
+}
+
+// find_best_neighbour (quant_iq.rs:137-167).  The reference keeps the first
+// candidate whose d2 = sum_i waux_i*(scale*g_i - x_i)^2 (a serial sum over
+// the lattice dimension) is strictly below the running best, which starts at
+// f32::MAX: the candidate with the smallest (d2, list position) among those
+// with d2 < f32::MAX.  d2 >= +0, so its bits order like its value and
+// (bits << 32 | position) is one 64-bit key.
+
+// Per-lane scan of one list (IQ3): returns the winner's packed levels, or ~0u.
+// Kept out of line: its callers are unrolled over the groups.
 template <int V>
-__host__ __device__ constexpr bool lists_in_smem() { return V != 1; }
+__device__ __noinline__ uint32_t lane_search(const uint16_t *l16, int m, const float *xg, const float *wg,
+                                                float scale) {
+    using C = IqCfg<V>;
+    constexpr uint32_t MASK = (1u << C::BITS) - 1;
+    const uint16_t *p = l16 + (-m - 1);
+    const int n = p[0];
+    float xi[C::G], wi[C::G];
+#pragma unroll
+    for (int i = 0; i < C::G; i++) {
+        xi[i] = xg[i];
+        wi[i] = wg[i];
+    }
+    float best = FLT_MAX;
+    uint32_t bc = ~0u;
+    for (int c = 0; c < n; c++) {
+        const uint32_t cc = p[1 + c];
+        float d2 = 0.0f;
+#pragma unroll
+        for (int i = 0; i < C::G; i++) {
+            const float diff = scale * odd_level((cc >> (C::BITS * i)) & MASK) - xi[i];
+            d2 += wi[i] * diff * diff;
+        }
+        if (d2 < best) {
+            best = d2;
+            bc = cc;
+        }
+    }
+    return bc;
+}
+
+// Cooperative scan of the queued tasks [0, T) (IQ2), 32 per round: each lane
+// tabulates one task's terms per (dimension, level); the round's lists are
+// then laid end to end and cut into 32 equal contiguous ranges, one per lane,
+// so every lane scores the same number of candidates whatever the lists'
+// lengths.  A lane keeps the first minimum of its part of each list and
+// merges it into that list's key (shared-memory atomicMin); only neighbouring
+// lanes ever share a list.  On return key[q] holds task q's winning packed
+// levels, or ~0u.
+template <int V>
+__device__ __noinline__ void search_tasks(IqWarpSmem<V> &S, int T, const void *lists, const uint16_t *gco, int lane) {
+    using C = IqCfg<V>;
+    constexpr int KM = C::KM, G = C::G, TS = IqWarpSmem<V>::TS;
+    constexpr uint32_t MASK = (1u << C::BITS) - 1;
+    const uint8_t *l8 = static_cast<const uint8_t *>(lists);
+    const uint16_t *l16 = static_cast<const uint16_t *>(lists);
+    auto entry = [&](int base, int c) -> uint32_t {
+        return V == 0 ? (uint32_t)gco[__ldg(l8 + base + 1 + c)] : (uint32_t)__ldg(l16 + base + 1 + c);
+    };
+    for (int r0 = 0; r0 < T; r0 += 32) {
+        const int q = r0 + lane;
+        int n = 0;
+        if (q < T) {
+            const int base = -S.tq_m[q] - 1;
+            n = V == 0 ? (int)__ldg(l8 + base) : (int)__ldg(l16 + base);
+            S.rbase[lane] = base;
+            const float scale = S.tq_s[q];
+            const int xo = S.tq_x[q];
+            float *tb = S.tab + lane * TS;
+#pragma unroll
+            for (int i = 0; i < G; i++) {
+                const float xi = S.xv[xo + i], wi = S.wa[xo + i];
+#pragma unroll
+                for (int l = 0; l < KM; l++) {
+                    const float diff = scale * (float)(2 * l + 1) - xi;
+                    tb[i * KM + l] = wi * diff * diff;
+                }
+            }
+        }
+        S.rkey[lane] = ~0ull;
+        int tot;
+        S.pre[lane] = warp_exclusive_scan(n, lane, tot);
+        if (lane == 0) S.pre[32] = tot;
+        __syncwarp();
+        const int k0 = (int)(((int64_t)tot * lane) >> 5), k1 = (int)(((int64_t)tot * (lane + 1)) >> 5);
+        if (k0 < k1) {
+            int t = 0;  // the slot holding candidate k0: smallest t with pre[t+1] > k0
+            for (int hi = 31; t < hi;) {
+                const int mid = (t + hi) >> 1;
+                if (S.pre[mid + 1] > k0) hi = mid;
+                else t = mid + 1;
+            }
+            int k = k0;
+            for (;;) {
+                const int start = S.pre[t], end = min(S.pre[t + 1], k1), base = S.rbase[t];
+                const float *tb = S.tab + t * TS;
+                uint32_t bh = 0xFFFFFFFFu, bl = 0xFFFFFFFFu;
+                for (; k < end; k++) {
+                    const uint32_t cc = entry(base, k - start);
+                    float d2 = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < G; i++) d2 += tb[i * KM + ((cc >> (C::BITS * i)) & MASK)];
+                    const uint32_t kh = __float_as_uint(d2);
+                    if (d2 < FLT_MAX && kh < bh) {  // positions rise within the lane: strict keeps the first
+                        bh = kh;
+                        bl = (uint32_t)(k - start);
+                    }
+                }
+                if (bh != 0xFFFFFFFFu) atomicMin(&S.rkey[t], ((unsigned long long)bh << 32) | bl);
+                if (k >= k1) break;
+                do {
+                    t++;
+                } while (S.pre[t + 1] <= k);
+            }
+        }
+        __syncwarp();
+        if (q < T) {
+            const unsigned long long kk = S.rkey[lane];
+            S.key[q] = kk == ~0ull ? 0xFFFFFFFFull : (unsigned long long)entry(S.rbase[lane], (int)(uint32_t)kk);
+        }
+        __syncwarp();
+    }
+}
+
+// Round the groups `todo` of one block at `id` (the trial loops of
+// quant_iq.rs): on-grid groups go into lv.  Off-grid groups are searched
+// here at `scale` (IQ3, per lane) or leave their kmap entry in mk for the
+// cooperative search (IQ2).  Returns the off-grid mask.
+template <int V>
+__device__ __forceinline__ uint32_t round_block(IqWarpSmem<V> &S, const int *kmap, const uint16_t *l16, int xb,
+                                                float id, float scale, uint32_t todo, Levels<V> &lv,
+                                                int (&mk)[IqCfg<V>::NG], int *status) {
+    using C = IqCfg<V>;
+    uint32_t offm = 0;
+    if (IqSearch<V>::COOP) {
+#pragma unroll
+        for (int k = 0; k < C::NG; k++) {
+            mk[k] = 0;
+            if (!((todo >> k) & 1u)) continue;
+            const uint32_t g = round_group<V>(S.xv + xb + k * C::G, id);
+            const int m = kmap[kmap_index<V>(g)];
+            if (m >= 0) {
+                lv.set_group(k, g);
+            } else {
+                offm |= 1u << k;
+                mk[k] = m;
+            }
+        }
+    } else {
+#pragma unroll 1
+        for (int k = 0; k < C::NG; k++) {
+            if (!((todo >> k) & 1u)) continue;
+            uint32_t g = round_group<V>(S.xv + xb + k * C::G, id);
+            const int m = kmap[kmap_index<V>(g)];
+            if (m < 0) {
+                offm |= 1u << k;
+                g = lane_search<V>(l16, m, S.xv + xb + k * C::G, S.wa + xb + k * C::G, scale);
+                if (g == ~0u) {
+                    set_status(status, SHC_ENONEIGHBOUR);
+                    g = 0;
+                }
+            }
+            lv.set_group(k, g);
+        }
+    }
+    return offm;
+}
 
 template <int V>
-__global__ void __launch_bounds__(256) enc_iq_lattice_kernel(EncArgs a, const int32_t *__restrict__ g_kmap,
-                                                             const uint8_t *__restrict__ g_lists, int lists_bytes,
-                                                             const uint32_t *__restrict__ g_coords) {
+__device__ __forceinline__ void queue_tasks(IqWarpSmem<V> &S, int pos, uint32_t offm, const int (&mk)[IqCfg<V>::NG],
+                                            int xb, float scale) {
+    using C = IqCfg<V>;
+#pragma unroll
+    for (int k = 0; k < C::NG; k++) {
+        if (!((offm >> k) & 1u)) continue;
+        S.tq_m[pos] = mk[k];
+        S.tq_s[pos] = scale;
+        S.tq_x[pos] = (uint16_t)(xb + k * C::G);
+        pos++;
+    }
+}
+
+template <int V>
+__device__ __forceinline__ void take_results(IqWarpSmem<V> &S, int pos, uint32_t offm, Levels<V> &lv, int *status) {
+    using C = IqCfg<V>;
+#pragma unroll
+    for (int k = 0; k < C::NG; k++) {
+        if (!((offm >> k) & 1u)) continue;
+        uint32_t c = (uint32_t)S.key[pos++];
+        if (c == ~0u) {
+            set_status(status, SHC_ENONEIGHBOUR);
+            c = 0;
+        }
+        lv.set_group(k, c);
+    }
+}
+
+template <int V>
+__global__ void __launch_bounds__(IqSearch<V>::WARPS * 32, IqSearch<V>::COOP ? 2 : 1)
+    enc_iq_lattice_kernel(EncArgs a, const int32_t *__restrict__ g_kmap, const void *__restrict__ g_lists,
+                          int lists_bytes, const uint32_t *__restrict__ g_coords) {
     using C = IqCfg<V>;
     constexpr int BP = C::BS + 1;
+    constexpr int NJ = C::NB * C::NT;
+    constexpr int NW = IqSearch<V>::WARPS;
+    constexpr bool COOP = IqSearch<V>::COOP;
     extern __shared__ __align__(16) uint8_t smem_raw[];
-    // shared memory: compact kmap | per-warp state | grid coords | lists
+    // shared memory: compact kmap | per-warp state | grid coords (IQ2_XXS)
     int *kmap = reinterpret_cast<int *>(smem_raw);
     IqWarpSmem<V> *wsm_all = reinterpret_cast<IqWarpSmem<V> *>(smem_raw + ((C::KMAP * 4 + 15) & ~15));
-    uint16_t *gco = reinterpret_cast<uint16_t *>(reinterpret_cast<uint8_t *>(wsm_all + 8));
+    uint16_t *gco = reinterpret_cast<uint16_t *>(reinterpret_cast<uint8_t *>(wsm_all + NW));
     uint8_t *s_lists = reinterpret_cast<uint8_t *>(gco + 256);
     for (int i = threadIdx.x; i < C::KMAP; i += blockDim.x) kmap[i] = g_kmap[i];
     if (V == 0)
         for (int i = threadIdx.x; i < 256; i += blockDim.x) gco[i] = (uint16_t)g_coords[i];
-    if (lists_in_smem<V>()) {
-        const uint4 *src4 = reinterpret_cast<const uint4 *>(g_lists);
+    if (IqSearch<V>::LISTS_SMEM) {
+        const uint4 *src4 = static_cast<const uint4 *>(g_lists);
         uint4 *dst4 = reinterpret_cast<uint4 *>(s_lists);
         for (int i = threadIdx.x; i < lists_bytes / 16; i += blockDim.x) dst4[i] = src4[i];
     }
     __syncthreads();
-    const void *nbs = lists_in_smem<V>() ? (const void *)s_lists : (const void *)g_lists;
+    const void *lists = IqSearch<V>::LISTS_SMEM ? (const void *)s_lists : g_lists;
+    const uint16_t *l16 = static_cast<const uint16_t *>(lists);
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     IqWarpSmem<V> &S = wsm_all[wid];
     const int64_t ne0 = a.src.ne0, nsb = ne0 >> 8, total = a.n_rows * nsb;
-    for (int64_t g = (int64_t)blockIdx.x * 8 + wid; g < total; g += (int64_t)gridDim.x * 8) {
+    for (int64_t g = (int64_t)blockIdx.x * NW + wid; g < total; g += (int64_t)gridDim.x * NW) {
         const int64_t row = g / nsb;
         const int64_t sbi = g - row * nsb;
         const int64_t col0 = sbi << 8;
@@ -608,67 +769,125 @@ __global__ void __launch_bounds__(256) enc_iq_lattice_kernel(EncArgs a, const in
             S.bmax[b] = ref;
         }
         __syncwarp();
-        // ---- P2: every (block, trial) pair ----
-        for (int j = lane; j < C::NB * C::NT; j += 32) {
-            const int b = j / C::NT, t = j - b * C::NT;
-            if (!S.live[b]) continue;
-            const float id = ((float)(2 * C::KM - 1) + (float)(C::IS_LO + t) * C::STEP) / S.bmax[b];
-            Levels<V> lv;
-            uint32_t off;
-            float sx, s2;
-            iq_trial<V>(S.xv + b * BP, S.w + b * BP, S.wa + b * BP, id, 1.0f / id, kmap, nbs, gco, lv, off, sx, s2,
-                        a.status);
-            S.res[j] = make_float2(sx, s2);
+        // ---- P2: every (block, trial) job: lattice rounding, neighbour
+        // searches, the trial's weighted sums (quant_iq.rs trial loops) ----
+        if (COOP) {
+            // CJ jobs per chunk, one per lane; the chunk's off-grid groups
+            // are searched together
+            constexpr int CJ = IqSearch<V>::CJ;
+            for (int c0 = 0; c0 < NJ; c0 += CJ) {
+                const int j = c0 + lane;
+                const int b = j / C::NT, t = j - b * C::NT;
+                const bool job = lane < CJ && j < NJ && S.live[b];
+                float sc = 0.0f;
+                Levels<V> lv;
+                int mk[C::NG];
+                uint32_t offm = 0;
+                if (job) {
+                    const float id = ((float)(2 * C::KM - 1) + (float)(C::IS_LO + t) * C::STEP) / S.bmax[b];
+                    sc = 1.0f / id;
+                    offm = round_block<V>(S, kmap, l16, b * BP, id, sc, (1u << C::NG) - 1, lv, mk, a.status);
+                }
+                int T;
+                const int pos = warp_exclusive_scan(__popc(offm), lane, T);
+                if (offm) queue_tasks<V>(S, pos, offm, mk, b * BP, sc);
+                __syncwarp();
+                if (T > 0) search_tasks<V>(S, T, lists, gco, lane);
+                if (job) {
+                    take_results<V>(S, pos, offm, lv, a.status);
+                    float sx, s2;
+                    block_sums<V>(S.xv + b * BP, S.w + b * BP, lv, sx, s2);
+                    S.jres[j] = make_float2(sx, s2);
+                }
+                __syncwarp();
+            }
+        } else {
+            for (int j = lane; j < NJ; j += 32) {
+                const int b = j / C::NT, t = j - b * C::NT;
+                if (!S.live[b]) continue;
+                const float id = ((float)(2 * C::KM - 1) + (float)(C::IS_LO + t) * C::STEP) / S.bmax[b];
+                Levels<V> lv;
+                int mk[C::NG];
+                round_block<V>(S, kmap, l16, b * BP, id, 1.0f / id, (1u << C::NG) - 1, lv, mk, a.status);
+                float sx, s2;
+                block_sums<V>(S.xv + b * BP, S.w + b * BP, lv, sx, s2);
+                S.jres[j] = make_float2(sx, s2);
+            }
+            __syncwarp();
         }
-        __syncwarp();
-        // ---- P3: per block: replay the chain, re-run the winner, re-project ----
-        if (lane < C::NB) {
+        // the reference's sequential `sumqx^2 > best*sumq2` chain over the
+        // trials, one lane per block
+        float cscale = 0.0f;
+        int cwin = -1;
+        if (lane < C::NB && S.live[lane]) {
+            cscale = S.bscale0[lane];
+            float cbest = 0.0f;
+            for (int tt = 0; tt < C::NT; tt++) {
+                const float2 r = S.jres[lane * C::NT + tt];
+                if (r.y > 0.0f && r.x * r.x > cbest * r.y) {
+                    cscale = r.x / r.y;
+                    cbest = cscale * r.x;
+                    cwin = tt;
+                }
+            }
+        }
+        // the winning trial's lattice points: that trial again, for the
+        // blocks that have one
+        Levels<V> wl;
+        uint32_t woff = 0;
+        {
+            float sc = 0.0f;
+            int mk[C::NG];
+            if (cwin >= 0) {
+                const float id = ((float)(2 * C::KM - 1) + (float)(C::IS_LO + cwin) * C::STEP) / S.bmax[lane];
+                sc = 1.0f / id;
+                woff = round_block<V>(S, kmap, l16, lane * BP, id, sc, (1u << C::NG) - 1, wl, mk, a.status);
+            }
+            if (COOP) {
+                int T;
+                const int pos = warp_exclusive_scan(__popc(woff), lane, T);
+                if (woff) queue_tasks<V>(S, pos, woff, mk, lane * BP, sc);
+                __syncwarp();
+                if (T > 0) search_tasks<V>(S, T, lists, gco, lane);
+                if (cwin >= 0) take_results<V>(S, pos, woff, wl, a.status);
+            }
+            __syncwarp();
+        }
+        // ---- P3: per block: the winner's points, re-projection at the final
+        // scale (quant_iq.rs, e.g. 364-384), sign flip and grid indices ----
+        {
             const int b = lane;
-            const float *xb = S.xv + b * BP, *wb = S.w + b * BP, *ab = S.wa + b * BP;
-            float scale = 0.0f;
-            if (S.live[b]) {
-                scale = S.bscale0[b];
-                float best = 0.0f;
-                int win = -1;
-                for (int t = 0; t < C::NT; t++) {
-                    const float2 r = S.res[b * C::NT + t];
-                    if (r.y > 0.0f && r.x * r.x > best * r.y) {
-                        scale = r.x / r.y;
-                        best = scale * r.x;
-                        win = t;
-                    }
-                }
-                Levels<V> ls;
-                // on-grid flags start true (IQ3_S: false) and follow the winning trial
-                uint32_t off = (V == 4) ? ((1u << C::NG) - 1) : 0u;
-                if (win >= 0) {
-                    const float id = ((float)(2 * C::KM - 1) + (float)(C::IS_LO + win) * C::STEP) / S.bmax[b];
-                    float sx, s2;
-                    iq_trial<V>(xb, wb, ab, id, 1.0f / id, kmap, nbs, gco, ls, off, sx, s2, a.status);
-                }
-                const bool reproject = (V == 0) ? (scale > 0.0f) : (off != 0 && scale > 0.0f);
-                if (reproject) {
-                    const float id = 1.0f / scale;
-#pragma unroll 1
-                    for (int k = 0; k < C::NG; k++) {
-                        const bool redo = (V == 0 || V == 4) ? true : ((off >> k) & 1u);
-                        if (!redo) continue;
-                        uint32_t gq = round_group<V>(xb + k * C::G, id);
-                        const int m = kmap[kmap_index<V>(gq)];
-                        if (m < 0) {
-                            uint32_t c = best_neighbour<V>(nbs, gco, m, xb + k * C::G, ab + k * C::G, scale);
-                            if (c == ~0u) {
-                                set_status(a.status, SHC_ENONEIGHBOUR);
-                                c = 0;
-                            }
-                            gq = c;
-                        }
-                        ls.set_group(k, gq);
-                    }
-                    float sx, s2;
-                    block_sums<V>(xb, wb, ls, sx, s2);
-                    if (s2 > 0.0f) scale = sx / s2;
-                }
+            const bool blk = lane < C::NB && S.live[b];
+            float scale = cscale;
+            // on-grid flags start true (IQ3_S: false) and follow the winning trial
+            uint32_t off = (V == 4) ? ((1u << C::NG) - 1) : 0u;
+            Levels<V> ls;
+            if (blk && cwin >= 0) {
+                ls = wl;
+                off = woff;
+            }
+            const bool reproject = blk && ((V == 0) ? (scale > 0.0f) : (off != 0 && scale > 0.0f));
+            uint32_t offm = 0;
+            int mk[C::NG];
+            if (reproject) {
+                const uint32_t todo = (V == 0 || V == 4) ? ((1u << C::NG) - 1) : off;
+                offm = round_block<V>(S, kmap, l16, b * BP, 1.0f / scale, scale, todo, ls, mk, a.status);
+            }
+            int pos = 0;
+            if (COOP) {
+                int T;
+                pos = warp_exclusive_scan(__popc(offm), lane, T);
+                if (offm) queue_tasks<V>(S, pos, offm, mk, b * BP, scale);
+                __syncwarp();
+                if (T > 0) search_tasks<V>(S, T, lists, gco, lane);
+            }
+            if (reproject) {
+                if (COOP) take_results<V>(S, pos, offm, ls, a.status);
+                float sx, s2;
+                block_sums<V>(S.xv + b * BP, S.w + b * BP, ls, sx, s2);
+                if (s2 > 0.0f) scale = sx / s2;
+            }
+            if (blk) {
                 if (scale < 0.0f) {
                     scale = -scale;
                     for (int k = 0; k < C::NSG; k++) {
@@ -682,11 +901,12 @@ __global__ void __launch_bounds__(256) enc_iq_lattice_kernel(EncArgs a, const in
                     if (m < 0) set_status(a.status, SHC_EOFFGRID);
                     S.gidx[b * C::NG + k] = (uint16_t)(m < 0 ? 0 : m);
                 }
-            } else {
+                S.bscale[b] = scale;
+            } else if (lane < C::NB) {
                 for (int k = 0; k < C::NG; k++) S.gidx[b * C::NG + k] = 0;
                 for (int k = 0; k < C::NSG; k++) S.signs[b * C::NSG + k] = 0;
+                S.bscale[b] = 0.0f;
             }
-            S.bscale[b] = scale;
         }
         __syncwarp();
         // ---- P4: super-block scale and packing (lane 0) ----
@@ -798,21 +1018,21 @@ __global__ void __launch_bounds__(256) enc_iq_lattice_kernel(EncArgs a, const in
 template <int V>
 static cudaError_t launch_lattice(const EncArgs &a, const IqTables &iq, int num_sms, cudaStream_t st) {
     using C = IqCfg<V>;
-    const size_t smem = ((C::KMAP * 4 + 15) & ~(size_t)15) + 8 * sizeof(IqWarpSmem<V>) + 512 +
-                        (lists_in_smem<V>() ? (size_t)iq.lists_bytes[V] : 0);
+    constexpr int NW = IqSearch<V>::WARPS;
+    const size_t smem = ((C::KMAP * 4 + 15) & ~(size_t)15) + NW * sizeof(IqWarpSmem<V>) + 512 +
+                        (IqSearch<V>::LISTS_SMEM ? (size_t)iq.lists_bytes[V] : 0);
     auto fn = enc_iq_lattice_kernel<V>;
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     int per_sm = 1;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, NW * 32, smem);
     if (per_sm < 1) per_sm = 1;
     const int64_t work = a.n_rows * (a.src.ne0 / 256);
-    int64_t grid = (work + 7) / 8;
+    int64_t grid = (work + NW - 1) / NW;
     const int64_t cap = (int64_t)num_sms * per_sm;
     if (grid > cap) grid = cap;
     if (grid < 1) grid = 1;
-    fn<<<(unsigned)grid, 256, smem, st>>>(a, iq.dkmap[V], static_cast<const uint8_t *>(iq.lists[V]),
-                                          iq.lists_bytes[V], iq.grid_coords[V]);
+    fn<<<(unsigned)grid, NW * 32, smem, st>>>(a, iq.dkmap[V], iq.lists[V], iq.lists_bytes[V], iq.grid_coords[V]);
     return cudaGetLastError();
 }
 
