@@ -329,73 +329,102 @@ __device__ __forceinline__ void block_sums(const float *xv, const float *w, cons
     s2 = c;
 }
 
-// make_qp_quants (quant_iq.rs:170-241), n = 32, nmax = 4: the IQ2_XXS seed.
-__device__ float make_qp_quants32(const float *x, const float *w) {
+// nearest_int for the make_qp_quants values: f32::round half away from zero
+// with three adds, and the integer read from the mantissa of r + 1.5*2^23,
+// exact for |r| < 2^22; NaN and larger magnitudes take the general path.
+__device__ __forceinline__ int nearest_int_qp(float y) {
+    if (!(fabsf(y) < 4194304.0f)) return nearest_int(y);
+    return (int)__float_as_uint(__fadd_rn(round_away_small(y), 12582912.0f)) - 0x4B400000;
+}
+
+// make_qp_quants (quant_iq.rs:170-241), n = 32, nmax = 4: the IQ2_XXS seed,
+// computed by the four lanes 4b..4b+3 of block b (u = lane & 3).  The max
+// fold is order-independent (NaN-ignoring, from +0) and is split over the
+// four lanes; the nine candidate scales' errors (each a serial sum over the
+// block, as in the reference) are split over the lanes as well; the choice
+// among them (first strict minimum), the final levels and the coordinate
+// descent are sequential and run on lane u == 0, with the levels `ls` in
+// shared memory.  Every lane of the warp must call it.
+__device__ float make_qp_quants32_x4(const float *x, const float *w, uint8_t *ls, int lane) {
     constexpr int n = 32, nmax = 4;
+    const int u = lane & 3, grp = lane & ~3;
     float max = 0.0f;
-    for (int i = 0; i < n; i++) max = rmaxf(max, x[i]);
-    if (max < kGroupMaxEps) return 0.0f;
-    float iscale = (float)nmax / max;
-    uint8_t ls[32];
-    for (int i = 0; i < n; i++) ls[i] = (uint8_t)nearest_int(iscale * x[i]);
-    const float scale = 1.0f / iscale;
-    float best_mse = 0.0f;
-    for (int i = 0; i < n; i++) {
-        const float diff = x[i] - scale * (float)ls[i];
-        best_mse += w[i] * diff * diff;
-    }
-    for (int is = -4; is <= 4; is++) {
-        if (is == 0) continue;
-        const float iscale_is = (0.1f * (float)is + (float)nmax) / max;
-        const float scale_is = 1.0f / iscale_is;
+#pragma unroll
+    for (int i = 0; i < 8; i++) max = rmaxf(max, x[u * 8 + i]);
+    max = rmaxf(max, __shfl_xor_sync(0xffffffffu, max, 1));
+    max = rmaxf(max, __shfl_xor_sync(0xffffffffu, max, 2));
+    const bool dead = max < kGroupMaxEps;
+    // trial t: 0 the initial iscale (levels wrap as u8, no clamp), 1..8 is = -4..-1, 1..4
+    auto iscale_of = [&](int t) -> float {
+        if (t == 0) return (float)nmax / max;
+        const int is = t <= 4 ? t - 5 : t - 4;
+        return (0.1f * (float)is + (float)nmax) / max;
+    };
+    float mine[3];
+#pragma unroll
+    for (int r = 0; r < 3; r++) {
+        const int t = u + 4 * r;
         float mse = 0.0f;
-        for (int i = 0; i < n; i++) {
-            const int l = min(nearest_int(iscale_is * x[i]), nmax);
-            const float diff = x[i] - scale_is * (float)l;
-            mse += w[i] * diff * diff;
+        if (!dead && t < 9) {
+            const float isc = iscale_of(t);
+            const float scale = 1.0f / isc;
+            for (int i = 0; i < n; i++) {
+                const int l = t == 0 ? (int)(uint8_t)nearest_int_qp(isc * x[i]) : min(nearest_int_qp(isc * x[i]), nmax);
+                const float diff = x[i] - scale * (float)l;
+                mse += w[i] * diff * diff;
+            }
         }
-        if (mse < best_mse) {
-            best_mse = mse;
-            iscale = iscale_is;
+        mine[r] = mse;
+    }
+    float best = 0.0f, iscale = 0.0f;
+#pragma unroll
+    for (int t = 0; t < 9; t++) {
+        const float mse = __shfl_sync(0xffffffffu, mine[t >> 2], grp | (t & 3));
+        if (t == 0) {
+            best = mse;
+            iscale = iscale_of(0);
+        } else if (mse < best) {
+            best = mse;
+            iscale = iscale_of(t);
         }
     }
-    float sumlx = 0.0f, suml2 = 0.0f;
-    for (int i = 0; i < n; i++) {
-        const int l = min(nearest_int(iscale * x[i]), nmax);
-        ls[i] = (uint8_t)l;
-        sumlx += w[i] * x[i] * (float)l;
-        suml2 += w[i] * (float)(l * l);
-    }
-    for (int it = 0; it < 5; it++) {
-        int n_changed = 0;
+    float res = 0.0f;
+    if (!dead && u == 0) {
+        float sumlx = 0.0f, suml2 = 0.0f;
         for (int i = 0; i < n; i++) {
-            const float wi = w[i];
-            const float li = (float)ls[i];
-            const float slx = sumlx - wi * x[i] * li;
-            const float sl2 = suml2 - wi * li * li;
-            if (slx > 0.0f && sl2 > 0.0f) {
-                const int new_l = min(nearest_int(x[i] * sl2 / slx), nmax);
-                if ((uint8_t)new_l != ls[i]) {
-                    const float slx2 = slx + wi * x[i] * (float)new_l;
-                    const float sl22 = sl2 + wi * (float)(new_l * new_l);
-                    if (slx2 * slx2 * suml2 > sumlx * sumlx * sl22) {
-                        ls[i] = (uint8_t)new_l;
-                        sumlx = slx2;
-                        suml2 = sl22;
-                        n_changed++;
+            const int l = min(nearest_int_qp(iscale * x[i]), nmax);
+            ls[i] = (uint8_t)l;
+            sumlx += w[i] * x[i] * (float)l;
+            suml2 += w[i] * (float)(l * l);
+        }
+        for (int it = 0; it < 5; it++) {
+            int n_changed = 0;
+            for (int i = 0; i < n; i++) {
+                const float wi = w[i];
+                const float li = (float)ls[i];
+                const float slx = sumlx - wi * x[i] * li;
+                const float sl2 = suml2 - wi * li * li;
+                if (slx > 0.0f && sl2 > 0.0f) {
+                    const int new_l = min(nearest_int_qp(x[i] * sl2 / slx), nmax);
+                    if ((uint8_t)new_l != ls[i]) {
+                        const float slx2 = slx + wi * x[i] * (float)new_l;
+                        const float sl22 = sl2 + wi * (float)(new_l * new_l);
+                        if (slx2 * slx2 * suml2 > sumlx * sumlx * sl22) {
+                            ls[i] = (uint8_t)new_l;
+                            sumlx = slx2;
+                            suml2 = sl22;
+                            n_changed++;
+                        }
                     }
                 }
             }
+            if (n_changed == 0) break;
         }
-        if (n_changed == 0) break;
+        res = suml2 > 0.0f ? sumlx / suml2 : 0.0f;
     }
-    return suml2 > 0.0f ? sumlx / suml2 : 0.0f;
+    return res;
 }
 
-// Search layout per variant: jobs per chunk (each chunk's off-grid groups
-// are searched in one pass) and whether candidates are scored from a per-task
-// term table (IQ2: 8 dimensions x 3 levels, lists of ~10-60 entries) or
-// directly (IQ3: 4 dimensions x 8 levels, lists of ~10).
 // Neighbour search layout per variant.  IQ2 lists (8 dimensions, ~10-60
 // entries) are scanned cooperatively: a chunk of CJ jobs queues its off-grid
 // groups as tasks, and rounds of 32 tasks share the warp (term tables, equal
@@ -439,6 +468,8 @@ struct IqWarpSmem {
     float bscale[C::NB];                         // final block scale
     uint8_t live[C::NB];
     uint8_t signs[32];                           // per 8-element sign group
+    uint8_t qpl[C::QP ? 256 : 1];                // make_qp_quants levels per block (IQ2_XXS)
+    float qps[C::QP ? C::NB : 1];                // make_qp_quants result per block (IQ2_XXS)
     uint16_t gidx[64];                           // grid index per lattice group
     __align__(16) uint8_t out[112];
 };
@@ -744,6 +775,12 @@ __global__ void __launch_bounds__(IqSearch<V>::WARPS * 32, IqSearch<V>::COOP ? 2
         }
         __syncwarp();
         // ---- P1: per-block max and starting scale ----
+        if (C::QP) {  // IQ2_XXS: eight blocks of 32, four lanes each
+            const int b = lane >> 2;
+            const float s = make_qp_quants32_x4(S.xv + b * BP, S.w + b * BP, S.qpl + b * 32, lane);
+            if ((lane & 3) == 0) S.qps[b] = s;
+            __syncwarp();
+        }
         if (lane < C::NB) {
             const int b = lane;
             const float *xb = S.xv + b * BP;
@@ -757,7 +794,7 @@ __global__ void __launch_bounds__(IqSearch<V>::WARPS * 32, IqSearch<V>::COOP ? 2
             float s0 = 0.0f, ref = mx;
             if (live) {
                 if (C::QP) {
-                    s0 = make_qp_quants32(xb, S.w + b * BP);
+                    s0 = S.qps[b];
                     ref = s0 * (float)C::KM;  // eff_max
                     if (ref <= 0.0f) live = false;
                 } else {
