@@ -29,7 +29,7 @@ struct shc_ctx {
     std::atomic<int64_t> launches{0};
     // host-buffer pipeline resources (one host call at a time)
     std::mutex host_mu;
-    cudaStream_t hs[3] = {nullptr, nullptr, nullptr};  // h2d, compute, d2h
+    cudaStream_t hs[4] = {nullptr, nullptr, nullptr, nullptr};  // h2d, compute, d2h, row sigma^2
     void *pin[4] = {nullptr, nullptr, nullptr, nullptr};  // in0, in1, out0, out1 (pageable staging)
     size_t pin_bytes[4] = {0, 0, 0, 0};
 };
@@ -139,10 +139,12 @@ cudaError_t scratch_alloc(shc_ctx *ctx, void **p, size_t bytes, cudaStream_t st)
 
 // Encode one view of rows on `st` (sigma^2 pre-pass into stream-ordered
 // scratch when the type needs it).
-int encode_view(shc_ctx *ctx, uint32_t type, EncArgs a, cudaStream_t st) {
+// sms: SMs the encoder's persistent grid is sized for (0: all of them).
+int encode_view(shc_ctx *ctx, uint32_t type, EncArgs a, cudaStream_t st, int sms = 0) {
+    const int num_sms = sms > 0 ? sms : ctx->num_sms;
     if (a.n_rows == 0) return SHC_OK;
     float *sig = nullptr;
-    if (needs_sigma2(type)) {
+    if (needs_sigma2(type) && !a.sigma2) {  // a caller may have computed it already
         SHC_TRY(scratch_alloc(ctx, (void **)&sig, sizeof(float) * (size_t)a.n_rows, st));
         cudaError_t e = launch_row_sigma2(a.src, a.n_rows, sig, st);
         ctx->launches++;
@@ -153,9 +155,9 @@ int encode_view(shc_ctx *ctx, uint32_t type, EncArgs a, cudaStream_t st) {
         a.sigma2 = sig;
     }
     cudaError_t e;
-    if (block_elems(type) == 1) e = launch_plain(type, a, ctx->num_sms, st);
-    else if (is_iq(type)) e = launch_iq(type, a, ctx->iq, ctx->num_sms, st);
-    else e = launch_kquant(type, a, ctx->num_sms, st);
+    if (block_elems(type) == 1) e = launch_plain(type, a, num_sms, st);
+    else if (is_iq(type)) e = launch_iq(type, a, ctx->iq, num_sms, st);
+    else e = launch_kquant(type, a, num_sms, st);
     ctx->launches++;
     if (sig) cudaFreeAsync(sig, st);
     return cuda_status(e);
@@ -306,7 +308,7 @@ int shc_init(int device, shc_ctx **out) {
             rc = SHC_ECUDA;
     }
     if (rc == SHC_OK) rc = upload_iq_tables(ctx);
-    for (int i = 0; rc == SHC_OK && i < 3; i++)
+    for (int i = 0; rc == SHC_OK && i < 4; i++)
         if (cudaStreamCreateWithFlags(&ctx->hs[i], cudaStreamNonBlocking) != cudaSuccess) rc = SHC_ECUDA;
     if (rc != SHC_OK) {
         shc_free(ctx);
@@ -321,7 +323,7 @@ int shc_free(shc_ctx *ctx) {
     {
         DevGuard g(ctx->device);
         cudaDeviceSynchronize();
-        for (int i = 0; i < 3; i++)
+        for (int i = 0; i < 4; i++)
             if (ctx->hs[i]) cudaStreamDestroy(ctx->hs[i]);
         for (int i = 0; i < 4; i++)
             if (ctx->pin[i]) cudaFreeHost(ctx->pin[i]);
@@ -456,16 +458,25 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
     chunk = std::min(chunk, n_rows);
     const int64_t n_chunks = (n_rows + chunk - 1) / chunk;
     const bool pin_src = is_pinned(host_src), pin_dst = is_pinned(host_dst);
-    cudaStream_t s_in = ctx->hs[0], s_cmp = ctx->hs[1], s_out = ctx->hs[2];
+    cudaStream_t s_in = ctx->hs[0], s_cmp = ctx->hs[1], s_out = ctx->hs[2], s_sig = ctx->hs[3];
+    // The row sigma^2 pre-pass (one thread per row, bound by its serial sums)
+    // runs on its own stream for chunk k+1 while chunk k encodes; the
+    // encoder's persistent grid leaves kSigmaSms SMs' worth of blocks free so
+    // that the pre-pass has room beside it.
+    constexpr int kSigmaSms = 4;
+    const bool pre_sig = needs_sigma2(type) && n_rows > 1;
+    const int enc_sms = pre_sig ? std::max(1, ctx->num_sms - kSigmaSms) : 0;
     int rc = SHC_OK;
     void *d_in[2] = {nullptr, nullptr};
     uint8_t *d_out[2] = {nullptr, nullptr};
+    float *d_sig[2] = {nullptr, nullptr};
     float *d_im = nullptr;
-    cudaEvent_t ev_in[2], ev_cmp[2], ev_out[2];
+    cudaEvent_t ev_in[2], ev_cmp[2], ev_out[2], ev_sig[2];
     for (int b = 0; b < 2; b++) {
         cudaEventCreateWithFlags(&ev_in[b], cudaEventDisableTiming);
         cudaEventCreateWithFlags(&ev_cmp[b], cudaEventDisableTiming);
         cudaEventCreateWithFlags(&ev_out[b], cudaEventDisableTiming);
+        cudaEventCreateWithFlags(&ev_sig[b], cudaEventDisableTiming);
     }
     auto fail = [&](int code) {
         if (rc == SHC_OK) rc = code;
@@ -473,6 +484,9 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
     for (int b = 0; b < 2 && rc == SHC_OK; b++) {
         if (scratch_alloc(ctx, &d_in[b], in_row * (size_t)chunk, s_cmp) != cudaSuccess) fail(SHC_ENOMEM);
         if (scratch_alloc(ctx, (void **)&d_out[b], (size_t)rb * (size_t)chunk, s_cmp) != cudaSuccess) fail(SHC_ENOMEM);
+        if (pre_sig && rc == SHC_OK &&
+            scratch_alloc(ctx, (void **)&d_sig[b], sizeof(float) * (size_t)chunk, s_cmp) != cudaSuccess)
+            fail(SHC_ENOMEM);
         if (!pin_src && rc == SHC_OK) fail(ensure_pinned(ctx, b, in_row * (size_t)chunk));
         if (!pin_dst && rc == SHC_OK) fail(ensure_pinned(ctx, 2 + b, (size_t)rb * (size_t)chunk));
     }
@@ -486,6 +500,7 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
         cudaEventRecord(ev_cmp[0], s_cmp);
         cudaStreamWaitEvent(s_in, ev_cmp[0], 0);
         cudaStreamWaitEvent(s_out, ev_cmp[0], 0);
+        cudaStreamWaitEvent(s_sig, ev_cmp[0], 0);
         cudaEventRecord(ev_cmp[1], s_cmp);
         for (int b = 0; b < 2; b++) {
             cudaEventRecord(ev_out[b], s_out);
@@ -521,11 +536,22 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
             if (cudaMemcpyAsync(d_in[b], ctx->pin[b], in_bytes, cudaMemcpyHostToDevice, s_in) != cudaSuccess) fail(SHC_ECUDA);
         }
         cudaEventRecord(ev_in[b], s_in);
-        // encode chunk k once its input landed and d_out[b] was drained
-        cudaStreamWaitEvent(s_cmp, ev_in[b], 0);
-        cudaStreamWaitEvent(s_cmp, ev_out[b], 0);
         EncArgs a = make_args(ctx, src_type, d_in[b], nr, ne0, ne0, d_im, im_len, rows_per_mat, row0 + r0, 1, d_out[b], rb);
-        int e = encode_view(ctx, type, a, s_cmp);
+        // sigma^2 of chunk k once its input landed (d_sig[b] is free: the
+        // chunk's H2D already waited for the encode of chunk k-2)
+        cudaEvent_t ready = ev_in[b];
+        if (pre_sig) {
+            cudaStreamWaitEvent(s_sig, ev_in[b], 0);
+            if (launch_row_sigma2(a.src, nr, d_sig[b], s_sig) != cudaSuccess) { fail(SHC_ECUDA); break; }
+            ctx->launches++;
+            cudaEventRecord(ev_sig[b], s_sig);
+            ready = ev_sig[b];
+            a.sigma2 = d_sig[b];
+        }
+        // encode chunk k once its input (and sigma^2) landed and d_out[b] was drained
+        cudaStreamWaitEvent(s_cmp, ready, 0);
+        cudaStreamWaitEvent(s_cmp, ev_out[b], 0);
+        int e = encode_view(ctx, type, a, s_cmp, enc_sms);
         if (e != SHC_OK) { fail(e); break; }
         cudaEventRecord(ev_cmp[b], s_cmp);
         // D2H of chunk k
@@ -549,9 +575,12 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
     cudaStreamWaitEvent(s_cmp, done, 0);
     cudaEventRecord(done, s_out);
     cudaStreamWaitEvent(s_cmp, done, 0);
+    cudaEventRecord(done, s_sig);
+    cudaStreamWaitEvent(s_cmp, done, 0);
     for (int b = 0; b < 2; b++) {
         if (d_in[b]) cudaFreeAsync(d_in[b], s_cmp);
         if (d_out[b]) cudaFreeAsync(d_out[b], s_cmp);
+        if (d_sig[b]) cudaFreeAsync(d_sig[b], s_cmp);
     }
     if (d_im) cudaFreeAsync(d_im, s_cmp);
     cudaEventRecord(done, s_cmp);
@@ -562,6 +591,7 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
         cudaEventDestroy(ev_in[b]);
         cudaEventDestroy(ev_cmp[b]);
         cudaEventDestroy(ev_out[b]);
+        cudaEventDestroy(ev_sig[b]);
     }
     if (rc == SHC_OK) {
         int st = shc_sync(ctx, s_cmp, timeout_ms);
