@@ -137,10 +137,10 @@ int main(int argc, char **argv) {
             uint64_t elems = 0;
             for (auto &t : sm->view.tensors) elems += t.n_elements();
             printf("{\"model\": \"%s\", \"gpus\": %d, \"exact_errors\": %s, \"uniform\": \"%s\", \"elements\": %llu, "
-                   "\"generate_s\": %.3f, \"measure_s\": %.3f, \"solve_s\": %.4f, \"encode_s\": %.3f, \"wall_s\": %.3f, "
-                   "\"plan_bytes\": %llu, \"budget_bytes\": %llu}\n",
+                   "\"generate_s\": %.3f, \"measure_s\": %.3f, \"solve_s\": %.4f, \"setup_s\": %.3f, "
+                   "\"encode_s\": %.3f, \"wall_s\": %.3f, \"plan_bytes\": %llu, \"budget_bytes\": %llu}\n",
                    synth_name.c_str(), pool.gpus(), a.exact_errors ? "true" : "false", a.uniform.c_str(),
-                   (unsigned long long)elems, gen_s, tm.measure_s, tm.solve_s, tm.encode_s, wall,
+                   (unsigned long long)elems, gen_s, tm.measure_s, tm.solve_s, tm.setup_s, tm.encode_s, wall,
                    (unsigned long long)plan.total_bytes, (unsigned long long)plan.budget.model_budget);
             return 0;
         }

@@ -281,6 +281,25 @@ void GpuPool::run(size_t n_jobs, const std::function<void(int, size_t)> &fn) {
     if (err) std::rethrow_exception(err);
 }
 
+void GpuPool::each(const std::function<void(int)> &fn) {
+    std::exception_ptr err;
+    std::mutex mu;
+    std::vector<std::thread> th;
+    for (int w = 0; w < size(); w++) {
+        th.emplace_back([&, w]() {
+            cudaSetDevice(workers_[(size_t)w]->dev);
+            try {
+                fn(w);
+            } catch (...) {
+                std::lock_guard<std::mutex> lk(mu);
+                if (!err) err = std::current_exception();
+            }
+        });
+    }
+    for (auto &t : th) t.join();
+    if (err) std::rethrow_exception(err);
+}
+
 // Bring rows of one tensor to the device as an f32/f16/bf16 view: a strided
 // host->device gather, then a device decode for block-quantized storage
 // (the reference decodes with quant.rs:581 decode_row before measuring).
@@ -587,7 +606,7 @@ uint32_t file_type_code(const std::vector<PlanEntry> &entries) {
 // ---------------------------------------------------------------------------
 void write_quantized(const std::string &out_path, const Plan &plan, const ModelView &m, const Imatrix &im,
                      GpuPool &pool, Timing &tm) {
-    const auto t0 = Clock::now();
+    const auto s0 = Clock::now();
     std::vector<TensorInfo> infos;
     for (auto &e : plan.entries) {
         const auto &t = m.tensors[e.tensor_idx];
@@ -623,6 +642,17 @@ void write_quantized(const std::string &out_path, const Plan &plan, const ModelV
         map = static_cast<uint8_t *>(mmap(nullptr, L.total, PROT_READ | PROT_WRITE, MAP_PRIVATE | MAP_ANONYMOUS, -1, 0));
         if (map == MAP_FAILED) throw Error("mapping the output");
         madvise(map, L.total, MADV_HUGEPAGE);
+        // faulted in up front by several threads (an in-memory consumer hands
+        // over a buffer it owns; the kernel's page zeroing is the cost)
+        const unsigned nt = std::max(1u, std::min(32u, std::thread::hardware_concurrency()));
+        std::vector<std::thread> th;
+        const uint64_t per = (L.total + nt - 1) / nt;
+        for (unsigned i = 0; i < nt; i++)
+            th.emplace_back([map, per, i, total = L.total]() {
+                const uint64_t a = per * i, b = std::min<uint64_t>(total, a + per);
+                for (uint64_t o = a; o < b; o += 4096) map[o] = 0;
+            });
+        for (auto &t : th) t.join();
     }
     auto put = [&](uint64_t off, const void *p, size_t n) {
         if (!to_file) {
@@ -638,9 +668,6 @@ void write_quantized(const std::string &out_path, const Plan &plan, const ModelV
             n -= (size_t)w;
         }
     };
-    const auto hdr = header_bytes(kvs, infos, m.alignment, L);
-    put(0, hdr.data(), hdr.size());
-
     struct Job {
         size_t e;
         uint64_t r0, r1;
@@ -654,10 +681,7 @@ void write_quantized(const std::string &out_path, const Plan &plan, const ModelV
         const auto &e = plan.entries[ei];
         const auto &t = m.tensors[e.tensor_idx];
         const uint64_t n_rows = t.n_rows(), ne0 = t.ne0(), rpm = rows_per_mat_of(t);
-        if (e.ty == t.ty) {  // copied untouched (main.rs:735-737)
-            put(L.data_start + L.offsets[ei], m.data(e.tensor_idx), t.byte_size());
-            continue;
-        }
+        if (e.ty == t.ty) continue;  // copied untouched, below
         const uint64_t rows_cap = std::max<uint64_t>(1, cap_elems / std::max<uint64_t>(ne0, 1));
         for (uint64_t r = 0; r < n_rows;) {
             uint64_t end = std::min(n_rows, r + rows_cap);
@@ -668,6 +692,38 @@ void write_quantized(const std::string &out_path, const Plan &plan, const ModelV
         }
     }
     std::stable_sort(jobs.begin(), jobs.end(), [](const Job &a, const Job &b) { return a.cost > b.cost; });
+    // Every worker's buffers sized once for the largest job: growing them
+    // inside the encode would cudaMalloc/cudaFree (device-wide
+    // synchronisations) and pin host pages mid-stream.
+    size_t need_raw = 16, need_f = 0, need_im = 16, need_out = 16;
+    for (const Job &jb : jobs) {
+        const auto &e = plan.entries[jb.e];
+        const auto &t = m.tensors[e.tensor_idx];
+        const uint64_t ne0 = t.ne0(), n = jb.r1 - jb.r0;
+        need_raw = std::max<size_t>(need_raw, (size_t)(n * row_bytes(t.ty, ne0) + 16));
+        if (!(t.ty == T_F32 || t.ty == T_F16 || t.ty == T_BF16))
+            need_f = std::max<size_t>(need_f, (size_t)(n * ne0 * 4 + 16));
+        need_im = std::max<size_t>(need_im, (size_t)(ne0 * 4));
+        need_out = std::max<size_t>(need_out, (size_t)(n * row_bytes(e.ty, ne0) + 16));
+    }
+    if (!jobs.empty())
+        pool.each([&](int w) {
+            auto &wk = pool.worker(w);
+            wk.d(0, need_raw);
+            if (need_f) wk.d(1, need_f);
+            wk.d(2, need_im);
+            wk.d(4, need_out);
+            wk.h(1, need_out);
+        });
+    tm.setup_s = secs_since(s0);
+    const auto t0 = Clock::now();
+    const auto hdr = header_bytes(kvs, infos, m.alignment, L);
+    put(0, hdr.data(), hdr.size());
+    for (size_t ei = 0; ei < plan.entries.size(); ei++) {  // tensors copied untouched (main.rs:735-737)
+        const auto &e = plan.entries[ei];
+        const auto &t = m.tensors[e.tensor_idx];
+        if (e.ty == t.ty) put(L.data_start + L.offsets[ei], m.data(e.tensor_idx), t.byte_size());
+    }
     pool.run(jobs.size(), [&](int w, size_t j) {
         auto &wk = pool.worker(w);
         const Job &jb = jobs[j];

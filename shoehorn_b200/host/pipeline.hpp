@@ -62,7 +62,10 @@ struct PlanEntry {
 };
 
 struct Timing {
-    double measure_s = 0, solve_s = 0, encode_s = 0;
+    // setup_s: the encode's buffer set-up (pinned staging and device buffers
+    // sized for the largest job on every worker, the in-memory output faulted
+    // in), kept out of encode_s
+    double measure_s = 0, solve_s = 0, encode_s = 0, setup_s = 0;
 };
 
 struct Plan {
@@ -96,6 +99,9 @@ class GpuPool {
     // Runs fn(worker, job) for jobs 0..n_jobs-1, pulled dynamically by the
     // workers in index order; rethrows the first failure.
     void run(size_t n_jobs, const std::function<void(int, size_t)> &fn);
+    // Runs fn(worker) once on every worker, each on its own thread with its
+    // device current; rethrows the first failure.
+    void each(const std::function<void(int)> &fn);
     struct Worker;
     Worker &worker(int w) { return *workers_[(size_t)w]; }
 
