@@ -107,6 +107,24 @@ def captured_traffic(type_name, in_bytes):
     return None
 
 
+def max_over_ranks(x, dev):
+    """The maximum of a per-rank float over all ranks (one all-reduce outside
+    any timed region); x itself when no process group is running."""
+    import torch
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return float(x)
+    tt = torch.tensor([float(x)], device=dev, dtype=torch.float64)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    return float(tt.item())
+
+
+def aggregate_gbs(world, n_types, in_bytes, seconds):
+    """Whole-job BF16 GB/s for weak scaling: every rank encodes its own copy of
+    the workload to every type, and the job takes the slowest rank's time."""
+    return world * n_types * in_bytes / seconds / 1e9
+
+
 def dist_env():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     return int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")), ws
@@ -292,11 +310,7 @@ def run_ours(args):
                     for k in range(args.steps)]
         per_type_ms[t] = statistics.median(steps_ms)
         per_type_min[t] = min(steps_ms)
-    step_ms = sum(per_type_ms.values())
-    if world > 1:
-        tt = torch.tensor([step_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        step_ms = float(tt.item())
+    step_ms = max_over_ranks(sum(per_type_ms.values()), dev)
 
     # end to end: host (pinned) buffers through the C-ABI host entry point
     htens = []
@@ -316,17 +330,13 @@ def run_ours(args):
             for src_h, im, outs_h in htens:
                 ctx.encode_tensor_host(TYPE_IDS[t], src_h, im, out=outs_h[t])
             e2e_t[t].append(time.perf_counter() - t0)
-    e2e_step = sum(statistics.median(v) for v in e2e_t.values())
-    if world > 1:
-        tt = torch.tensor([e2e_step], device=dev, dtype=torch.float64)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e_step = float(tt.item())
+    e2e_step = max_over_ranks(sum(statistics.median(v) for v in e2e_t.values()), dev)
     clocks = sampler.stop()
 
     in_bytes = sum(int(d[1].numel()) * 2 for d in dtens)
     elts = in_bytes // 2
-    value = world * len(types) * in_bytes / (step_ms * 1e-3) / 1e9
-    e2e_value = world * len(types) * in_bytes / e2e_step / 1e9
+    value = aggregate_gbs(world, len(types), in_bytes, step_ms * 1e-3)
+    e2e_value = aggregate_gbs(world, len(types), in_bytes, e2e_step)
     per_type = {t: round(in_bytes / (per_type_ms[t] * 1e-3) / 1e9, 3) for t in types}
 
     # roofline of the dominant kernel (largest share of the step)
