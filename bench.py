@@ -48,10 +48,11 @@ OUT_BYTES_PER_ELT = {"Q8_0": 34 / 32, "Q4_K": 144 / 256, "Q5_K": 176 / 256, "Q6_
 FLOPS_PER_ELT = {"Q4_K": 745.4, "Q5_K": 745.4, "Q6_K": 151.0, "Q8_0": 5.1,
                  "IQ2_XXS": 1839.0, "IQ2_XS": 3738.2, "IQ2_S": 713.8, "IQ3_XXS": 1498.4, "IQ3_S": 963.8,
                  "IQ4_NL": 274.7, "IQ4_XS": 274.7}
-# FP32 issue ceiling for separately rounded adds and multiplies on sm_100:
-# packed f32x2 add/mul retire 2 operations per lane per clock, 256 per SM
-# (shoehorn_b200/fp32-rate measures 251/clk/SM; scalar FADD/FMUL reach 122).
-FP32_OPS_PER_CLK_PER_SM = 256
+# FP32 ceiling for separately rounded adds and multiplies on sm_100: 128 per
+# clock per SM, scalar or packed f32x2 alike (shoehorn_b200/fp32-rate measures
+# 121-126 for add-only/mul-only chains); fused multiply-adds would reach 250
+# flops/clk/SM but are excluded by the parity contract.
+FP32_OPS_PER_CLK_PER_SM = 128
 
 
 IQ_TYPES = ["IQ2_XXS", "IQ2_XS", "IQ2_S", "IQ3_XXS", "IQ3_S", "IQ4_NL", "IQ4_XS"]
@@ -354,13 +355,13 @@ def run_ours(args):
     else:
         alg = elts * FLOPS_PER_ELT[dom]
         # no multiply-add contraction is allowed (parity), so the ceiling is
-        # separate f32 adds/multiplies at the packed f32x2 rate
+        # separate f32 adds/multiplies
         peak = props.multi_processor_count * FP32_OPS_PER_CLK_PER_SM * sm_mhz * 1e6 / 1e12
         roof = {"bound": "fp32", "achieved": round(alg / (per_type_ms[dom] * 1e-3) / 1e12, 3),
                 "peak": round(peak, 3), "unit": "TFLOP/s",
-                "peak_source": f"{props.multi_processor_count} SMs x {FP32_OPS_PER_CLK_PER_SM} f32 add/mul per clock "
-                               f"(packed f32x2; 251 measured by fp32-rate) x median SM clock {sm_mhz:.0f} MHz "
-                               "(MEASURED_PEAKS.json has no FP32 figure)",
+                "peak_source": f"{props.multi_processor_count} SMs x {FP32_OPS_PER_CLK_PER_SM} separate f32 add/mul "
+                               f"per clock (no FMA by the parity contract; 121-126 measured by fp32-rate) x median "
+                               f"SM clock {sm_mhz:.0f} MHz (MEASURED_PEAKS.json has no FP32 figure)",
                 "flops_per_elt": FLOPS_PER_ELT[dom], "flops_source": "oracle op-count build, as-written algorithm"}
     roof["frac"] = round(roof["achieved"] / roof["peak"], 4)
     roof["kernel"] = f"{dom} encoder"

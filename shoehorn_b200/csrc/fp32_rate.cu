@@ -2,11 +2,13 @@
 //
 // The encoders may not contract multiply-adds (their results must equal the
 // reference's separately rounded f32 operations), so their ceiling is the
-// rate of separate adds and multiplies: scalar FADD/FMUL, or packed f32x2
-// add/mul (two f32 operations per lane per instruction).  This program times
-// long independent chains of each form, plus the rounding and min/max forms
-// the encoders use, and prints operations per clock per SM at the device's
-// reported maximum clock.  Every kernel touches only registers and writes
+// rate of separate adds and multiplies, scalar or packed f32x2 (two f32
+// operations per lane per instruction, issued at half the scalar rate).  This
+// program times long independent chains of each form, a fused multiply-add
+// for comparison, and the rounding and min/max forms the encoders use, and
+// prints f32 operations per clock per SM at the device's reported maximum
+// clock.  Packed chains are add-only or multiply-only: a packed multiply
+// feeding a packed add can be contracted into FFMA2 by code generation.  Every kernel touches only registers and writes
 // one float per thread.
 #include <cstdio>
 #include <cuda_runtime.h>
@@ -26,15 +28,40 @@ __global__ void scalar_mul_add(float *out, float a, float b) {
     out[blockIdx.x * blockDim.x + threadIdx.x] = s;
 }
 
-__global__ void packed_mul_add(float *out, float a, float b) {
+// Add-only and multiply-only chains: nothing for the compiler to contract.
+__global__ void packed_add(float *out, float a, float) {
     float2 x[kChains];
     for (int i = 0; i < kChains; i++) x[i] = make_float2(threadIdx.x * 1e-3f + i, i * 0.5f);
-    const float2 A = make_float2(a, a), B = make_float2(b, b);
+    const float2 A = make_float2(a, a);
     for (int it = 0; it < kIters; it++)
 #pragma unroll
-        for (int i = 0; i < kChains; i++) x[i] = __fadd2_rn(__fmul2_rn(x[i], A), B);
+        for (int i = 0; i < kChains; i++) x[i] = __fadd2_rn(x[i], A);
     float s = 0.0f;
     for (int i = 0; i < kChains; i++) s += x[i].x + x[i].y;
+    out[blockIdx.x * blockDim.x + threadIdx.x] = s;
+}
+
+__global__ void packed_mul(float *out, float a, float) {
+    float2 x[kChains];
+    for (int i = 0; i < kChains; i++) x[i] = make_float2(threadIdx.x * 1e-3f + i, i * 0.5f);
+    const float2 A = make_float2(a, a);
+    for (int it = 0; it < kIters; it++)
+#pragma unroll
+        for (int i = 0; i < kChains; i++) x[i] = __fmul2_rn(x[i], A);
+    float s = 0.0f;
+    for (int i = 0; i < kChains; i++) s += x[i].x + x[i].y;
+    out[blockIdx.x * blockDim.x + threadIdx.x] = s;
+}
+
+// Fused multiply-add, for reference: the encoders may not use it.
+__global__ void scalar_fma(float *out, float a, float b) {
+    float x[kChains];
+    for (int i = 0; i < kChains; i++) x[i] = threadIdx.x * 1e-3f + i;
+    for (int it = 0; it < kIters; it++)
+#pragma unroll
+        for (int i = 0; i < kChains; i++) x[i] = __fmaf_rn(x[i], a, b);
+    float s = 0.0f;
+    for (int i = 0; i < kChains; i++) s += x[i];
     out[blockIdx.x * blockDim.x + threadIdx.x] = s;
 }
 
@@ -90,7 +117,9 @@ int main() {
         void (*fn)(float *, float, float);
         int ops;  // f32 operations per chain step (counted as the encoders' op counter does)
     } probes[] = {{"scalar mul + add", scalar_mul_add, 2},
-                  {"packed f32x2 mul + add", packed_mul_add, 4},
+                  {"packed f32x2 add", packed_add, 2},
+                  {"packed f32x2 mul", packed_mul, 2},
+                  {"scalar fma (2 flops)", scalar_fma, 2},
                   {"mul + roundf", mul_roundf, 2},
                   {"mul + 3-add exact rounding", mul_add_rounding, 2},
                   {"fmaxf + fminf", min_max, 2}};
