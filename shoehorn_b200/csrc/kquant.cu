@@ -181,7 +181,7 @@ __global__ void __launch_bounds__(256) enc_q8_0_kernel(EncArgs a) {
 // 16-element sub-block.  Two lanes per sub-block split the 19 candidate
 // grids; the selection chain is replayed serially from shared memory.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) enc_q6_k_kernel(EncArgs a) {
+__global__ void __launch_bounds__(256, 3) enc_q6_k_kernel(EncArgs a) {
     __shared__ float s_x[8][16 * 17];
     __shared__ float s_w[8][16 * 17];
     __shared__ float2 s_cand[8][16][20];
@@ -235,11 +235,21 @@ __global__ void __launch_bounds__(256) enc_q6_k_kernel(EncArgs a) {
                 const float iscale = -(32.0f + 0.1f * (float)is) / mx;
                 float sumlx = 0.0f, suml2 = 0.0f;
                 if (finite) {
+                    // element pairs in packed f32x2: the products feed the
+                    // rounding's round-toward-zero add or the scalar sums only
+                    const float2 is2 = make_float2(iscale, iscale);
 #pragma unroll
-                    for (int i = 0; i < 16; i++) {
-                        const float l = fminf(fmaxf(round_away_small(iscale * x[i]), -32.0f), 31.0f);
-                        sumlx += wx[i] * l;
-                        suml2 += w[i] * (l * l);
+                    for (int i = 0; i < 16; i += 2) {
+                        const float2 y = __fmul2_rn(is2, make_float2(x[i], x[i + 1]));
+                        const float2 r = floor_half_up2(make_float2(fabsf(y.x), fabsf(y.y)));
+                        const float2 l = make_float2(fminf(fmaxf(copysignf(r.x, y.x), -32.0f), 31.0f),
+                                                     fminf(fmaxf(copysignf(r.y, y.y), -32.0f), 31.0f));
+                        const float2 lx = __fmul2_rn(make_float2(wx[i], wx[i + 1]), l);
+                        const float2 l2 = __fmul2_rn(make_float2(w[i], w[i + 1]), __fmul2_rn(l, l));
+                        sumlx = __fadd_rn(sumlx, lx.x);
+                        suml2 = __fadd_rn(suml2, l2.x);
+                        sumlx = __fadd_rn(sumlx, lx.y);
+                        suml2 = __fadd_rn(suml2, l2.y);
                     }
                 } else {
 #pragma unroll
