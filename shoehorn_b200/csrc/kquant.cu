@@ -33,15 +33,44 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
+// Squares of the 8 elements in one 16-byte chunk (4 for F32), folded into s
+// in element order; the products are packed, the adds stay serial.
+template <int SRC>
+__device__ __forceinline__ void sigma_fold(const uint4 q, float &s) {
+    const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
+    if (SRC == SHC_SRC_F32) {
+        const float2 p0 = __fmul2_rn(make_float2(__uint_as_float(wv[0]), __uint_as_float(wv[1])),
+                                     make_float2(__uint_as_float(wv[0]), __uint_as_float(wv[1])));
+        const float2 p1 = __fmul2_rn(make_float2(__uint_as_float(wv[2]), __uint_as_float(wv[3])),
+                                     make_float2(__uint_as_float(wv[2]), __uint_as_float(wv[3])));
+        s = __fadd_rn(s, p0.x);
+        s = __fadd_rn(s, p0.y);
+        s = __fadd_rn(s, p1.x);
+        s = __fadd_rn(s, p1.y);
+    } else {
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            float2 v;
+            if (SRC == SHC_SRC_BF16) v = make_float2(__uint_as_float(wv[k] << 16), __uint_as_float(wv[k] & 0xFFFF0000u));
+            else v = make_float2(f16_val((uint16_t)(wv[k] & 0xFFFF)), f16_val((uint16_t)(wv[k] >> 16)));
+            const float2 p = __fmul2_rn(v, v);
+            s = __fadd_rn(s, p.x);
+            s = __fadd_rn(s, p.y);
+        }
+    }
+}
+
+template <int SRC>
 __global__ void __launch_bounds__(32) row_sigma2_kernel(RowSrc src, int64_t n_rows, float *out) {
     __shared__ __align__(16) uint4 ring[kSigStages][256];
     const int lane = threadIdx.x;
     const int64_t rbase = (int64_t)blockIdx.x * 32;
     const int64_t ne0 = src.ne0;
-    const int esz = src.src_type == SHC_SRC_F32 ? 4 : 2;
-    const int per_chunk = 16 / esz;            // elements per 16-byte chunk
-    const int64_t tile_cols = 8 * per_chunk;   // 128 bytes of every row per tile
+    constexpr int esz = SRC == SHC_SRC_F32 ? 4 : 2;
+    constexpr int per_chunk = 16 / esz;            // elements per 16-byte chunk
+    constexpr int64_t tile_cols = 8 * per_chunk;   // 128 bytes of every row per tile
     const int64_t ntiles = (ne0 + tile_cols - 1) / tile_cols;
+    const int64_t full_tiles = ne0 / tile_cols;
     const char *base = static_cast<const char *>(src.ptr);
     const int64_t row_bytes = src.row_stride * esz;
     auto issue = [&](int64_t t) {
@@ -66,33 +95,13 @@ __global__ void __launch_bounds__(32) row_sigma2_kernel(RowSrc src, int64_t n_ro
         cp_async_wait<kSigStages - 1>();
         __syncwarp();
         const uint4 *slot = ring[t % kSigStages];
-        const int64_t c0 = t * tile_cols;
-        const int nchunks = (int)((ne0 - c0 >= tile_cols) ? 8 : (ne0 - c0 + per_chunk - 1) / per_chunk);
         if (mine) {
-            for (int j = 0; j < nchunks; j++) {
-                const uint4 q = slot[j * 32 + lane];
-                const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
-                if (src.src_type == SHC_SRC_F32) {
+            if (t < full_tiles) {
 #pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        const float x = __uint_as_float(wv[k]);
-                        s += x * x;
-                    }
-                } else if (src.src_type == SHC_SRC_BF16) {
-#pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        const float x0 = __uint_as_float(wv[k] << 16), x1 = __uint_as_float(wv[k] & 0xFFFF0000u);
-                        s += x0 * x0;
-                        s += x1 * x1;
-                    }
-                } else {
-#pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        const float x0 = f16_val((uint16_t)(wv[k] & 0xFFFF)), x1 = f16_val((uint16_t)(wv[k] >> 16));
-                        s += x0 * x0;
-                        s += x1 * x1;
-                    }
-                }
+                for (int j = 0; j < 8; j++) sigma_fold<SRC>(slot[j * 32 + lane], s);
+            } else {  // the row's ragged end: whole chunks only (ne0 is a multiple of 8)
+                const int nchunks = (int)((ne0 - t * tile_cols + per_chunk - 1) / per_chunk);
+                for (int j = 0; j < nchunks; j++) sigma_fold<SRC>(slot[j * 32 + lane], s);
             }
         }
         __syncwarp();
@@ -104,7 +113,9 @@ __global__ void __launch_bounds__(32) row_sigma2_kernel(RowSrc src, int64_t n_ro
 cudaError_t launch_row_sigma2(const RowSrc &src, int64_t n_rows, float *out, cudaStream_t st) {
     if (n_rows <= 0) return cudaSuccess;
     const int64_t blocks = (n_rows + 31) / 32;
-    row_sigma2_kernel<<<(unsigned)blocks, 32, 0, st>>>(src, n_rows, out);
+    if (src.src_type == SHC_SRC_BF16) row_sigma2_kernel<SHC_SRC_BF16><<<(unsigned)blocks, 32, 0, st>>>(src, n_rows, out);
+    else if (src.src_type == SHC_SRC_F16) row_sigma2_kernel<SHC_SRC_F16><<<(unsigned)blocks, 32, 0, st>>>(src, n_rows, out);
+    else row_sigma2_kernel<SHC_SRC_F32><<<(unsigned)blocks, 32, 0, st>>>(src, n_rows, out);
     return cudaGetLastError();
 }
 
