@@ -27,18 +27,33 @@ __device__ const float d_kv_f[16] = {-127.f, -104.f, -83.f, -65.f, -49.f, -35.f,
 // (v0, v15) the binary search ends at the unique mu with v[mu-1] <= x < v[mu];
 // the codebook values are integers, so v[k] <= x <=> v[k] <= floor(x) and
 // mu = 1 + cnt[floor(x)], with cnt[f] = #{k in 1..14 : v[k] <= f}.
+// Outside, clamping x to [-128, 127] keeps the answer: for x <= -127 the
+// pair (v0, v1) picks v0, for x >= 113 the pair (v14, v15) picks v15, and
+// fminf before fmaxf sends NaN to 127, hence v15, where the reference's
+// search ends for NaN.  floor() of the clamped value is read from the
+// mantissa of RD(x + 1.5*2^23): no conversion instruction.
 struct Iq4Lut {
     float v[16];
-    uint8_t cnt[256];  // indexed by floor(x) + 128
+    float2 pair[256];  // (v[mu-1], v[mu]) by floor(x) + 128
+    uint8_t cnt[256];  // mu - 1 by floor(x) + 128
 };
 
+__device__ __forceinline__ float iq4_clamp(float x) { return fmaxf(fminf(x, 127.0f), -128.0f); }
+__device__ __forceinline__ int iq4_slot(float xc) {  // floor(xc) + 128 for xc in [-128, 127]
+    return (int)__float_as_uint(__fadd_rd(xc, 12582912.0f)) - 0x4B400000 + 128;
+}
 __device__ __forceinline__ int best_index_iq4(const Iq4Lut &L, float x) {
-    if (x <= -127.0f) return 0;
-    if (x >= 113.0f) return 15;
-    if (x != x) return 15;  // the reference's search walks to the top for NaN
-    const int f = (int)floorf(x);
-    const int mu = 1 + L.cnt[f + 128];
-    return (x - L.v[mu - 1] < L.v[mu] - x) ? mu - 1 : mu;
+    const float xc = iq4_clamp(x);
+    const int f = iq4_slot(xc);
+    const float2 p = L.pair[f];
+    const int mu = 1 + L.cnt[f];
+    return (xc - p.x < p.y - xc) ? mu - 1 : mu;
+}
+// The codebook value best_index_iq4 selects.
+__device__ __forceinline__ float best_value_iq4(const Iq4Lut &L, float x) {
+    const float xc = iq4_clamp(x);
+    const float2 p = L.pair[iq4_slot(xc)];
+    return (xc - p.x < p.y - xc) ? p.x : p.y;
 }
 
 __device__ void init_iq4_lut(Iq4Lut &L) {
@@ -47,6 +62,7 @@ __device__ void init_iq4_lut(Iq4Lut &L) {
         int c = 0;
         for (int k = 1; k <= 14; k++) c += (d_kv_f[k] <= (float)(f - 128)) ? 1 : 0;
         L.cnt[f] = (uint8_t)c;
+        L.pair[f] = make_float2(d_kv_f[c], d_kv_f[c + 1]);
     }
 }
 
@@ -135,11 +151,17 @@ __global__ void __launch_bounds__(256) enc_iq4_kernel(EncArgs a) {
                 const float id = j == 0 ? 1.0f / (-mx / -127.0f) : ((float)(j - 8) + -127.0f) / mx;
                 float sumqx = 0.0f, sumq2 = 0.0f;
 #pragma unroll
-                for (int i = 0; i < 32; i++) {
-                    const float qv = lut.v[best_index_iq4(lut, id * x[i])];
-                    const float wq = w[i] * qv;
-                    sumqx += wq * x[i];
-                    sumq2 += wq * qv;
+                for (int i = 0; i < 32; i += 2) {  // element pairs; products feed scalar sums only
+                    const float2 xi = make_float2(x[i], x[i + 1]);
+                    const float2 y = __fmul2_rn(make_float2(id, id), xi);
+                    const float2 qv = make_float2(best_value_iq4(lut, y.x), best_value_iq4(lut, y.y));
+                    const float2 wq = __fmul2_rn(make_float2(w[i], w[i + 1]), qv);
+                    const float2 sx = __fmul2_rn(wq, xi);
+                    const float2 s2 = __fmul2_rn(wq, qv);
+                    sumqx = __fadd_rn(sumqx, sx.x);
+                    sumq2 = __fadd_rn(sumq2, s2.x);
+                    sumqx = __fadd_rn(sumqx, sx.y);
+                    sumq2 = __fadd_rn(sumq2, s2.y);
                 }
                 s_res[wid][b][j] = make_float2(sumqx, sumq2);
             }
