@@ -600,28 +600,34 @@ __device__ __noinline__ void search_tasks(IqWarpSmem<V> &S, int T, const void *l
                 if (S.pre[mid + 1] > k0) hi = mid;
                 else t = mid + 1;
             }
-            int k = k0;
-            for (;;) {
-                const int start = S.pre[t], end = min(S.pre[t + 1], k1), base = S.rbase[t];
-                const float *tb = S.tab + t * TS;
-                uint32_t bh = 0xFFFFFFFFu, bl = 0xFFFFFFFFu;
-                for (; k < end; k++) {
-                    const uint32_t cc = entry(base, k - start);
-                    float d2 = 0.0f;
-#pragma unroll
-                    for (int i = 0; i < G; i++) d2 += tb[i * KM + ((cc >> (C::BITS * i)) & MASK)];
-                    const uint32_t kh = __float_as_uint(d2);
-                    if (d2 < FLT_MAX && kh < bh) {  // positions rise within the lane: strict keeps the first
-                        bh = kh;
-                        bl = (uint32_t)(k - start);
-                    }
+            // one candidate per iteration for every lane (the ranges differ in
+            // length by at most one); a list boundary is a short branch
+            int start = S.pre[t], end = S.pre[t + 1], base = S.rbase[t];
+            const float *tb = S.tab + t * TS;
+            uint32_t bh = 0xFFFFFFFFu, bl = 0xFFFFFFFFu;
+            for (int k = k0; k < k1; k++) {
+                if (k == end) {  // this lane's part of slot t is done: merge, move to the next nonempty slot
+                    if (bh != 0xFFFFFFFFu) atomicMin(&S.rkey[t], ((unsigned long long)bh << 32) | bl);
+                    bh = bl = 0xFFFFFFFFu;
+                    do {
+                        t++;
+                    } while (S.pre[t + 1] <= k);
+                    start = S.pre[t];
+                    end = S.pre[t + 1];
+                    base = S.rbase[t];
+                    tb = S.tab + t * TS;
                 }
-                if (bh != 0xFFFFFFFFu) atomicMin(&S.rkey[t], ((unsigned long long)bh << 32) | bl);
-                if (k >= k1) break;
-                do {
-                    t++;
-                } while (S.pre[t + 1] <= k);
+                const uint32_t cc = entry(base, k - start);
+                float d2 = 0.0f;
+#pragma unroll
+                for (int i = 0; i < G; i++) d2 += tb[i * KM + ((cc >> (C::BITS * i)) & MASK)];
+                const uint32_t kh = __float_as_uint(d2);
+                if (d2 < FLT_MAX && kh < bh) {  // positions rise within the lane: strict keeps the first
+                    bh = kh;
+                    bl = (uint32_t)(k - start);
+                }
             }
+            if (bh != 0xFFFFFFFFu) atomicMin(&S.rkey[t], ((unsigned long long)bh << 32) | bl);
         }
         __syncwarp();
         if (q < T) {
