@@ -358,7 +358,7 @@ __global__ void __launch_bounds__(256, 3) enc_q6_k_kernel(EncArgs a) {
 // finite, so y = iscale*(x - vmin) is >= 0 or +inf and the clamp at 0 is not
 // needed.
 template <bool CLEAN, int NG>
-__device__ __forceinline__ void qkx3_grids(const float *snx, const float *sw, float vmin, const float (&iscale)[NG],
+__device__ __forceinline__ void qkx3_grids(const float *snx, const float *sw, const float *su, const float (&iscale)[NG],
                                            float fn, float2 (&l)[NG][16], float (&sl)[NG], float (&sl2)[NG],
                                            float (&sxl)[NG]) {
     float2 nis[NG];
@@ -375,7 +375,8 @@ __device__ __forceinline__ void qkx3_grids(const float *snx, const float *sw, fl
         const float4 w4 = reinterpret_cast<const float4 *>(sw)[i >> 1];
         const float2 nxi = (i & 1) ? make_float2(n4.z, n4.w) : make_float2(n4.x, n4.y);
         const float2 wi = (i & 1) ? make_float2(w4.z, w4.w) : make_float2(w4.x, w4.y);
-        const float2 ui = __fadd2_rn(nxi, make_float2(vmin, vmin));  // -(x - vmin)
+        const float4 u4 = reinterpret_cast<const float4 *>(su)[i >> 1];
+        const float2 ui = (i & 1) ? make_float2(u4.z, u4.w) : make_float2(u4.x, u4.y);  // -(x - vmin)
 #pragma unroll
         for (int g = 0; g < NG; g++) {
             const float2 r = floor_half_up2(__fmul2_rn(nis[g], ui));  // the first add is RZ
@@ -435,6 +436,7 @@ __global__ void __launch_bounds__(256, 2) enc_qk45_kernel(EncArgs a) {
     // 16-byte reads of one instruction fall in distinct bank groups
     __shared__ __align__(16) float s_nx[8][8 * 36];
     __shared__ __align__(16) float s_w[8][8 * 36];
+    __shared__ __align__(16) float s_u[8][8 * 36];
     __shared__ __align__(16) uint8_t s_out[8][BB];
     __shared__ uint8_t s_l[8][256];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -442,6 +444,7 @@ __global__ void __launch_bounds__(256, 2) enc_qk45_kernel(EncArgs a) {
     const int64_t ne0 = a.src.ne0, nsb = ne0 >> 8, total = a.n_rows * nsb;
     float *snx = &s_nx[wid][s * 36];
     float *sw = &s_w[wid][s * 36];
+    float *su = &s_u[wid][s * 36];
     for (int64_t g = (int64_t)blockIdx.x * 8 + wid; g < total; g += (int64_t)gridDim.x * 8) {
         const int64_t row = g / nsb;
         const int64_t sbi = g - row * nsb;
@@ -484,6 +487,14 @@ __global__ void __launch_bounds__(256, 2) enc_qk45_kernel(EncArgs a) {
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
             vmin = fminf(fminf(INFINITY, mn), 0.0f);
             vmax = fmaxf(-INFINITY, mx);
+        }
+        // u = nx + vmin = -(x - vmin): the same rounded value for every grid
+        {
+            float4 *pu = reinterpret_cast<float4 *>(su + q * 8);
+            pu[0] = make_float4(__fadd_rn(-v[0], vmin), __fadd_rn(-v[1], vmin), __fadd_rn(-v[2], vmin),
+                                __fadd_rn(-v[3], vmin));
+            pu[1] = make_float4(__fadd_rn(-v[4], vmin), __fadd_rn(-v[5], vmin), __fadd_rn(-v[6], vmin),
+                                __fadd_rn(-v[7], vmin));
         }
         __syncwarp();
         // Shuffles below run on every lane, so the per-lane candidate loop
@@ -530,8 +541,8 @@ __global__ void __launch_bounds__(256, 2) enc_qk45_kernel(EncArgs a) {
                 bool clean = range_finite;
 #pragma unroll
                 for (int g = 0; g < NG; g++) clean = clean && isc[g] < INFINITY;
-                if (clean) qkx3_grids<true, NG>(snx, sw, vmin, isc, FN, l, sl, sl2, sxl);
-                else qkx3_grids<false, NG>(snx, sw, vmin, isc, FN, l, sl, sl2, sxl);
+                if (clean) qkx3_grids<true, NG>(snx, sw, su, isc, FN, l, sl, sl2, sxl);
+                else qkx3_grids<false, NG>(snx, sw, su, isc, FN, l, sl, sl2, sxl);
                 float ts[NG], tm[NG];
                 bool valid[NG];
 #pragma unroll
