@@ -32,9 +32,9 @@ N_ROWS, NE0 = 4096, 14336
 SEED = 20261201
 SWEEP = ["Q4_K", "Q5_K", "Q6_K", "Q8_0"]
 METRIC = "BF16 GB/s encoded per quant type"
-TYPE_IDS = {"Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "IQ2_XXS": 16, "IQ2_XS": 17, "IQ3_XXS": 18,
+TYPE_IDS = {"Q8_0": 8, "Q2_K": 10, "Q3_K": 11, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "IQ2_XXS": 16, "IQ2_XS": 17, "IQ3_XXS": 18,
             "IQ4_NL": 20, "IQ3_S": 21, "IQ2_S": 22, "IQ4_XS": 23}
-OUT_BYTES_PER_ELT = {"Q8_0": 34 / 32, "Q4_K": 144 / 256, "Q5_K": 176 / 256, "Q6_K": 210 / 256,
+OUT_BYTES_PER_ELT = {"Q8_0": 34 / 32, "Q2_K": 84 / 256, "Q3_K": 110 / 256, "Q4_K": 144 / 256, "Q5_K": 176 / 256, "Q6_K": 210 / 256,
                      "IQ2_XXS": 66 / 256, "IQ2_XS": 74 / 256, "IQ2_S": 82 / 256, "IQ3_XXS": 98 / 256,
                      "IQ3_S": 110 / 256, "IQ4_NL": 18 / 32, "IQ4_XS": 136 / 256}
 # Algorithmic f32 operations per input element of the reference encoders,
@@ -45,7 +45,7 @@ OUT_BYTES_PER_ELT = {"Q8_0": 34 / 32, "Q4_K": 144 / 256, "Q5_K": 176 / 256, "Q6_
 # included.  The kernels execute fewer operations than this (loop invariants
 # hoisted, products shared), so the figure is the work done, not the
 # instructions issued.
-FLOPS_PER_ELT = {"Q4_K": 745.4, "Q5_K": 745.4, "Q6_K": 151.0, "Q8_0": 5.1,
+FLOPS_PER_ELT = {"Q4_K": 745.4, "Q5_K": 745.4, "Q6_K": 151.0, "Q8_0": 5.1, "Q2_K": 768.8, "Q3_K": 152.1,
                  "IQ2_XXS": 1839.0, "IQ2_XS": 3738.2, "IQ2_S": 713.8, "IQ3_XXS": 1498.4, "IQ3_S": 963.8,
                  "IQ4_NL": 274.7, "IQ4_XS": 274.7}
 # FP32 ceiling for separately rounded adds and multiplies on sm_100: 128 per

@@ -48,6 +48,11 @@ extern "C" {
 #define SHC_TYPE_Q5_0 6u
 #define SHC_TYPE_Q5_1 7u
 #define SHC_TYPE_Q8_0 8u
+/* Q2_K and Q3_K have no encoder in the reference (its GgmlType stops at the
+ * types above); blocks follow ggml's block_q2_K (84 bytes) and block_q3_K
+ * (110 bytes) layouts with the reference's K-quant search routines. */
+#define SHC_TYPE_Q2_K 10u
+#define SHC_TYPE_Q3_K 11u
 #define SHC_TYPE_Q4_K 12u
 #define SHC_TYPE_Q5_K 13u
 #define SHC_TYPE_Q6_K 14u

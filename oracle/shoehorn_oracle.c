@@ -46,7 +46,7 @@
 /* ---------------- ggml type ids (gguf.rs:36-83) ---------------- */
 enum {
     T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8,
-    T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_IQ2_XXS = 16, T_IQ2_XS = 17, T_IQ3_XXS = 18,
+    T_Q2_K = 10, T_Q3_K = 11, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_IQ2_XXS = 16, T_IQ2_XS = 17, T_IQ3_XXS = 18,
     T_IQ4_NL = 20, T_IQ3_S = 21, T_IQ2_S = 22, T_IQ4_XS = 23, T_BF16 = 30
 };
 
@@ -74,6 +74,8 @@ static int block_layout(uint32_t t, int64_t *bs, int64_t *tb) {
     case T_Q5_0: *bs = 32; *tb = 22; return 1;
     case T_Q5_1: *bs = 32; *tb = 24; return 1;
     case T_Q8_0: *bs = 32; *tb = 34; return 1;
+    case T_Q2_K: *bs = 256; *tb = 84; return 1;
+    case T_Q3_K: *bs = 256; *tb = 110; return 1;
     case T_Q4_K: *bs = 256; *tb = 144; return 1;
     case T_Q5_K: *bs = 256; *tb = 176; return 1;
     case T_Q6_K: *bs = 256; *tb = 210; return 1;
@@ -523,6 +525,91 @@ static void enc_qk45(const float *x, int64_t n, const float *im, float sigma2, i
     }
 }
 
+/* Q2_K and Q3_K.  The reference has no encoder for either type
+ * (gguf.rs:13-34 lists no Q2_K/Q3_K), so these restate its own K-quant
+ * recipes at 16-element sub-blocks, in the ggml block layouts that gguf-py
+ * 0.19.0 decodes:
+ *   Q2_K = enc_qk45 with make_qkx3_quants(n 16, nmax 3) and 4-bit scale/min
+ *          codes (max/15), bytes scales[16] (scale | min << 4), qs[64], d, dmin;
+ *   Q3_K = enc_q6_k with make_qx_quants(n 16, nmax 4) and 6-bit signed scale
+ *          codes (iscale = -32/max), bytes hmask[32], qs[64], scales[12], d.
+ * Element e of a super-block: qs byte (e/128)*32 + e%32 at bit 2*((e%128)/32);
+ * Q3_K's high bit in hmask byte e%32, bit e/32. */
+static void enc_q2_k(const float *x, int64_t n, const float *im, float sigma2, uint8_t *out) {
+    uint8_t l_all[256];
+    float w[16];
+    for (int64_t bi = 0; bi < n / 256; bi++) {
+        const float *blk = x + 256 * bi;
+        uint8_t *o = out + 84 * bi;
+        float scales[16], mins[16];
+        for (int sb = 0; sb < 16; sb++) {
+            const float *xs = blk + sb * 16;
+            element_weights(xs, 16, im ? im + bi * 256 + sb * 16 : NULL, sigma2, w);
+            uint8_t ls[16];
+            float sc, mn;
+            make_qkx3_quants(xs, 16, 3, w, ls, -0.9f, 0.05f, 36, &sc, &mn);
+            scales[sb] = sc;
+            mins[sb] = -mn;
+        }
+        float max_scale = 0.0f, max_min = 0.0f;
+        for (int sb = 0; sb < 16; sb++) max_scale = rmaxf(max_scale, scales[sb]);
+        for (int sb = 0; sb < 16; sb++) max_min = rmaxf(max_min, mins[sb]);
+        float inv_scale = max_scale > 0.0f ? 15.0f / max_scale : 0.0f;
+        float inv_min = max_min > 0.0f ? 15.0f / max_min : 0.0f;
+        float d = max_scale / 15.0f;
+        float dmin = max_min / 15.0f;
+        memset(o, 0, 84);
+        for (int sb = 0; sb < 16; sb++) {
+            int32_t lsq = clampi(nearest_int(inv_scale * scales[sb]), 0, 15);
+            int32_t lmq = clampi(nearest_int(inv_min * mins[sb]), 0, 15);
+            o[sb] = (uint8_t)(lsq | (lmq << 4));
+            float dsub = d * (float)lsq;
+            float msub = dmin * (float)lmq;
+            for (int j = 0; j < 16; j++)
+                l_all[sb * 16 + j] = dsub == 0.0f ? 0 : (uint8_t)clampi(nearest_int((blk[sb * 16 + j] + msub) / dsub), 0, 3);
+        }
+        for (int e = 0; e < 256; e++) o[16 + (e / 128) * 32 + e % 32] |= (uint8_t)(l_all[e] << (2 * ((e % 128) / 32)));
+        put_f16(o + 80, d);
+        put_f16(o + 82, dmin);
+    }
+}
+static void enc_q3_k(const float *x, int64_t n, const float *im, float sigma2, uint8_t *out) {
+    uint8_t l_all[256];
+    float w[16];
+    for (int64_t bi = 0; bi < n / 256; bi++) {
+        const float *blk = x + 256 * bi;
+        uint8_t *o = out + 110 * bi;
+        float scales[16];
+        float max_abs_scale = 0.0f, max_scale = 0.0f;
+        for (int sb = 0; sb < 16; sb++) {
+            const float *xs = blk + sb * 16;
+            element_weights(xs, 16, im ? im + bi * 256 + sb * 16 : NULL, sigma2, w);
+            uint8_t ls[16];
+            float sc = make_qx_quants(xs, 16, 4, w, ls);
+            scales[sb] = sc;
+            if (fabsf(sc) > max_abs_scale) { max_abs_scale = fabsf(sc); max_scale = sc; }
+        }
+        memset(o, 0, 110);
+        if (max_abs_scale < GROUP_MAX_EPS) continue;
+        float iscale = -32.0f / max_scale;
+        float d = 1.0f / iscale;
+        for (int sb = 0; sb < 16; sb++) {
+            int32_t q = clampi(nearest_int(iscale * scales[sb]), -32, 31);
+            uint32_t u = (uint32_t)(q + 32);
+            o[96 + sb % 8] |= (uint8_t)((u & 0xF) << (4 * (sb / 8)));
+            o[96 + 8 + sb % 4] |= (uint8_t)((u >> 4) << (2 * (sb / 4)));
+            float dd = d * (float)q;
+            for (int j = 0; j < 16; j++)
+                l_all[sb * 16 + j] = dd == 0.0f ? 4 : (uint8_t)(clampi(nearest_int(blk[sb * 16 + j] / dd), -4, 3) + 4);
+        }
+        for (int e = 0; e < 256; e++) {
+            o[32 + (e / 128) * 32 + e % 32] |= (uint8_t)((l_all[e] & 3) << (2 * ((e % 128) / 32)));
+            if (l_all[e] & 4) o[e % 32] |= (uint8_t)(1u << (e / 32));
+        }
+        put_f16(o + 108, d);
+    }
+}
+
 /* ---------------- quant.rs decoders ---------------- */
 
 static void dec_q8_0(const uint8_t *data, int64_t n, float *out) {
@@ -606,6 +693,30 @@ static void dec_q6_k(const uint8_t *data, int64_t n, float *out) {
                 y[o + l + 64] = d * (float)sc[is + 4] * (float)q3;
                 y[o + l + 96] = d * (float)sc[is + 6] * (float)q4;
             }
+        }
+    }
+}
+static void dec_q2_k(const uint8_t *data, int64_t n, float *out) {
+    for (int64_t bi = 0; bi < n / 256; bi++) {
+        const uint8_t *b = data + 84 * bi;
+        const float d = get_f16(b + 80), dmin = get_f16(b + 82);
+        for (int e = 0; e < 256; e++) {
+            const uint8_t sc = b[e / 16];
+            const int q = (b[16 + (e / 128) * 32 + e % 32] >> (2 * ((e % 128) / 32))) & 3;
+            out[256 * bi + e] = (d * (float)(sc & 0xF)) * (float)q - dmin * (float)(sc >> 4);
+        }
+    }
+}
+static void dec_q3_k(const uint8_t *data, int64_t n, float *out) {
+    for (int64_t bi = 0; bi < n / 256; bi++) {
+        const uint8_t *b = data + 110 * bi;
+        const float d = get_f16(b + 108);
+        for (int e = 0; e < 256; e++) {
+            const int sb = e / 16;
+            const int u = ((b[96 + sb % 8] >> (4 * (sb / 8))) & 0xF) | (((b[104 + sb % 4] >> (2 * (sb / 4))) & 3) << 4);
+            const int lo = (b[32 + (e / 128) * 32 + e % 32] >> (2 * ((e % 128) / 32))) & 3;
+            const int hi = (b[e % 32] >> (e / 32)) & 1;
+            out[256 * bi + e] = (d * (float)(u - 32)) * (float)(lo - (hi ? 0 : 4));
         }
     }
 }
@@ -1643,6 +1754,8 @@ int oq_encode_row(uint32_t type, const float *x, int64_t n, const float *im, uin
     case T_Q5_0: enc_q5_0(x, n, im, sigma2, out); return OQ_OK;
     case T_Q5_1: enc_q5_1(x, n, im, sigma2, out); return OQ_OK;
     case T_Q6_K: enc_q6_k(x, n, im, sigma2, out); return OQ_OK;
+    case T_Q2_K: enc_q2_k(x, n, im, sigma2, out); return OQ_OK;
+    case T_Q3_K: enc_q3_k(x, n, im, sigma2, out); return OQ_OK;
     case T_Q4_K: enc_qk45(x, n, im, sigma2, 15, out); return OQ_OK;
     case T_Q5_K: enc_qk45(x, n, im, sigma2, 31, out); return OQ_OK;
     case T_IQ2_XXS: return enc_iq2_xxs(x, n, im, out);
@@ -1673,6 +1786,8 @@ int oq_decode_row(uint32_t type, const uint8_t *data, int64_t n, float *out) {
     case T_Q5_0: dec_q5_0(data, n, out); return OQ_OK;
     case T_Q5_1: dec_q5_1(data, n, out); return OQ_OK;
     case T_Q6_K: dec_q6_k(data, n, out); return OQ_OK;
+    case T_Q2_K: dec_q2_k(data, n, out); return OQ_OK;
+    case T_Q3_K: dec_q3_k(data, n, out); return OQ_OK;
     case T_Q4_K: dec_q4_k(data, n, out); return OQ_OK;
     case T_Q5_K: dec_q5_k(data, n, out); return OQ_OK;
     case T_IQ2_XXS: dec_iq2_xxs(data, n, out); return OQ_OK;

@@ -35,6 +35,8 @@ class GgmlType(enum.IntEnum):
     Q5_0 = 6
     Q5_1 = 7
     Q8_0 = 8
+    Q2_K = 10  # no reference counterpart: ggml's block_q2_K layout
+    Q3_K = 11  # no reference counterpart: ggml's block_q3_K layout
     Q4_K = 12
     Q5_K = 13
     Q6_K = 14
@@ -65,12 +67,13 @@ class GgmlType(enum.IntEnum):
 _LAYOUT = {
     GgmlType.F32: (1, 4), GgmlType.F16: (1, 2), GgmlType.BF16: (1, 2), GgmlType.Q4_0: (32, 18),
     GgmlType.Q4_1: (32, 20), GgmlType.Q5_0: (32, 22), GgmlType.Q5_1: (32, 24), GgmlType.Q8_0: (32, 34),
-    GgmlType.Q4_K: (256, 144), GgmlType.Q5_K: (256, 176), GgmlType.Q6_K: (256, 210),
+    GgmlType.Q2_K: (256, 84), GgmlType.Q3_K: (256, 110), GgmlType.Q4_K: (256, 144), GgmlType.Q5_K: (256, 176), GgmlType.Q6_K: (256, 210),
     GgmlType.IQ2_XXS: (256, 66), GgmlType.IQ2_XS: (256, 74), GgmlType.IQ2_S: (256, 82),
     GgmlType.IQ3_XXS: (256, 98), GgmlType.IQ3_S: (256, 110), GgmlType.IQ4_NL: (32, 18),
     GgmlType.IQ4_XS: (256, 136),
 }
-_NAMES = {GgmlType.Q4_K: "Q4_K", GgmlType.Q5_K: "Q5_K", GgmlType.Q6_K: "Q6_K"}
+_NAMES = {GgmlType.Q2_K: "Q2_K", GgmlType.Q3_K: "Q3_K", GgmlType.Q4_K: "Q4_K", GgmlType.Q5_K: "Q5_K",
+          GgmlType.Q6_K: "Q6_K"}
 
 
 class ShoehornError(RuntimeError):

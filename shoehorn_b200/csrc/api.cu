@@ -69,7 +69,7 @@ bool encodable(uint32_t t) {
     switch (t) {
     case SHC_TYPE_F32: case SHC_TYPE_F16: case SHC_TYPE_BF16: case SHC_TYPE_Q8_0: case SHC_TYPE_Q4_K:
     case SHC_TYPE_Q5_K: case SHC_TYPE_Q6_K: case SHC_TYPE_Q4_0: case SHC_TYPE_Q4_1: case SHC_TYPE_Q5_0:
-    case SHC_TYPE_Q5_1:
+    case SHC_TYPE_Q5_1: case SHC_TYPE_Q2_K: case SHC_TYPE_Q3_K:
         return true;
     default:
         return is_iq(t) ? iq_supported(t) : false;

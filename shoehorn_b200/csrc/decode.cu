@@ -96,6 +96,37 @@ __device__ void decode_sub32(uint32_t type, const uint8_t *blk, int sub, float y
         }
         break;
     }
+    case SHC_TYPE_Q2_K: {
+        // element sub*32 + l: sub-block 2*sub + l/16, 2-bit plane sub&3 of
+        // byte 16 + (sub>>2)*32 + l; (d*sc)*q - dmin*m as ggml's dequantizer
+        const float d = ldh(blk + 80), dmin = ldh(blk + 82);
+        const uint8_t *qs = blk + 16 + (sub >> 2) * 32;
+        const int shift = 2 * (sub & 3);
+#pragma unroll
+        for (int l = 0; l < 32; l++) {
+            const uint8_t sc = blk[2 * sub + l / 16];
+            const int qv = (qs[l] >> shift) & 3;
+            y[l] = (d * (float)(sc & 0xF)) * (float)qv - dmin * (float)(sc >> 4);
+        }
+        break;
+    }
+    case SHC_TYPE_Q3_K: {
+        // element sub*32 + l: 6-bit signed scale code of sub-block 2*sub + l/16,
+        // low 2 bits in plane sub&3 of byte 32 + (sub>>2)*32 + l, high bit
+        // sub of hmask byte l (a clear bit subtracts 4)
+        const float d = ldh(blk + 108);
+        const uint8_t *qs = blk + 32 + (sub >> 2) * 32;
+        const int shift = 2 * (sub & 3);
+#pragma unroll
+        for (int l = 0; l < 32; l++) {
+            const int sb = 2 * sub + l / 16;
+            const int u = ((blk[96 + (sb & 7)] >> (4 * (sb >> 3))) & 0xF) | (((blk[104 + (sb & 3)] >> (2 * (sb >> 2))) & 3) << 4);
+            const int lo = (qs[l] >> shift) & 3;
+            const int hi = (blk[l] >> sub) & 1;
+            y[l] = (d * (float)(u - 32)) * (float)(lo - (hi ? 0 : 4));
+        }
+        break;
+    }
     case SHC_TYPE_Q4_K:
     case SHC_TYPE_Q5_K: {
         const bool five = type == SHC_TYPE_Q5_K;

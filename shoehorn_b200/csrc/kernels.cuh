@@ -47,8 +47,9 @@ __host__ __device__ inline int64_t block_elems(uint32_t t) {
     case SHC_TYPE_F32: case SHC_TYPE_F16: case SHC_TYPE_BF16: return 1;
     case SHC_TYPE_Q4_0: case SHC_TYPE_Q4_1: case SHC_TYPE_Q5_0: case SHC_TYPE_Q5_1: case SHC_TYPE_Q8_0:
     case SHC_TYPE_IQ4_NL: return 32;
-    case SHC_TYPE_Q4_K: case SHC_TYPE_Q5_K: case SHC_TYPE_Q6_K: case SHC_TYPE_IQ2_XXS: case SHC_TYPE_IQ2_XS:
-    case SHC_TYPE_IQ2_S: case SHC_TYPE_IQ3_XXS: case SHC_TYPE_IQ3_S: case SHC_TYPE_IQ4_XS: return 256;
+    case SHC_TYPE_Q2_K: case SHC_TYPE_Q3_K: case SHC_TYPE_Q4_K: case SHC_TYPE_Q5_K: case SHC_TYPE_Q6_K:
+    case SHC_TYPE_IQ2_XXS: case SHC_TYPE_IQ2_XS: case SHC_TYPE_IQ2_S: case SHC_TYPE_IQ3_XXS: case SHC_TYPE_IQ3_S:
+    case SHC_TYPE_IQ4_XS: return 256;
     default: return 0;
     }
 }
@@ -61,6 +62,8 @@ __host__ __device__ inline int64_t block_bytes(uint32_t t) {
     case SHC_TYPE_Q5_0: return 22;
     case SHC_TYPE_Q5_1: return 24;
     case SHC_TYPE_Q8_0: return 34;
+    case SHC_TYPE_Q2_K: return 84;
+    case SHC_TYPE_Q3_K: return 110;
     case SHC_TYPE_Q4_K: return 144;
     case SHC_TYPE_Q5_K: return 176;
     case SHC_TYPE_Q6_K: return 210;
@@ -78,8 +81,8 @@ __host__ __device__ inline int64_t block_bytes(uint32_t t) {
 // recompute their own per super-block).
 __host__ __device__ inline bool needs_sigma2(uint32_t t) {
     switch (t) {
-    case SHC_TYPE_Q4_0: case SHC_TYPE_Q4_1: case SHC_TYPE_Q5_0: case SHC_TYPE_Q5_1: case SHC_TYPE_Q4_K:
-    case SHC_TYPE_Q5_K: case SHC_TYPE_Q6_K: return true;
+    case SHC_TYPE_Q4_0: case SHC_TYPE_Q4_1: case SHC_TYPE_Q5_0: case SHC_TYPE_Q5_1: case SHC_TYPE_Q2_K:
+    case SHC_TYPE_Q3_K: case SHC_TYPE_Q4_K: case SHC_TYPE_Q5_K: case SHC_TYPE_Q6_K: return true;
     default: return false;
     }
 }

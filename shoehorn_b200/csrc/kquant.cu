@@ -189,10 +189,15 @@ __global__ void __launch_bounds__(256) enc_q8_0_kernel(EncArgs a) {
 
 // ---------------------------------------------------------------------------
 // Q6_K (quant.rs:231-291) with make_qx_quants(nmax=32) (quant.rs:34-73) per
-// 16-element sub-block.  Two lanes per sub-block split the 19 candidate
-// grids; the selection chain is replayed serially from shared memory.
+// 16-element sub-block, and Q3_K (ggml block_q3_K layout) with nmax 4, 6-bit
+// signed scale codes and 3-bit levels split into a high-bit mask and 2-bit
+// planes.  Two lanes per sub-block split the 19 candidate grids; the
+// selection chain is replayed serially from shared memory.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256, 3) enc_q6_k_kernel(EncArgs a) {
+template <int NMAX>
+__global__ void __launch_bounds__(256, 3) enc_qx16_kernel(EncArgs a) {
+    constexpr float FN = (float)NMAX;
+    constexpr int OUT = NMAX == 32 ? 210 : 110;
     __shared__ float s_x[8][16 * 17];
     __shared__ float s_w[8][16 * 17];
     __shared__ float2 s_cand[8][16][20];
@@ -243,7 +248,7 @@ __global__ void __launch_bounds__(256, 3) enc_q6_k_kernel(EncArgs a) {
             const int ncand = q == 0 ? 10 : 9;
             for (int t = 0; t < ncand; t++) {
                 const int is = is0 + t;
-                const float iscale = -(32.0f + 0.1f * (float)is) / mx;
+                const float iscale = -(FN + 0.1f * (float)is) / mx;
                 float sumlx = 0.0f, suml2 = 0.0f;
                 if (finite) {
                     // element pairs in packed f32x2: the products feed the
@@ -253,8 +258,8 @@ __global__ void __launch_bounds__(256, 3) enc_q6_k_kernel(EncArgs a) {
                     for (int i = 0; i < 16; i += 2) {
                         const float2 y = __fmul2_rn(is2, make_float2(x[i], x[i + 1]));
                         const float2 r = floor_half_up2(make_float2(fabsf(y.x), fabsf(y.y)));
-                        const float2 l = make_float2(fminf(fmaxf(copysignf(r.x, y.x), -32.0f), 31.0f),
-                                                     fminf(fmaxf(copysignf(r.y, y.y), -32.0f), 31.0f));
+                        const float2 l = make_float2(fminf(fmaxf(copysignf(r.x, y.x), -FN), FN - 1.0f),
+                                                     fminf(fmaxf(copysignf(r.y, y.y), -FN), FN - 1.0f));
                         const float2 lx = __fmul2_rn(make_float2(wx[i], wx[i + 1]), l);
                         const float2 l2 = __fmul2_rn(make_float2(w[i], w[i + 1]), __fmul2_rn(l, l));
                         sumlx = __fadd_rn(sumlx, lx.x);
@@ -265,7 +270,7 @@ __global__ void __launch_bounds__(256, 3) enc_q6_k_kernel(EncArgs a) {
                 } else {
 #pragma unroll
                     for (int i = 0; i < 16; i++) {
-                        const float l = round_clamp_f(iscale * x[i], -32.0f, 31.0f);
+                        const float l = round_clamp_f(iscale * x[i], -FN, FN - 1.0f);
                         sumlx += wx[i] * l;
                         suml2 += w[i] * (l * l);
                     }
@@ -301,8 +306,8 @@ __global__ void __launch_bounds__(256, 3) enc_q6_k_kernel(EncArgs a) {
         }
         uint8_t *o = s_out[wid];
         if (max_abs < kGroupMaxEps) {
-            for (int i = lane; i < 210; i += 32) o[i] = 0;
-        } else {
+            for (int i = lane; i < OUT; i += 32) o[i] = 0;
+        } else if (NMAX == 32) {  // Q6_K (quant.rs:258-290)
             const float iscale = -128.0f / max_scale;
             const float d = 1.0f / iscale;
             const int8_t qsc = (int8_t)(uint8_t)(min(nearest_int(iscale * best_scale), 127) & 0xFF);
@@ -330,9 +335,47 @@ __global__ void __launch_bounds__(256, 3) enc_q6_k_kernel(EncArgs a) {
                 o[128 + h * 32 + l] = (uint8_t)((lo[l] >> 4) | ((lo[l + 32] >> 4) << 2) | ((lo[l + 64] >> 4) << 4) |
                                                 ((lo[l + 96] >> 4) << 6));
             }
+        } else {  // Q3_K: 6-bit signed scale codes, 3-bit levels (hmask + 2-bit planes)
+            const float iscale = -32.0f / max_scale;
+            const float d = 1.0f / iscale;
+            const int qsc = (int)round_clamp_f(iscale * best_scale, -32.0f, 31.0f);
+            const float dd = d * (float)qsc;
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const int l = dd == 0.0f ? 4 : (int)round_clamp_f(v[k] / dd, -4.0f, 3.0f) + 4;
+                s_l[wid][lane * 8 + k] = (uint8_t)l;
+            }
+            // scale codes u = qsc + 32 of every sub-block, from its even lane
+            const int u = qsc + 32;
+            const int ua = __shfl_sync(0xffffffffu, u, 2 * (lane & 7));           // sub-block lane & 7
+            const int ub = __shfl_sync(0xffffffffu, u, 2 * ((lane & 7) + 8));     // sub-block (lane & 7) + 8
+            const int uc[4] = {__shfl_sync(0xffffffffu, u, 2 * ((lane & 3) + 0)), __shfl_sync(0xffffffffu, u, 2 * ((lane & 3) + 4)),
+                               __shfl_sync(0xffffffffu, u, 2 * ((lane & 3) + 8)), __shfl_sync(0xffffffffu, u, 2 * ((lane & 3) + 12))};
+            if (lane < 8) o[96 + lane] = (uint8_t)((ua & 0xF) | ((ub & 0xF) << 4));
+            if (lane >= 8 && lane < 12)
+                o[104 + (lane & 3)] = (uint8_t)(((uc[0] >> 4) & 3) | (((uc[1] >> 4) & 3) << 2) | (((uc[2] >> 4) & 3) << 4) |
+                                                (((uc[3] >> 4) & 3) << 6));
+            if (lane == 0) {
+                const uint16_t h = f16_bits(d);
+                o[108] = (uint8_t)(h & 0xFF);
+                o[109] = (uint8_t)(h >> 8);
+            }
+            __syncwarp();
+            const uint8_t *L = s_l[wid];
+            uint8_t hm = 0;  // hmask byte `lane`: bit j = high bit of element j*32 + lane
+#pragma unroll
+            for (int j = 0; j < 8; j++) hm |= (uint8_t)(((L[j * 32 + lane] >> 2) & 1) << j);
+            o[lane] = hm;
+#pragma unroll
+            for (int h = 0; h < 2; h++) {  // qs byte h*32 + lane: elements h*128 + j*32 + lane at bits 2j
+                uint8_t b = 0;
+#pragma unroll
+                for (int j = 0; j < 4; j++) b |= (uint8_t)((L[h * 128 + j * 32 + lane] & 3) << (2 * j));
+                o[32 + h * 32 + lane] = b;
+            }
         }
         __syncwarp();
-        store_block(a.dst + row * a.dst_row_bytes + sbi * 210, o, 210, false, lane);
+        store_block(a.dst + row * a.dst_row_bytes + sbi * OUT, o, OUT, false, lane);
         __syncwarp();
     }
 }
@@ -357,9 +400,9 @@ __global__ void __launch_bounds__(256, 3) enc_q6_k_kernel(EncArgs a) {
 // the three weighted sums per grid.  CLEAN: every iscale and (x - vmin) is
 // finite, so y = iscale*(x - vmin) is >= 0 or +inf and the clamp at 0 is not
 // needed.
-template <bool CLEAN, int NG>
+template <bool CLEAN, int NG, int NP>
 __device__ __forceinline__ void qkx3_grids(const float *snx, const float *sw, const float *su, const float (&iscale)[NG],
-                                           float fn, float2 (&l)[NG][16], float (&sl)[NG], float (&sl2)[NG],
+                                           float fn, float2 (&l)[NG][NP], float (&sl)[NG], float (&sl2)[NG],
                                            float (&sxl)[NG]) {
     float2 nis[NG];
 #pragma unroll
@@ -370,7 +413,7 @@ __device__ __forceinline__ void qkx3_grids(const float *snx, const float *sw, co
         sxl[g] = 0.0f;
     }
 #pragma unroll
-    for (int i = 0; i < 16; i++) {
+    for (int i = 0; i < NP; i++) {
         const float4 n4 = reinterpret_cast<const float4 *>(snx)[i >> 1];
         const float4 w4 = reinterpret_cast<const float4 *>(sw)[i >> 1];
         const float2 nxi = (i & 1) ? make_float2(n4.z, n4.w) : make_float2(n4.x, n4.y);
@@ -402,13 +445,13 @@ __device__ __forceinline__ void qkx3_grids(const float *snx, const float *sw, co
 
 // Weighted squared error of NG candidate (scale, min) fits, interleaved
 // (quant.rs:125-128 and 100-101): diff = scale*l + min - x, err += w*diff*diff.
-template <int NG>
-__device__ __forceinline__ void qkx3_errors(const float *snx, const float *sw, const float2 (&l)[NG][16],
+template <int NG, int NP>
+__device__ __forceinline__ void qkx3_errors(const float *snx, const float *sw, const float2 (&l)[NG][NP],
                                             const float (&ts)[NG], const float (&tm)[NG], float (&err)[NG]) {
 #pragma unroll
     for (int g = 0; g < NG; g++) err[g] = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 16; i++) {
+    for (int i = 0; i < NP; i++) {
         const float4 n4 = reinterpret_cast<const float4 *>(snx)[i >> 1];
         const float4 w4 = reinterpret_cast<const float4 *>(sw)[i >> 1];
         const float2 nxi = (i & 1) ? make_float2(n4.z, n4.w) : make_float2(n4.x, n4.y);
@@ -541,8 +584,8 @@ __global__ void __launch_bounds__(256, 2) enc_qk45_kernel(EncArgs a) {
                 bool clean = range_finite;
 #pragma unroll
                 for (int g = 0; g < NG; g++) clean = clean && isc[g] < INFINITY;
-                if (clean) qkx3_grids<true, NG>(snx, sw, su, isc, FN, l, sl, sl2, sxl);
-                else qkx3_grids<false, NG>(snx, sw, su, isc, FN, l, sl, sl2, sxl);
+                if (clean) qkx3_grids<true, NG, 16>(snx, sw, su, isc, FN, l, sl, sl2, sxl);
+                else qkx3_grids<false, NG, 16>(snx, sw, su, isc, FN, l, sl, sl2, sxl);
                 float ts[NG], tm[NG];
                 bool valid[NG];
 #pragma unroll
@@ -563,7 +606,7 @@ __global__ void __launch_bounds__(256, 2) enc_qk45_kernel(EncArgs a) {
                     }
                 }
                 float err[NG];
-                qkx3_errors<NG>(snx, sw, l, ts, tm, err);
+                qkx3_errors<NG, 16>(snx, sw, l, ts, tm, err);
 #pragma unroll
                 for (int g = 0; g < NG; g++) {
                     const int j = j0 + 4 * g;
@@ -679,6 +722,226 @@ __global__ void __launch_bounds__(256, 2) enc_qk45_kernel(EncArgs a) {
 
 template __global__ void enc_qk45_kernel<15>(EncArgs);
 template __global__ void enc_qk45_kernel<31>(EncArgs);
+
+// ---------------------------------------------------------------------------
+// Q2_K (ggml block_q2_K layout): make_qkx3_quants (quant.rs:77-141, nmax 3,
+// rmin -0.9, rdelta 0.05, 37 grids) per 16-element sub-block, 4-bit scale and
+// min codes against the super-block's largest scale and min, 2-bit levels.
+// Two lanes per sub-block: lane q evaluates jobs j = q, q+2, ..., j < 38
+// (j == 37, on the odd lane, is the initial nmax/(vmax-vmin) grid), two jobs
+// per round; the search arithmetic is the Q4_K/Q5_K kernel's on 8 pairs.
+// ---------------------------------------------------------------------------
+constexpr int kQ2kGridsPerRound = 2;
+__global__ void __launch_bounds__(256, 2) enc_q2_k_kernel(EncArgs a) {
+    constexpr float FN = 3.0f;
+    // per warp: 16 sub-blocks of 16, padded to 20 floats (the 16 distinct
+    // 16-byte reads of one instruction cover the 32 banks twice)
+    __shared__ __align__(16) float s_nx[8][16 * 20];
+    __shared__ __align__(16) float s_w[8][16 * 20];
+    __shared__ __align__(16) float s_u[8][16 * 20];
+    __shared__ __align__(16) uint8_t s_out[8][96];
+    __shared__ uint8_t s_l[8][256];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int s = lane >> 1, q = lane & 1;
+    const int64_t ne0 = a.src.ne0, nsb = ne0 >> 8, total = a.n_rows * nsb;
+    float *snx = &s_nx[wid][s * 20];
+    float *sw = &s_w[wid][s * 20];
+    float *su = &s_u[wid][s * 20];
+    for (int64_t g = (int64_t)blockIdx.x * 8 + wid; g < total; g += (int64_t)gridDim.x * 8) {
+        const int64_t row = g / nsb;
+        const int64_t sbi = g - row * nsb;
+        const int64_t col0 = sbi << 8;
+        const float sig = a.sigma2[row];
+        const float *imr = im_row(a.im, ne0, a.row0 + row * a.row_step);
+        float v[8], base[8];
+        load8(a.src, row, col0 + lane * 8, v);
+        load_im8(imr, col0 + lane * 8, base);
+        {
+            float wk[8];
+#pragma unroll
+            for (int k = 0; k < 8; k += 2) {
+                const float2 vv = make_float2(v[k], v[k + 1]);
+                const float2 vv2 = __fmul2_rn(vv, vv);
+                const float2 sq = make_float2(sqrtf(__fadd_rn(sig, vv2.x)), sqrtf(__fadd_rn(sig, vv2.y)));
+                const float2 ww = __fmul2_rn(make_float2(base[k], base[k + 1]), sq);
+                wk[k] = ww.x;
+                wk[k + 1] = ww.y;
+            }
+            float4 *pn = reinterpret_cast<float4 *>(snx + q * 8);
+            float4 *pw = reinterpret_cast<float4 *>(sw + q * 8);
+            pn[0] = make_float4(-v[0], -v[1], -v[2], -v[3]);
+            pn[1] = make_float4(-v[4], -v[5], -v[6], -v[7]);
+            pw[0] = make_float4(wk[0], wk[1], wk[2], wk[3]);
+            pw[1] = make_float4(wk[4], wk[5], wk[6], wk[7]);
+        }
+        float vmin, vmax;
+        {
+            float mn = fminf(fminf(fminf(v[0], v[1]), fminf(v[2], v[3])), fminf(fminf(v[4], v[5]), fminf(v[6], v[7])));
+            float mx = fmaxf(fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3])), fmaxf(fmaxf(v[4], v[5]), fmaxf(v[6], v[7])));
+            mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            vmin = fminf(fminf(INFINITY, mn), 0.0f);
+            vmax = fmaxf(-INFINITY, mx);
+        }
+        {
+            float4 *pu = reinterpret_cast<float4 *>(su + q * 8);
+            pu[0] = make_float4(__fadd_rn(-v[0], vmin), __fadd_rn(-v[1], vmin), __fadd_rn(-v[2], vmin),
+                                __fadd_rn(-v[3], vmin));
+            pu[1] = make_float4(__fadd_rn(-v[4], vmin), __fadd_rn(-v[5], vmin), __fadd_rn(-v[6], vmin),
+                                __fadd_rn(-v[7], vmin));
+        }
+        __syncwarp();
+        const bool degen = vmax <= vmin;
+        const float range = vmax - vmin;
+        const float iscale0 = FN / range;
+        const float scale0 = 1.0f / iscale0;
+        float init_err = 0.0f, best_e = 0.0f, best_s = 0.0f, best_m = 0.0f;
+        int best_j = -1;
+        if (!degen) {
+            float sum_w = 0.0f, sum_x = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const float4 n4 = reinterpret_cast<const float4 *>(snx)[c];
+                const float4 w4 = reinterpret_cast<const float4 *>(sw)[c];
+                const float2 a = __fmul2_rn(make_float2(w4.x, w4.y), make_float2(n4.x, n4.y));
+                const float2 b = __fmul2_rn(make_float2(w4.z, w4.w), make_float2(n4.z, n4.w));
+                sum_w = __fadd_rn(sum_w, w4.x);
+                sum_x = __fsub_rn(sum_x, a.x);
+                sum_w = __fadd_rn(sum_w, w4.y);
+                sum_x = __fsub_rn(sum_x, a.y);
+                sum_w = __fadd_rn(sum_w, w4.z);
+                sum_x = __fsub_rn(sum_x, b.x);
+                sum_w = __fadd_rn(sum_w, w4.w);
+                sum_x = __fsub_rn(sum_x, b.y);
+            }
+            const bool range_finite = range < INFINITY;
+            // lane q takes jobs q + 2k in increasing order, NG per round, so
+            // the strict `<` keeps the first minimum as the reference's chain
+            // does; jobs 38 and 39 (last round) are padding
+            constexpr int NG = kQ2kGridsPerRound;
+#pragma unroll 1
+            for (int r = 0; r < 20 / NG; r++) {
+                const int j0 = q + 2 * NG * r;
+                float isc[NG];
+#pragma unroll
+                for (int g = 0; g < NG; g++) {
+                    const int j = j0 + 2 * g;
+                    isc[g] = j == 37 ? iscale0 : (-0.9f + 0.05f * (float)j + FN) / range;
+                }
+                float sl[NG], sl2[NG], sxl[NG];
+                float2 l[NG][8];
+                bool clean = range_finite;
+#pragma unroll
+                for (int g = 0; g < NG; g++) clean = clean && isc[g] < INFINITY;
+                if (clean) qkx3_grids<true, NG, 8>(snx, sw, su, isc, FN, l, sl, sl2, sxl);
+                else qkx3_grids<false, NG, 8>(snx, sw, su, isc, FN, l, sl, sl2, sxl);
+                float ts[NG], tm[NG];
+                bool valid[NG];
+#pragma unroll
+                for (int g = 0; g < NG; g++) {
+                    if (j0 + 2 * g == 37) {
+                        ts[g] = scale0;
+                        tm[g] = vmin;
+                        valid[g] = true;
+                    } else {
+                        const float D = __fsub_rn(__fmul_rn(sum_w, sl2[g]), __fmul_rn(sl[g], sl[g]));
+                        valid[g] = D > 0.0f;
+                        ts[g] = __fsub_rn(__fmul_rn(sum_w, sxl[g]), __fmul_rn(sum_x, sl[g])) / D;
+                        tm[g] = __fsub_rn(__fmul_rn(sl2[g], sum_x), __fmul_rn(sl[g], sxl[g])) / D;
+                        if (tm[g] > 0.0f) {
+                            tm[g] = 0.0f;
+                            ts[g] = sl2[g] > 0.0f ? sxl[g] / sl2[g] : 0.0f;
+                        }
+                    }
+                }
+                float err[NG];
+                qkx3_errors<NG, 8>(snx, sw, l, ts, tm, err);
+#pragma unroll
+                for (int g = 0; g < NG; g++) {
+                    const int j = j0 + 2 * g;
+                    if (j >= 38 || !valid[g]) continue;
+                    if (j == 37) {
+                        init_err = err[g];
+                    } else if (err[g] == err[g] && (best_j < 0 || err[g] < best_e)) {
+                        best_e = err[g];
+                        best_j = j;
+                        best_s = ts[g];
+                        best_m = tm[g];
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        {  // argmin (err, j) over the lane pair
+            const float oe = __shfl_xor_sync(0xffffffffu, best_e, 1);
+            const int oj = __shfl_xor_sync(0xffffffffu, best_j, 1);
+            const float os = __shfl_xor_sync(0xffffffffu, best_s, 1);
+            const float om = __shfl_xor_sync(0xffffffffu, best_m, 1);
+            if (oj >= 0 && (best_j < 0 || oe < best_e || (oe == best_e && oj < best_j))) {
+                best_e = oe;
+                best_j = oj;
+                best_s = os;
+                best_m = om;
+            }
+        }
+        init_err = __shfl_sync(0xffffffffu, init_err, lane | 1);
+        float scale, mn;
+        if (degen) {
+            scale = 0.0f;
+            mn = vmin;
+        } else if (best_j >= 0 && best_e < init_err) {
+            scale = best_s;
+            mn = best_m;
+        } else {
+            scale = scale0;
+            mn = vmin;
+        }
+        const float mins_s = -mn;
+        float max_scale = scale, max_min = mins_s;
+#pragma unroll
+        for (int off = 2; off <= 16; off <<= 1) {
+            max_scale = rmaxf(max_scale, __shfl_xor_sync(0xffffffffu, max_scale, off));
+            max_min = rmaxf(max_min, __shfl_xor_sync(0xffffffffu, max_min, off));
+        }
+        max_scale = rmaxf(0.0f, max_scale);
+        max_min = rmaxf(0.0f, max_min);
+        const float inv_scale = max_scale > 0.0f ? 15.0f / max_scale : 0.0f;
+        const float inv_min = max_min > 0.0f ? 15.0f / max_min : 0.0f;
+        const int lsq = (int)round_clamp0_f(inv_scale * scale, 15.0f);
+        const int lmq = (int)round_clamp0_f(inv_min * mins_s, 15.0f);
+        const float d = max_scale / 15.0f;
+        const float dmin = max_min / 15.0f;
+        const float dsub = d * (float)lsq;
+        const float msub = dmin * (float)lmq;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            // (x + msub) = (msub - nx)
+            const int l = dsub == 0.0f ? 0 : (int)round_clamp0_f(__fsub_rn(msub, snx[q * 8 + k]) / dsub, FN);
+            s_l[wid][lane * 8 + k] = (uint8_t)l;
+        }
+        uint8_t *o = s_out[wid];
+        if (q == 0) o[s] = (uint8_t)(lsq | (lmq << 4));
+        if (lane == 0) {
+            const uint16_t hd = f16_bits(d), hm = f16_bits(dmin);
+            o[80] = (uint8_t)(hd & 0xFF);
+            o[81] = (uint8_t)(hd >> 8);
+            o[82] = (uint8_t)(hm & 0xFF);
+            o[83] = (uint8_t)(hm >> 8);
+        }
+        __syncwarp();
+        const uint8_t *L = s_l[wid];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {  // qs byte h*32 + lane: elements h*128 + j*32 + lane at bits 2j
+            uint8_t b = 0;
+#pragma unroll
+            for (int j = 0; j < 4; j++) b |= (uint8_t)(L[h * 128 + j * 32 + lane] << (2 * j));
+            o[16 + h * 32 + lane] = b;
+        }
+        __syncwarp();
+        store_block(a.dst + row * a.dst_row_bytes + sbi * 84, o, 84, false, lane);
+        __syncwarp();
+    }
+}
 
 // ---------------------------------------------------------------------------
 // Legacy 32-blocks (quant.rs:171-229): Q4_0/Q5_0 with make_qx_quants (nmax 8
@@ -974,8 +1237,18 @@ cudaError_t launch_kquant(uint32_t type, const EncArgs &a, int num_sms, cudaStre
         break;
     }
     case SHC_TYPE_Q6_K: {
-        unsigned grid = persistent_grid((const void *)enc_q6_k_kernel, 256, num_sms, a.n_rows * nsb);
-        enc_q6_k_kernel<<<grid, 256, 0, st>>>(a);
+        unsigned grid = persistent_grid((const void *)enc_qx16_kernel<32>, 256, num_sms, a.n_rows * nsb);
+        enc_qx16_kernel<32><<<grid, 256, 0, st>>>(a);
+        break;
+    }
+    case SHC_TYPE_Q3_K: {
+        unsigned grid = persistent_grid((const void *)enc_qx16_kernel<4>, 256, num_sms, a.n_rows * nsb);
+        enc_qx16_kernel<4><<<grid, 256, 0, st>>>(a);
+        break;
+    }
+    case SHC_TYPE_Q2_K: {
+        unsigned grid = persistent_grid((const void *)enc_q2_k_kernel, 256, num_sms, a.n_rows * nsb);
+        enc_q2_k_kernel<<<grid, 256, 0, st>>>(a);
         break;
     }
     case SHC_TYPE_Q4_K: {

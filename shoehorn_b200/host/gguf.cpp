@@ -20,6 +20,8 @@ std::pair<uint64_t, uint64_t> block_layout(uint32_t t) {
     case T_Q5_0: return {32, 22};
     case T_Q5_1: return {32, 24};
     case T_Q8_0: return {32, 34};
+    case T_Q2_K: return {256, 84};
+    case T_Q3_K: return {256, 110};
     case T_Q4_K: return {256, 144};
     case T_Q5_K: return {256, 176};
     case T_Q6_K: return {256, 210};
@@ -42,7 +44,7 @@ uint64_t row_bytes(uint32_t ty, uint64_t n) {
 
 static const struct { uint32_t ty; const char *name; } kNames[] = {
     {T_F32, "F32"}, {T_F16, "F16"}, {T_BF16, "BF16"}, {T_Q4_0, "Q4_0"}, {T_Q4_1, "Q4_1"}, {T_Q5_0, "Q5_0"},
-    {T_Q5_1, "Q5_1"}, {T_Q8_0, "Q8_0"}, {T_Q4_K, "Q4_K"}, {T_Q5_K, "Q5_K"}, {T_Q6_K, "Q6_K"},
+    {T_Q5_1, "Q5_1"}, {T_Q8_0, "Q8_0"}, {T_Q2_K, "Q2_K"}, {T_Q3_K, "Q3_K"}, {T_Q4_K, "Q4_K"}, {T_Q5_K, "Q5_K"}, {T_Q6_K, "Q6_K"},
     {T_IQ2_XXS, "IQ2_XXS"}, {T_IQ2_XS, "IQ2_XS"}, {T_IQ2_S, "IQ2_S"}, {T_IQ3_XXS, "IQ3_XXS"}, {T_IQ3_S, "IQ3_S"},
     {T_IQ4_NL, "IQ4_NL"}, {T_IQ4_XS, "IQ4_XS"}};
 

@@ -580,6 +580,8 @@ uint32_t file_type_code(const std::vector<PlanEntry> &entries) {
         case T_Q5_0: code = 8; break;
         case T_Q5_1: code = 9; break;
         case T_Q8_0: code = 7; break;
+        case T_Q2_K: code = 10; break;
+        case T_Q3_K: code = 11; break;
         case T_Q4_K: code = 15; break;
         case T_Q5_K: code = 17; break;
         case T_Q6_K: code = 18; break;

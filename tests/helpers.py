@@ -3,16 +3,18 @@ import numpy as np
 
 # Type ids (reference gguf.rs:36-83).
 F32, F16, Q4_0, Q4_1, Q5_0, Q5_1, Q8_0 = 0, 1, 2, 3, 6, 7, 8
-Q4_K, Q5_K, Q6_K = 12, 13, 14
+Q2_K, Q3_K, Q4_K, Q5_K, Q6_K = 10, 11, 12, 13, 14
 IQ2_XXS, IQ2_XS, IQ3_XXS, IQ4_NL, IQ3_S, IQ2_S, IQ4_XS, BF16 = 16, 17, 18, 20, 21, 22, 23, 30
 
 NAMES = {F32: "F32", F16: "F16", Q4_0: "Q4_0", Q4_1: "Q4_1", Q5_0: "Q5_0", Q5_1: "Q5_1", Q8_0: "Q8_0",
-         Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K", IQ2_XXS: "IQ2_XXS", IQ2_XS: "IQ2_XS", IQ3_XXS: "IQ3_XXS",
+         Q2_K: "Q2_K", Q3_K: "Q3_K", Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K", IQ2_XXS: "IQ2_XXS", IQ2_XS: "IQ2_XS", IQ3_XXS: "IQ3_XXS",
          IQ4_NL: "IQ4_NL", IQ3_S: "IQ3_S", IQ2_S: "IQ2_S", IQ4_XS: "IQ4_XS", BF16: "BF16"}
 KQUANT = [Q8_0, Q6_K, Q4_K, Q5_K, Q4_0, Q4_1, Q5_0, Q5_1]
 LEGACY = [Q4_0, Q4_1, Q5_0, Q5_1]
 IQ = [IQ2_XXS, IQ2_XS, IQ2_S, IQ3_XXS, IQ3_S, IQ4_NL, IQ4_XS]
 PLAIN = [F32, F16, BF16]
+# K-quants beyond the reference's type set (ggml block layouts)
+KQUANT_EXTRA = [Q2_K, Q3_K]
 
 
 def lcg_vec(n, seed=0x12345678):

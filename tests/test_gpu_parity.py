@@ -6,8 +6,8 @@ import numpy as np
 import pytest
 
 from oracle import oracle as O
-from tests.helpers import (BF16, F16, F32, IQ, KQUANT, NAMES, PLAIN, bf16_bits_to_f32, edge_rows, f32_to_bf16_bits,
-                           student_rows, sweep_rows)
+from tests.helpers import (BF16, F16, F32, IQ, KQUANT, KQUANT_EXTRA, NAMES, PLAIN, bf16_bits_to_f32, edge_rows,
+                           f32_to_bf16_bits, student_rows, sweep_rows)
 
 pytestmark = pytest.mark.gpu
 
@@ -19,7 +19,9 @@ def supported(types):
     return [t for t in types if sh.type_supported(t)]
 
 
-ENC_TYPES = supported(KQUANT + IQ) + PLAIN
+# the reference's K-quants and the two ggml K-quants it lacks (Q2_K, Q3_K)
+KQ = KQUANT + KQUANT_EXTRA
+ENC_TYPES = supported(KQ + IQ) + PLAIN
 
 
 def dev(a):
@@ -67,7 +69,7 @@ def test_encode_matches_oracle_sweep_rows(ctx, ty):
     assert_bytes_equal(gpu_encode(ctx, ty, bits, im), oracle_encode(ty, bits, im), ty)
 
 
-@pytest.mark.parametrize("ty", supported(KQUANT) + supported([20, 23]), ids=lambda t: NAMES[t])
+@pytest.mark.parametrize("ty", supported(KQ) + supported([20, 23]), ids=lambda t: NAMES[t])
 def test_encode_matches_oracle_many_rows(ctx, ty):
     """4096 rows x 1024 (16384 super-blocks): enough near-ties between grid
     errors that a single contracted multiply-add in a search shows up."""
@@ -90,7 +92,7 @@ def test_encode_matches_oracle_edge_rows(ctx, ty):
     assert_bytes_equal(gpu_encode(ctx, ty, bits, None), oracle_encode(ty, bits, None), ty)
 
 
-@pytest.mark.parametrize("ty", supported(KQUANT + IQ), ids=lambda t: NAMES[t])
+@pytest.mark.parametrize("ty", supported(KQ + IQ), ids=lambda t: NAMES[t])
 def test_expert_imatrix_slicing_and_row0(ctx, ty):
     """imatrix.rs:124-141: an imatrix of n_mats*ne0 selects matrix row/rows_per_mat."""
     bits, _ = sweep_rows(24, 512, seed=300 + ty)
@@ -111,13 +113,13 @@ def test_f32_and_f16_sources(ctx, src_dtype):
     if src_dtype == "f16":
         x = x.astype(np.float16).astype(np.float32)
     src = dev(x if src_dtype == "f32" else x.astype(np.float16))
-    for ty in supported(KQUANT + IQ):
+    for ty in supported(KQ + IQ):
         got = ctx.encode_rows(ty, src, dev(im), sync=True).cpu().numpy()
         want = np.stack([O.encode_row(ty, r, im) for r in x])
         assert_bytes_equal(got, want, ty)
 
 
-@pytest.mark.parametrize("ty", supported(KQUANT + IQ) + [F16, BF16, F32], ids=lambda t: NAMES[t])
+@pytest.mark.parametrize("ty", supported(KQ + IQ) + [F16, BF16, F32], ids=lambda t: NAMES[t])
 def test_decode_matches_oracle(ctx, ty):
     bits, im = student_rows(8, 1024, seed=400 + ty)
     x = bf16_bits_to_f32(bits)
@@ -130,7 +132,7 @@ def test_decode_matches_oracle(ctx, ty):
 @pytest.mark.parametrize("row_step", [1, 3])
 def test_row_errors_match_oracle(ctx, row_step):
     bits, im = sweep_rows(20, 1024, seed=500)
-    types = supported(KQUANT + IQ) + [F16]
+    types = supported(KQ + IQ) + [F16]
     got = ctx.row_errors(types, dev(bits.view(np.int16)), dev(im), row_step=row_step).cpu().numpy()
     for t, ty in enumerate(types):
         want = O.row_errors_bf16(ty, bits, im, row_step=row_step)
@@ -140,7 +142,7 @@ def test_row_errors_match_oracle(ctx, row_step):
 def test_row_errors_without_imatrix_and_edges(ctx):
     x = edge_rows(512)
     bits = f32_to_bf16_bits(x)
-    types = supported(KQUANT + IQ) + [F16, BF16]
+    types = supported(KQ + IQ) + [F16, BF16]
     got = ctx.row_errors(types, dev(bits.view(np.int16)), None).cpu().numpy()
     for t, ty in enumerate(types):
         want = O.row_errors_bf16(ty, bits, None)
@@ -149,7 +151,7 @@ def test_row_errors_without_imatrix_and_edges(ctx):
 
 def test_row_api_mirrors_reference(ctx):
     x = bf16_bits_to_f32(sweep_rows(1, 512, seed=9)[0])[0]
-    for ty in supported(KQUANT):
+    for ty in supported(KQ):
         enc = sh.encode_row(ty, x)
         assert np.array_equal(enc, O.encode_row(ty, x))
         assert np.array_equal(sh.decode_row(ty, enc, 512).view(np.uint32), O.decode_row(ty, enc, 512).view(np.uint32))
@@ -161,7 +163,7 @@ def test_row_api_mirrors_reference(ctx):
 @pytest.mark.parametrize("pinned", [False, True])
 def test_host_entry_point_matches_device(ctx, pinned):
     bits, im = sweep_rows(300, 1024, seed=21)
-    for ty in supported(KQUANT + IQ):
+    for ty in supported(KQ + IQ):
         want = oracle_encode(ty, bits, im)
         if pinned:
             src = torch.from_numpy(bits.view(np.int16)).pin_memory()
@@ -175,7 +177,7 @@ def test_host_entry_point_matches_device(ctx, pinned):
 
 def test_host_row_errors_match_oracle(ctx):
     bits, im = sweep_rows(37, 1024, seed=31)
-    types = supported(KQUANT + IQ) + [F16]
+    types = supported(KQ + IQ) + [F16]
     got = ctx.row_errors_host(types, bits, im, row_step=4)
     for t, ty in enumerate(types):
         want = O.row_errors_bf16(ty, bits, im, row_step=4)
@@ -195,7 +197,7 @@ def big_tensor():
     return bits, im
 
 
-@pytest.mark.parametrize("ty", supported(KQUANT + IQ), ids=lambda t: NAMES[t])
+@pytest.mark.parametrize("ty", supported(KQ + IQ), ids=lambda t: NAMES[t])
 def test_full_size_encode(ctx, big_tensor, ty):
     bits, im = big_tensor
     src = dev(bits.view(np.int16))

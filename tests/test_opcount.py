@@ -7,9 +7,9 @@ import pytest
 import bench
 from oracle import oracle as O
 from oracle.opcount import count_flops as C
-from tests.helpers import IQ, KQUANT, NAMES, bf16_bits_to_f32, edge_rows, student_rows, sweep_rows
+from tests.helpers import IQ, KQUANT, KQUANT_EXTRA, NAMES, bf16_bits_to_f32, edge_rows, student_rows, sweep_rows
 
-ALL = KQUANT + IQ
+ALL = KQUANT + KQUANT_EXTRA + IQ
 
 
 @pytest.mark.parametrize("ty", ALL, ids=lambda t: NAMES[t])
@@ -27,7 +27,7 @@ def test_counting_build_matches_oracle_bytes(ty):
 @pytest.mark.parametrize("name", list(bench.FLOPS_PER_ELT), ids=str)
 def test_bench_flop_table_matches_counter(name):
     ty = bench.TYPE_IDS[name]
-    if name in bench.SWEEP:
+    if name in bench.SWEEP or name in ("Q2_K", "Q3_K"):
         bits, im = sweep_rows(8, 14336, seed=7)
     else:
         bits, im = student_rows(8, 4096, seed=7)

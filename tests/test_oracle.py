@@ -6,8 +6,8 @@ import numpy as np
 import pytest
 
 from oracle import oracle as O
-from tests.helpers import (BF16, F16, IQ2_S, IQ2_XS, IQ2_XXS, IQ3_S, IQ3_XXS, IQ4_NL, IQ4_XS, NAMES, Q4_0, Q4_1,
-                           Q4_K, Q5_0, Q5_1, Q5_K, Q6_K, Q8_0, edge_rows, lcg_vec, student_rows, sweep_rows,
+from tests.helpers import (BF16, F16, IQ2_S, IQ2_XS, IQ2_XXS, IQ3_S, IQ3_XXS, IQ4_NL, IQ4_XS, NAMES, Q2_K, Q3_K,
+                           Q4_0, Q4_1, Q4_K, Q5_0, Q5_1, Q5_K, Q6_K, Q8_0, edge_rows, lcg_vec, student_rows, sweep_rows,
                            bf16_bits_to_f32)
 
 gguf = pytest.importorskip("gguf")
@@ -26,6 +26,43 @@ def test_roundtrips(ty, tol):
     d = (x - dec).astype(np.float32)
     rmse = np.sqrt(np.float32(np.sum(d * d, dtype=np.float32)) / np.float32(512))
     assert rmse < tol, f"{NAMES[ty]} rmse {rmse}"
+
+
+# ---- Q2_K / Q3_K: no reference counterpart; the reference's search routines
+# in ggml's block layouts (decoder layouts pinned through gguf-py below) ----
+@pytest.mark.parametrize("ty,bpb,tol", [(Q3_K, 110, 0.2), (Q2_K, 84, 0.35)])
+def test_extra_kquant_roundtrips(ty, bpb, tol):
+    x = lcg_vec(512)
+    enc = O.encode_row(ty, x)
+    assert enc.size == 2 * bpb == O.row_bytes(ty, 512)
+    d = (x - O.decode_row(ty, enc, 512)).astype(np.float32)
+    assert np.sqrt(np.sum(d * d, dtype=np.float32) / np.float32(512)) < tol
+
+
+def test_extra_kquant_error_ladder():
+    """More bits, less weighted error: Q2_K > Q3_K > Q4_K on the same rows."""
+    bits, im = student_rows(8, 1024, seed=5)
+    x = bf16_bits_to_f32(bits)
+    for r in range(8):
+        e2, e3, e4 = (O.row_error(t, x[r], im) for t in (Q2_K, Q3_K, Q4_K))
+        assert e2 > e3 > e4 > 0.0
+
+
+def test_extra_kquant_zero_and_scale_codes():
+    z = np.zeros(256, np.float32)
+    assert not O.encode_row(Q3_K, z).any()  # zero block: every byte 0
+    e2 = O.encode_row(Q2_K, z)
+    assert not e2.any()
+    # one large positive element per 16-element sub-block: the largest scale
+    # code is 15 (Q2_K) and the largest |signed scale code| is 32 (Q3_K)
+    x = lcg_vec(256) * np.float32(0.01)
+    x[::16] = np.float32(3.0)
+    e2 = O.encode_row(Q2_K, x)
+    assert max(b & 0xF for b in e2[:16]) == 15
+    e3 = O.encode_row(Q3_K, x).astype(np.int64)
+    u = [((e3[96 + sb % 8] >> (4 * (sb // 8))) & 0xF) | (((e3[104 + sb % 4] >> (2 * (sb // 4))) & 3) << 4)
+         for sb in range(16)]
+    assert max(abs(c - 32) for c in u) == 32
 
 
 # ---- quant.rs:673-695 imatrix weighting ----
@@ -103,7 +140,7 @@ def test_nearest_int_is_half_away_and_saturating():
 
 
 # ---- independent layout pins through gguf-py ----
-_GQ = {Q8_0: GQT.Q8_0, Q4_0: GQT.Q4_0, Q4_1: GQT.Q4_1, Q5_0: GQT.Q5_0, Q5_1: GQT.Q5_1, Q4_K: GQT.Q4_K,
+_GQ = {Q8_0: GQT.Q8_0, Q2_K: GQT.Q2_K, Q3_K: GQT.Q3_K, Q4_0: GQT.Q4_0, Q4_1: GQT.Q4_1, Q5_0: GQT.Q5_0, Q5_1: GQT.Q5_1, Q4_K: GQT.Q4_K,
        Q5_K: GQT.Q5_K, Q6_K: GQT.Q6_K, IQ2_XXS: GQT.IQ2_XXS, IQ2_XS: GQT.IQ2_XS, IQ2_S: GQT.IQ2_S,
        IQ3_XXS: GQT.IQ3_XXS, IQ3_S: GQT.IQ3_S, IQ4_NL: GQT.IQ4_NL, IQ4_XS: GQT.IQ4_XS}
 
@@ -129,7 +166,7 @@ def test_q8_0_bytes_match_gguf_py_quantizer():
 
 
 @pytest.mark.parametrize("ty", [Q8_0, Q6_K, Q4_K, Q5_K, Q4_0, Q4_1, Q5_0, Q5_1, IQ4_NL, IQ4_XS, IQ3_S, IQ3_XXS,
-                                IQ2_S, IQ2_XS, IQ2_XXS])
+                                IQ2_S, IQ2_XS, IQ2_XXS, Q2_K, Q3_K])
 def test_edge_rows_encode_and_decode(ty):
     rows = edge_rows(512)
     for r in rows:
