@@ -381,12 +381,11 @@ __global__ void __launch_bounds__(256, 3) enc_qx16_kernel(EncArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// Q4_K / Q5_K (quant.rs:294-379) with make_qkx3_quants (quant.rs:77-141,
-// rmin -0.9, rdelta 0.05, 37 grids) per 32-element sub-block.  Four lanes per
-// sub-block: lane q evaluates jobs j = q, q+4, ..., j < 38, where j < 37 is
-// grid `is = j` and j == 37 is the initial nmax/(vmax-vmin) grid.
+// Q4_K / Q5_K (quant.rs:294-379) and Q2_K with make_qkx3_quants
+// (quant.rs:77-141, rmin -0.9, rdelta 0.05, 37 grids) per 32-element (Q4_K,
+// Q5_K) or 16-element (Q2_K) sub-block; a warp per super-block.
 //
-// Each lane holds its sub-block as 16 float2 pairs and runs the element-wise
+// A lane evaluating a grid reads the sub-block as float2 pairs and runs the element-wise
 // products of a grid with packed f32x2 multiplies and adds (two IEEE-rounded
 // f32 operations per instruction, the same results as scalar code); the
 // reference's running sums stay scalar and in element order.  x is kept
@@ -467,28 +466,92 @@ __device__ __forceinline__ void qkx3_errors(const float *snx, const float *sw, c
     }
 }
 
-// One grid per round and two blocks (16 warps) per SM: the lane's sub-block
-// is read from shared memory in each pass instead of being held in
-// registers, which keeps the kernel within 128 registers per thread.
-constexpr int kQk45GridsPerRound = 1;
-template <int NMAX>
-__global__ void __launch_bounds__(256, 2) enc_qk45_kernel(EncArgs a) {
-    constexpr int BB = NMAX == 31 ? 176 : 144;
+// make_qkx3_quants over a whole super-block per warp, with duplicate grids
+// skipped.  For u = x - vmin >= 0 the grid scales iscale_j = (rmin + rdelta*j
+// + nmax)/(vmax - vmin) are non-decreasing in j (each rounded step is
+// monotone), so every level l_i(j) = min(round(iscale_j * u_i), nmax) is
+// non-decreasing in j, and the level vector of grid j equals that of grid
+// j-1 unless some element crosses a rounding threshold k - 1/2 between them.
+// Equal level vectors give equal sums, (scale, min) and error, so such a
+// grid never replaces the earlier one under the reference's strict `<`
+// (quant.rs:129): only the first grid of each run of equal level vectors is
+// evaluated.  y_36 - y_0 = 1.8 u / (vmax - vmin) <= 1.8 (plus rounding), so
+// an element crosses at most two thresholds; each crossing grid is found by
+// a binary search on y_j = iscale_j * u >= k - 1/2 (round half away from zero
+// of y >= 0 is floor(y + 1/2)).  Sub-blocks with a non-finite range or
+// scale evaluate every grid.
+//
+// The distinct (sub-block, grid) jobs of the warp's super-block, plus each
+// sub-block's initial nmax/(vmax-vmin) grid, are listed in shared memory in
+// (sub-block, grid) order and dealt to the 32 lanes round by round; a
+// sub-block's best (error, grid) is kept with a 64-bit shared-memory
+// atomicMin on (order-preserving error bits, grid), which keeps the first
+// minimum as the reference's chain does.
+template <int N>
+struct __align__(16) Qkx3Warp {
+    static constexpr int LPS = N / 8;    // lanes per sub-block (8 elements each)
+    static constexpr int NSB = 256 / N;  // sub-blocks per super-block
+    static constexpr int PAD = N + 4;    // float stride of a staged sub-block
+    float4 par[NSB];                     // sum_w, sum_x, vmin, nmax/(vmax-vmin)
+    float nx[NSB * PAD];                 // -x
+    float w[NSB * PAD];                  // element weights
+    float u[NSB * PAD];                  // -(x - vmin)
+    float isc[NSB][40];                  // iscale of grids 0..36
+    float ts[NSB][38];                   // (scale, min) of evaluated grids
+    float tm[NSB][38];
+    float init_err[NSB];
+    float2 par2[NSB];                    // 1/iscale0, clean
+    unsigned long long best[NSB];
+    uint16_t jobs[NSB * 38];             // (sub-block << 8) | grid
+    uint8_t out[176];
+    uint8_t l[256];
+};
+
+__device__ __forceinline__ unsigned int err_key(float e) {
+    const unsigned int b = __float_as_uint(e);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float err_from_key(unsigned int k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+// First grid j in [1, 36] with iscale_j * u >= thr, given that grid 0 is
+// below and grid 36 at or above the threshold (y_j is non-decreasing in j).
+// z estimates the answer from iscale_j ~ (nmax - 0.9 + 0.05 j)/range; the
+// three grids around it are evaluated exactly and decide when the estimate
+// is within one grid, otherwise a binary search over the table does.
+__device__ __forceinline__ int crossing_grid(const float *tab, float u, float thr, float z) {
+    const int je = min(max(__float2int_ru(z), 1), 35);
+    const bool p0 = __fmul_rn(tab[je - 1], u) >= thr;
+    const bool p1 = __fmul_rn(tab[je], u) >= thr;
+    const bool p2 = __fmul_rn(tab[je + 1], u) >= thr;
+    if (!p0 && p2) return p1 ? je : je + 1;
+    if (p0 && je >= 2 && !(__fmul_rn(tab[je - 2], u) >= thr)) return je - 1;
+    int lo = 0, hi = 36;
+#pragma unroll 1
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (__fmul_rn(tab[mid], u) >= thr) hi = mid;
+        else lo = mid;
+    }
+    return hi;
+}
+
+template <int N, int NMAX>
+__device__ __forceinline__ void qkx3_super_blocks(const EncArgs &a, Qkx3Warp<N> *W) {
+    using Wp = Qkx3Warp<N>;
+    constexpr int LPS = Wp::LPS, PAD = Wp::PAD;
     constexpr float FN = (float)NMAX;
-    // per warp: 8 sub-blocks of 32, padded to 36 floats so that the eight
-    // 16-byte reads of one instruction fall in distinct bank groups
-    __shared__ __align__(16) float s_nx[8][8 * 36];
-    __shared__ __align__(16) float s_w[8][8 * 36];
-    __shared__ __align__(16) float s_u[8][8 * 36];
-    __shared__ __align__(16) uint8_t s_out[8][BB];
-    __shared__ uint8_t s_l[8][256];
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    const int s = lane >> 2, q = lane & 3;
+    constexpr bool Q2 = N == 16;
+    constexpr int BB = Q2 ? 84 : (NMAX == 31 ? 176 : 144);
+    const int lane = threadIdx.x & 31;
+    const int s = lane / LPS, q = lane % LPS;
     const int64_t ne0 = a.src.ne0, nsb = ne0 >> 8, total = a.n_rows * nsb;
-    float *snx = &s_nx[wid][s * 36];
-    float *sw = &s_w[wid][s * 36];
-    float *su = &s_u[wid][s * 36];
-    for (int64_t g = (int64_t)blockIdx.x * 8 + wid; g < total; g += (int64_t)gridDim.x * 8) {
+    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    float *snx = &W->nx[s * PAD];
+    float *sw = &W->w[s * PAD];
+    float *su = &W->u[s * PAD];
+    for (int64_t g = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); g < total; g += nwarps) {
         const int64_t row = g / nsb;
         const int64_t sbi = g - row * nsb;
         const int64_t col0 = sbi << 8;
@@ -517,430 +580,273 @@ __global__ void __launch_bounds__(256, 2) enc_qk45_kernel(EncArgs a) {
             pw[1] = make_float4(wk[4], wk[5], wk[6], wk[7]);
         }
         // vmin/vmax folds (quant.rs:87-88) are order-independent (NaN is
-        // skipped): this lane's 8 values, then the 4 lanes of the sub-block.
-        // The sign of a zero vmin/vmax never reaches Q4_K/Q5_K bytes (it
-        // only enters x - vmin, scale*l + vmin, and -vmin folded with +0 by max).
+        // skipped): this lane's 8 values, then the lanes of the sub-block.
+        // The sign of a zero vmin/vmax never reaches the bytes (it only
+        // enters x - vmin, scale*l + vmin, and -vmin folded with +0 by max).
         float vmin, vmax;
         {
             float mn = fminf(fminf(fminf(v[0], v[1]), fminf(v[2], v[3])), fminf(fminf(v[4], v[5]), fminf(v[6], v[7])));
             float mx = fmaxf(fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3])), fmaxf(fmaxf(v[4], v[5]), fmaxf(v[6], v[7])));
-            mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, 1));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-            mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, 2));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+#pragma unroll
+            for (int off = 1; off < LPS; off <<= 1) {
+                mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            }
             vmin = fminf(fminf(INFINITY, mn), 0.0f);
             vmax = fmaxf(-INFINITY, mx);
         }
-        // u = nx + vmin = -(x - vmin): the same rounded value for every grid
+        const bool degen = vmax <= vmin;
+        const float range = vmax - vmin;
         {
+            // u = nx + vmin = -(x - vmin): the same rounded value for every grid
             float4 *pu = reinterpret_cast<float4 *>(su + q * 8);
             pu[0] = make_float4(__fadd_rn(-v[0], vmin), __fadd_rn(-v[1], vmin), __fadd_rn(-v[2], vmin),
                                 __fadd_rn(-v[3], vmin));
             pu[1] = make_float4(__fadd_rn(-v[4], vmin), __fadd_rn(-v[5], vmin), __fadd_rn(-v[6], vmin),
                                 __fadd_rn(-v[7], vmin));
+            // iscale of the 37 grids (quant.rs:108), split over the sub-block's lanes
+            for (int j = q; j < 37; j += LPS) W->isc[s][j] = (-0.9f + 0.05f * (float)j + FN) / range;
         }
         __syncwarp();
-        // Shuffles below run on every lane, so the per-lane candidate loop
-        // is the only code inside the data-dependent branch.
-        const bool degen = vmax <= vmin;
-        const float range = vmax - vmin;
         const float iscale0 = FN / range;
         const float scale0 = 1.0f / iscale0;
-        float init_err = 0.0f, best_e = 0.0f, best_s = 0.0f, best_m = 0.0f;
-        int best_j = -1;
+        const bool clean = !degen && range < INFINITY && W->isc[s][36] < INFINITY;
+        // grids whose level vector differs from the previous grid's
+        unsigned long long mask = 0;
         if (!degen) {
-            float sum_w = 0.0f, sum_x = 0.0f;
-#pragma unroll
-            for (int c = 0; c < 8; c++) {
-                const float4 n4 = reinterpret_cast<const float4 *>(snx)[c];
-                const float4 w4 = reinterpret_cast<const float4 *>(sw)[c];
-                const float2 a = __fmul2_rn(make_float2(w4.x, w4.y), make_float2(n4.x, n4.y));
-                const float2 b = __fmul2_rn(make_float2(w4.z, w4.w), make_float2(n4.z, n4.w));
-                sum_w = __fadd_rn(sum_w, w4.x);
-                sum_x = __fsub_rn(sum_x, a.x);
-                sum_w = __fadd_rn(sum_w, w4.y);
-                sum_x = __fsub_rn(sum_x, a.y);
-                sum_w = __fadd_rn(sum_w, w4.z);
-                sum_x = __fsub_rn(sum_x, b.x);
-                sum_w = __fadd_rn(sum_w, w4.w);
-                sum_x = __fsub_rn(sum_x, b.y);
-            }
-            const bool range_finite = range < INFINITY;
-            // lane q takes jobs q, q+4, ..., two per round in increasing order,
-            // so the strict `<` below keeps the first minimum as the reference's
-            // chain does; jobs 38 and 39 (lanes 2 and 3, last round) are padding
-            constexpr int NG = kQk45GridsPerRound;
+            if (clean) {
+                const float *tab = W->isc[s];
+                const float i0 = tab[0], i36 = tab[36];
 #pragma unroll 1
-            for (int r = 0; r < 10 / NG; r++) {
-                const int j0 = q + 4 * NG * r;
-                float isc[NG];
+                for (int k = 0; k < 8; k++) {
+                    const float uk = -su[q * 8 + k];  // x - vmin
+                    const float l0 = fminf(floor_half_up(__fmul_rn(i0, uk)), FN);
+                    const float l36 = fminf(floor_half_up(__fmul_rn(i36, uk)), FN);
+                    if (l36 > l0) {
+                        const float ru = __fdividef(range, uk);  // an estimate only: verified below
 #pragma unroll
-                for (int g = 0; g < NG; g++) {
-                    const int j = j0 + 4 * g;
-                    isc[g] = j == 37 ? iscale0 : (-0.9f + 0.05f * (float)j + FN) / range;
-                }
-                float sl[NG], sl2[NG], sxl[NG];
-                float2 l[NG][16];
-                bool clean = range_finite;
-#pragma unroll
-                for (int g = 0; g < NG; g++) clean = clean && isc[g] < INFINITY;
-                if (clean) qkx3_grids<true, NG, 16>(snx, sw, su, isc, FN, l, sl, sl2, sxl);
-                else qkx3_grids<false, NG, 16>(snx, sw, su, isc, FN, l, sl, sl2, sxl);
-                float ts[NG], tm[NG];
-                bool valid[NG];
-#pragma unroll
-                for (int g = 0; g < NG; g++) {
-                    if (j0 + 4 * g == 37) {
-                        ts[g] = scale0;
-                        tm[g] = vmin;
-                        valid[g] = true;
-                    } else {
-                        const float D = __fsub_rn(__fmul_rn(sum_w, sl2[g]), __fmul_rn(sl[g], sl[g]));
-                        valid[g] = D > 0.0f;
-                        ts[g] = __fsub_rn(__fmul_rn(sum_w, sxl[g]), __fmul_rn(sum_x, sl[g])) / D;
-                        tm[g] = __fsub_rn(__fmul_rn(sl2[g], sum_x), __fmul_rn(sl[g], sxl[g])) / D;
-                        if (tm[g] > 0.0f) {
-                            tm[g] = 0.0f;
-                            ts[g] = sl2[g] > 0.0f ? sxl[g] / sl2[g] : 0.0f;
+                        for (int c = 1; c <= 2; c++) {
+                            const float kk = l0 + (float)c;
+                            if (kk <= l36) {
+                                const float thr = kk - 0.5f;
+                                mask |= 1ull << crossing_grid(tab, uk, thr, 20.0f * (thr * ru - (FN - 0.9f)));
+                            }
                         }
                     }
                 }
-                float err[NG];
-                qkx3_errors<NG, 16>(snx, sw, l, ts, tm, err);
+                mask |= 1ull;
+            } else {
+                mask = (1ull << 37) - 1;
+            }
+            mask |= 1ull << 37;  // the initial grid
+        }
 #pragma unroll
-                for (int g = 0; g < NG; g++) {
-                    const int j = j0 + 4 * g;
-                    if (j >= 38 || !valid[g]) continue;
-                    if (j == 37) {
-                        init_err = err[g];
-                    } else if (err[g] == err[g] && (best_j < 0 || err[g] < best_e)) {
-                        best_e = err[g];
-                        best_j = j;
-                        best_s = ts[g];
-                        best_m = tm[g];
-                    }
+        for (int off = 1; off < LPS; off <<= 1) mask |= __shfl_xor_sync(0xffffffffu, mask, off);
+        // job list: exclusive prefix of the sub-blocks' job counts; lane q of
+        // a sub-block lists the grids among bits [q*B, q*B + B) of its mask
+        const int cnt = __popcll(mask);
+        int incl = q == 0 ? cnt : 0;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, incl, off);
+            if (lane >= off) incl += t;
+        }
+        const int njobs = __shfl_sync(0xffffffffu, incl, 31);
+        {
+            constexpr int B = (38 + LPS - 1) / LPS;
+            const int lo_bit = q * B;
+            int pos = __shfl_sync(0xffffffffu, incl, lane - q) - cnt + __popcll(mask & ((1ull << lo_bit) - 1));
+            unsigned int bits = (unsigned int)((mask >> lo_bit) & ((1ull << B) - 1));
+            while (bits != 0) {
+                W->jobs[pos++] = (uint16_t)((s << 8) | (lo_bit + __ffs(bits) - 1));
+                bits &= bits - 1;
+            }
+        }
+        float sum_w = 0.0f, sum_x = 0.0f;
+        if (!degen) {
+#pragma unroll
+            for (int c = 0; c < N / 4; c++) {
+                const float4 n4 = reinterpret_cast<const float4 *>(snx)[c];
+                const float4 w4 = reinterpret_cast<const float4 *>(sw)[c];
+                const float2 p0 = __fmul2_rn(make_float2(w4.x, w4.y), make_float2(n4.x, n4.y));
+                const float2 p1 = __fmul2_rn(make_float2(w4.z, w4.w), make_float2(n4.z, n4.w));
+                sum_w = __fadd_rn(sum_w, w4.x);
+                sum_x = __fsub_rn(sum_x, p0.x);
+                sum_w = __fadd_rn(sum_w, w4.y);
+                sum_x = __fsub_rn(sum_x, p0.y);
+                sum_w = __fadd_rn(sum_w, w4.z);
+                sum_x = __fsub_rn(sum_x, p1.x);
+                sum_w = __fadd_rn(sum_w, w4.w);
+                sum_x = __fsub_rn(sum_x, p1.y);
+            }
+        }
+        if (q == 0) {
+            W->par[s] = make_float4(sum_w, sum_x, vmin, iscale0);
+            W->par2[s] = make_float2(scale0, clean ? 1.0f : 0.0f);
+            W->best[s] = ~0ull;
+        }
+        __syncwarp();
+        // evaluate the listed grids (quant.rs:109-135), one per lane per round
+#pragma unroll 1
+        for (int t = lane; t < njobs; t += 32) {
+            const int code = W->jobs[t];
+            const int js = code >> 8, j = code & 0xFF;
+            const float4 pa = W->par[js];
+            const float2 pb = W->par2[js];
+            const float *jnx = &W->nx[js * PAD], *jw = &W->w[js * PAD], *ju = &W->u[js * PAD];
+            float isc[1] = {j == 37 ? pa.w : W->isc[js][j]};
+            float sl[1], sl2[1], sxl[1];
+            float2 l[1][N / 2];
+            if (pb.y != 0.0f) qkx3_grids<true, 1, N / 2>(jnx, jw, ju, isc, FN, l, sl, sl2, sxl);
+            else qkx3_grids<false, 1, N / 2>(jnx, jw, ju, isc, FN, l, sl, sl2, sxl);
+            float ts[1], tm[1];
+            bool valid = true;
+            if (j == 37) {
+                ts[0] = pb.x;
+                tm[0] = pa.z;
+            } else {
+                const float D = __fsub_rn(__fmul_rn(pa.x, sl2[0]), __fmul_rn(sl[0], sl[0]));
+                valid = D > 0.0f;
+                ts[0] = __fsub_rn(__fmul_rn(pa.x, sxl[0]), __fmul_rn(pa.y, sl[0])) / D;
+                tm[0] = __fsub_rn(__fmul_rn(sl2[0], pa.y), __fmul_rn(sl[0], sxl[0])) / D;
+                if (tm[0] > 0.0f) {
+                    tm[0] = 0.0f;
+                    ts[0] = sl2[0] > 0.0f ? sxl[0] / sl2[0] : 0.0f;
                 }
+            }
+            float err[1];
+            qkx3_errors<1, N / 2>(jnx, jw, l, ts, tm, err);
+            if (j == 37) {
+                W->init_err[js] = err[0];
+            } else if (valid && err[0] == err[0]) {
+                W->ts[js][j] = ts[0];
+                W->tm[js][j] = tm[0];
+                atomicMin(&W->best[js], ((unsigned long long)err_key(err[0]) << 32) | (unsigned)j);
             }
         }
         __syncwarp();
-        // argmin (err, j) over the four lanes of this sub-block
-#pragma unroll
-        for (int off = 1; off <= 2; off <<= 1) {
-            const float oe = __shfl_xor_sync(0xffffffffu, best_e, off);
-            const int oj = __shfl_xor_sync(0xffffffffu, best_j, off);
-            const float os = __shfl_xor_sync(0xffffffffu, best_s, off);
-            const float om = __shfl_xor_sync(0xffffffffu, best_m, off);
-            if (oj >= 0 && (best_j < 0 || oe < best_e || (oe == best_e && oj < best_j))) {
-                best_e = oe;
-                best_j = oj;
-                best_s = os;
-                best_m = om;
-            }
-        }
-        init_err = __shfl_sync(0xffffffffu, init_err, (lane & ~3) | 1);
         float scale, mn;
-        if (degen) {
-            scale = 0.0f;
-            mn = vmin;
-        } else if (best_j >= 0 && best_e < init_err) {
-            scale = best_s;
-            mn = best_m;
-        } else {
-            scale = scale0;
-            mn = vmin;
+        {
+            const unsigned long long bk = W->best[s];
+            const int best_j = bk == ~0ull ? -1 : (int)(bk & 0xFFu);
+            if (degen) {
+                scale = 0.0f;
+                mn = vmin;
+            } else if (best_j >= 0 && err_from_key((unsigned)(bk >> 32)) < W->init_err[s]) {
+                scale = W->ts[s][best_j];
+                mn = W->tm[s][best_j];
+            } else {
+                scale = scale0;
+                mn = vmin;
+            }
         }
         const float mins_s = -mn;
         float max_scale = scale, max_min = mins_s;
 #pragma unroll
-        for (int off = 4; off <= 16; off <<= 1) {
+        for (int off = LPS; off <= 16; off <<= 1) {
             max_scale = rmaxf(max_scale, __shfl_xor_sync(0xffffffffu, max_scale, off));
             max_min = rmaxf(max_min, __shfl_xor_sync(0xffffffffu, max_min, off));
         }
         max_scale = rmaxf(0.0f, max_scale);
         max_min = rmaxf(0.0f, max_min);
-        const float inv_scale = max_scale > 0.0f ? 63.0f / max_scale : 0.0f;
-        const float inv_min = max_min > 0.0f ? 63.0f / max_min : 0.0f;
-        const int lsq = (int)round_clamp0_f(inv_scale * scale, 63.0f);
-        const int lmq = (int)round_clamp0_f(inv_min * mins_s, 63.0f);
-        const float d = max_scale / 63.0f;
-        const float dmin = max_min / 63.0f;
+        constexpr float QS = Q2 ? 15.0f : 63.0f;  // scale/min code range
+        const float inv_scale = max_scale > 0.0f ? QS / max_scale : 0.0f;
+        const float inv_min = max_min > 0.0f ? QS / max_min : 0.0f;
+        const int lsq = (int)round_clamp0_f(inv_scale * scale, QS);
+        const int lmq = (int)round_clamp0_f(inv_min * mins_s, QS);
+        const float d = max_scale / QS;
+        const float dmin = max_min / QS;
         const float dsub = d * (float)lsq;
         const float msub = dmin * (float)lmq;
 #pragma unroll
         for (int k = 0; k < 8; k++) {
             // (x + msub) = (msub - nx); x re-read from shared memory
             const int l = dsub == 0.0f ? 0 : (int)round_clamp0_f(__fsub_rn(msub, snx[q * 8 + k]) / dsub, FN);
-            s_l[wid][lane * 8 + k] = (uint8_t)l;
+            W->l[lane * 8 + k] = (uint8_t)l;
         }
-        // 6-bit scale/min packing (quant.rs:316-327): lane t < 4 writes bytes
-        // t, t+4, t+8 of the 12 from sub-blocks t and t+4
-        uint8_t *o = s_out[wid];
-        {
-            const int t = lane & 3;
-            const int ls_a = __shfl_sync(0xffffffffu, lsq, t * 4), ls_b = __shfl_sync(0xffffffffu, lsq, t * 4 + 16);
-            const int lm_a = __shfl_sync(0xffffffffu, lmq, t * 4), lm_b = __shfl_sync(0xffffffffu, lmq, t * 4 + 16);
-            if (lane < 4) {
-                o[4 + t] = (uint8_t)(ls_a | ((ls_b >> 4) << 6));
-                o[8 + t] = (uint8_t)(lm_a | ((lm_b >> 4) << 6));
-                o[12 + t] = (uint8_t)((ls_b & 0xF) | ((lm_b & 0xF) << 4));
+        uint8_t *o = W->out;
+        const uint8_t *L = W->l;
+        if (Q2) {
+            // Q2_K: 4-bit scale | min << 4 per sub-block, d/dmin f16 at 80/82
+            if (q == 0) o[s] = (uint8_t)(lsq | (lmq << 4));
+            if (lane == 0) {
+                const uint16_t hd = f16_bits(d), hm = f16_bits(dmin);
+                o[80] = (uint8_t)(hd & 0xFF);
+                o[81] = (uint8_t)(hd >> 8);
+                o[82] = (uint8_t)(hm & 0xFF);
+                o[83] = (uint8_t)(hm >> 8);
             }
-        }
-        if (lane == 0) {
-            const uint16_t hd = f16_bits(d), hm = f16_bits(dmin);
-            o[0] = (uint8_t)(hd & 0xFF);
-            o[1] = (uint8_t)(hd >> 8);
-            o[2] = (uint8_t)(hm & 0xFF);
-            o[3] = (uint8_t)(hm >> 8);
-        }
-        __syncwarp();
-        const uint8_t *L = s_l[wid];
-        if (NMAX == 31) {
-            uint8_t qh = 0;
+            __syncwarp();
 #pragma unroll
-            for (int chunk = 0; chunk < 4; chunk++) {
-                if (L[chunk * 64 + lane] >= 16) qh |= (uint8_t)(1u << (chunk * 2));
-                if (L[chunk * 64 + 32 + lane] >= 16) qh |= (uint8_t)(2u << (chunk * 2));
-            }
-            o[16 + lane] = qh;
+            for (int h = 0; h < 2; h++) {  // qs byte h*32 + lane: elements h*128 + j*32 + lane at bits 2j
+                uint8_t b = 0;
 #pragma unroll
-            for (int t = 0; t < 4; t++) {
-                const int b = lane * 4 + t, chunk = b >> 5, l = b & 31;
-                o[48 + b] = (uint8_t)((L[chunk * 64 + l] & 0xF) | ((L[chunk * 64 + 32 + l] & 0xF) << 4));
+                for (int j = 0; j < 4; j++) b |= (uint8_t)(L[h * 128 + j * 32 + lane] << (2 * j));
+                o[16 + h * 32 + lane] = b;
             }
         } else {
+            // 6-bit scale/min packing (quant.rs:316-327): lane t < 4 writes bytes
+            // t, t+4, t+8 of the 12 from sub-blocks t and t+4
+            {
+                const int t = lane & 3;
+                const int ls_a = __shfl_sync(0xffffffffu, lsq, t * 4), ls_b = __shfl_sync(0xffffffffu, lsq, t * 4 + 16);
+                const int lm_a = __shfl_sync(0xffffffffu, lmq, t * 4), lm_b = __shfl_sync(0xffffffffu, lmq, t * 4 + 16);
+                if (lane < 4) {
+                    o[4 + t] = (uint8_t)(ls_a | ((ls_b >> 4) << 6));
+                    o[8 + t] = (uint8_t)(lm_a | ((lm_b >> 4) << 6));
+                    o[12 + t] = (uint8_t)((ls_b & 0xF) | ((lm_b & 0xF) << 4));
+                }
+            }
+            if (lane == 0) {
+                const uint16_t hd = f16_bits(d), hm = f16_bits(dmin);
+                o[0] = (uint8_t)(hd & 0xFF);
+                o[1] = (uint8_t)(hd >> 8);
+                o[2] = (uint8_t)(hm & 0xFF);
+                o[3] = (uint8_t)(hm >> 8);
+            }
+            __syncwarp();
+            if (NMAX == 31) {
+                uint8_t qh = 0;
 #pragma unroll
-            for (int t = 0; t < 4; t++) {
-                const int b = lane * 4 + t, chunk = b >> 5, l = b & 31;
-                o[16 + b] = (uint8_t)((L[chunk * 64 + l] & 0xF) | (L[chunk * 64 + 32 + l] << 4));
+                for (int chunk = 0; chunk < 4; chunk++) {
+                    if (L[chunk * 64 + lane] >= 16) qh |= (uint8_t)(1u << (chunk * 2));
+                    if (L[chunk * 64 + 32 + lane] >= 16) qh |= (uint8_t)(2u << (chunk * 2));
+                }
+                o[16 + lane] = qh;
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+                    const int b = lane * 4 + t, chunk = b >> 5, l = b & 31;
+                    o[48 + b] = (uint8_t)((L[chunk * 64 + l] & 0xF) | ((L[chunk * 64 + 32 + l] & 0xF) << 4));
+                }
+            } else {
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+                    const int b = lane * 4 + t, chunk = b >> 5, l = b & 31;
+                    o[16 + b] = (uint8_t)((L[chunk * 64 + l] & 0xF) | (L[chunk * 64 + 32 + l] << 4));
+                }
             }
         }
         __syncwarp();
-        store_block(a.dst + row * a.dst_row_bytes + sbi * BB, o, BB, a.dst_aligned16 != 0, lane);
+        store_block(a.dst + row * a.dst_row_bytes + sbi * BB, o, BB, !Q2 && a.dst_aligned16 != 0, lane);
         __syncwarp();
     }
 }
 
+constexpr int kQkx3Warps = 8;
+template <int NMAX>
+__global__ void __launch_bounds__(256, 2) enc_qk45_kernel(EncArgs a) {
+    extern __shared__ __align__(16) uint8_t qkx3_smem[];
+    qkx3_super_blocks<32, NMAX>(a, reinterpret_cast<Qkx3Warp<32> *>(qkx3_smem) + (threadIdx.x >> 5));
+}
 template __global__ void enc_qk45_kernel<15>(EncArgs);
 template __global__ void enc_qk45_kernel<31>(EncArgs);
 
-// ---------------------------------------------------------------------------
 // Q2_K (ggml block_q2_K layout): make_qkx3_quants (quant.rs:77-141, nmax 3,
 // rmin -0.9, rdelta 0.05, 37 grids) per 16-element sub-block, 4-bit scale and
 // min codes against the super-block's largest scale and min, 2-bit levels.
-// Two lanes per sub-block: lane q evaluates jobs j = q, q+2, ..., j < 38
-// (j == 37, on the odd lane, is the initial nmax/(vmax-vmin) grid), two jobs
-// per round; the search arithmetic is the Q4_K/Q5_K kernel's on 8 pairs.
-// ---------------------------------------------------------------------------
-constexpr int kQ2kGridsPerRound = 2;
 __global__ void __launch_bounds__(256, 2) enc_q2_k_kernel(EncArgs a) {
-    constexpr float FN = 3.0f;
-    // per warp: 16 sub-blocks of 16, padded to 20 floats (the 16 distinct
-    // 16-byte reads of one instruction cover the 32 banks twice)
-    __shared__ __align__(16) float s_nx[8][16 * 20];
-    __shared__ __align__(16) float s_w[8][16 * 20];
-    __shared__ __align__(16) float s_u[8][16 * 20];
-    __shared__ __align__(16) uint8_t s_out[8][96];
-    __shared__ uint8_t s_l[8][256];
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    const int s = lane >> 1, q = lane & 1;
-    const int64_t ne0 = a.src.ne0, nsb = ne0 >> 8, total = a.n_rows * nsb;
-    float *snx = &s_nx[wid][s * 20];
-    float *sw = &s_w[wid][s * 20];
-    float *su = &s_u[wid][s * 20];
-    for (int64_t g = (int64_t)blockIdx.x * 8 + wid; g < total; g += (int64_t)gridDim.x * 8) {
-        const int64_t row = g / nsb;
-        const int64_t sbi = g - row * nsb;
-        const int64_t col0 = sbi << 8;
-        const float sig = a.sigma2[row];
-        const float *imr = im_row(a.im, ne0, a.row0 + row * a.row_step);
-        float v[8], base[8];
-        load8(a.src, row, col0 + lane * 8, v);
-        load_im8(imr, col0 + lane * 8, base);
-        {
-            float wk[8];
-#pragma unroll
-            for (int k = 0; k < 8; k += 2) {
-                const float2 vv = make_float2(v[k], v[k + 1]);
-                const float2 vv2 = __fmul2_rn(vv, vv);
-                const float2 sq = make_float2(sqrtf(__fadd_rn(sig, vv2.x)), sqrtf(__fadd_rn(sig, vv2.y)));
-                const float2 ww = __fmul2_rn(make_float2(base[k], base[k + 1]), sq);
-                wk[k] = ww.x;
-                wk[k + 1] = ww.y;
-            }
-            float4 *pn = reinterpret_cast<float4 *>(snx + q * 8);
-            float4 *pw = reinterpret_cast<float4 *>(sw + q * 8);
-            pn[0] = make_float4(-v[0], -v[1], -v[2], -v[3]);
-            pn[1] = make_float4(-v[4], -v[5], -v[6], -v[7]);
-            pw[0] = make_float4(wk[0], wk[1], wk[2], wk[3]);
-            pw[1] = make_float4(wk[4], wk[5], wk[6], wk[7]);
-        }
-        float vmin, vmax;
-        {
-            float mn = fminf(fminf(fminf(v[0], v[1]), fminf(v[2], v[3])), fminf(fminf(v[4], v[5]), fminf(v[6], v[7])));
-            float mx = fmaxf(fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3])), fmaxf(fmaxf(v[4], v[5]), fmaxf(v[6], v[7])));
-            mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, 1));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-            vmin = fminf(fminf(INFINITY, mn), 0.0f);
-            vmax = fmaxf(-INFINITY, mx);
-        }
-        {
-            float4 *pu = reinterpret_cast<float4 *>(su + q * 8);
-            pu[0] = make_float4(__fadd_rn(-v[0], vmin), __fadd_rn(-v[1], vmin), __fadd_rn(-v[2], vmin),
-                                __fadd_rn(-v[3], vmin));
-            pu[1] = make_float4(__fadd_rn(-v[4], vmin), __fadd_rn(-v[5], vmin), __fadd_rn(-v[6], vmin),
-                                __fadd_rn(-v[7], vmin));
-        }
-        __syncwarp();
-        const bool degen = vmax <= vmin;
-        const float range = vmax - vmin;
-        const float iscale0 = FN / range;
-        const float scale0 = 1.0f / iscale0;
-        float init_err = 0.0f, best_e = 0.0f, best_s = 0.0f, best_m = 0.0f;
-        int best_j = -1;
-        if (!degen) {
-            float sum_w = 0.0f, sum_x = 0.0f;
-#pragma unroll
-            for (int c = 0; c < 4; c++) {
-                const float4 n4 = reinterpret_cast<const float4 *>(snx)[c];
-                const float4 w4 = reinterpret_cast<const float4 *>(sw)[c];
-                const float2 a = __fmul2_rn(make_float2(w4.x, w4.y), make_float2(n4.x, n4.y));
-                const float2 b = __fmul2_rn(make_float2(w4.z, w4.w), make_float2(n4.z, n4.w));
-                sum_w = __fadd_rn(sum_w, w4.x);
-                sum_x = __fsub_rn(sum_x, a.x);
-                sum_w = __fadd_rn(sum_w, w4.y);
-                sum_x = __fsub_rn(sum_x, a.y);
-                sum_w = __fadd_rn(sum_w, w4.z);
-                sum_x = __fsub_rn(sum_x, b.x);
-                sum_w = __fadd_rn(sum_w, w4.w);
-                sum_x = __fsub_rn(sum_x, b.y);
-            }
-            const bool range_finite = range < INFINITY;
-            // lane q takes jobs q + 2k in increasing order, NG per round, so
-            // the strict `<` keeps the first minimum as the reference's chain
-            // does; jobs 38 and 39 (last round) are padding
-            constexpr int NG = kQ2kGridsPerRound;
-#pragma unroll 1
-            for (int r = 0; r < 20 / NG; r++) {
-                const int j0 = q + 2 * NG * r;
-                float isc[NG];
-#pragma unroll
-                for (int g = 0; g < NG; g++) {
-                    const int j = j0 + 2 * g;
-                    isc[g] = j == 37 ? iscale0 : (-0.9f + 0.05f * (float)j + FN) / range;
-                }
-                float sl[NG], sl2[NG], sxl[NG];
-                float2 l[NG][8];
-                bool clean = range_finite;
-#pragma unroll
-                for (int g = 0; g < NG; g++) clean = clean && isc[g] < INFINITY;
-                if (clean) qkx3_grids<true, NG, 8>(snx, sw, su, isc, FN, l, sl, sl2, sxl);
-                else qkx3_grids<false, NG, 8>(snx, sw, su, isc, FN, l, sl, sl2, sxl);
-                float ts[NG], tm[NG];
-                bool valid[NG];
-#pragma unroll
-                for (int g = 0; g < NG; g++) {
-                    if (j0 + 2 * g == 37) {
-                        ts[g] = scale0;
-                        tm[g] = vmin;
-                        valid[g] = true;
-                    } else {
-                        const float D = __fsub_rn(__fmul_rn(sum_w, sl2[g]), __fmul_rn(sl[g], sl[g]));
-                        valid[g] = D > 0.0f;
-                        ts[g] = __fsub_rn(__fmul_rn(sum_w, sxl[g]), __fmul_rn(sum_x, sl[g])) / D;
-                        tm[g] = __fsub_rn(__fmul_rn(sl2[g], sum_x), __fmul_rn(sl[g], sxl[g])) / D;
-                        if (tm[g] > 0.0f) {
-                            tm[g] = 0.0f;
-                            ts[g] = sl2[g] > 0.0f ? sxl[g] / sl2[g] : 0.0f;
-                        }
-                    }
-                }
-                float err[NG];
-                qkx3_errors<NG, 8>(snx, sw, l, ts, tm, err);
-#pragma unroll
-                for (int g = 0; g < NG; g++) {
-                    const int j = j0 + 2 * g;
-                    if (j >= 38 || !valid[g]) continue;
-                    if (j == 37) {
-                        init_err = err[g];
-                    } else if (err[g] == err[g] && (best_j < 0 || err[g] < best_e)) {
-                        best_e = err[g];
-                        best_j = j;
-                        best_s = ts[g];
-                        best_m = tm[g];
-                    }
-                }
-            }
-        }
-        __syncwarp();
-        {  // argmin (err, j) over the lane pair
-            const float oe = __shfl_xor_sync(0xffffffffu, best_e, 1);
-            const int oj = __shfl_xor_sync(0xffffffffu, best_j, 1);
-            const float os = __shfl_xor_sync(0xffffffffu, best_s, 1);
-            const float om = __shfl_xor_sync(0xffffffffu, best_m, 1);
-            if (oj >= 0 && (best_j < 0 || oe < best_e || (oe == best_e && oj < best_j))) {
-                best_e = oe;
-                best_j = oj;
-                best_s = os;
-                best_m = om;
-            }
-        }
-        init_err = __shfl_sync(0xffffffffu, init_err, lane | 1);
-        float scale, mn;
-        if (degen) {
-            scale = 0.0f;
-            mn = vmin;
-        } else if (best_j >= 0 && best_e < init_err) {
-            scale = best_s;
-            mn = best_m;
-        } else {
-            scale = scale0;
-            mn = vmin;
-        }
-        const float mins_s = -mn;
-        float max_scale = scale, max_min = mins_s;
-#pragma unroll
-        for (int off = 2; off <= 16; off <<= 1) {
-            max_scale = rmaxf(max_scale, __shfl_xor_sync(0xffffffffu, max_scale, off));
-            max_min = rmaxf(max_min, __shfl_xor_sync(0xffffffffu, max_min, off));
-        }
-        max_scale = rmaxf(0.0f, max_scale);
-        max_min = rmaxf(0.0f, max_min);
-        const float inv_scale = max_scale > 0.0f ? 15.0f / max_scale : 0.0f;
-        const float inv_min = max_min > 0.0f ? 15.0f / max_min : 0.0f;
-        const int lsq = (int)round_clamp0_f(inv_scale * scale, 15.0f);
-        const int lmq = (int)round_clamp0_f(inv_min * mins_s, 15.0f);
-        const float d = max_scale / 15.0f;
-        const float dmin = max_min / 15.0f;
-        const float dsub = d * (float)lsq;
-        const float msub = dmin * (float)lmq;
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-            // (x + msub) = (msub - nx)
-            const int l = dsub == 0.0f ? 0 : (int)round_clamp0_f(__fsub_rn(msub, snx[q * 8 + k]) / dsub, FN);
-            s_l[wid][lane * 8 + k] = (uint8_t)l;
-        }
-        uint8_t *o = s_out[wid];
-        if (q == 0) o[s] = (uint8_t)(lsq | (lmq << 4));
-        if (lane == 0) {
-            const uint16_t hd = f16_bits(d), hm = f16_bits(dmin);
-            o[80] = (uint8_t)(hd & 0xFF);
-            o[81] = (uint8_t)(hd >> 8);
-            o[82] = (uint8_t)(hm & 0xFF);
-            o[83] = (uint8_t)(hm >> 8);
-        }
-        __syncwarp();
-        const uint8_t *L = s_l[wid];
-#pragma unroll
-        for (int h = 0; h < 2; h++) {  // qs byte h*32 + lane: elements h*128 + j*32 + lane at bits 2j
-            uint8_t b = 0;
-#pragma unroll
-            for (int j = 0; j < 4; j++) b |= (uint8_t)(L[h * 128 + j * 32 + lane] << (2 * j));
-            o[16 + h * 32 + lane] = b;
-        }
-        __syncwarp();
-        store_block(a.dst + row * a.dst_row_bytes + sbi * 84, o, 84, false, lane);
-        __syncwarp();
-    }
+    extern __shared__ __align__(16) uint8_t qkx3_smem[];
+    qkx3_super_blocks<16, 3>(a, reinterpret_cast<Qkx3Warp<16> *>(qkx3_smem) + (threadIdx.x >> 5));
 }
 
 // ---------------------------------------------------------------------------
@@ -1227,6 +1133,24 @@ static unsigned persistent_grid(const void *fn, int threads, int num_sms, int64_
     return (unsigned)want;
 }
 
+// Warp-per-super-block make_qkx3_quants kernels: dynamic shared memory of
+// kQkx3Warps per-warp workspaces, a persistent grid of resident blocks.
+template <int N>
+static cudaError_t launch_qkx3(void (*fn)(EncArgs), const EncArgs &a, int num_sms, cudaStream_t st) {
+    const size_t smem = kQkx3Warps * sizeof(Qkx3Warp<N>);
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 1;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kQkx3Warps * 32, smem);
+    if (per_sm < 1) per_sm = 1;
+    int64_t grid = (a.n_rows * (a.src.ne0 / 256) + kQkx3Warps - 1) / kQkx3Warps;
+    const int64_t cap = (int64_t)num_sms * per_sm;
+    if (grid > cap) grid = cap;
+    if (grid < 1) grid = 1;
+    fn<<<(unsigned)grid, kQkx3Warps * 32, smem, st>>>(a);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_kquant(uint32_t type, const EncArgs &a, int num_sms, cudaStream_t st) {
     const int64_t nsb = a.src.ne0 / 256;
     switch (type) {
@@ -1246,21 +1170,9 @@ cudaError_t launch_kquant(uint32_t type, const EncArgs &a, int num_sms, cudaStre
         enc_qx16_kernel<4><<<grid, 256, 0, st>>>(a);
         break;
     }
-    case SHC_TYPE_Q2_K: {
-        unsigned grid = persistent_grid((const void *)enc_q2_k_kernel, 256, num_sms, a.n_rows * nsb);
-        enc_q2_k_kernel<<<grid, 256, 0, st>>>(a);
-        break;
-    }
-    case SHC_TYPE_Q4_K: {
-        unsigned grid = persistent_grid((const void *)enc_qk45_kernel<15>, 256, num_sms, a.n_rows * nsb);
-        enc_qk45_kernel<15><<<grid, 256, 0, st>>>(a);
-        break;
-    }
-    case SHC_TYPE_Q5_K: {
-        unsigned grid = persistent_grid((const void *)enc_qk45_kernel<31>, 256, num_sms, a.n_rows * nsb);
-        enc_qk45_kernel<31><<<grid, 256, 0, st>>>(a);
-        break;
-    }
+    case SHC_TYPE_Q2_K: return launch_qkx3<16>(enc_q2_k_kernel, a, num_sms, st);
+    case SHC_TYPE_Q4_K: return launch_qkx3<32>(enc_qk45_kernel<15>, a, num_sms, st);
+    case SHC_TYPE_Q5_K: return launch_qkx3<32>(enc_qk45_kernel<31>, a, num_sms, st);
     case SHC_TYPE_Q4_0: case SHC_TYPE_Q5_0: case SHC_TYPE_Q4_1: case SHC_TYPE_Q5_1: {
         const int64_t ngrp = (a.n_rows * (a.src.ne0 / 32) + 7) / 8;
         const void *fn = type == SHC_TYPE_Q4_0 ? (const void *)enc_legacy_kernel<0>
