@@ -121,68 +121,93 @@ cudaError_t launch_row_sigma2(const RowSrc &src, int64_t n_rows, float *out, cud
 
 // ---------------------------------------------------------------------------
 // Q8_0 (quant.rs:159-169): per 32-block amax, d = amax/127, q = round(x/d).
-// HBM-bound.  A warp handles 8 blocks (256 elements) per group, 4 lanes per
-// block, 8 elements per lane; groups are flat over the tensor's blocks.
+// HBM-bound.  A lane owns one block (32 consecutive elements, 4-8 16-byte
+// loads), so the per-block divisions and the f16 store run once per block;
+// a warp covers 32 consecutive blocks and writes their 1088 output bytes from
+// shared memory with 16-byte stores.  Blocks with a NaN or infinite element
+// or an infinite 1/d take the general rounding path (NaN -> 0, saturating
+// clamp); otherwise |x/d| <= 127 (1 + 2^-23)^2 and the code is the magnitude
+// rounded half up, sign applied in two's complement.
 // ---------------------------------------------------------------------------
-constexpr int kQ80Unroll = 4;
+__device__ __forceinline__ float max_nan(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
 
-__global__ void __launch_bounds__(256) enc_q8_0_kernel(EncArgs a) {
-    __shared__ __align__(16) uint8_t s_out[8][kQ80Unroll][272];
+__global__ void __launch_bounds__(256, 4) enc_q8_0_kernel(EncArgs a) {
+    __shared__ __align__(16) uint8_t s_out[8][32 * 34];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int64_t bpr = a.src.ne0 >> 5;
     const int64_t nblk = a.n_rows * bpr;
-    const int64_t ngrp = (nblk + 7) >> 3;
-    const int64_t stride = (int64_t)gridDim.x * 8 * kQ80Unroll;
+    const int64_t nwi = (nblk + 31) >> 5;
     const bool contiguous = a.src.row_stride == a.src.ne0;
-    for (int64_t g0 = ((int64_t)blockIdx.x * 8 + wid) * kQ80Unroll; g0 < ngrp; g0 += stride) {
-        float v[kQ80Unroll][8];
+    uint8_t *so = s_out[wid];
+    for (int64_t it = (int64_t)blockIdx.x * 8 + wid; it < nwi; it += (int64_t)gridDim.x * 8) {
+        const int64_t blk = (it << 5) + lane;
+        float v[32];
+        if (blk < nblk) {
+            int64_t row = 0, col = blk * 32;  // rows back to back: the block index is the element offset / 32
+            if (!contiguous) {
+                row = blk / bpr;
+                col = (blk - row * bpr) * 32;
+            }
 #pragma unroll
-        for (int u = 0; u < kQ80Unroll; u++) {
-            const int64_t blk = (g0 + u) * 8 + (lane >> 2);
-            if (g0 + u < ngrp && blk < nblk) {
-                if (contiguous) {  // rows back to back: the block index is the element offset / 32
-                    load8(a.src, 0, blk * 32 + (lane & 3) * 8, v[u]);
-                } else {
-                    const int64_t row = blk / bpr;
-                    const int64_t col = (blk - row * bpr) * 32 + (lane & 3) * 8;
-                    load8(a.src, row, col, v[u]);
+            for (int m = 0; m < 4; m++) load8(a.src, row, col + m * 8, &v[m * 8]);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 32; k++) v[k] = 0.0f;
+        }
+        // amax over |x| ignoring NaN as the reference's max fold does; the
+        // NaN-propagating fold flags the blocks that need the general path
+        float amax = 0.0f, amaxn = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 32; k++) {
+            amax = fmaxf(amax, fabsf(v[k]));
+            amaxn = max_nan(amaxn, fabsf(v[k]));
+        }
+        const float d = amax / 127.0f;
+        const float id = d > 0.0f ? 1.0f / d : 0.0f;
+        uint32_t w[8];
+        if (amaxn < INFINITY && id < INFINITY) {
+#pragma unroll
+            for (int m = 0; m < 8; m++) {
+                uint32_t word = 0;
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+                    const float y = v[m * 4 + t] * id;
+                    // 2^23 + round-half-up(|y|) (identities of floor_half_up)
+                    const uint32_t r = __float_as_uint(__fadd_rd(__fadd_rz(fabsf(y), 0.5f), 8388608.0f)) & 0xFFu;
+                    const uint32_t sg = (uint32_t)((int32_t)__float_as_uint(y) >> 31);
+                    word |= (((r ^ sg) - sg) & 0xFFu) << (8 * t);
                 }
-            } else {
+                w[m] = word;
+            }
+        } else {
 #pragma unroll
-                for (int k = 0; k < 8; k++) v[u][k] = 0.0f;
+            for (int m = 0; m < 8; m++) {
+                uint32_t word = 0;
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+                    // the int8 code is the low byte of r + 1.5 * 2^23 (exact for |r| <= 127)
+                    const float r = round_clamp_f(v[m * 4 + t] * id, -127.0f, 127.0f);
+                    word |= (__float_as_uint(__fadd_rn(r, 12582912.0f)) & 0xFFu) << (8 * t);
+                }
+                w[m] = word;
             }
         }
+        // 34 bytes per lane at 34 * lane (2-byte aligned): f16 d, then the codes
+        uint16_t *o16 = reinterpret_cast<uint16_t *>(so + 34 * lane);
+        o16[0] = f16_bits(d);
 #pragma unroll
-        for (int u = 0; u < kQ80Unroll; u++) {
-            float amax = 0.0f;
-#pragma unroll
-            // rmaxf(a, |x|) from a = +0: the operand is never -0, so fmaxf agrees
-            for (int k = 0; k < 8; k++) amax = fmaxf(amax, fabsf(v[u][k]));
-            amax = rmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-            amax = rmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-            const float d = amax / 127.0f;
-            const float id = d > 0.0f ? 1.0f / d : 0.0f;
-            uint8_t *o = &s_out[wid][u][(lane >> 2) * 34];
-#pragma unroll
-            for (int k = 0; k < 8; k++)
-                // the int8 code is the low byte of r + 1.5 * 2^23 (exact for |r| <= 127)
-                o[2 + (lane & 3) * 8 + k] =
-                    (uint8_t)__float_as_uint(__fadd_rn(round_clamp_f(v[u][k] * id, -127.0f, 127.0f), 12582912.0f));
-            if ((lane & 3) == 0) {
-                const uint16_t h = f16_bits(d);
-                o[0] = (uint8_t)(h & 0xFF);
-                o[1] = (uint8_t)(h >> 8);
-            }
+        for (int m = 0; m < 8; m++) {
+            o16[1 + 2 * m] = (uint16_t)(w[m] & 0xFFFFu);
+            o16[2 + 2 * m] = (uint16_t)(w[m] >> 16);
         }
         __syncwarp();
-#pragma unroll
-        for (int u = 0; u < kQ80Unroll; u++) {
-            const int64_t blk0 = (g0 + u) * 8;
-            if (g0 + u < ngrp) {
-                const int nb = (int)(nblk - blk0 < 8 ? nblk - blk0 : 8);
-                store_block(a.dst + blk0 * 34, s_out[wid][u], nb * 34, a.dst_aligned16 && nb == 8, lane);
-            }
-        }
+        const int64_t left = nblk - (it << 5);
+        const int nb = (int)(left < 32 ? left : 32);
+        store_block(a.dst + (it << 5) * 34, so, nb * 34, a.dst_aligned16 && nb == 32, lane);
         __syncwarp();
     }
 }
@@ -1155,8 +1180,7 @@ cudaError_t launch_kquant(uint32_t type, const EncArgs &a, int num_sms, cudaStre
     const int64_t nsb = a.src.ne0 / 256;
     switch (type) {
     case SHC_TYPE_Q8_0: {
-        const int64_t ngrp = (a.n_rows * (a.src.ne0 / 32) + 7) / 8;
-        unsigned grid = persistent_grid((const void *)enc_q8_0_kernel, 256, num_sms, (ngrp + kQ80Unroll - 1) / kQ80Unroll);
+        unsigned grid = persistent_grid((const void *)enc_q8_0_kernel, 256, num_sms, (a.n_rows * (a.src.ne0 / 32) + 31) / 32);
         enc_q8_0_kernel<<<grid, 256, 0, st>>>(a);
         break;
     }

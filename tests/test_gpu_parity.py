@@ -92,6 +92,30 @@ def test_encode_matches_oracle_edge_rows(ctx, ty):
     assert_bytes_equal(gpu_encode(ctx, ty, bits, None), oracle_encode(ty, bits, None), ty)
 
 
+def q8_0_special_rows():
+    """Blocks with NaN, +-inf, a subnormal d with finite 1/d, a d whose
+    reciprocal overflows, and exact .5 ties after scaling (Q8_0's general
+    rounding path and the edges of its fast path)."""
+    rng = np.random.default_rng(17)
+    x = rng.normal(0, 0.02, (4, 1024)).astype(np.float32)
+    x[0, 3] = np.nan
+    x[0, 40] = np.inf
+    x[0, 70] = -np.inf
+    x[0, 96:128] = np.nan
+    x[1, 0:32] = rng.uniform(-1, 1, 32).astype(np.float32) * np.float32(5.3e-37)   # d in [2^-128, 2^-126)
+    x[1, 32:64] = rng.uniform(-1, 1, 32).astype(np.float32) * np.float32(1e-38)    # 1/d overflows
+    x[1, 64:96] = np.float32(3e-39)
+    x[2, 0:32] = (np.arange(32) - 16).astype(np.float32) * np.float32(127.0 / 16.0) / np.float32(254.0)
+    x[2, 32:64] = np.float32(-0.0)
+    x[3, :] = np.float32(-1.5)
+    return f32_to_bf16_bits(x)
+
+
+def test_q8_0_special_values(ctx):
+    bits = q8_0_special_rows()
+    assert_bytes_equal(gpu_encode(ctx, 8, bits), oracle_encode(8, bits), 8)
+
+
 @pytest.mark.parametrize("ty", supported(KQ + IQ), ids=lambda t: NAMES[t])
 def test_expert_imatrix_slicing_and_row0(ctx, ty):
     """imatrix.rs:124-141: an imatrix of n_mats*ne0 selects matrix row/rows_per_mat."""
