@@ -68,6 +68,11 @@ __device__ void init_iq4_lut(Iq4Lut &L) {
 
 // XS: a warp encodes one 256-element super-block (8 blocks of 32).
 // NL: a warp encodes 8 consecutive 32-element blocks (each its own super-block).
+// Each warp owns a contiguous, balanced range of units and walks it in
+// batches of up to 32: the sequential sigma^2 folds of quant_iq.rs:1037 (256
+// elements for XS, 32 per block for NL) run one unit per lane first, so each
+// serial chain is issued once instead of on all 32 lanes; the batch's units
+// are then encoded one after another.
 template <bool XS>
 __global__ void __launch_bounds__(256) enc_iq4_kernel(EncArgs a) {
     __shared__ Iq4Lut lut;
@@ -75,6 +80,7 @@ __global__ void __launch_bounds__(256) enc_iq4_kernel(EncArgs a) {
     __shared__ float s_w[8][8 * 33];
     __shared__ float2 s_res[8][8][16];
     __shared__ float s_scale[8][8];
+    __shared__ float s_sig[8][32][8];
     __shared__ __align__(16) uint8_t s_out[8][144];
     __shared__ uint8_t s_l[8][256];
     init_iq4_lut(lut);
@@ -85,7 +91,48 @@ __global__ void __launch_bounds__(256) enc_iq4_kernel(EncArgs a) {
     const int64_t nunits = XS ? a.n_rows * (ne0 >> 8) : (a.n_rows * (ne0 >> 5) + 7) >> 3;
     const int64_t bpr = ne0 >> 5;
     const int64_t nblk = a.n_rows * bpr;
-    for (int64_t g = (int64_t)blockIdx.x * 8 + wid; g < nunits; g += (int64_t)gridDim.x * 8) {
+    const int64_t nwarps = (int64_t)gridDim.x * 8, wg = (int64_t)blockIdx.x * 8 + wid;
+    const int64_t u_lo = nunits * wg / nwarps, u_hi = nunits * (wg + 1) / nwarps;
+    for (int64_t b0 = u_lo; b0 < u_hi; b0 += 32) {
+    const int batch = (int)(u_hi - b0 < 32 ? u_hi - b0 : 32);
+    // sigma2 = 2 * (sequential sum of x^2 over the super-block) / size, one unit per lane
+    {
+        const int64_t gu = b0 + lane;
+        if (lane < batch) {
+            if (XS) {
+                const int64_t nsb = ne0 >> 8;
+                const int64_t row = gu / nsb, col = (gu - row * nsb) * 256;
+                float s = 0.0f;
+#pragma unroll 4
+                for (int m = 0; m < 32; m++) {
+                    float v[8];
+                    load8(a.src, row, col + m * 8, v);
+#pragma unroll
+                    for (int k = 0; k < 8; k++) s += v[k] * v[k];
+                }
+                s_sig[wid][lane][0] = 2.0f * s / 256.0f;
+            } else {
+#pragma unroll 1
+                for (int bb = 0; bb < 8; bb++) {
+                    const int64_t blk = gu * 8 + bb;
+                    if (blk >= nblk) break;
+                    const int64_t row = blk / bpr, col = (blk - row * bpr) * 32;
+                    float s = 0.0f;
+#pragma unroll
+                    for (int m = 0; m < 4; m++) {
+                        float v[8];
+                        load8(a.src, row, col + m * 8, v);
+#pragma unroll
+                        for (int k = 0; k < 8; k++) s += v[k] * v[k];
+                    }
+                    s_sig[wid][lane][bb] = 2.0f * s / 32.0f;
+                }
+            }
+        }
+        __syncwarp();
+    }
+    for (int u = 0; u < batch; u++) {
+        const int64_t g = b0 + u;
         // this lane group's 32-block: row and column
         int64_t row, col;
         bool valid = true;
@@ -115,19 +162,7 @@ __global__ void __launch_bounds__(256) enc_iq4_kernel(EncArgs a) {
 #pragma unroll
         for (int k = 0; k < 8; k++) xs[q * 8 + k] = v[k];
         __syncwarp();
-        // sigma2 = 2 * (sequential sum of x^2 over the super-block) / size
-        float sig;
-        {
-            float s = 0.0f;
-            if (XS) {
-                for (int bb = 0; bb < 8; bb++)
-                    for (int i = 0; i < 32; i++) s += s_x[wid][bb * 33 + i] * s_x[wid][bb * 33 + i];
-                sig = 2.0f * s / 256.0f;
-            } else {
-                for (int i = 0; i < 32; i++) s += xs[i] * xs[i];
-                sig = 2.0f * s / 32.0f;
-            }
-        }
+        const float sig = s_sig[wid][u][XS ? 0 : b];
         float *ws = &s_w[wid][b * 33];
 #pragma unroll
         for (int k = 0; k < 8; k++) ws[q * 8 + k] = imr ? base[k] * sqrtf(sig + v[k] * v[k]) : v[k] * v[k];
@@ -250,6 +285,7 @@ __global__ void __launch_bounds__(256) enc_iq4_kernel(EncArgs a) {
             store_block(a.dst + blk0 * 18, o, nb * 18, a.dst_aligned16 && nb == 8, lane);
         }
         __syncwarp();
+    }
     }
 }
 
@@ -1108,8 +1144,8 @@ static cudaError_t launch_iq4(const EncArgs &a, int num_sms, cudaStream_t st) {
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, 0);
     if (per_sm < 1) per_sm = 1;
     const int64_t units = XS ? a.n_rows * (a.src.ne0 / 256) : (a.n_rows * (a.src.ne0 / 32) + 7) / 8;
-    int64_t grid = (units + 7) / 8;
     const int64_t cap = (int64_t)num_sms * per_sm;
+    int64_t grid = (units + 7) / 8;
     if (grid > cap) grid = cap;
     if (grid < 1) grid = 1;
     fn<<<(unsigned)grid, 256, 0, st>>>(a);

@@ -499,12 +499,12 @@ __device__ __forceinline__ void qkx3_errors(const float *snx, const float *sw, c
 // j-1 unless some element crosses a rounding threshold k - 1/2 between them.
 // Equal level vectors give equal sums, (scale, min) and error, so such a
 // grid never replaces the earlier one under the reference's strict `<`
-// (quant.rs:129): only the first grid of each run of equal level vectors is
-// evaluated.  y_36 - y_0 = 1.8 u / (vmax - vmin) <= 1.8 (plus rounding), so
-// an element crosses at most two thresholds; each crossing grid is found by
-// a binary search on y_j = iscale_j * u >= k - 1/2 (round half away from zero
-// of y >= 0 is floor(y + 1/2)).  Sub-blocks with a non-finite range or
-// scale evaluate every grid.
+// (quant.rs:129): only grids where some element may cross are evaluated.
+// y_36 - y_0 = 1.8 u / (vmax - vmin) <= 1.8 (plus rounding), so an element
+// crosses at most two thresholds (round half away from zero of y >= 0 is
+// floor(y + 1/2), so l_i(j) >= k iff y_j >= k - 1/2); the exact levels at
+// grids 0 and 36 count them and a bounded estimate places them.  Sub-blocks
+// with a non-finite range or scale evaluate every grid.
 //
 // The distinct (sub-block, grid) jobs of the warp's super-block, plus each
 // sub-block's initial nmax/(vmax-vmin) grid, are listed in shared memory in
@@ -540,26 +540,10 @@ __device__ __forceinline__ float err_from_key(unsigned int k) {
     return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
 }
 
-// First grid j in [1, 36] with iscale_j * u >= thr, given that grid 0 is
-// below and grid 36 at or above the threshold (y_j is non-decreasing in j).
-// z estimates the answer from iscale_j ~ (nmax - 0.9 + 0.05 j)/range; the
-// three grids around it are evaluated exactly and decide when the estimate
-// is within one grid, otherwise a binary search over the table does.
-__device__ __forceinline__ int crossing_grid(const float *tab, float u, float thr, float z) {
-    const int je = min(max(__float2int_ru(z), 1), 35);
-    const bool p0 = __fmul_rn(tab[je - 1], u) >= thr;
-    const bool p1 = __fmul_rn(tab[je], u) >= thr;
-    const bool p2 = __fmul_rn(tab[je + 1], u) >= thr;
-    if (!p0 && p2) return p1 ? je : je + 1;
-    if (p0 && je >= 2 && !(__fmul_rn(tab[je - 2], u) >= thr)) return je - 1;
-    int lo = 0, hi = 36;
-#pragma unroll 1
-    while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (__fmul_rn(tab[mid], u) >= thr) hi = mid;
-        else lo = mid;
-    }
-    return hi;
+// ceil(t) for 0 <= t <= 2^22 as an int, without the conversion pipe: RU(t +
+// 2^23) is 2^23 + ceil(t), whose low mantissa bits are the result.
+__device__ __forceinline__ int ceil_small(float t) {
+    return (int)(__float_as_uint(__fadd_ru(t, 8388608.0f)) & 0x7FFFFFu);
 }
 
 template <int N, int NMAX>
@@ -636,30 +620,46 @@ __device__ __forceinline__ void qkx3_super_blocks(const EncArgs &a, Qkx3Warp<N> 
         const float iscale0 = FN / range;
         const float scale0 = 1.0f / iscale0;
         const bool clean = !degen && range < INFINITY && W->isc[s][36] < INFINITY;
-        // grids whose level vector differs from the previous grid's
+        // grids whose level vector may differ from the previous grid's: a
+        // superset of the crossing grids (evaluating a repeated grid changes
+        // nothing), from the estimate j ~ 20 (thr (vmax-vmin)/u - (nmax-0.9)).
+        // Its error against the first grid with iscale_j*u >= thr is below
+        // 5e-4 grid steps (rounding of iscale_j, the product and the estimate,
+        // 2-ulp quotient for normal u), so every integer in
+        // [ceil(z - 0.004), ceil(z + 0.004)] (one or two grids) is marked.
         unsigned long long mask = 0;
         if (!degen) {
             if (clean) {
-                const float *tab = W->isc[s];
-                const float i0 = tab[0], i36 = tab[36];
+                const float i0 = W->isc[s][0], i36 = W->isc[s][36];
+                uint32_t mlo = 1u, mhi = 0u;  // grids 0-31 and 32-36
 #pragma unroll 1
                 for (int k = 0; k < 8; k++) {
                     const float uk = -su[q * 8 + k];  // x - vmin
                     const float l0 = fminf(floor_half_up(__fmul_rn(i0, uk)), FN);
                     const float l36 = fminf(floor_half_up(__fmul_rn(i36, uk)), FN);
                     if (l36 > l0) {
-                        const float ru = __fdividef(range, uk);  // an estimate only: verified below
+                        if (uk >= 1.17549435e-38f && uk <= 8.50705917e37f) {
+                            const float ru = __fdividef(range, uk);
 #pragma unroll
-                        for (int c = 1; c <= 2; c++) {
-                            const float kk = l0 + (float)c;
-                            if (kk <= l36) {
-                                const float thr = kk - 0.5f;
-                                mask |= 1ull << crossing_grid(tab, uk, thr, 20.0f * (thr * ru - (FN - 0.9f)));
+                            for (int c = 1; c <= 2; c++) {
+                                const float thr = l0 + ((float)c - 0.5f);
+                                if (thr < l36) {
+                                    const float z = 20.0f * (thr * ru - (FN - 0.9f));
+                                    const int jl = ceil_small(fminf(fmaxf(z - 0.004f, 0.5f), 36.0f));
+                                    const int jh = ceil_small(fminf(fmaxf(z + 0.004f, 0.5f), 36.0f));
+                                    if (jl < 32) mlo |= 1u << jl;
+                                    else mhi |= 1u << (jl - 32);
+                                    if (jh < 32) mlo |= 1u << jh;
+                                    else mhi |= 1u << (jh - 32);
+                                }
                             }
+                        } else {  // subnormal or huge u: no usable estimate
+                            mlo = ~0u;
+                            mhi = 0x1Fu;
                         }
                     }
                 }
-                mask |= 1ull;
+                mask = ((unsigned long long)mhi << 32) | mlo;
             } else {
                 mask = (1ull << 37) - 1;
             }
