@@ -452,11 +452,12 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
     const bool bounded = timeout_ms >= 0;
     const size_t eb = src_elem_bytes(src_type);
     const size_t in_row = (size_t)ne0 * eb;
-    // ~16 MiB of source per chunk: copies of one chunk overlap the encode of
-    // the previous one, and the first and last chunks (not overlapped) stay short
-    int64_t chunk = std::max<int64_t>(1, (int64_t)((16u << 20) / in_row));
-    chunk = std::min(chunk, n_rows);
-    const int64_t n_chunks = (n_rows + chunk - 1) / chunk;
+    // equal chunks of at most ~16 MiB of source: copies of one chunk overlap
+    // the encode of the previous one, and no short tail chunk pays a whole
+    // row sigma^2 pass (a fixed serial-chain latency) for a few rows
+    const int64_t max_chunk = std::max<int64_t>(1, (int64_t)((16u << 20) / in_row));
+    const int64_t n_chunks = (n_rows + max_chunk - 1) / max_chunk;
+    const int64_t chunk = (n_rows + n_chunks - 1) / n_chunks;
     const bool pin_src = is_pinned(host_src), pin_dst = is_pinned(host_dst);
     cudaStream_t s_in = ctx->hs[0], s_cmp = ctx->hs[1], s_out = ctx->hs[2], s_sig = ctx->hs[3];
     // The row sigma^2 pre-pass (one thread per row, bound by its serial sums)
