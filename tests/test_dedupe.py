@@ -1,0 +1,69 @@
+"""The grid-skipping rule of the make_qkx3_quants kernels (Q4_K, Q5_K, Q2_K),
+checked on the CPU: for x - vmin >= 0 a grid's level vector can differ from
+the previous grid's only where some element crosses a rounding threshold,
+and every such grid lies in the one or two grids the kernels mark from the
+estimate j ~ 20 (thr (vmax - vmin)/u - (nmax - 0.9)) with a 0.004 window.
+The kernels evaluate only marked grids (plus grid 0 and the initial grid),
+so this is the property their byte parity rests on; the GPU parity tests
+check the bytes themselves."""
+import numpy as np
+import pytest
+
+from tests.helpers import bf16_bits_to_f32, edge_rows, student_rows, sweep_rows
+
+f32 = np.float32
+
+
+def level_changes_and_marks(x, nmax):
+    """x: (n_sub, n) f32 sub-blocks. Returns boolean (n_sub, 37) arrays of the
+    grids whose levels differ from the previous grid's, and of marked grids."""
+    vmin = np.minimum(x.min(1), f32(0))
+    vmax = x.max(1)
+    keep = vmax > vmin
+    x, vmin, vmax = x[keep], vmin[keep], vmax[keep]
+    rng = (vmax - vmin).astype(f32)
+    u = (x - vmin[:, None]).astype(f32)
+    fn = f32(nmax)
+    j = np.arange(37, dtype=f32)
+    # iscale_j = (rmin + rdelta*j + nmax) / (vmax - vmin), rounded as the reference does
+    with np.errstate(over="ignore", divide="ignore"):
+        isc = (((f32(-0.9) + (f32(0.05) * j).astype(f32)).astype(f32) + fn).astype(f32)[None, :] /
+               rng[:, None]).astype(f32)
+    # sub-blocks with a non-finite range or scale evaluate every grid
+    clean = np.isfinite(rng) & np.isfinite(isc[:, 36])
+    isc, u, rng = isc[clean], u[clean], rng[clean]
+    y = (isc[:, :, None] * u[:, None, :]).astype(f32)              # (n_sub, 37, n)
+    lev = np.minimum(np.floor(y.astype(np.float64) + 0.5), nmax)    # round half up of y >= 0, clamped
+    changed = np.zeros(lev.shape[:2], bool)
+    changed[:, 1:] = (lev[:, 1:] != lev[:, :-1]).any(2)
+    marks = np.zeros_like(changed)
+    marks[:, 0] = True
+    l0, l36 = lev[:, 0, :], lev[:, 36, :]
+    with np.errstate(divide="ignore", invalid="ignore"):
+        ru = (rng[:, None] / u).astype(f32)
+    for c in (1, 2):
+        thr = (l0 + (c - 0.5)).astype(f32)
+        active = thr < l36
+        z = (f32(20.0) * ((thr * ru).astype(f32) - (fn - f32(0.9))).astype(f32)).astype(f32)
+        for eps in (-0.004, 0.004):
+            jj = np.ceil(np.clip(np.where(active, z + f32(eps), 0.5), 0.5, 36.0)).astype(int)
+            rows, cols = np.nonzero(active)
+            marks[rows, jj[rows, cols]] = True
+    assert (l36 - l0).max() <= 2  # at most two crossings per element
+    return changed, marks
+
+
+@pytest.mark.parametrize("n,nmax", [(32, 15), (32, 31), (16, 3)], ids=["Q4_K", "Q5_K", "Q2_K"])
+def test_marked_grids_cover_every_level_change(n, nmax):
+    subs = []
+    bits, _ = sweep_rows(8, 14336, seed=21)
+    subs.append(bf16_bits_to_f32(bits).reshape(-1, n))
+    bits, _ = student_rows(16, 4096, seed=22)
+    subs.append(bf16_bits_to_f32(bits).reshape(-1, n))
+    subs.append(edge_rows(512).astype(np.float32).reshape(-1, n))
+    x = np.concatenate(subs)
+    changed, marks = level_changes_and_marks(x, nmax)
+    missed = changed & ~marks
+    assert not missed.any(), f"{missed.sum()} level changes outside the marked grids"
+    # the marks stay a small superset: most grids are still skipped
+    assert marks.sum(1).mean() < 0.7 * 37
