@@ -66,6 +66,12 @@ __device__ void init_iq4_lut(Iq4Lut &L) {
     }
 }
 
+// ceil(t) for 0 <= t <= 2^22 as an int: RU(t + 2^23) is 2^23 + ceil(t),
+// whose low mantissa bits are the result (no conversion instruction).
+__device__ __forceinline__ int iq4_ceil(float t) {
+    return (int)(__float_as_uint(__fadd_ru(t, 8388608.0f)) & 0x7FFFFFu);
+}
+
 // XS: a warp encodes one 256-element super-block (8 blocks of 32).
 // NL: a warp encodes 8 consecutive 32-element blocks (each its own super-block).
 // Each warp owns a contiguous, balanced range of units and walks it in
@@ -81,6 +87,8 @@ __global__ void __launch_bounds__(256) enc_iq4_kernel(EncArgs a) {
     __shared__ float2 s_res[8][8][16];
     __shared__ float s_scale[8][8];
     __shared__ float s_sig[8][32][8];
+    __shared__ float s_mx[8][8];
+    __shared__ uint8_t s_job[8][128];
     __shared__ __align__(16) uint8_t s_out[8][144];
     __shared__ uint8_t s_l[8][256];
     init_iq4_lut(lut);
@@ -167,30 +175,86 @@ __global__ void __launch_bounds__(256) enc_iq4_kernel(EncArgs a) {
 #pragma unroll
         for (int k = 0; k < 8; k++) ws[q * 8 + k] = imr ? base[k] * sqrtf(sig + v[k] * v[k]) : v[k] * v[k];
         __syncwarp();
-        float x[32], w[32];
-#pragma unroll
-        for (int i = 0; i < 32; i++) {
-            x[i] = xs[i];
-            w[i] = ws[i];
-        }
         float amax = 0.0f, mx = 0.0f;
 #pragma unroll
         for (int i = 0; i < 32; i++) {
-            const float av = fabsf(x[i]);
-            if (av > amax) { amax = av; mx = x[i]; }
+            const float av = fabsf(xs[i]);
+            if (av > amax) { amax = av; mx = xs[i]; }
         }
         const bool live = !(amax < kGroupMaxEps);
+        // Trials whose code vector repeats the previous trial's are skipped.
+        // For jobs 1..15, id_j = (j - 135)/max moves monotonically with j, so
+        // each element's code (a monotone step function of id*x) changes
+        // only where id_j*x crosses a decision point between neighbouring
+        // codebook values: (j - 135) x/max = T at j* = 135 + T max/x.  A
+        // repeated trial has the same (sumqx, sumq2) as the one before it
+        // and leaves the selection chain's state as it is, accepted or not.
+        // The codes at trials 1 and 15 (exact) count the crossings (at most
+        // two: the span of id*x is 14 |x|/|max|, the codebook steps are >= 11);
+        // j* is known to well within 0.01 (rounding of id, of the product and
+        // of the decision, and of the estimate, for |x| >= |max|/30 as any
+        // crossing needs), so the grids ceil(j* -+ 0.01) are marked.
+        unsigned int jmask = 0;
         if (live) {
+            if (fabsf(mx) < INFINITY) {
+                const float id1 = (-7.0f + -127.0f) / mx, id15 = (7.0f + -127.0f) / mx;
+#pragma unroll
+                for (int k = 0; k < 8; k++) {
+                    const int i1 = best_index_iq4(lut, id1 * v[k]), i15 = best_index_iq4(lut, id15 * v[k]);
+                    if (i1 != i15) {
+                        const float r = mx / v[k];
+                        const int lo = min(i1, i15), hi = max(i1, i15);
+#pragma unroll
+                        for (int c = 0; c < 2; c++) {
+                            if (lo + c < hi) {
+                                const float T = (lut.v[lo + c] + lut.v[lo + c + 1]) * 0.5f;
+                                const float js = 135.0f + T * r;
+                                jmask |= 1u << iq4_ceil(fminf(fmaxf(js - 0.01f, 2.0f), 15.0f));
+                                jmask |= 1u << iq4_ceil(fminf(fmaxf(js + 0.01f, 2.0f), 15.0f));
+                            }
+                        }
+                    }
+                }
+            } else {
+                jmask = 0xFFFFu;
+            }
+            jmask |= 3u;  // the initial grid and trial 1
+        }
+        jmask |= __shfl_xor_sync(0xffffffffu, jmask, 1);
+        jmask |= __shfl_xor_sync(0xffffffffu, jmask, 2);
+        // (block, job) list of the unit, dealt to the warp's 32 lanes; lane q
+        // of a block lists the jobs among bits [4q, 4q + 4)
+        {
+            const int cnt = __popc(jmask);
+            int incl = q == 0 ? cnt : 0;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int t = __shfl_up_sync(0xffffffffu, incl, off);
+                if (lane >= off) incl += t;
+            }
+            const int njobs = __shfl_sync(0xffffffffu, incl, 31);
+            int pos = __shfl_sync(0xffffffffu, incl, lane - q) - cnt + __popc(jmask & ((1u << (4 * q)) - 1u));
+            unsigned int bits = (jmask >> (4 * q)) & 0xFu;
+            while (bits != 0) {
+                s_job[wid][pos++] = (uint8_t)((b << 4) | (4 * q + __ffs(bits) - 1));
+                bits &= bits - 1;
+            }
+            if (q == 0) s_mx[wid][b] = mx;
+            __syncwarp();
             // job 0: the initial grid d = -max/v0; jobs 1..15: itry = job - 8
-            for (int j = q; j < 16; j += 4) {
-                const float id = j == 0 ? 1.0f / (-mx / -127.0f) : ((float)(j - 8) + -127.0f) / mx;
+            for (int t = lane; t < njobs; t += 32) {
+                const int code = s_job[wid][t];
+                const int jb = code >> 4, j = code & 15;
+                const float jmx = s_mx[wid][jb];
+                const float *jx = &s_x[wid][jb * 33], *jw = &s_w[wid][jb * 33];
+                const float id = j == 0 ? 1.0f / (-jmx / -127.0f) : ((float)(j - 8) + -127.0f) / jmx;
                 float sumqx = 0.0f, sumq2 = 0.0f;
 #pragma unroll
                 for (int i = 0; i < 32; i += 2) {  // element pairs; products feed scalar sums only
-                    const float2 xi = make_float2(x[i], x[i + 1]);
+                    const float2 xi = make_float2(jx[i], jx[i + 1]);
                     const float2 y = __fmul2_rn(make_float2(id, id), xi);
                     const float2 qv = make_float2(best_value_iq4(lut, y.x), best_value_iq4(lut, y.y));
-                    const float2 wq = __fmul2_rn(make_float2(w[i], w[i + 1]), qv);
+                    const float2 wq = __fmul2_rn(make_float2(jw[i], jw[i + 1]), qv);
                     const float2 sx = __fmul2_rn(wq, xi);
                     const float2 s2 = __fmul2_rn(wq, qv);
                     sumqx = __fadd_rn(sumqx, sx.x);
@@ -198,7 +262,7 @@ __global__ void __launch_bounds__(256) enc_iq4_kernel(EncArgs a) {
                     sumqx = __fadd_rn(sumqx, sx.y);
                     sumq2 = __fadd_rn(sumq2, s2.y);
                 }
-                s_res[wid][b][j] = make_float2(sumqx, sumq2);
+                s_res[wid][jb][j] = make_float2(sumqx, sumq2);
             }
         }
         __syncwarp();
@@ -208,7 +272,10 @@ __global__ void __launch_bounds__(256) enc_iq4_kernel(EncArgs a) {
                 const float2 r0 = s_res[wid][b][0];
                 d = r0.y > 0.0f ? r0.x / r0.y : 0.0f;
                 float best = d * r0.x;
-                for (int j = 1; j < 16; j++) {
+                unsigned int m = jmask & ~1u;  // evaluated trials, in order
+                while (m != 0) {
+                    const int j = __ffs(m) - 1;
+                    m &= m - 1;
                     const float2 r = s_res[wid][b][j];
                     if (r.y > 0.0f && r.x * r.x > best * r.y) {
                         d = r.x / r.y;

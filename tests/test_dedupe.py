@@ -67,3 +67,55 @@ def test_marked_grids_cover_every_level_change(n, nmax):
     assert not missed.any(), f"{missed.sum()} level changes outside the marked grids"
     # the marks stay a small superset: most grids are still skipped
     assert marks.sum(1).mean() < 0.7 * 37
+
+
+# ---- IQ4_NL / IQ4_XS: the 15 scale trials of quant_iq.rs:1078-1095 ----
+KV = np.array([-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113], f32)
+_CNT = np.array([sum(1 for k in range(1, 15) if KV[k] <= f - 128) for f in range(256)])
+
+
+def iq4_index(y):
+    """best_index_int8 (quant_iq.rs:1002-1024) as the kernel evaluates it:
+    clamp to [-128, 127] (NaN to the top), neighbouring pair from floor(x),
+    rounded distances compared."""
+    xc = np.maximum(np.minimum(y, f32(127)), f32(-128)).astype(f32)
+    xc = np.where(np.isnan(y), f32(127), xc)
+    mu = 1 + _CNT[np.floor(xc.astype(np.float64)).astype(int) + 128]
+    lower = (xc - KV[mu - 1]).astype(f32) < (KV[mu] - xc).astype(f32)
+    return np.where(lower, mu - 1, mu)
+
+
+def iq4_changes_and_marks(x):
+    ax = np.abs(x)
+    mx = x[np.arange(len(x)), ax.argmax(1)]
+    keep = ax.max(1) >= 1e-15
+    x, mx = x[keep], mx[keep]
+    ids = np.stack([((f32(j - 8) + f32(-127)) / mx).astype(f32) for j in range(1, 16)], 1)
+    idx = iq4_index((ids[:, :, None] * x[:, None, :]).astype(f32))     # trials 1..15
+    changed = np.zeros((len(x), 16), bool)
+    changed[:, 2:] = (idx[:, 1:] != idx[:, :-1]).any(2)
+    marks = np.zeros_like(changed)
+    marks[:, :2] = True
+    lo, hi = np.minimum(idx[:, 0], idx[:, 14]), np.maximum(idx[:, 0], idx[:, 14])
+    assert (hi - lo).max() <= 2
+    with np.errstate(divide="ignore", invalid="ignore"):
+        r = (mx[:, None] / x).astype(f32)
+    for c in (0, 1):
+        k = lo + c
+        active = k < hi
+        t = ((KV[np.clip(k, 0, 14)] + KV[np.clip(k + 1, 0, 15)]) * f32(0.5)).astype(f32)
+        js = (f32(135) + (t * r).astype(f32)).astype(f32)
+        for eps in (-0.01, 0.01):
+            jj = np.ceil(np.clip(np.where(active, js + f32(eps), 2.0), 2.0, 15.0)).astype(int)
+            rows, cols = np.nonzero(active)
+            marks[rows, jj[rows, cols]] = True
+    return changed, marks
+
+
+def test_iq4_marked_trials_cover_every_code_change():
+    x = np.concatenate([bf16_bits_to_f32(student_rows(32, 4096, seed=23)[0]).reshape(-1, 32),
+                        bf16_bits_to_f32(sweep_rows(8, 14336, seed=24)[0]).reshape(-1, 32),
+                        edge_rows(512).astype(np.float32).reshape(-1, 32)])
+    changed, marks = iq4_changes_and_marks(x)
+    assert not (changed & ~marks).any()
+    assert marks.sum(1).mean() < 0.6 * 16
