@@ -1,12 +1,14 @@
 // K-quant and Q8_0 encoders for sm_100a.
 //
 // Parity contract: every kernel reproduces src/quant.rs bit for bit.  The
-// scale searches evaluate all candidate grids in parallel (one lane owns one
+// scale searches evaluate candidate grids in parallel (one lane owns one
 // (sub-block, candidate) pair and folds its sums serially over the elements,
 // in the reference's order) and then reproduce the reference's sequential
 // selection: a strict `err < best_err` chain is an argmin with first-index
-// tie-break, computed with warp shuffles; the cross-multiplied
-// `sumlx^2 > best*suml2` chain of make_qx_quants is replayed serially.
+// tie-break (warp shuffles, or a shared-memory atomicMin on (error, grid));
+// the cross-multiplied `sumlx^2 > best*suml2` chain of make_qx_quants is
+// replayed serially.  The make_qkx3_quants kernels skip grids whose level
+// vector repeats the previous grid's, which cannot change either choice.
 //
 // Work decomposition: one warp per 256-element super-block (grid-stride over
 // all super-blocks of the tensor), 128-bit loads of the source row into
