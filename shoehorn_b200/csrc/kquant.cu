@@ -214,27 +214,57 @@ __global__ void __launch_bounds__(256, 4) enc_q8_0_kernel(EncArgs a) {
     }
 }
 
+// ceil(t) for 0 <= t <= 2^22 as an int, without the conversion pipe: RU(t +
+// 2^23) is 2^23 + ceil(t), whose low mantissa bits are the result.
+__device__ __forceinline__ int ceil_small(float t) {
+    return (int)(__float_as_uint(__fadd_ru(t, 8388608.0f)) & 0x7FFFFFu);
+}
+
+
 // ---------------------------------------------------------------------------
 // Q6_K (quant.rs:231-291) with make_qx_quants(nmax=32) (quant.rs:34-73) per
 // 16-element sub-block, and Q3_K (ggml block_q3_K layout) with nmax 4, 6-bit
 // signed scale codes and 3-bit levels split into a high-bit mask and 2-bit
-// planes.  Two lanes per sub-block split the 19 candidate grids; the
-// selection chain is replayed serially from shared memory.
+// planes.  A warp per super-block; the candidate grids that differ from
+// their predecessor are dealt over the lanes and the selection chain is
+// replayed serially from shared memory.
 // ---------------------------------------------------------------------------
+// Per-warp workspace of the make_qx_quants kernel.
+struct __align__(16) Qx16Warp {
+    float x[16 * 20];       // sub-block s at 20 s (16-byte aligned rows)
+    float w[16 * 20];
+    float wx[16 * 20];
+    float tab[16][20];      // |iscale| of grids t = is + 9 = 0..18
+    float2 cand[16][20];    // (sumlx, suml2) of evaluated grids
+    float scale[16];
+    float mx[16];
+    unsigned int mask[16];  // evaluated grids; bit 31: finite sub-block
+    uint16_t jobs[16 * 19 + 8];
+    uint8_t out[224];
+    uint8_t l[256];
+};
+
+// make_qx_quants (quant.rs:34-73) with repeated grids skipped: |iscale_t| =
+// (nmax + 0.1 (t - 9))/|max| is non-decreasing in t, so |l_i(t)| =
+// min(round(|iscale_t x_i|), nmax - 1 or nmax by the sign of iscale*x) is
+// non-decreasing with a fixed sign, and grid t repeats grid t-1's levels
+// unless an element crosses a threshold k - 1/2 in between (at most two per
+// element: |y| spans 1.8 |x|/|max|). A repeated candidate has the same
+// (sumlx, suml2) as the one before it, and the selection chain keeps its
+// state whether or not it accepts it, so only marked grids are evaluated:
+// the exact levels at grids 0 and 18 count the crossings and the estimate
+// t ~ 10 (thr |max|/|x| - nmax) + 9, good to well within 0.01 of a grid,
+// places each one. The (sub-block, grid) jobs are dealt over the 32 lanes.
 template <int NMAX>
 __global__ void __launch_bounds__(256, 3) enc_qx16_kernel(EncArgs a) {
     constexpr float FN = (float)NMAX;
     constexpr int OUT = NMAX == 32 ? 210 : 110;
-    __shared__ float s_x[8][16 * 17];
-    __shared__ float s_w[8][16 * 17];
-    __shared__ float2 s_cand[8][16][20];
-    __shared__ float s_scale[8][16];
-    __shared__ __align__(16) uint8_t s_out[8][224];
-    __shared__ uint8_t s_l[8][256];
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    extern __shared__ __align__(16) uint8_t qx16_smem[];
+    Qx16Warp *W = reinterpret_cast<Qx16Warp *>(qx16_smem) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
     const int s = lane >> 1, q = lane & 1;
     const int64_t ne0 = a.src.ne0, nsb = ne0 >> 8, total = a.n_rows * nsb;
-    for (int64_t g = (int64_t)blockIdx.x * 8 + wid; g < total; g += (int64_t)gridDim.x * 8) {
+    for (int64_t g = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); g < total; g += (int64_t)gridDim.x * 8) {
         const int64_t row = g / nsb;
         const int64_t sbi = g - row * nsb;
         const int64_t col0 = sbi << 8;
@@ -243,75 +273,148 @@ __global__ void __launch_bounds__(256, 3) enc_qx16_kernel(EncArgs a) {
         float v[8], base[8];
         load8(a.src, row, col0 + lane * 8, v);
         load_im8(imr, col0 + lane * 8, base);
+        {
+            float wk[8];
 #pragma unroll
-        for (int k = 0; k < 8; k++) {
-            s_x[wid][s * 17 + q * 8 + k] = v[k];
-            s_w[wid][s * 17 + q * 8 + k] = base[k] * sqrtf(sig + v[k] * v[k]);
+            for (int k = 0; k < 8; k++) wk[k] = base[k] * sqrtf(sig + v[k] * v[k]);
+            float4 *px = reinterpret_cast<float4 *>(&W->x[s * 20 + q * 8]);
+            float4 *pw = reinterpret_cast<float4 *>(&W->w[s * 20 + q * 8]);
+            float4 *pwx = reinterpret_cast<float4 *>(&W->wx[s * 20 + q * 8]);
+            px[0] = make_float4(v[0], v[1], v[2], v[3]);
+            px[1] = make_float4(v[4], v[5], v[6], v[7]);
+            pw[0] = make_float4(wk[0], wk[1], wk[2], wk[3]);
+            pw[1] = make_float4(wk[4], wk[5], wk[6], wk[7]);
+            pwx[0] = make_float4(wk[0] * v[0], wk[1] * v[1], wk[2] * v[2], wk[3] * v[3]);
+            pwx[1] = make_float4(wk[4] * v[4], wk[5] * v[5], wk[6] * v[6], wk[7] * v[7]);
         }
-        __syncwarp();
-        float x[16], w[16], wx[16];
-#pragma unroll
-        for (int i = 0; i < 16; i++) {
-            x[i] = s_x[wid][s * 17 + i];
-            w[i] = s_w[wid][s * 17 + i];
-            wx[i] = w[i] * x[i];
-        }
-        // make_qx_quants: max |x| (first strict maximum wins)
+        // max |x| of the sub-block, first strict maximum (quant.rs:38-44)
         float amax = 0.0f, mx = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-            const float av = fabsf(x[i]);
-            if (av > amax) { amax = av; mx = x[i]; }
+        for (int k = 0; k < 8; k++) {
+            const float av = fabsf(v[k]);
+            if (av > amax) { amax = av; mx = v[k]; }
+        }
+        {
+            const float oa = __shfl_xor_sync(0xffffffffu, amax, 1), om = __shfl_xor_sync(0xffffffffu, mx, 1);
+            if (q == 0 ? oa > amax : !(amax > oa)) { amax = oa; mx = om; }
         }
         const bool live = !(amax < kGroupMaxEps);
         // with finite inputs iscale*x is finite, so the NaN -> 0 rule of the
         // saturating cast cannot trigger and the plain clamp is exact
         float xsum = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 16; i++) xsum += x[i] * 0.0f;
+        for (int k = 0; k < 8; k++) xsum += v[k] * 0.0f;
+        xsum += __shfl_xor_sync(0xffffffffu, xsum, 1);
         const bool finite = xsum == 0.0f;
         if (live) {
-            const int is0 = q == 0 ? -9 : 1;
-            const int ncand = q == 0 ? 10 : 9;
-            for (int t = 0; t < ncand; t++) {
-                const int is = is0 + t;
-                const float iscale = -(FN + 0.1f * (float)is) / mx;
-                float sumlx = 0.0f, suml2 = 0.0f;
-                if (finite) {
-                    // element pairs in packed f32x2: the products feed the
-                    // rounding's round-toward-zero add or the scalar sums only
-                    const float2 is2 = make_float2(iscale, iscale);
-#pragma unroll
-                    for (int i = 0; i < 16; i += 2) {
-                        const float2 y = __fmul2_rn(is2, make_float2(x[i], x[i + 1]));
-                        const float2 r = floor_half_up2(make_float2(fabsf(y.x), fabsf(y.y)));
-                        const float2 l = make_float2(fminf(fmaxf(copysignf(r.x, y.x), -FN), FN - 1.0f),
-                                                     fminf(fmaxf(copysignf(r.y, y.y), -FN), FN - 1.0f));
-                        const float2 lx = __fmul2_rn(make_float2(wx[i], wx[i + 1]), l);
-                        const float2 l2 = __fmul2_rn(make_float2(w[i], w[i + 1]), __fmul2_rn(l, l));
-                        sumlx = __fadd_rn(sumlx, lx.x);
-                        suml2 = __fadd_rn(suml2, l2.x);
-                        sumlx = __fadd_rn(sumlx, lx.y);
-                        suml2 = __fadd_rn(suml2, l2.y);
-                    }
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 16; i++) {
-                        const float l = round_clamp_f(iscale * x[i], -FN, FN - 1.0f);
-                        sumlx += wx[i] * l;
-                        suml2 += w[i] * (l * l);
-                    }
-                }
-                s_cand[wid][s][is + 9] = make_float2(sumlx, suml2);
-            }
+            for (int t = q; t < 19; t += 2) W->tab[s][t] = fabsf(-(FN + 0.1f * (float)(t - 9)) / mx);
         }
         __syncwarp();
-        float best_scale = 0.0f;
-        if (live && q == 0) {
-            float best = 0.0f;
+        unsigned int mask = 0;
+        if (live && finite) {
+            const float t0 = W->tab[s][0], t18 = W->tab[s][18];
+            const float amx = fabsf(mx);
+            mask = 1u;
+#pragma unroll 1
+            for (int k = 0; k < 8; k++) {
+                const float xv = W->x[s * 20 + q * 8 + k];
+                const float ax = fabsf(xv);
+                // iscale*x > 0 (sign of x differs from max's) clamps at nmax - 1
+                const float cap = (xv != 0.0f && (signbit(xv) != signbit(mx))) ? FN - 1.0f : FN;
+                const float m0 = fminf(floor_half_up(__fmul_rn(t0, ax)), cap);
+                const float m18 = fminf(floor_half_up(__fmul_rn(t18, ax)), cap);
+                if (m18 > m0) {
+                    const float ru = amx / ax;
+#pragma unroll
+                    for (int c = 1; c <= 2; c++) {
+                        const float thr = m0 + ((float)c - 0.5f);
+                        if (thr < m18) {
+                            const float z = 10.0f * (thr * ru - FN) + 9.0f;
+                            mask |= 1u << ceil_small(fminf(fmaxf(z - 0.01f, 0.5f), 18.0f));
+                            mask |= 1u << ceil_small(fminf(fmaxf(z + 0.01f, 0.5f), 18.0f));
+                        }
+                    }
+                }
+            }
+        } else if (live) {
+            mask = (1u << 19) - 1;
+        }
+        mask |= __shfl_xor_sync(0xffffffffu, mask, 1);
+        // job list: lane q lists the grids among bits [10 q, 10 q + 10)
+        const int cnt = __popc(mask);
+        int incl = q == 0 ? cnt : 0;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, incl, off);
+            if (lane >= off) incl += t;
+        }
+        const int njobs = __shfl_sync(0xffffffffu, incl, 31);
+        {
+            int pos = __shfl_sync(0xffffffffu, incl, lane - q) - cnt + (q ? __popc(mask & 0x3FFu) : 0);
+            unsigned int bits = q ? (mask >> 10) : (mask & 0x3FFu);
+            while (bits != 0) {
+                W->jobs[pos++] = (uint16_t)((s << 8) | ((q ? 10 : 0) + __ffs(bits) - 1));
+                bits &= bits - 1;
+            }
+        }
+        if (q == 0) {
+            W->mask[s] = mask | (finite ? 0x80000000u : 0u);
+            W->mx[s] = mx;
+        }
+        __syncwarp();
+        // (sumlx, suml2) of the listed grids (quant.rs:48-63)
+#pragma unroll 1
+        for (int jj = lane; jj < njobs; jj += 32) {
+            const int code = W->jobs[jj];
+            const int js = code >> 8, t = code & 0xFF;
+            float x[16], w[16], wx[16];
+#pragma unroll
+            for (int i = 0; i < 16; i += 4) {
+                const float4 a4 = *reinterpret_cast<const float4 *>(&W->x[js * 20 + i]);
+                const float4 b4 = *reinterpret_cast<const float4 *>(&W->w[js * 20 + i]);
+                const float4 c4 = *reinterpret_cast<const float4 *>(&W->wx[js * 20 + i]);
+                x[i] = a4.x; x[i + 1] = a4.y; x[i + 2] = a4.z; x[i + 3] = a4.w;
+                w[i] = b4.x; w[i + 1] = b4.y; w[i + 2] = b4.z; w[i + 3] = b4.w;
+                wx[i] = c4.x; wx[i + 1] = c4.y; wx[i + 2] = c4.z; wx[i + 3] = c4.w;
+            }
+            // -(nmax + 0.1 is)/max: the magnitude from the table, the sign of -max
+            const float iscale = copysignf(W->tab[js][t], -W->mx[js]);
+            float sumlx = 0.0f, suml2 = 0.0f;
+            if (W->mask[js] & 0x80000000u) {
+                const float2 is2 = make_float2(iscale, iscale);
+#pragma unroll
+                for (int i = 0; i < 16; i += 2) {
+                    const float2 y = __fmul2_rn(is2, make_float2(x[i], x[i + 1]));
+                    const float2 r = floor_half_up2(make_float2(fabsf(y.x), fabsf(y.y)));
+                    const float2 l = make_float2(fminf(fmaxf(copysignf(r.x, y.x), -FN), FN - 1.0f),
+                                                 fminf(fmaxf(copysignf(r.y, y.y), -FN), FN - 1.0f));
+                    const float2 lx = __fmul2_rn(make_float2(wx[i], wx[i + 1]), l);
+                    const float2 l2 = __fmul2_rn(make_float2(w[i], w[i + 1]), __fmul2_rn(l, l));
+                    sumlx = __fadd_rn(sumlx, lx.x);
+                    suml2 = __fadd_rn(suml2, l2.x);
+                    sumlx = __fadd_rn(sumlx, lx.y);
+                    suml2 = __fadd_rn(suml2, l2.y);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    const float l = round_clamp_f(iscale * x[i], -FN, FN - 1.0f);
+                    sumlx += wx[i] * l;
+                    suml2 += w[i] * (l * l);
+                }
+            }
+            W->cand[js][t] = make_float2(sumlx, suml2);
+        }
+        __syncwarp();
+        // the selection chain (quant.rs:64-70) over the evaluated grids
+        if (q == 0) {
+            float best_scale = 0.0f, best = 0.0f;
             bool first = true;
-            for (int c = 0; c < 19; c++) {
-                const float2 cs = s_cand[wid][s][c];
+            unsigned int m = mask;
+            while (m != 0) {
+                const int c = __ffs(m) - 1;
+                m &= m - 1;
+                const float2 cs = W->cand[s][c];
                 if (cs.y > 0.0f && (first || cs.x * cs.x > best * cs.y)) {
                     const float sc = cs.x / cs.y;
                     best_scale = sc;
@@ -319,19 +422,17 @@ __global__ void __launch_bounds__(256, 3) enc_qx16_kernel(EncArgs a) {
                     first = false;
                 }
             }
-            s_scale[wid][s] = best_scale;
-        } else if (!live && q == 0) {
-            s_scale[wid][s] = 0.0f;
+            W->scale[s] = best_scale;
         }
         __syncwarp();
-        best_scale = s_scale[wid][s];
+        const float best_scale = W->scale[s];
         float max_abs = 0.0f, max_scale = 0.0f;
 #pragma unroll
         for (int sb = 0; sb < 16; sb++) {
-            const float sv = s_scale[wid][sb];
+            const float sv = W->scale[sb];
             if (fabsf(sv) > max_abs) { max_abs = fabsf(sv); max_scale = sv; }
         }
-        uint8_t *o = s_out[wid];
+        uint8_t *o = W->out;
         if (max_abs < kGroupMaxEps) {
             for (int i = lane; i < OUT; i += 32) o[i] = 0;
         } else if (NMAX == 32) {  // Q6_K (quant.rs:258-290)
@@ -343,7 +444,7 @@ __global__ void __launch_bounds__(256, 3) enc_qx16_kernel(EncArgs a) {
 #pragma unroll
             for (int k = 0; k < 8; k++) {
                 const int l = dd == 0.0f ? 32 : (int)round_clamp_f(v[k] / dd, -32.0f, 31.0f) + 32;
-                s_l[wid][lane * 8 + k] = (uint8_t)l;
+                W->l[lane * 8 + k] = (uint8_t)l;
             }
             if (q == 0) o[192 + s] = (uint8_t)qsc;
             if (lane == 0) {
@@ -352,7 +453,7 @@ __global__ void __launch_bounds__(256, 3) enc_qx16_kernel(EncArgs a) {
                 o[209] = (uint8_t)(h >> 8);
             }
             __syncwarp();
-            const uint8_t *L = s_l[wid];
+            const uint8_t *L = W->l;
 #pragma unroll
             for (int h = 0; h < 2; h++) {
                 const uint8_t *lo = L + h * 128;
@@ -370,7 +471,7 @@ __global__ void __launch_bounds__(256, 3) enc_qx16_kernel(EncArgs a) {
 #pragma unroll
             for (int k = 0; k < 8; k++) {
                 const int l = dd == 0.0f ? 4 : (int)round_clamp_f(v[k] / dd, -4.0f, 3.0f) + 4;
-                s_l[wid][lane * 8 + k] = (uint8_t)l;
+                W->l[lane * 8 + k] = (uint8_t)l;
             }
             // scale codes u = qsc + 32 of every sub-block, from its even lane
             const int u = qsc + 32;
@@ -388,7 +489,7 @@ __global__ void __launch_bounds__(256, 3) enc_qx16_kernel(EncArgs a) {
                 o[109] = (uint8_t)(h >> 8);
             }
             __syncwarp();
-            const uint8_t *L = s_l[wid];
+            const uint8_t *L = W->l;
             uint8_t hm = 0;  // hmask byte `lane`: bit j = high bit of element j*32 + lane
 #pragma unroll
             for (int j = 0; j < 8; j++) hm |= (uint8_t)(((L[j * 32 + lane] >> 2) & 1) << j);
@@ -542,11 +643,6 @@ __device__ __forceinline__ float err_from_key(unsigned int k) {
     return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
 }
 
-// ceil(t) for 0 <= t <= 2^22 as an int, without the conversion pipe: RU(t +
-// 2^23) is 2^23 + ceil(t), whose low mantissa bits are the result.
-__device__ __forceinline__ int ceil_small(float t) {
-    return (int)(__float_as_uint(__fadd_ru(t, 8388608.0f)) & 0x7FFFFFu);
-}
 
 template <int N, int NMAX>
 __device__ __forceinline__ void qkx3_super_blocks(const EncArgs &a, Qkx3Warp<N> *W) {
@@ -1178,24 +1274,30 @@ static cudaError_t launch_qkx3(void (*fn)(EncArgs), const EncArgs &a, int num_sm
     return cudaGetLastError();
 }
 
+static cudaError_t launch_qx16(void (*fn)(EncArgs), const EncArgs &a, int num_sms, cudaStream_t st) {
+    const size_t smem = 8 * sizeof(Qx16Warp);
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 1;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, smem);
+    if (per_sm < 1) per_sm = 1;
+    int64_t grid = (a.n_rows * (a.src.ne0 / 256) + 7) / 8;
+    const int64_t cap = (int64_t)num_sms * per_sm;
+    if (grid > cap) grid = cap;
+    if (grid < 1) grid = 1;
+    fn<<<(unsigned)grid, 256, smem, st>>>(a);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_kquant(uint32_t type, const EncArgs &a, int num_sms, cudaStream_t st) {
-    const int64_t nsb = a.src.ne0 / 256;
     switch (type) {
     case SHC_TYPE_Q8_0: {
         unsigned grid = persistent_grid((const void *)enc_q8_0_kernel, 256, num_sms, (a.n_rows * (a.src.ne0 / 32) + 31) / 32);
         enc_q8_0_kernel<<<grid, 256, 0, st>>>(a);
         break;
     }
-    case SHC_TYPE_Q6_K: {
-        unsigned grid = persistent_grid((const void *)enc_qx16_kernel<32>, 256, num_sms, a.n_rows * nsb);
-        enc_qx16_kernel<32><<<grid, 256, 0, st>>>(a);
-        break;
-    }
-    case SHC_TYPE_Q3_K: {
-        unsigned grid = persistent_grid((const void *)enc_qx16_kernel<4>, 256, num_sms, a.n_rows * nsb);
-        enc_qx16_kernel<4><<<grid, 256, 0, st>>>(a);
-        break;
-    }
+    case SHC_TYPE_Q6_K: return launch_qx16(enc_qx16_kernel<32>, a, num_sms, st);
+    case SHC_TYPE_Q3_K: return launch_qx16(enc_qx16_kernel<4>, a, num_sms, st);
     case SHC_TYPE_Q2_K: return launch_qkx3<16>(enc_q2_k_kernel, a, num_sms, st);
     case SHC_TYPE_Q4_K: return launch_qkx3<32>(enc_qk45_kernel<15>, a, num_sms, st);
     case SHC_TYPE_Q5_K: return launch_qkx3<32>(enc_qk45_kernel<31>, a, num_sms, st);

@@ -119,3 +119,47 @@ def test_iq4_marked_trials_cover_every_code_change():
     changed, marks = iq4_changes_and_marks(x)
     assert not (changed & ~marks).any()
     assert marks.sum(1).mean() < 0.6 * 16
+
+
+# ---- make_qx_quants (Q6_K nmax 32, Q3_K nmax 4): 19 grids is = -9..9 ----
+def qx_changes_and_marks(x, nmax):
+    ax = np.abs(x)
+    mx = x[np.arange(len(x)), ax.argmax(1)]
+    keep = (ax.max(1) >= 1e-15) & np.isfinite(x).all(1)
+    x, mx = x[keep], mx[keep]
+    fn = f32(nmax)
+    t = np.arange(19)
+    a = ((fn + (f32(0.1) * (t - 9).astype(f32)).astype(f32)).astype(f32))
+    tab = np.abs((-a[None, :] / mx[:, None]).astype(f32))                # |iscale_t|
+    axv = np.abs(x)
+    y = (tab[:, :, None] * axv[:, None, :]).astype(f32)                   # |iscale_t x|
+    positive = (x != 0) & (np.signbit(x) != np.signbit(mx)[:, None])      # iscale*x > 0
+    cap = np.where(positive, nmax - 1, nmax)
+    lev = np.minimum(np.floor(y.astype(np.float64) + 0.5), cap[:, None, :])
+    changed = np.zeros((len(x), 19), bool)
+    changed[:, 1:] = (lev[:, 1:] != lev[:, :-1]).any(2)
+    marks = np.zeros_like(changed)
+    marks[:, 0] = True
+    m0, m18 = lev[:, 0], lev[:, 18]
+    assert (m18 - m0).max() <= 2
+    with np.errstate(divide="ignore", invalid="ignore"):
+        ru = (np.abs(mx)[:, None] / axv).astype(f32)
+    for c in (1, 2):
+        thr = (m0 + (c - 0.5)).astype(f32)
+        active = thr < m18
+        z = ((f32(10) * ((thr * ru).astype(f32) - fn).astype(f32)).astype(f32) + f32(9)).astype(f32)
+        for eps in (-0.01, 0.01):
+            jj = np.ceil(np.clip(np.where(active, z + f32(eps), 0.5), 0.5, 18.0)).astype(int)
+            rows, cols = np.nonzero(active)
+            marks[rows, jj[rows, cols]] = True
+    return changed, marks
+
+
+@pytest.mark.parametrize("nmax", [32, 4], ids=["Q6_K", "Q3_K"])
+def test_qx_marked_grids_cover_every_level_change(nmax):
+    x = np.concatenate([bf16_bits_to_f32(sweep_rows(8, 14336, seed=25)[0]).reshape(-1, 16),
+                        bf16_bits_to_f32(student_rows(16, 4096, seed=26)[0]).reshape(-1, 16),
+                        edge_rows(512).astype(np.float32).reshape(-1, 16)])
+    changed, marks = qx_changes_and_marks(x, nmax)
+    assert not (changed & ~marks).any()
+    assert marks.sum(1).mean() < 0.6 * 19
