@@ -21,7 +21,6 @@ HOST_SOURCES = ["gguf.cpp", "imatrix.cpp", "solver.cpp", "pipeline.cpp", "synthe
 HOST_HEADERS = ["gguf.hpp", "imatrix.hpp", "solver.hpp", "pipeline.hpp"]
 HOST_LIB = os.path.join(HERE, "libshoehorn_host.so")
 CLI = os.path.join(HERE, "shoehorn-gpu")
-PROBE = os.path.join(HERE, "fp32-rate")
 CUDA_INC = "/usr/local/cuda/include"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FP = ["-fmad=false", "-prec-div=true", "-prec-sqrt=true", "-ftz=false"]
@@ -81,10 +80,6 @@ def build(verbose=False, extra=()):
             hjobs.append([*gxx, "-c", sp, "-o", o])
     with concurrent.futures.ThreadPoolExecutor(max_workers=min(8, max(1, len(hjobs)))) as ex:
         list(ex.map(run, hjobs))
-    # FP32 issue-rate probe (the encoder roofline's denominator)
-    probe_src = os.path.join(CSRC, "fp32_rate.cu")
-    if _stale(PROBE, [probe_src, __file__]):
-        run([nvcc(), *_flags(), *extra, "-o", PROBE, probe_src])
     lib_objs = hobjs[:-1]
     link_common = ["-L" + HERE, "-lshoehorn_cuda", "-Xlinker", "-rpath=$ORIGIN", "-lpthread"]
     if hjobs or _stale(HOST_LIB, lib_objs + [OUT]):

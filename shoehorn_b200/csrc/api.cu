@@ -123,9 +123,14 @@ EncArgs make_args(shc_ctx *ctx, uint32_t src_type, const void *src, int64_t n_ro
     return a;
 }
 
-int check_common(shc_ctx *ctx, uint32_t src_type, const void *src, int64_t n_rows, int64_t ne0, const float *im) {
+int check_common(shc_ctx *ctx, uint32_t src_type, const void *src, int64_t n_rows, int64_t ne0, const float *im,
+                 int64_t rows_per_mat, int64_t row0) {
     if (!ctx) return SHC_EINVAL;
     if (!valid_src_type(src_type) || n_rows < 0 || ne0 <= 0) return SHC_EINVAL;
+    // global row indices and matrix heights are unsigned in the reference
+    // (imatrix.rs:124 row_slice takes usize); a negative one would select a
+    // matrix before the imatrix
+    if (rows_per_mat < 0 || row0 < 0) return SHC_EINVAL;
     if (n_rows > 0 && !src) return SHC_EINVAL;
     if (((uintptr_t)src & 15) != 0) return SHC_EINVAL;  // 128-bit row loads
     if (im && ((uintptr_t)im & 15) != 0) return SHC_EINVAL;
@@ -340,7 +345,7 @@ int64_t shc_launch_count(const shc_ctx *ctx) { return ctx ? ctx->launches.load()
 
 int shc_encode_rows(shc_ctx *ctx, uint32_t type, uint32_t src_type, const void *src, int64_t n_rows, int64_t ne0,
                     const float *im, int64_t im_len, int64_t rows_per_mat, int64_t row0, uint8_t *dst, void *stream) {
-    int rc = check_common(ctx, src_type, src, n_rows, ne0, im);
+    int rc = check_common(ctx, src_type, src, n_rows, ne0, im, rows_per_mat, row0);
     if (rc != SHC_OK) return rc;
     const int64_t rb = shc_row_bytes(type, ne0);
     if (rb < 0 || !encodable(type) || (n_rows > 0 && !dst)) return SHC_EINVAL;
@@ -367,7 +372,7 @@ int shc_decode_rows(shc_ctx *ctx, uint32_t type, const uint8_t *src, int64_t n_r
 int shc_row_errors(shc_ctx *ctx, const uint32_t *types, int n_types, uint32_t src_type, const void *src,
                    int64_t n_rows, int64_t ne0, const float *im, int64_t im_len, int64_t rows_per_mat, int64_t row0,
                    int64_t row_step, double *err, void *stream) {
-    int rc = check_common(ctx, src_type, src, n_rows, ne0, im);
+    int rc = check_common(ctx, src_type, src, n_rows, ne0, im, rows_per_mat, row0);
     if (rc != SHC_OK) return rc;
     if (!types || n_types < 1 || n_types > 32 || row_step < 1) return SHC_EINVAL;
     for (int t = 0; t < n_types; t++)
@@ -442,6 +447,7 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
                            int64_t ne0, const float *host_im, int64_t im_len, int64_t rows_per_mat, int64_t row0,
                            uint8_t *host_dst, int64_t timeout_ms) {
     if (!ctx || !valid_src_type(src_type) || n_rows < 0 || ne0 <= 0 || ne0 % 8 != 0) return SHC_EINVAL;
+    if (rows_per_mat < 0 || row0 < 0) return SHC_EINVAL;
     const int64_t rb = shc_row_bytes(type, ne0);
     if (rb < 0 || !encodable(type)) return SHC_EINVAL;
     if (n_rows == 0) return SHC_OK;
@@ -605,7 +611,7 @@ int shc_row_errors_host(shc_ctx *ctx, const uint32_t *types, int n_types, uint32
                         int64_t n_rows, int64_t ne0, const float *host_im, int64_t im_len, int64_t rows_per_mat,
                         int64_t row0, int64_t row_step, double *err, int64_t timeout_ms) {
     if (!ctx || !valid_src_type(src_type) || n_rows < 0 || ne0 <= 0 || row_step < 1 || !types || n_types < 1 ||
-        n_types > 32)
+        n_types > 32 || rows_per_mat < 0 || row0 < 0)
         return SHC_EINVAL;
     const int64_t n_s = (n_rows + row_step - 1) / row_step;
     if (n_s == 0) return SHC_OK;

@@ -180,7 +180,7 @@ __device__ __forceinline__ const float *im_row(const ImSrc &im, int64_t ne0, int
         int64_t mat = grow / im.rows_per_mat;
         int64_t n_mats = im.len / ne0;
         int64_t m = mat < n_mats - 1 ? mat : n_mats - 1;
-        return im.ptr + m * ne0;
+        return im.ptr + (m > 0 ? m : 0) * ne0;
     }
     return nullptr;
 }

@@ -1190,11 +1190,9 @@ static cudaError_t launch_lattice(const EncArgs &a, const IqTables &iq, int num_
     const size_t smem = ((C::KMAP * 4 + 15) & ~(size_t)15) + NW * sizeof(IqWarpSmem<V>) + 512 +
                         (IqSearch<V>::LISTS_SMEM ? (size_t)iq.lists_bytes[V] : 0);
     auto fn = enc_iq_lattice_kernel<V>;
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
     int per_sm = 1;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, NW * 32, smem);
-    if (per_sm < 1) per_sm = 1;
+    cudaError_t e = resident_blocks((const void *)fn, NW * 32, smem, &per_sm);
+    if (e != cudaSuccess) return e;
     const int64_t work = a.n_rows * (a.src.ne0 / 256);
     int64_t grid = (work + NW - 1) / NW;
     const int64_t cap = (int64_t)num_sms * per_sm;
@@ -1208,8 +1206,8 @@ template <bool XS>
 static cudaError_t launch_iq4(const EncArgs &a, int num_sms, cudaStream_t st) {
     auto fn = enc_iq4_kernel<XS>;
     int per_sm = 1;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, 0);
-    if (per_sm < 1) per_sm = 1;
+    cudaError_t e = resident_blocks((const void *)fn, 256, 0, &per_sm);
+    if (e != cudaSuccess) return e;
     const int64_t units = XS ? a.n_rows * (a.src.ne0 / 256) : (a.n_rows * (a.src.ne0 / 32) + 7) / 8;
     const int64_t cap = (int64_t)num_sms * per_sm;
     int64_t grid = (units + 7) / 8;

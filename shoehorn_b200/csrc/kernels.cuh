@@ -94,6 +94,12 @@ __host__ __device__ inline bool is_iq(uint32_t t) {
     }
 }
 
+// Resident blocks per SM of kernel `fn` launched with `threads` threads and
+// `smem` bytes of dynamic shared memory on the current device, after raising
+// the kernel's dynamic shared-memory limit to `smem`.  Computed once per
+// (device, kernel, shape) and cached, so a launch pays no occupancy query.
+cudaError_t resident_blocks(const void *fn, int threads, size_t smem, int *per_sm);
+
 // Launchers (return a cudaError_t).  num_sms sizes the persistent grids.
 cudaError_t launch_row_sigma2(const RowSrc &src, int64_t n_rows, float *out, cudaStream_t st);
 cudaError_t launch_kquant(uint32_t type, const EncArgs &a, int num_sms, cudaStream_t st);

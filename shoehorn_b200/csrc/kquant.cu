@@ -13,6 +13,10 @@
 // Work decomposition: one warp per 256-element super-block (grid-stride over
 // all super-blocks of the tensor), 128-bit loads of the source row into
 // registers/shared memory, the imatrix slice read through the read-only path.
+#include <map>
+#include <mutex>
+#include <tuple>
+
 #include "kernels.cuh"
 
 namespace shc {
@@ -980,6 +984,58 @@ __global__ void __launch_bounds__(256, 2) enc_q2_k_kernel(EncArgs a) {
 // rows may change inside a group), 4 lanes per block.
 // KIND: 0 Q4_0, 1 Q5_0, 2 Q4_1, 3 Q5_1
 // ---------------------------------------------------------------------------
+// Levels (l + nmax) that make_qx_quants (quant.rs:34-73) writes for one
+// 32-element block of row `row` starting at column `col`, recomputed
+// serially by one lane; false when the block accepts no grid and writes
+// nothing.  Same arithmetic, in the same order, as the cooperative search
+// in enc_legacy_kernel.
+template <int NMAX>
+__device__ bool legacy_sym_levels(const EncArgs &a, int64_t row, int64_t col, uint8_t *out) {
+    constexpr float FN = (float)NMAX;
+    float x[32], w[32];
+    const float sig = a.sigma2[row];
+    const float *imr = im_row(a.im, a.src.ne0, a.row0 + row * a.row_step);
+    for (int m = 0; m < 4; m++) {
+        float v[8], base[8];
+        load8(a.src, row, col + m * 8, v);
+        load_im8(imr, col + m * 8, base);
+        for (int k = 0; k < 8; k++) {
+            x[m * 8 + k] = v[k];
+            w[m * 8 + k] = base[k] * sqrtf(sig + v[k] * v[k]);
+        }
+    }
+    float amax = 0.0f, mx = 0.0f;
+    for (int i = 0; i < 32; i++) {
+        const float av = fabsf(x[i]);
+        if (av > amax) { amax = av; mx = x[i]; }
+    }
+    if (amax < kGroupMaxEps) {
+        for (int i = 0; i < 32; i++) out[i] = (uint8_t)NMAX;
+        return true;
+    }
+    float best = 0.0f;
+    bool first = true;
+    int win = -1;
+    for (int t = 0; t < 19; t++) {
+        const float iscale = -(FN + 0.1f * (float)(t - 9)) / mx;
+        float sumlx = 0.0f, suml2 = 0.0f;
+        for (int i = 0; i < 32; i++) {
+            const float l = round_clamp_f(iscale * x[i], -FN, FN - 1.0f);
+            sumlx += w[i] * x[i] * l;
+            suml2 += w[i] * (l * l);
+        }
+        if (suml2 > 0.0f && (first || sumlx * sumlx > best * suml2)) {
+            best = (sumlx / suml2) * sumlx;
+            first = false;
+            win = t;
+        }
+    }
+    if (win < 0) return false;
+    const float iscale = -(FN + 0.1f * (float)(win - 9)) / mx;
+    for (int i = 0; i < 32; i++) out[i] = (uint8_t)(clampi(nearest_int(iscale * x[i]), -NMAX, NMAX - 1) + NMAX);
+    return true;
+}
+
 template <int KIND>
 __global__ void __launch_bounds__(256) enc_legacy_kernel(EncArgs a) {
     constexpr bool SYM = KIND < 2;
@@ -1067,7 +1123,7 @@ __global__ void __launch_bounds__(256) enc_legacy_kernel(EncArgs a) {
                     mode = 1;
                     win_iscale = -(FN + 0.1f * (float)(win - 9)) / mx;
                 } else {
-                    mode = 2;  // no grid accepted: the level vector stays all zero
+                    mode = 2;  // no grid accepted: the previous block's levels stay (below)
                 }
             }
         } else {
@@ -1170,12 +1226,26 @@ __global__ void __launch_bounds__(256) enc_legacy_kernel(EncArgs a) {
             win_vmin = vmin;
         }
         // levels of this lane's 8 elements
+        if (!SYM || mode != 2) {
 #pragma unroll
-        for (int k = 0; k < 8; k++) {
-            int l;
-            if (SYM) l = mode == 1 ? clampi(nearest_int(win_iscale * v[k]), -NMAX, NMAX - 1) + NMAX : (mode == 0 ? NMAX : 0);
-            else l = mode == 1 ? clampi(nearest_int(win_iscale * (v[k] - win_vmin)), 0, NMAX) : 0;
-            s_l[wid][lane * 8 + k] = (uint8_t)l;
+            for (int k = 0; k < 8; k++) {
+                int l;
+                if (SYM) l = mode == 1 ? clampi(nearest_int(win_iscale * v[k]), -NMAX, NMAX - 1) + NMAX : NMAX;
+                else l = mode == 1 ? clampi(nearest_int(win_iscale * (v[k] - win_vmin)), 0, NMAX) : 0;
+                s_l[wid][lane * 8 + k] = (uint8_t)l;
+            }
+        } else if (q == 0) {
+            // make_qx_quants wrote nothing: the reference's level buffer `ls`
+            // outlives the block loop (quant.rs:172, 186) and still holds the
+            // levels of the nearest earlier block of this row that wrote
+            // some, or zeros (it starts zeroed for every row).  Rare (a block
+            // whose weighted level energy is zero or NaN for every grid), so
+            // one lane walks back through the row recomputing blocks.
+            uint8_t *lv = &s_l[wid][b * 32];
+            bool found = false;
+            for (int64_t c = col - 32; c >= 0 && !found; c -= 32) found = legacy_sym_levels<NMAX>(a, row, c, lv);
+            if (!found)
+                for (int i = 0; i < 32; i++) lv[i] = 0;
         }
         __syncwarp();
         {
@@ -1243,12 +1313,41 @@ cudaError_t launch_plain(uint32_t type, const EncArgs &a, int num_sms, cudaStrea
     return cudaGetLastError();
 }
 
+cudaError_t resident_blocks(const void *fn, int threads, size_t smem, int *per_sm) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    using Key = std::tuple<int, const void *, int, size_t>;
+    static std::mutex mu;
+    static std::map<Key, int> cache;
+    const Key key{dev, fn, threads, smem};
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) {
+            *per_sm = it->second;
+            return cudaSuccess;
+        }
+    }
+    if (smem > 0) {
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    int n = 1;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, threads, smem);
+    if (e != cudaSuccess) return e;
+    if (n < 1) n = 1;
+    std::lock_guard<std::mutex> lk(mu);
+    cache[key] = n;
+    *per_sm = n;
+    return cudaSuccess;
+}
+
 // Grid for the persistent warp-per-super-block kernels: enough CTAs to fill
 // every SM at the occupancy the kernel reaches, never more than the work.
 static unsigned persistent_grid(const void *fn, int threads, int num_sms, int64_t work_warps) {
     int per_sm = 1;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, 0);
-    if (per_sm < 1) per_sm = 1;
+    if (resident_blocks(fn, threads, 0, &per_sm) != cudaSuccess) per_sm = 1;
     int64_t want = (work_warps + threads / 32 - 1) / (threads / 32);
     int64_t cap = (int64_t)num_sms * per_sm;
     if (want > cap) want = cap;
@@ -1261,11 +1360,9 @@ static unsigned persistent_grid(const void *fn, int threads, int num_sms, int64_
 template <int N>
 static cudaError_t launch_qkx3(void (*fn)(EncArgs), const EncArgs &a, int num_sms, cudaStream_t st) {
     const size_t smem = kQkx3Warps * sizeof(Qkx3Warp<N>);
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
     int per_sm = 1;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kQkx3Warps * 32, smem);
-    if (per_sm < 1) per_sm = 1;
+    cudaError_t e = resident_blocks((const void *)fn, kQkx3Warps * 32, smem, &per_sm);
+    if (e != cudaSuccess) return e;
     int64_t grid = (a.n_rows * (a.src.ne0 / 256) + kQkx3Warps - 1) / kQkx3Warps;
     const int64_t cap = (int64_t)num_sms * per_sm;
     if (grid > cap) grid = cap;
@@ -1276,11 +1373,9 @@ static cudaError_t launch_qkx3(void (*fn)(EncArgs), const EncArgs &a, int num_sm
 
 static cudaError_t launch_qx16(void (*fn)(EncArgs), const EncArgs &a, int num_sms, cudaStream_t st) {
     const size_t smem = 8 * sizeof(Qx16Warp);
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
     int per_sm = 1;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, smem);
-    if (per_sm < 1) per_sm = 1;
+    cudaError_t e = resident_blocks((const void *)fn, 256, smem, &per_sm);
+    if (e != cudaSuccess) return e;
     int64_t grid = (a.n_rows * (a.src.ne0 / 256) + 7) / 8;
     const int64_t cap = (int64_t)num_sms * per_sm;
     if (grid > cap) grid = cap;

@@ -54,7 +54,7 @@ extern "C" int shc_encode_rows_noalloc(uint32_t type, uint32_t src_type, const v
                                        int64_t row0, uint8_t *dst, void *stream) {
     if (type != SHC_TYPE_Q4_K && type != SHC_TYPE_Q5_K && type != SHC_TYPE_Q6_K) return SHC_EINVAL;
     if (src_type != SHC_SRC_F32 && src_type != SHC_SRC_F16 && src_type != SHC_SRC_BF16) return SHC_EINVAL;
-    if (n_rows < 0 || ne0 <= 0 || ne0 % 256 != 0) return SHC_EINVAL;
+    if (n_rows < 0 || ne0 <= 0 || ne0 % 256 != 0 || rows_per_mat < 0 || row0 < 0) return SHC_EINVAL;
     if (n_rows > kMaxRows) return SHC_ETOOLARGE;
     if (n_rows == 0) return SHC_OK;
     if (!src || !dst || ((uintptr_t)src & 15) != 0 || (im && ((uintptr_t)im & 15) != 0)) return SHC_EINVAL;

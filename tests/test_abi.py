@@ -69,3 +69,17 @@ def test_grid_info_host_only():
     assert int((kmap >= 0).sum()) == 256
     gs, kmap, nb = sh.grid_info(4)
     assert gs == 512 and kmap.size == 4096 and int((kmap >= 0).sum()) == 512
+
+
+def test_negative_row_indices_rejected_before_any_launch():
+    """Global row indices and matrix heights are unsigned in the reference
+    (imatrix.rs:124 row_slice takes usize): negative ones are refused before
+    anything touches a device."""
+    L = sh.lib()
+    f = L.shc_encode_rows_noalloc
+    f.argtypes = [ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                  ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]
+    f.restype = ctypes.c_int
+    assert f(12, 30, 256, 4, 256, 256, 512, 2, -1, 256, None) == -1   # row0 < 0
+    assert f(12, 30, 256, 4, 256, 256, 512, -2, 0, 256, None) == -1   # rows_per_mat < 0
+    assert L.shc_encode_tensor_host(None, 12, 30, None, 1, 256, None, 0, 0, -1, None, 0) == -1

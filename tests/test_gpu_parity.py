@@ -69,12 +69,37 @@ def test_encode_matches_oracle_sweep_rows(ctx, ty):
     assert_bytes_equal(gpu_encode(ctx, ty, bits, im), oracle_encode(ty, bits, im), ty)
 
 
-@pytest.mark.parametrize("ty", supported(KQ) + supported([20, 23]), ids=lambda t: NAMES[t])
+@pytest.mark.parametrize("ty", supported(KQ + IQ), ids=lambda t: NAMES[t])
 def test_encode_matches_oracle_many_rows(ctx, ty):
     """4096 rows x 1024 (16384 super-blocks): enough near-ties between grid
     errors that a single contracted multiply-add in a search shows up."""
     bits, im = sweep_rows(4096, 1024, seed=5)
     assert_bytes_equal(gpu_encode(ctx, ty, bits, im), oracle_encode(ty, bits, im), ty)
+
+
+@pytest.fixture(scope="module")
+def iq_config():
+    """The IQ codebook configuration's tensors ([4096 x 4096] and
+    [14336 x 4096] Student-t, nu = 5, with the log-normal imatrix)."""
+    from shoehorn_b200 import workloads
+    return workloads.iq_tensors()
+
+
+@pytest.mark.parametrize("ty", supported(IQ), ids=lambda t: NAMES[t])
+def test_iq_configuration_rows_match_oracle(ctx, iq_config, ty):
+    """quant_iq.rs:275-1157 on the IQ configuration as configured (Student-t
+    weights AND the imatrix): 1024 rows spread over each of the two tensors,
+    32768 super-blocks per type, byte for byte."""
+    for name, bits, im in iq_config:
+        rows = np.linspace(0, bits.shape[0] - 1, 1024).astype(np.int64)
+        sub = np.ascontiguousarray(bits[rows])
+        assert_bytes_equal(gpu_encode(ctx, ty, sub, im), oracle_encode(ty, sub, im), ty)
+
+
+def test_negative_row0_is_rejected(ctx):
+    bits, im = sweep_rows(4, 256, seed=1)
+    with pytest.raises(sh.ShoehornError):
+        gpu_encode(ctx, 12, bits, np.concatenate([im, im]), rows_per_mat=2, row0=-1)
 
 
 @pytest.mark.parametrize("ty", ENC_TYPES, ids=lambda t: NAMES[t])
@@ -109,6 +134,27 @@ def q8_0_special_rows():
     x[2, 32:64] = np.float32(-0.0)
     x[3, :] = np.float32(-1.5)
     return f32_to_bf16_bits(x)
+
+
+@pytest.mark.parametrize("ty", [2, 6, 3, 7], ids=lambda t: NAMES[t])
+def test_legacy_blocks_without_an_accepted_grid_keep_earlier_levels(ctx, ty):
+    """quant.rs:171-198: make_qx_quants writes no levels when no grid is
+    accepted (zero or NaN weighted level energy for all 19 grids), and the
+    row's level buffer keeps the nearest earlier block's levels, or zeros.
+    Zero imatrix windows over whole blocks, a NaN (its row's sigma^2 and so
+    every weight turns NaN) and a sub-epsilon block (which writes nmax)."""
+    bits, im = sweep_rows(6, 1024, seed=77)
+    im = im.copy()
+    im[0:32] = 0.0        # block 0: nothing accepted, nothing earlier -> zeros
+    im[64:128] = 0.0      # blocks 2, 3 carry block 1's levels
+    im[500:540] = 0.0     # partial windows: still accepted
+    x = bf16_bits_to_f32(bits)
+    x[3, 200] = np.nan    # row 3: every block rejects -> zeros... or an earlier block
+    x[4, 0:32] = 0.0      # row 4: block 0 is below GROUP_MAX_EPS and writes nmax,
+    x[4, 40] = np.nan     #        every later block carries those levels
+    bits = f32_to_bf16_bits(x)
+    assert_bytes_equal(gpu_encode(ctx, ty, bits, im), oracle_encode(ty, bits, im), ty)
+    assert_bytes_equal(gpu_encode(ctx, ty, bits, None), oracle_encode(ty, bits, None), ty)
 
 
 def test_q8_0_special_values(ctx):
@@ -231,8 +277,8 @@ def test_full_size_encode(ctx, big_tensor, ty):
     assert torch.equal(a, b)  # deterministic
     codes = a.cpu().numpy()
     rng = np.random.default_rng(ty)
-    rows = np.sort(rng.choice(4096, size=6, replace=False))
-    rows[0], rows[-1] = 0, 4095
+    rows = np.sort(rng.choice(np.arange(1, 4095), size=62, replace=False))
+    rows = np.concatenate([[0], rows, [4095]])  # 64 rows, first and last included
     want = O.encode_tensor_bf16(ty, bits[rows], im)
     assert_bytes_equal(codes[rows], want, ty)
     # decode of every row stays within the reference's round-trip tolerance band
