@@ -18,7 +18,7 @@ SOURCES = ["api.cu", "kquant.cu", "decode.cu", "iq.cu", "iq_host.cpp", "noalloc.
 HEADERS = ["common.cuh", "kernels.cuh", "iq_host.h", "iq_tables.h"]
 HOST = os.path.join(HERE, "host")
 HOST_SOURCES = ["gguf.cpp", "imatrix.cpp", "solver.cpp", "pipeline.cpp", "synthetic.cpp", "host_api.cpp"]
-HOST_HEADERS = ["gguf.hpp", "imatrix.hpp", "solver.hpp", "pipeline.hpp"]
+HOST_HEADERS = ["gguf.hpp", "imatrix.hpp", "solver.hpp", "pipeline.hpp", "shard.hpp"]
 HOST_LIB = os.path.join(HERE, "libshoehorn_host.so")
 CLI = os.path.join(HERE, "shoehorn-gpu")
 CUDA_INC = "/usr/local/cuda/include"

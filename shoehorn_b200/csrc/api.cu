@@ -170,34 +170,43 @@ int encode_view(shc_ctx *ctx, uint32_t type, EncArgs a, cudaStream_t st, int sms
 
 // Re-encode the host lists (quant_iq.rs neighbour order kept) into the layout
 // the device encoder of variant w reads, with kmap offsets remapped.
+//   IQ2 (w 0..2, scanned cooperatively in groups of four): the count sits in
+//   the entry slot just before a four-entry boundary and the entries follow,
+//   padded to a multiple of four with copies of the list's last entry (a
+//   later copy never wins: the scan keeps the first of equal distances).
+//   IQ2_XXS entries are 8-bit grid indices (lists of at most 255), IQ2_XS
+//   and IQ2_S entries 16-bit packed coordinates.
+//   IQ3 (w 3, 4, scanned per lane from shared memory): 16-bit count, then
+//   the 16-bit packed coordinates.
 void device_lists(int w, const IqHostTable &t, std::vector<int32_t> &kmap, std::vector<uint8_t> &bytes) {
     kmap = t.kmap;
     bytes.clear();
+    const size_t esz = w == 0 ? 1 : 2;
+    auto put = [&](size_t slot, uint32_t v) {
+        if ((slot + 1) * esz > bytes.size()) bytes.resize((slot + 1) * esz, 0);
+        if (esz == 1) bytes[slot] = (uint8_t)v;
+        else reinterpret_cast<uint16_t *>(bytes.data())[slot] = (uint16_t)v;
+    };
     for (size_t c = 0; c < t.kmap.size(); c++) {
         const int32_t m = t.kmap[c];
         if (m >= 0) continue;
         const size_t off = (size_t)(-m - 1);
         const uint32_t n = t.neighbours[off];
-        if (w == 0) {  // 8-bit grid indices (256-point grid, lists of at most 255)
-            kmap[c] = -(int32_t)(bytes.size() + 1);
-            bytes.push_back((uint8_t)n);
-            for (uint32_t k = 1; k <= n; k++) bytes.push_back((uint8_t)(t.neighbours[off + k] & 0xFFFF));
-        } else if (w == 1) {  // 16-bit coords, entries 16-byte aligned
-            size_t slot = bytes.size() / 2;
-            while ((slot + 1) % 8 != 0) slot++;
-            bytes.resize((slot + 1 + ((n + 7) / 8) * 8) * 2, 0);
-            uint16_t *p16 = reinterpret_cast<uint16_t *>(bytes.data());
-            p16[slot] = (uint16_t)n;
-            for (uint32_t k = 1; k <= n; k++) p16[slot + k] = (uint16_t)(t.neighbours[off + k] >> 16);
-            kmap[c] = -(int32_t)(slot + 1);
-        } else {  // 16-bit coords, packed
-            const size_t slot = bytes.size() / 2;
-            bytes.resize((slot + 1 + n) * 2);
-            uint16_t *p16 = reinterpret_cast<uint16_t *>(bytes.data());
-            p16[slot] = (uint16_t)n;
-            for (uint32_t k = 1; k <= n; k++) p16[slot + k] = (uint16_t)(t.neighbours[off + k] >> 16);
-            kmap[c] = -(int32_t)(slot + 1);
+        auto entry = [&](uint32_t k) {  // k-th entry of the list, 1-based
+            const uint32_t e = t.neighbours[off + k];
+            return w == 0 ? (e & 0xFFFF) : (e >> 16);
+        };
+        size_t slot = bytes.size() / esz;
+        if (w <= 2) {
+            while ((slot + 1) % 4 != 0) slot++;
+            put(slot, n);
+            const uint32_t padded = (n + 3) / 4 * 4;
+            for (uint32_t k = 1; k <= padded; k++) put(slot + k, entry(k <= n ? k : n));
+        } else {
+            put(slot, n);
+            for (uint32_t k = 1; k <= n; k++) put(slot + k, entry(k));
         }
+        kmap[c] = -(int32_t)(slot + 1);
     }
     while (bytes.size() % 16) bytes.push_back(0);
 }

@@ -572,12 +572,15 @@ struct IqWarpSmem {
     static constexpr bool COOP = IqSearch<V>::COOP;
     static constexpr int BP = C::BS + 1;
     static constexpr int MAXT = COOP ? IqSearch<V>::CJ * C::NG : 1;  // search tasks per chunk of jobs
-    static constexpr int TS = C::G * C::KM + 1;  // term table row (padded: the lanes' rows fall in distinct banks)
+    static constexpr int TS = C::G * C::KM;      // terms per round slot
     unsigned long long key[MAXT];                // task: winning packed levels, or ~0u
     unsigned long long rkey[COOP ? 32 : 1];      // round slot: best (d2 bits, list position)
     union {
         float x[256];                            // the super-block (weights and sigma^2 only)
-        float tab[COOP ? 32 * TS : 1];           // round slot: waux_i*diff*diff per (dimension, level)
+        // waux_i*diff*diff of round slot t for (dimension i, level l) at
+        // [(i*KM + l)*32 + t]: a slot's terms share one bank, so lanes
+        // scanning different lists never collide
+        float tab[COOP ? 32 * TS : 1];
     };
     float xv[C::NB * BP];
     float w[C::NB * BP];
@@ -654,80 +657,108 @@ __device__ __noinline__ uint32_t lane_search(const uint16_t *l16, int m, const f
 
 // Cooperative scan of the queued tasks [0, T) (IQ2), 32 per round: each lane
 // tabulates one task's terms per (dimension, level); the round's lists are
-// then laid end to end and cut into 32 equal contiguous ranges, one per lane,
-// so every lane scores the same number of candidates whatever the lists'
-// lengths.  A lane keeps the first minimum of its part of each list and
-// merges it into that list's key (shared-memory atomicMin); only neighbouring
-// lanes ever share a list.  On return key[q] holds task q's winning packed
-// levels, or ~0u.
+// then laid end to end in groups of four entries (each list padded with
+// copies of its last entry) and cut into 32 equal contiguous ranges of
+// groups, one per lane, so every lane scores the same number of candidates
+// whatever the lists' lengths.  A group is one 32- or 64-bit load and four
+// independent distance chains, so the loads and the serial sums of several
+// candidates are in flight together.  A lane keeps the first minimum of its
+// part of each list and merges it into that list's key (shared-memory
+// atomicMin on (d2 bits, position)); only neighbouring lanes ever share a
+// list.  On return key[q] holds task q's winning packed levels, or ~0u.
 template <int V>
 __device__ __noinline__ void search_tasks(IqWarpSmem<V> &S, int T, const void *lists, const uint16_t *gco, int lane) {
     using C = IqCfg<V>;
-    constexpr int KM = C::KM, G = C::G, TS = IqWarpSmem<V>::TS;
+    constexpr int KM = C::KM, G = C::G;
     constexpr uint32_t MASK = (1u << C::BITS) - 1;
     const uint8_t *l8 = static_cast<const uint8_t *>(lists);
     const uint16_t *l16 = static_cast<const uint16_t *>(lists);
-    auto entry = [&](int base, int c) -> uint32_t {
-        return V == 0 ? (uint32_t)gco[__ldg(l8 + base + 1 + c)] : (uint32_t)__ldg(l16 + base + 1 + c);
-    };
     for (int r0 = 0; r0 < T; r0 += 32) {
         const int q = r0 + lane;
-        int n = 0;
+        int ng = 0;
         if (q < T) {
-            const int base = -S.tq_m[q] - 1;
-            n = V == 0 ? (int)__ldg(l8 + base) : (int)__ldg(l16 + base);
-            S.rbase[lane] = base;
+            const int base = -S.tq_m[q] - 1;  // the count; entries start at base + 1, a multiple of 4
+            const int n = V == 0 ? (int)__ldg(l8 + base) : (int)__ldg(l16 + base);
+            ng = (n + 3) >> 2;
+            S.rbase[lane] = base + 1;
             const float scale = S.tq_s[q];
             const int xo = S.tq_x[q];
-            float *tb = S.tab + lane * TS;
+            float *tb = S.tab + lane;
 #pragma unroll
             for (int i = 0; i < G; i++) {
                 const float xi = S.xv[xo + i], wi = S.wa[xo + i];
 #pragma unroll
                 for (int l = 0; l < KM; l++) {
                     const float diff = scale * (float)(2 * l + 1) - xi;
-                    tb[i * KM + l] = wi * diff * diff;
+                    tb[(i * KM + l) * 32] = wi * diff * diff;
                 }
             }
         }
         S.rkey[lane] = ~0ull;
         int tot;
-        S.pre[lane] = warp_exclusive_scan(n, lane, tot);
+        S.pre[lane] = warp_exclusive_scan(ng, lane, tot);  // in groups of four entries
         if (lane == 0) S.pre[32] = tot;
         __syncwarp();
-        const int k0 = (int)(((int64_t)tot * lane) >> 5), k1 = (int)(((int64_t)tot * (lane + 1)) >> 5);
-        if (k0 < k1) {
-            int t = 0;  // the slot holding candidate k0: smallest t with pre[t+1] > k0
+        const int g0 = (int)(((int64_t)tot * lane) >> 5), g1 = (int)(((int64_t)tot * (lane + 1)) >> 5);
+        if (g0 < g1) {
+            int t = 0;  // the slot holding group g0: smallest t with pre[t+1] > g0
             for (int hi = 31; t < hi;) {
                 const int mid = (t + hi) >> 1;
-                if (S.pre[mid + 1] > k0) hi = mid;
+                if (S.pre[mid + 1] > g0) hi = mid;
                 else t = mid + 1;
             }
-            // one candidate per iteration for every lane (the ranges differ in
-            // length by at most one); a list boundary is a short branch
-            int start = S.pre[t], end = S.pre[t + 1], base = S.rbase[t];
-            const float *tb = S.tab + t * TS;
+            // Loads run two groups ahead of the scoring: (lt, lend, lent) is the
+            // slot of the next group to load, whose entries sit at lent + 4*g.
+            int lt = t, lend = S.pre[t + 1], lent = S.rbase[t] - 4 * S.pre[t];
+            auto load = [&](int g) -> uint2 {
+                while (g >= lend) {
+                    lt++;
+                    lend = S.pre[lt + 1];
+                    lent = S.rbase[lt] - 4 * S.pre[lt];
+                }
+                if (V == 0) return make_uint2(__ldg(reinterpret_cast<const uint32_t *>(l8 + lent + 4 * g)), 0u);
+                return __ldg(reinterpret_cast<const uint2 *>(l16 + lent + 4 * g));
+            };
+            uint2 w1 = load(g0), w2 = make_uint2(0u, 0u);
+            if (g0 + 1 < g1) w2 = load(g0 + 1);
+            int end = S.pre[t + 1];
+            const float *tb = S.tab + t;
             uint32_t bh = 0xFFFFFFFFu, bl = 0xFFFFFFFFu;
-            for (int k = k0; k < k1; k++) {
-                if (k == end) {  // this lane's part of slot t is done: merge, move to the next nonempty slot
+            for (int g = g0; g < g1; g++) {
+                const uint2 w4 = w1;
+                w1 = w2;
+                if (g + 2 < g1) w2 = load(g + 2);
+                if (g == end) {  // this lane's part of slot t is done: merge, move to the next nonempty slot
                     if (bh != 0xFFFFFFFFu) atomicMin(&S.rkey[t], ((unsigned long long)bh << 32) | bl);
                     bh = bl = 0xFFFFFFFFu;
                     do {
                         t++;
-                    } while (S.pre[t + 1] <= k);
-                    start = S.pre[t];
+                    } while (S.pre[t + 1] <= g);
                     end = S.pre[t + 1];
-                    base = S.rbase[t];
-                    tb = S.tab + t * TS;
+                    tb = S.tab + t;
                 }
-                const uint32_t cc = entry(base, k - start);
-                float d2 = 0.0f;
+                uint32_t cc[4];
+                if (V == 0) {
 #pragma unroll
-                for (int i = 0; i < G; i++) d2 += tb[i * KM + ((cc >> (C::BITS * i)) & MASK)];
-                const uint32_t kh = __float_as_uint(d2);
-                if (d2 < FLT_MAX && kh < bh) {  // positions rise within the lane: strict keeps the first
-                    bh = kh;
-                    bl = (uint32_t)(k - start);
+                    for (int u = 0; u < 4; u++) cc[u] = gco[(w4.x >> (8 * u)) & 255u];
+                } else {
+                    cc[0] = w4.x & 0xFFFFu;
+                    cc[1] = w4.x >> 16;
+                    cc[2] = w4.y & 0xFFFFu;
+                    cc[3] = w4.y >> 16;
+                }
+                float d2[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                for (int i = 0; i < G; i++)
+#pragma unroll
+                    for (int u = 0; u < 4; u++) d2[u] += tb[(i * KM + ((cc[u] >> (C::BITS * i)) & MASK)) * 32];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const uint32_t kh = __float_as_uint(d2[u]);
+                    if (d2[u] < FLT_MAX && kh < bh) {  // positions rise within the lane: strict keeps the first
+                        bh = kh;
+                        bl = (uint32_t)(4 * g + u);
+                    }
                 }
             }
             if (bh != 0xFFFFFFFFu) atomicMin(&S.rkey[t], ((unsigned long long)bh << 32) | bl);
@@ -735,7 +766,12 @@ __device__ __noinline__ void search_tasks(IqWarpSmem<V> &S, int T, const void *l
         __syncwarp();
         if (q < T) {
             const unsigned long long kk = S.rkey[lane];
-            S.key[q] = kk == ~0ull ? 0xFFFFFFFFull : (unsigned long long)entry(S.rbase[lane], (int)(uint32_t)kk);
+            uint32_t win = 0xFFFFFFFFu;
+            if (kk != ~0ull) {
+                const int at = S.rbase[lane] + (int)(uint32_t)kk - 4 * S.pre[lane];
+                win = V == 0 ? (uint32_t)gco[__ldg(l8 + at)] : (uint32_t)__ldg(l16 + at);
+            }
+            S.key[q] = win;
         }
         __syncwarp();
     }

@@ -1,6 +1,12 @@
 // C ABI of the host library (libshoehorn_host.so): the reference's host-side
 // pieces that tests and other hosts call directly.
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
 #include <cstring>
+#include <map>
+#include <thread>
 
 #include "pipeline.hpp"
 
@@ -65,6 +71,150 @@ int shh_gguf_rewrite(const char *in_path, const char *out_path) {
         });
         return 0;
     } catch (...) {
+        return -1;
+    }
+}
+
+
+
+// ---------------------------------------------------------------------------
+// Sharded runs driven by a host program with its own process group (one
+// process per GPU).  Communication goes through two callbacks:
+//   allgather(user, mine, n_mine, all, cap, sizes): called twice per
+//     exchange.  First with all == NULL: gather every rank's blob and return
+//     the total size (or < 0 on failure).  Then with a buffer of that size:
+//     copy the blobs into it in rank order, write each rank's size to
+//     sizes[rank] and return the total.
+//   barrier(user): returns 0 once every rank has called it.
+// ---------------------------------------------------------------------------
+typedef int64_t (*shh_allgather_fn)(void *user, const uint8_t *mine, int64_t n_mine, uint8_t *all, int64_t cap,
+                                    int64_t *sizes);
+typedef int (*shh_barrier_fn)(void *user);
+
+static shh::Shard make_shard(int rank, int world, shh_allgather_fn ag, shh_barrier_fn bar, void *user) {
+    shh::Shard s;
+    s.rank = rank;
+    s.world = world;
+    if (ag)
+        s.allgather = [ag, user, world](const std::vector<uint8_t> &mine) {
+            const int64_t total = ag(user, mine.data(), (int64_t)mine.size(), nullptr, 0, nullptr);
+            if (total < 0) throw shh::Error("all-gather failed");
+            std::vector<uint8_t> all((size_t)total);
+            std::vector<int64_t> sizes((size_t)world, 0);
+            if (ag(user, mine.data(), (int64_t)mine.size(), all.data(), total, sizes.data()) != total)
+                throw shh::Error("all-gather failed");
+            std::vector<std::vector<uint8_t>> out((size_t)world);
+            int64_t at = 0;
+            for (int r = 0; r < world; r++) {
+                if (sizes[(size_t)r] < 0 || at + sizes[(size_t)r] > total) throw shh::Error("all-gather sizes");
+                out[(size_t)r].assign(all.begin() + at, all.begin() + at + sizes[(size_t)r]);
+                at += sizes[(size_t)r];
+            }
+            return out;
+        };
+    if (bar)
+        s.barrier = [bar, user]() {
+            if (bar(user) != 0) throw shh::Error("barrier failed");
+        };
+    return s;
+}
+
+// The error-table exchange alone, on made-up errors (no GPU): tensors of
+// n_rows[k] rows with n_cands[k] candidates, 128-row sampling unless
+// sample_rows says otherwise.  This rank fills the sampled rows it owns with
+// a fixed function of (tensor, candidate, row), exchanges them, and writes
+// each (tensor, candidate) error -- rows summed in row order and scaled as
+// the error table is -- to sums[k * max_cands + c].  0 on success.
+int shh_shard_exchange_check(int64_t n_tensors, const uint64_t *n_rows, const int32_t *n_cands, uint64_t sample_rows,
+                             int rank, int world, shh_allgather_fn ag, void *user, double *sums) {
+    try {
+        if (n_tensors < 0 || world < 1 || rank < 0 || rank >= world) return -1;
+        int32_t max_c = 1;
+        for (int64_t k = 0; k < n_tensors; k++) max_c = std::max(max_c, n_cands[k]);
+        std::vector<shh::MeasRows> m((size_t)n_tensors);
+        for (int64_t k = 0; k < n_tensors; k++) {
+            auto &t = m[(size_t)k];
+            t.n_rows = n_rows[k];
+            t.step = std::max<uint64_t>(t.n_rows / std::min(sample_rows, std::max<uint64_t>(t.n_rows, 1)), 1);
+            t.sampled = (t.n_rows + t.step - 1) / t.step;
+            t.err.assign((size_t)n_cands[k], std::vector<double>((size_t)t.sampled, 0.0));
+            uint64_t lo, hi, i0, i1;
+            shh::shard_rows(t.n_rows, rank, world, lo, hi);
+            shh::shard_samples(lo, hi, t.step, t.sampled, i0, i1);
+            for (int32_t c = 0; c < n_cands[k]; c++)
+                for (uint64_t i = i0; i < i1; i++) {
+                    uint64_t x = ((uint64_t)k << 40) ^ ((uint64_t)c << 32) ^ (i * t.step);
+                    x += 0x9E3779B97F4A7C15ull;
+                    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+                    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+                    x ^= x >> 31;
+                    // magnitudes over ~2^40 so that the summation order shows in the bits
+                    t.err[(size_t)c][i] = std::ldexp((double)(x >> 11), (int)(x & 63) - 73);
+                }
+        }
+        shh::exchange_rows(m, make_shard(rank, world, ag, nullptr, user));
+        for (int64_t k = 0; k < n_tensors; k++)
+            for (int32_t c = 0; c < n_cands[k]; c++)
+                sums[(size_t)k * (size_t)max_c + (size_t)c] = shh::tensor_error(m[(size_t)k], (size_t)c);
+        return 0;
+    } catch (...) {
+        return -1;
+    }
+}
+
+// Plan (error table + solve) and encode of a synthetic model configuration
+// ("qwen3-0.6b", "llama3-8b", "llama3-70b", "tiny") on this rank's rows,
+// on CUDA device `device`.  budget / reserve / uniform follow the CLI flags
+// (uniform non-empty: a fixed mix, no solve).  out_path empty: output in host
+// memory.  Writes one JSON line of timings into json.  0 on success, -1 with
+// the message in json on failure.
+int shh_bench_model(const char *name, uint64_t seed, int exact_errors, const char *budget, const char *reserve,
+                    uint64_t ctx, const char *uniform, int workers_per_gpu, int device, int rank, int world,
+                    shh_allgather_fn ag, shh_barrier_fn bar, void *user, const char *out_path, char *json,
+                    int64_t cap) {
+    try {
+        shh::FitArgs a;
+        a.exact_errors = exact_errors != 0;
+        if (budget) a.budget = budget;
+        if (reserve) a.reserve = reserve;
+        if (uniform) a.uniform = uniform;
+        a.ctx = ctx;
+        a.workers_per_gpu = workers_per_gpu;
+        const shh::Shard shard = make_shard(rank, world, ag, bar, user);
+        const int threads = (int)std::max(1u, std::thread::hardware_concurrency() / (unsigned)std::max(world, 1));
+        auto c0 = std::chrono::steady_clock::now();
+        auto sm = shh::synthetic_model(name, seed, threads, rank, world);
+        const double gen_s = std::chrono::duration<double>(std::chrono::steady_clock::now() - c0).count();
+        shh::GpuPool pool(1, a.timeout_ms, a.workers_per_gpu, device);
+        if (shard.active()) shard.barrier();
+        shh::Timing tm;
+        const auto t0 = std::chrono::steady_clock::now();
+        const shh::Plan plan = shh::build_plan(a, sm->view, sm->imatrix, pool, tm, shard);
+        shh::write_quantized(out_path ? out_path : "", plan, sm->view, sm->imatrix, pool, tm, shard);
+        const double wall = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        uint64_t elems = 0, mine = 0;
+        for (size_t i = 0; i < sm->view.tensors.size(); i++) {
+            const auto &t = sm->view.tensors[i];
+            uint64_t lo, hi;
+            shh::shard_rows(t.n_rows(), rank, world, lo, hi);
+            elems += t.n_elements();
+            mine += (hi - lo) * t.ne0();
+        }
+        std::map<std::string, uint64_t> by_type;
+        for (auto &e : plan.entries) by_type[shh::type_name(e.ty)] += sm->view.tensors[e.tensor_idx].n_elements();
+        std::string mix;
+        for (auto &kv : by_type) mix += (mix.empty() ? "" : ", ") + ("\"" + kv.first + "\": " + std::to_string(kv.second));
+        snprintf(json, (size_t)cap,
+                 "{\"model\": \"%s\", \"rank\": %d, \"world\": %d, \"exact_errors\": %s, \"elements\": %llu, "
+                 "\"rank_elements\": %llu, \"generate_s\": %.3f, \"measure_s\": %.4f, \"gather_s\": %.4f, "
+                 "\"solve_s\": %.4f, \"setup_s\": %.4f, \"encode_s\": %.4f, \"wall_s\": %.4f, \"plan_bytes\": %llu, "
+                 "\"budget_bytes\": %llu, \"mix_elements\": {%s}}",
+                 name, rank, world, a.exact_errors ? "true" : "false", (unsigned long long)elems,
+                 (unsigned long long)mine, gen_s, tm.measure_s, tm.gather_s, tm.solve_s, tm.setup_s, tm.encode_s, wall,
+                 (unsigned long long)plan.total_bytes, (unsigned long long)plan.budget.model_budget, mix.c_str());
+        return 0;
+    } catch (const std::exception &e) {
+        snprintf(json, (size_t)cap, "%s", e.what());
         return -1;
     }
 }

@@ -221,22 +221,24 @@ static void shc_check(int rc, const char *what) {
     if (rc != SHC_OK) throw Error(std::string(what) + ": " + shc_status_string(rc));
 }
 
-GpuPool::GpuPool(int n_gpus, int64_t timeout_ms, int per_gpu) : timeout_ms_(timeout_ms) {
+GpuPool::GpuPool(int n_gpus, int64_t timeout_ms, int per_gpu, int first_device) : timeout_ms_(timeout_ms) {
     int avail = 0;
     if (cudaGetDeviceCount(&avail) != cudaSuccess || avail < 1) throw Error("no CUDA device");
+    if (first_device < 0 || first_device >= avail) throw Error("no CUDA device " + std::to_string(first_device));
+    avail -= first_device;
     if (n_gpus < 1 || n_gpus > avail) n_gpus = n_gpus < 1 ? 1 : avail;
     n_gpus_ = n_gpus;
     if (per_gpu < 1) per_gpu = 1;
     // workers interleave the devices so the first jobs (the largest) spread
     for (int w = 0; w < n_gpus * per_gpu; w++) {
         auto wk = std::make_unique<Worker>();
-        wk->dev = w % n_gpus;
+        wk->dev = first_device + w % n_gpus;
         cuda_check(cudaSetDevice(wk->dev), "cudaSetDevice");
         shc_check(shc_init(wk->dev, &wk->ctx), "shc_init");
         cuda_check(cudaStreamCreateWithFlags(&wk->st, cudaStreamNonBlocking), "cudaStreamCreate");
         workers_.push_back(std::move(wk));
     }
-    cudaSetDevice(0);
+    cudaSetDevice(first_device);
 }
 
 GpuPool::~GpuPool() {
@@ -307,11 +309,12 @@ struct DevRows {
     const void *ptr;
     uint32_t src_type;
 };
-static DevRows rows_to_device(GpuPool::Worker &wk, const TensorInfo &t, const uint8_t *data, uint64_t r0, uint64_t n,
+// first: host address of the first row; consecutive rows `step` rows apart.
+static DevRows rows_to_device(GpuPool::Worker &wk, const TensorInfo &t, const uint8_t *first, uint64_t n,
                               uint64_t step) {
     const uint64_t ne0 = t.ne0(), srb = row_bytes(t.ty, ne0);
     void *raw = wk.d(0, (size_t)(n * srb + 16));
-    cuda_check(cudaMemcpy2DAsync(raw, srb, data + r0 * srb, srb * step, srb, n, cudaMemcpyHostToDevice, wk.st),
+    cuda_check(cudaMemcpy2DAsync(raw, srb, first, srb * step, srb, n, cudaMemcpyHostToDevice, wk.st),
                "row upload");
     if (t.ty == T_F32 || t.ty == T_F16 || t.ty == T_BF16) return {raw, t.ty};
     void *f = wk.d(1, (size_t)(n * ne0 * 4 + 16));
@@ -369,7 +372,8 @@ static std::pair<std::vector<PlanEntry>, uint64_t> assemble_entries(const ModelV
     return {entries, solved};
 }
 
-Plan build_plan(const FitArgs &args, const ModelView &m, const Imatrix &im, GpuPool &pool, Timing &tm) {
+Plan build_plan(const FitArgs &args, const ModelView &m, const Imatrix &im, GpuPool &pool, Timing &tm,
+                const Shard &shard) {
     Plan plan;
     const Hyper h = hyperparams(m.kvs);
     const bool uniform = !args.uniform.empty();
@@ -441,11 +445,7 @@ Plan build_plan(const FitArgs &args, const ModelView &m, const Imatrix &im, GpuP
     // ---- measure weighted error for every (tensor, candidate) on the GPUs ----
     const auto t0 = Clock::now();
     const uint64_t sample_rows = args.exact_errors ? UINT64_MAX : 128;
-    struct Meas {
-        uint64_t step, sampled;
-        std::vector<std::vector<double>> err;  // [cand][sampled row]
-    };
-    std::vector<Meas> meas(to_solve.size());
+    std::vector<MeasRows> meas(to_solve.size());  // err[cand][sampled row]
     struct Job {
         size_t k;        // index into to_solve
         uint64_t i0, i1; // sampled-row range
@@ -458,10 +458,11 @@ Plan build_plan(const FitArgs &args, const ModelView &m, const Imatrix &im, GpuP
         const uint64_t n_rows = t.n_rows();
         const uint64_t step = std::max<uint64_t>(n_rows / std::min(sample_rows, std::max<uint64_t>(n_rows, 1)), 1);
         const uint64_t sampled = (n_rows + step - 1) / step;
+        meas[k].n_rows = n_rows;
         meas[k].step = step;
         meas[k].sampled = sampled;
         meas[k].err.assign(to_solve[k].second.size(), std::vector<double>((size_t)sampled, 0.0));
-        total_cost += (double)sampled * (double)t.ne0() * (double)to_solve[k].second.size();
+        total_cost += (double)sampled * (double)t.ne0() * (double)to_solve[k].second.size() / (double)shard.world;
     }
     const double max_job_cost = std::max(total_cost / (8.0 * pool.size()), 1.0);
     for (size_t k = 0; k < to_solve.size(); k++) {
@@ -471,9 +472,13 @@ Plan build_plan(const FitArgs &args, const ModelView &m, const Imatrix &im, GpuP
         // rows per job: bounded by cost and by ~256 MiB of f32 rows; never across a matrix
         uint64_t cap = std::max<uint64_t>(1, (uint64_t)(max_job_cost / per_row));
         cap = std::min<uint64_t>(cap, std::max<uint64_t>(1, (256ull << 20) / (t.ne0() * 4)));
-        uint64_t i = 0;
-        while (i < sampled) {
-            uint64_t end = std::min(sampled, i + cap);
+        // this rank's sampled rows (all of them without a shard)
+        uint64_t lo, hi, i_lo, i_hi;
+        shard_rows(t.n_rows(), shard.rank, shard.world, lo, hi);
+        shard_samples(lo, hi, step, sampled, i_lo, i_hi);
+        uint64_t i = i_lo;
+        while (i < i_hi) {
+            uint64_t end = std::min(i_hi, i + cap);
             const uint64_t mat = (i * step) / rpm;
             while (end > i + 1 && ((end - 1) * step) / rpm != mat) end--;
             jobs.push_back({k, i, end, per_row * (double)(end - i)});
@@ -488,7 +493,7 @@ Plan build_plan(const FitArgs &args, const ModelView &m, const Imatrix &im, GpuP
         const auto &t = m.tensors[ti];
         const auto &types = to_solve[jb.k].second;
         const uint64_t ne0 = t.ne0(), step = meas[jb.k].step, ni = jb.i1 - jb.i0;
-        const DevRows src = rows_to_device(wk, t, m.data(ti), jb.i0 * step, ni, step);
+        const DevRows src = rows_to_device(wk, t, m.row(ti, jb.i0 * step), ni, step);
         const std::vector<float> *tim = lookup(im, t.name);
         const float *ims = row_slice(tim, ne0, rows_per_mat_of(t), jb.i0 * step);
         float *dim = nullptr;
@@ -506,20 +511,21 @@ Plan build_plan(const FitArgs &args, const ModelView &m, const Imatrix &im, GpuP
         for (size_t c = 0; c < types.size(); c++)
             std::memcpy(meas[jb.k].err[c].data() + jb.i0, herr + c * ni, ni * 8);
     });
+    tm.measure_s = secs_since(t0);
+    const auto tg = Clock::now();
+    exchange_rows(meas, shard);  // the other ranks' rows (a no-op without a shard)
+    tm.gather_s = secs_since(tg);
     for (size_t k = 0; k < to_solve.size(); k++) {
         const auto &t = m.tensors[to_solve[k].first];
-        const double scale = (double)t.n_rows() / (double)meas[k].sampled;
         TensorChoices tc;
         tc.tensor_idx = to_solve[k].first;
         for (size_t c = 0; c < to_solve[k].second.size(); c++) {
-            double err = 0.0;  // rows in row order, as the reference's closure folds them
-            for (double e : meas[k].err[c]) err += e;
             const uint32_t ty = to_solve[k].second[c];
-            tc.cands.push_back({ty, row_bytes(ty, t.ne0()) * t.n_rows(), err * scale});
+            // rows in row order, as the reference's closure folds them
+            tc.cands.push_back({ty, row_bytes(ty, t.ne0()) * t.n_rows(), tensor_error(meas[k], c)});
         }
         plan.choices.push_back(std::move(tc));
     }
-    tm.measure_s = secs_since(t0);
 
     const auto t1 = Clock::now();
     const uint64_t weight_budget = plan.budget.model_budget - plan.fixed_bytes;
@@ -607,7 +613,7 @@ uint32_t file_type_code(const std::vector<PlanEntry> &entries) {
 // by the GPUs in row ranges straight into a memory map of the temporary file
 // ---------------------------------------------------------------------------
 void write_quantized(const std::string &out_path, const Plan &plan, const ModelView &m, const Imatrix &im,
-                     GpuPool &pool, Timing &tm) {
+                     GpuPool &pool, Timing &tm, const Shard &shard) {
     const auto s0 = Clock::now();
     std::vector<TensorInfo> infos;
     for (auto &e : plan.entries) {
@@ -625,42 +631,65 @@ void write_quantized(const std::string &out_path, const Plan &plan, const ModelV
     kvs.emplace_back("general.file_type", Value::U32(file_type_code(plan.entries)));
     kvs.emplace_back("general.quantization_version", Value::U32(2));
     const Layout L = layout_for(kvs, infos, m.alignment);
-    // An empty out_path encodes into anonymous memory (benchmarks without a disk
-    // write); otherwise *.tmp next to the output, renamed when complete.  File
-    // output uses positional writes from the workers' pinned buffers, so no
-    // page of the output is faulted in through a mapping.
+    const bool lead = shard.rank == 0;
+    // rows [lo, hi) of every entry are this rank's (all rows without a shard)
+    std::vector<uint64_t> lo(plan.entries.size()), hi(plan.entries.size()), drb(plan.entries.size());
+    for (size_t ei = 0; ei < plan.entries.size(); ei++) {
+        const auto &t = m.tensors[plan.entries[ei].tensor_idx];
+        shard_rows(t.n_rows(), shard.rank, shard.world, lo[ei], hi[ei]);
+        drb[ei] = row_bytes(plan.entries[ei].ty, t.ne0());
+    }
+    // An empty out_path encodes into host memory (benchmarks without a disk
+    // write): this rank's header and rows, back to back.  Otherwise *.tmp
+    // next to the output, renamed when complete; every rank writes its rows
+    // with positional writes from the workers' pinned buffers at their final
+    // offsets, so no page of the output is faulted in through a mapping.
     const bool to_file = !out_path.empty();
     const std::string tmp = out_path + ".tmp";
     uint8_t *map = nullptr;
+    uint64_t map_len = 0;
+    std::vector<uint64_t> local_base(plan.entries.size(), 0);
     int fd = -1;
     if (to_file) {
-        fd = ::open(tmp.c_str(), O_RDWR | O_CREAT | O_TRUNC, 0644);
-        if (fd < 0) throw Error("creating " + tmp);
-        if (ftruncate(fd, (off_t)L.total) != 0) {
-            ::close(fd);
-            throw Error("sizing " + tmp);
+        if (lead) {
+            fd = ::open(tmp.c_str(), O_RDWR | O_CREAT | O_TRUNC, 0644);
+            if (fd < 0) throw Error("creating " + tmp);
+            if (ftruncate(fd, (off_t)L.total) != 0) {
+                ::close(fd);
+                throw Error("sizing " + tmp);
+            }
         }
-    } else if (L.total) {
-        map = static_cast<uint8_t *>(mmap(nullptr, L.total, PROT_READ | PROT_WRITE, MAP_PRIVATE | MAP_ANONYMOUS, -1, 0));
-        if (map == MAP_FAILED) throw Error("mapping the output");
-        madvise(map, L.total, MADV_HUGEPAGE);
-        // faulted in up front by several threads (an in-memory consumer hands
-        // over a buffer it owns; the kernel's page zeroing is the cost)
-        const unsigned nt = std::max(1u, std::min(32u, std::thread::hardware_concurrency()));
-        std::vector<std::thread> th;
-        const uint64_t per = (L.total + nt - 1) / nt;
-        for (unsigned i = 0; i < nt; i++)
-            th.emplace_back([map, per, i, total = L.total]() {
-                const uint64_t a = per * i, b = std::min<uint64_t>(total, a + per);
-                for (uint64_t o = a; o < b; o += 4096) map[o] = 0;
-            });
-        for (auto &t : th) t.join();
+        if (shard.active()) {
+            shard.barrier();  // the file exists at its full size before the other ranks open it
+            if (!lead) {
+                fd = ::open(tmp.c_str(), O_RDWR);
+                if (fd < 0) throw Error("opening " + tmp);
+            }
+        }
+    } else {
+        map_len = lead ? L.data_start : 0;
+        for (size_t ei = 0; ei < plan.entries.size(); ei++) {
+            local_base[ei] = map_len;
+            map_len += (hi[ei] - lo[ei]) * drb[ei];
+        }
+        if (map_len) {
+            map = static_cast<uint8_t *>(mmap(nullptr, map_len, PROT_READ | PROT_WRITE, MAP_PRIVATE | MAP_ANONYMOUS, -1, 0));
+            if (map == MAP_FAILED) throw Error("mapping the output");
+            madvise(map, map_len, MADV_HUGEPAGE);
+            // faulted in up front by several threads (an in-memory consumer hands
+            // over a buffer it owns; the kernel's page zeroing is the cost)
+            const unsigned nt = std::max(1u, std::min(32u, std::thread::hardware_concurrency()));
+            std::vector<std::thread> th;
+            const uint64_t per = (map_len + nt - 1) / nt;
+            for (unsigned i = 0; i < nt; i++)
+                th.emplace_back([map, per, i, total = map_len]() {
+                    const uint64_t a = per * i, b = std::min<uint64_t>(total, a + per);
+                    for (uint64_t o = a; o < b; o += 4096) map[o] = 0;
+                });
+            for (auto &t : th) t.join();
+        }
     }
-    auto put = [&](uint64_t off, const void *p, size_t n) {
-        if (!to_file) {
-            std::memcpy(map + off, p, n);
-            return;
-        }
+    auto pwrite_all = [&](uint64_t off, const void *p, size_t n) {
         const uint8_t *b = static_cast<const uint8_t *>(p);
         while (n) {
             const ssize_t w = pwrite(fd, b, n, (off_t)off);
@@ -670,6 +699,11 @@ void write_quantized(const std::string &out_path, const Plan &plan, const ModelV
             n -= (size_t)w;
         }
     };
+    // rows starting at row r0 of entry ei
+    auto put_rows = [&](size_t ei, uint64_t r0, const void *p, size_t n) {
+        if (to_file) pwrite_all(L.data_start + L.offsets[ei] + r0 * drb[ei], p, n);
+        else std::memcpy(map + local_base[ei] + (r0 - lo[ei]) * drb[ei], p, n);
+    };
     struct Job {
         size_t e;
         uint64_t r0, r1;
@@ -677,16 +711,17 @@ void write_quantized(const std::string &out_path, const Plan &plan, const ModelV
     };
     std::vector<Job> jobs;
     uint64_t total_elems = 0;
-    for (auto &e : plan.entries) total_elems += m.tensors[e.tensor_idx].n_elements();
+    for (size_t ei = 0; ei < plan.entries.size(); ei++)
+        total_elems += (hi[ei] - lo[ei]) * m.tensors[plan.entries[ei].tensor_idx].ne0();
     const uint64_t cap_elems = std::max<uint64_t>(1ull << 20, std::min<uint64_t>(64ull << 20, total_elems / (8 * pool.size())));
     for (size_t ei = 0; ei < plan.entries.size(); ei++) {
         const auto &e = plan.entries[ei];
         const auto &t = m.tensors[e.tensor_idx];
-        const uint64_t n_rows = t.n_rows(), ne0 = t.ne0(), rpm = rows_per_mat_of(t);
+        const uint64_t ne0 = t.ne0(), rpm = rows_per_mat_of(t);
         if (e.ty == t.ty) continue;  // copied untouched, below
         const uint64_t rows_cap = std::max<uint64_t>(1, cap_elems / std::max<uint64_t>(ne0, 1));
-        for (uint64_t r = 0; r < n_rows;) {
-            uint64_t end = std::min(n_rows, r + rows_cap);
+        for (uint64_t r = lo[ei]; r < hi[ei];) {
+            uint64_t end = std::min(hi[ei], r + rows_cap);
             const uint64_t mat = r / rpm;
             end = std::min(end, (mat + 1) * rpm);
             jobs.push_back({ei, r, end, (double)(end - r) * (double)ne0});
@@ -719,20 +754,23 @@ void write_quantized(const std::string &out_path, const Plan &plan, const ModelV
         });
     tm.setup_s = secs_since(s0);
     const auto t0 = Clock::now();
-    const auto hdr = header_bytes(kvs, infos, m.alignment, L);
-    put(0, hdr.data(), hdr.size());
+    if (lead) {
+        const auto hdr = header_bytes(kvs, infos, m.alignment, L);
+        if (to_file) pwrite_all(0, hdr.data(), hdr.size());
+        else if (map) std::memcpy(map, hdr.data(), hdr.size());
+    }
     for (size_t ei = 0; ei < plan.entries.size(); ei++) {  // tensors copied untouched (main.rs:735-737)
         const auto &e = plan.entries[ei];
-        const auto &t = m.tensors[e.tensor_idx];
-        if (e.ty == t.ty) put(L.data_start + L.offsets[ei], m.data(e.tensor_idx), t.byte_size());
+        if (e.ty == m.tensors[e.tensor_idx].ty && hi[ei] > lo[ei])
+            put_rows(ei, lo[ei], m.row(e.tensor_idx, lo[ei]), (size_t)((hi[ei] - lo[ei]) * drb[ei]));
     }
     pool.run(jobs.size(), [&](int w, size_t j) {
         auto &wk = pool.worker(w);
         const Job &jb = jobs[j];
         const auto &e = plan.entries[jb.e];
         const auto &t = m.tensors[e.tensor_idx];
-        const uint64_t ne0 = t.ne0(), n = jb.r1 - jb.r0, drb = row_bytes(e.ty, ne0);
-        const DevRows src = rows_to_device(wk, t, m.data(e.tensor_idx), jb.r0, n, 1);
+        const uint64_t ne0 = t.ne0(), n = jb.r1 - jb.r0, rb = drb[jb.e];
+        const DevRows src = rows_to_device(wk, t, m.row(e.tensor_idx, jb.r0), n, 1);
         const std::vector<float> *tim = lookup(im, t.name);
         const float *ims = row_slice(tim, ne0, rows_per_mat_of(t), jb.r0);
         float *dim = nullptr;
@@ -740,20 +778,23 @@ void write_quantized(const std::string &out_path, const Plan &plan, const ModelV
             dim = static_cast<float *>(wk.d(2, ne0 * 4));
             cuda_check(cudaMemcpyAsync(dim, ims, ne0 * 4, cudaMemcpyHostToDevice, wk.st), "imatrix upload");
         }
-        uint8_t *dout = static_cast<uint8_t *>(wk.d(4, n * drb + 16));
+        uint8_t *dout = static_cast<uint8_t *>(wk.d(4, n * rb + 16));
         shc_check(shc_encode_rows(wk.ctx, e.ty, src.src_type, src.ptr, (int64_t)n, (int64_t)ne0, dim,
                                   ims ? (int64_t)ne0 : 0, 0, 0, dout, wk.st),
                   "encode rows");
-        uint8_t *hout = static_cast<uint8_t *>(wk.h(1, n * drb));
-        cuda_check(cudaMemcpyAsync(hout, dout, n * drb, cudaMemcpyDeviceToHost, wk.st), "encoded download");
+        uint8_t *hout = static_cast<uint8_t *>(wk.h(1, n * rb));
+        cuda_check(cudaMemcpyAsync(hout, dout, n * rb, cudaMemcpyDeviceToHost, wk.st), "encoded download");
         shc_check(shc_sync(wk.ctx, wk.st, 3600 * 1000), "encode rows");
-        put(L.data_start + L.offsets[jb.e] + jb.r0 * drb, hout, n * drb);
+        put_rows(jb.e, jb.r0, hout, n * rb);
     });
-    if (map) munmap(map, L.total);
+    if (map) munmap(map, map_len);
     if (fd >= 0 && ::close(fd) != 0) throw Error("closing " + tmp);
-    if (to_file && rename(tmp.c_str(), out_path.c_str()) != 0) throw Error("renaming " + tmp + " -> " + out_path);
+    if (to_file && shard.active()) shard.barrier();  // every rank's rows are in the file
+    if (to_file && lead && rename(tmp.c_str(), out_path.c_str()) != 0)
+        throw Error("renaming " + tmp + " -> " + out_path);
     tm.encode_s = secs_since(t0);
-    fprintf(stderr, "wrote %s (%s)\n", to_file ? out_path.c_str() : "(memory)", fmt_size(L.total).c_str());
+    fprintf(stderr, "wrote %s (%s)\n", to_file ? out_path.c_str() : "(memory)",
+            fmt_size(to_file ? L.total : map_len).c_str());
 }
 
 }  // namespace shh

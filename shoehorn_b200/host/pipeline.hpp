@@ -13,6 +13,7 @@
 
 #include "gguf.hpp"
 #include "imatrix.hpp"
+#include "shard.hpp"
 #include "solver.hpp"
 
 struct shc_ctx;
@@ -64,8 +65,9 @@ struct PlanEntry {
 struct Timing {
     // setup_s: the encode's buffer set-up (pinned staging and device buffers
     // sized for the largest job on every worker, the in-memory output faulted
-    // in), kept out of encode_s
-    double measure_s = 0, solve_s = 0, encode_s = 0, setup_s = 0;
+    // in), kept out of encode_s; gather_s: the error-table exchange of a
+    // sharded run (waiting for the slowest rank included)
+    double measure_s = 0, gather_s = 0, solve_s = 0, encode_s = 0, setup_s = 0;
 };
 
 struct Plan {
@@ -79,12 +81,21 @@ struct Plan {
 
 // Tensor storage seen by the pipeline: infos plus a host pointer to each
 // tensor's raw bytes (an mmap'd GGUF, or synthetic data in host memory).
+// A rank of a sharded run may hold only rows [row_lo[i], ...) of tensor i:
+// data(i) then points at row row_lo[i] (row_lo empty: whole tensors).
 struct ModelView {
     std::vector<KV> kvs;
     std::vector<TensorInfo> tensors;
     uint64_t alignment = 32;
     std::function<const uint8_t *(size_t)> data;
     uint64_t total_bytes = 0;
+    std::vector<uint64_t> row_lo;
+    // host address of row r of tensor i
+    const uint8_t *row(size_t i, uint64_t r) const {
+        const auto &t = tensors[i];
+        const uint64_t lo = row_lo.empty() ? 0 : row_lo[i];
+        return data(i) + (r - lo) * row_bytes(t.ty, t.ne0());
+    }
 };
 ModelView view_of(const Model &m);
 
@@ -92,7 +103,8 @@ ModelView view_of(const Model &m);
 // GPU so that one job's copies overlap another's kernels.
 class GpuPool {
   public:
-    GpuPool(int n_gpus, int64_t timeout_ms, int per_gpu = 3);
+    // devices first_device .. first_device + n_gpus - 1
+    GpuPool(int n_gpus, int64_t timeout_ms, int per_gpu = 3, int first_device = 0);
     ~GpuPool();
     int size() const { return (int)workers_.size(); }
     int gpus() const { return n_gpus_; }
@@ -112,14 +124,20 @@ class GpuPool {
 };
 
 // main.rs:454-589 build_plan: measures every (tensor, candidate) error on
-// the GPUs and solves for the budget (or applies the uniform mix).
-Plan build_plan(const FitArgs &args, const ModelView &m, const Imatrix &im, GpuPool &pool, Timing &tm);
+// the GPUs and solves for the budget (or applies the uniform mix).  With an
+// active shard this rank measures the rows it owns and the table is
+// completed by the exchange; every rank returns the same plan.
+Plan build_plan(const FitArgs &args, const ModelView &m, const Imatrix &im, GpuPool &pool, Timing &tm,
+                const Shard &shard = Shard());
 void print_plan(const Plan &plan, const ModelView &m);
 uint32_t file_type_code(const std::vector<PlanEntry> &entries);  // main.rs:628-659
 // main.rs:691-751 write_quantized (without the calibration reuse path):
-// writes out_path via a temporary file and a rename.
+// writes out_path via a temporary file and a rename.  An empty out_path
+// encodes into host memory.  With an active shard every rank encodes the
+// rows it owns and writes them at their final offsets of the same file
+// (rank 0 writes the header; the barrier orders creation and the rename).
 void write_quantized(const std::string &out_path, const Plan &plan, const ModelView &m, const Imatrix &im,
-                     GpuPool &pool, Timing &tm);
+                     GpuPool &pool, Timing &tm, const Shard &shard = Shard());
 
 // Synthetic models of the benchmark configurations (weights generated from
 // a seed straight into host memory).
@@ -137,6 +155,10 @@ struct SyntheticModel {
     std::vector<std::unique_ptr<HostBuffer>> storage;
     Imatrix imatrix;
 };
-std::unique_ptr<SyntheticModel> synthetic_model(const std::string &name, uint64_t seed, int threads);
+// With world > 1 only rows [n*rank/world, n*(rank+1)/world) of each 2-D
+// tensor are generated (the rows that rank owns); values do not depend on
+// the split.
+std::unique_ptr<SyntheticModel> synthetic_model(const std::string &name, uint64_t seed, int threads, int rank = 0,
+                                                int world = 1);
 
 }  // namespace shh

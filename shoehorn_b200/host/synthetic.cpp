@@ -55,23 +55,25 @@ struct Spec {
     uint32_t ty;
 };
 
-void fill_normal_bf16(uint8_t *dst, uint64_t n, uint64_t key, float stdv, float boost_frac, int threads) {
+// Elements [e0, e0 + n) of a tensor whose element pair p is normal2(key, p):
+// any range of rows can be generated alone and equals the same rows of the
+// whole tensor (e0 even).
+void fill_normal_bf16(uint8_t *dst, uint64_t e0, uint64_t n, uint64_t key, float stdv, int threads) {
     uint16_t *o = reinterpret_cast<uint16_t *>(dst);
-    const uint64_t pairs = (n + 1) / 2;
+    const uint64_t p0 = e0 / 2, pairs = (n + 1) / 2;
     std::vector<std::thread> th;
     for (int t = 0; t < threads; t++) {
         th.emplace_back([=]() {
             const uint64_t a = pairs * (uint64_t)t / (uint64_t)threads, b = pairs * (uint64_t)(t + 1) / (uint64_t)threads;
             for (uint64_t p = a; p < b; p++) {
                 float z0, z1;
-                normal2(key, p, z0, z1);
+                normal2(key, p0 + p, z0, z1);
                 o[2 * p] = to_bf16(z0 * stdv);
                 if (2 * p + 1 < n) o[2 * p + 1] = to_bf16(z1 * stdv);
             }
         });
     }
     for (auto &x : th) x.join();
-    (void)boost_frac;
 }
 }  // namespace
 
@@ -120,8 +122,12 @@ static std::unique_ptr<SyntheticModel> e2e_model() {
     return sm;
 }
 
-std::unique_ptr<SyntheticModel> synthetic_model(const std::string &name, uint64_t seed, int threads) {
-    if (name == "e2e") return e2e_model();
+std::unique_ptr<SyntheticModel> synthetic_model(const std::string &name, uint64_t seed, int threads, int rank,
+                                                int world) {
+    if (name == "e2e") {
+        if (world > 1) throw Error("the e2e fixture is not generated in shards");
+        return e2e_model();
+    }
     auto sm = std::make_unique<SyntheticModel>();
     std::vector<Spec> specs;
     std::string arch;
@@ -184,12 +190,16 @@ std::unique_ptr<SyntheticModel> synthetic_model(const std::string &name, uint64_
         t.name = specs[i].name;
         t.dims = specs[i].dims;
         t.ty = specs[i].ty;
-        auto buf = std::make_unique<HostBuffer>((size_t)t.byte_size());
+        uint64_t lo, hi;  // the rows this rank holds
+        shard_rows(t.n_rows(), rank, world, lo, hi);
+        v.row_lo.push_back(lo);
+        const uint64_t rb = row_bytes(t.ty, t.ne0());
+        auto buf = std::make_unique<HostBuffer>((size_t)((hi - lo) * rb));
         if (t.ty == T_F32) {
             float *f = reinterpret_cast<float *>(buf->ptr);
-            for (uint64_t e = 0; e < t.n_elements(); e++) f[e] = 1.0f;
+            for (uint64_t e = 0; e < (hi - lo) * t.ne0(); e++) f[e] = 1.0f;
         } else {
-            fill_normal_bf16(buf->ptr, t.n_elements(), seed + i, stdv, 0.0f, threads);
+            fill_normal_bf16(buf->ptr, lo * t.ne0(), (hi - lo) * t.ne0(), seed + i, stdv, threads);
             if (t.name != "token_embd.weight" && t.dims.size() == 2) {
                 // per-column importance exp(N(0,1)) (1% of columns x100 for the 70B config)
                 std::vector<float> im((size_t)t.ne0());
