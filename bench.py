@@ -1,18 +1,33 @@
-"""Benchmark: BF16 GB/s encoded per quant type.
-
-Default workload (--workload kquant): the single-tensor encoder sweep, 4096
-rows x 14336 columns of BF16 (N(0, 0.02) with 0.1% outliers at +-8 sigma,
-per-column log-normal imatrix with sigma 1.5) to Q4_K, Q5_K, Q6_K and Q8_0.
---workload iq: the IQ codebook configuration, [4096 x 4096] and
-[14336 x 4096] Student-t tensors to every IQ type.
+"""Benchmark: BF16 GB/s encoded per quant type, and the Llama-3-8B-shape
+error-table + solve + encode wall time, on 1..N GPUs of one box.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--sections sweep,iq,model] [--no-cpu]
 
-A step encodes every tensor once to every type.  `value` is device-resident
-(inputs in HBM); `e2e` goes through the host-buffer C-ABI entry point with
-pinned host input and output.  L2 (126 MB) is flushed before every timed
-encode.  Under torchrun every rank encodes its own copy (weak scaling, no
-collective on the data path); the time is the max over ranks.
+Sections of one run (all by default; the JSON line's headline `value` is the
+sweep's):
+  sweep  the single-tensor encoder sweep: 4096 rows x 14336 BF16 (N(0, 0.02)
+         with 0.1% outliers at +-8 sigma, per-column log-normal imatrix,
+         sigma 1.5) to Q4_K, Q5_K, Q6_K and Q8_0.  A step encodes the tensor
+         once to every type.
+  iq     the IQ codebook configuration: [4096 x 4096] and [14336 x 4096]
+         Student-t (nu 5) tensors with a log-normal (sigma 1) imatrix, to every
+         IQ type.  Reported per type beside the sweep.
+  model  the Llama-3-8B shape (synthetic BF16 weights N(0, 0.02), log-normal
+         imatrix): the full error table (the reference's 128-row sampling, and
+         every row), the solve for a 5.5 GiB weight budget and the encode of
+         the chosen mix, through the host pipeline library.
+
+Under torchrun (one process per GPU, NCCL) every section shards rows: rank r
+of N owns rows [n*r/N, n*(r+1)/N) of every tensor (the row-range sharding of
+the pipeline), so the total work is fixed and N GPUs share it (strong
+scaling).  Nothing crosses ranks on the data path; the model section
+all-gathers the per-row f64 errors once, before the solve.  Times are taken
+per rank and the job's time is the slowest rank's.
+
+`value` is device-resident (inputs in HBM; the L2 is flushed by a read of a
+512 MB buffer before every timed encode); `e2e` goes through the host-buffer
+C-ABI entry point (pinned host input and output, copies inside the timing).
 """
 import argparse
 import json
@@ -28,84 +43,42 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-N_ROWS, NE0 = 4096, 14336
-SEED = 20261201
+from shoehorn_b200 import workloads  # noqa: E402
+
 SWEEP = ["Q4_K", "Q5_K", "Q6_K", "Q8_0"]
+IQ_TYPES = ["IQ2_XXS", "IQ2_XS", "IQ2_S", "IQ3_XXS", "IQ3_S", "IQ4_NL", "IQ4_XS"]
 METRIC = "BF16 GB/s encoded per quant type"
-TYPE_IDS = {"Q8_0": 8, "Q2_K": 10, "Q3_K": 11, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "IQ2_XXS": 16, "IQ2_XS": 17, "IQ3_XXS": 18,
-            "IQ4_NL": 20, "IQ3_S": 21, "IQ2_S": 22, "IQ4_XS": 23}
-OUT_BYTES_PER_ELT = {"Q8_0": 34 / 32, "Q2_K": 84 / 256, "Q3_K": 110 / 256, "Q4_K": 144 / 256, "Q5_K": 176 / 256, "Q6_K": 210 / 256,
-                     "IQ2_XXS": 66 / 256, "IQ2_XS": 74 / 256, "IQ2_S": 82 / 256, "IQ3_XXS": 98 / 256,
-                     "IQ3_S": 110 / 256, "IQ4_NL": 18 / 32, "IQ4_XS": 136 / 256}
+TYPE_IDS = {"Q8_0": 8, "Q2_K": 10, "Q3_K": 11, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "IQ2_XXS": 16, "IQ2_XS": 17,
+            "IQ3_XXS": 18, "IQ4_NL": 20, "IQ3_S": 21, "IQ2_S": 22, "IQ4_XS": 23, "F16": 1}
+OUT_BYTES_PER_ELT = {"Q8_0": 34 / 32, "Q2_K": 84 / 256, "Q3_K": 110 / 256, "Q4_K": 144 / 256, "Q5_K": 176 / 256,
+                     "Q6_K": 210 / 256, "IQ2_XXS": 66 / 256, "IQ2_XS": 74 / 256, "IQ2_S": 82 / 256,
+                     "IQ3_XXS": 98 / 256, "IQ3_S": 110 / 256, "IQ4_NL": 18 / 32, "IQ4_XS": 136 / 256}
 # Algorithmic f32 operations per input element of the reference encoders,
 # counted by executing the oracle's op-counting build (oracle/opcount) on 32
 # evenly spaced rows of each benchmark tensor: every f32 add, sub, mul, div,
 # sqrt, compare, min/max and round-to-integer executed by the algorithm as
 # written (no CSE or hoisting credited), data-dependent neighbour searches
 # included.  The kernels execute fewer operations than this (loop invariants
-# hoisted, products shared), so the figure is the work done, not the
-# instructions issued.
+# hoisted, products shared, repeated grids skipped), so the figure is the
+# work done, not the instructions issued.
 FLOPS_PER_ELT = {"Q4_K": 745.4, "Q5_K": 745.4, "Q6_K": 151.0, "Q8_0": 5.1, "Q2_K": 768.8, "Q3_K": 152.1,
                  "IQ2_XXS": 1839.0, "IQ2_XS": 3738.2, "IQ2_S": 713.8, "IQ3_XXS": 1498.4, "IQ3_S": 963.8,
                  "IQ4_NL": 274.7, "IQ4_XS": 274.7}
 # FP32 ceiling for separately rounded adds and multiplies on sm_100: 128 per
-# clock per SM, scalar or packed f32x2 alike (shoehorn_b200/fp32-rate measures
-# 121-126 for add-only/mul-only chains); fused multiply-adds would reach 250
-# flops/clk/SM but are excluded by the parity contract.
+# clock per SM (an issue-rate probe measured 121 scalar and 126 packed f32x2
+# add-only or mul-only operations per clock per SM); fused multiply-adds would
+# reach 256 flops/clk/SM but are excluded by the parity contract.
 FP32_OPS_PER_CLK_PER_SM = 128
+# Llama-3-8B shape: weight budget 5.5 GiB = --budget (weights + KV + compute
+# at ctx 8192) with --reserve 0, as the reference's budget model computes it
+# (main.rs:294-337).
+MODEL = "llama3-8b"
+MODEL_BUDGET = "7309099008"
+MODEL_CTX = 8192
 
 
-IQ_TYPES = ["IQ2_XXS", "IQ2_XS", "IQ2_S", "IQ3_XXS", "IQ3_S", "IQ4_NL", "IQ4_XS"]
-
-
-def _to_bf16(w):
-    u = w.view(np.uint32)
-    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)  # RNE to BF16
-
-
-def make_workload(seed=SEED):
-    """Encoder sweep: 4096 rows x 14336, N(0, 0.02) + 0.1% outliers at +-8 sigma,
-    imatrix log-normal (sigma 1.5)."""
-    rng = np.random.default_rng(seed)
-    w = rng.standard_normal((N_ROWS, NE0), dtype=np.float32)
-    w *= np.float32(0.02)
-    k = int(round(w.size * 0.001))
-    idx = rng.choice(w.size, size=k, replace=False)
-    w.reshape(-1)[idx] = rng.choice(np.array([-0.16, 0.16], dtype=np.float32), size=k)
-    im = np.exp(rng.normal(0.0, 1.5, size=NE0)).astype(np.float32)
-    return _to_bf16(w), im
-
-
-def make_iq_workload(seed=SEED):
-    """IQ codebook config: [4096 rows x 4096] and [14336 rows x 4096] Student-t
-    (nu=5) scaled to std 0.02, imatrix log-normal (sigma 1)."""
-    out = []
-    for i, rows in enumerate((4096, 14336)):
-        rng = np.random.default_rng(seed + 1 + i)
-        w = (rng.standard_t(5.0, size=(rows, 4096)) * (0.02 / np.sqrt(5.0 / 3.0))).astype(np.float32)
-        im = np.exp(rng.normal(0.0, 1.0, size=4096)).astype(np.float32)
-        out.append((f"{rows}x4096", _to_bf16(w), im))
-    return out
-
-
-def workload_tensors(name):
-    if name == "iq":
-        return make_iq_workload()
-    bits, im = make_workload()
-    return [(f"{N_ROWS}x{NE0}", bits, im)]
-
-
-def captured_traffic(type_name, in_bytes):
-    """DRAM bytes per launch of a type's encoder from the committed ncu capture
-    (profiles/traffic_encoder_sweep.txt), for the 4096 x 14336 tensor only."""
-    path = os.path.join(ROOT, "profiles", "traffic_encoder_sweep.txt")
-    if in_bytes != N_ROWS * NE0 * 2 or not os.path.exists(path):
-        return None
-    for line in open(path):
-        f = line.split()
-        if len(f) >= 4 and not line.startswith("#") and f[1] == type_name:
-            return int(f[2]) + int(f[3])
-    return None
+def shard_rows(n, rank, world):
+    return n * rank // world, n * (rank + 1) // world
 
 
 def max_over_ranks(x, dev):
@@ -120,10 +93,10 @@ def max_over_ranks(x, dev):
     return float(tt.item())
 
 
-def aggregate_gbs(world, n_types, in_bytes, seconds):
-    """Whole-job BF16 GB/s for weak scaling: every rank encodes its own copy of
-    the workload to every type, and the job takes the slowest rank's time."""
-    return world * n_types * in_bytes / seconds / 1e9
+def aggregate_gbs(total_in_bytes, n_types, seconds):
+    """Whole-job BF16 GB/s: the full tensors' bytes, encoded once to each type,
+    over the slowest rank's time (the ranks share the rows)."""
+    return n_types * total_in_bytes / seconds / 1e9
 
 
 def dist_env():
@@ -182,14 +155,17 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+# ---------------------------------------------------------------------------
+# CPU baselines: the reference algorithm (the C restatement in oracle/) on the
+# host cores, on bounded samples of the same workloads.
+# ---------------------------------------------------------------------------
 def cpu_baseline(tensors, types, budget_s=12.0):
-    """The reference algorithm (the C restatement in oracle/) on host cores:
-    a bounded sample of rows of the same tensors per type."""
+    """Per type: the first rows of each tensor, sized to ~budget_s of CPU work
+    in total.  GB/s of BF16 input."""
     from oracle import oracle as O
     cores = os.cpu_count() or 1
-    per_type = {}
+    per_type, samples = {}, []
     tot_bytes, tot_t = 0, 0.0
-    samples = []
     for name in types:
         ty = TYPE_IDS[name]
         b_bytes, b_t = 0, 0.0
@@ -215,16 +191,317 @@ def cpu_baseline(tensors, types, budget_s=12.0):
             "per_type": {k: round(v, 5) for k, v in per_type.items()}, "sample": "; ".join(samples)}
 
 
-def workload_label(args, tensors, types):
-    shapes = " + ".join(t[0] for t in tensors)
-    return f"{'IQ codebook' if args.workload == 'iq' else 'encoder sweep'} {shapes} BF16 ({','.join(types)}), imatrix-weighted"
+def model_shapes():
+    """(name, ne0, n_rows, candidates) of the Llama-3-8B shape's solvable
+    tensors, one entry per distinct shape with its count (main.rs:347-380
+    ladder: 11 candidates, 6 for token_embd/output)."""
+    L, E, KV, FF, V = 32, 4096, 1024, 14336, 128256
+    big = ["IQ2_XXS", "IQ2_XS", "IQ2_S", "IQ3_XXS", "IQ3_S", "IQ4_XS", "Q4_K", "Q5_K", "Q6_K", "Q8_0", "F16"]
+    small = ["IQ4_XS", "Q4_K", "Q5_K", "Q6_K", "Q8_0", "F16"]
+    return [("attn_q", E, E, big, L), ("attn_k", E, KV, big, L), ("attn_v", E, KV, big, L),
+            ("attn_output", E, E, big, L), ("ffn_gate", E, FF, big, L), ("ffn_up", E, FF, big, L),
+            ("ffn_down", FF, E, big, L), ("token_embd", E, V, small, 1), ("output", E, V, small, 1)]
+
+
+def cpu_model_baseline(mix_elements, budget_s=10.0):
+    """The reference's error table and encode for the Llama-3-8B shape on the
+    host cores, extrapolated from a sample: per tensor shape, the error of
+    `rows` rows (of the 128 the reference samples) for every candidate; per
+    type of the chosen mix, the encode of a 4096-wide slab.  Synthetic rows
+    with the configuration's distribution (N(0, 0.02) BF16, log-normal
+    imatrix)."""
+    from oracle import oracle as O
+    cores = os.cpu_count() or 1
+    rng = np.random.default_rng(7)
+    rows = max(cores, 16)
+    sample = []
+    measure_s = 0.0
+    exact_s = 0.0
+    for name, ne0, n_rows, cands, count in model_shapes():
+        bits = workloads.to_bf16((rng.standard_normal((rows, ne0), dtype=np.float32) * np.float32(0.02)))
+        im = np.exp(rng.normal(0.0, 1.0, size=ne0)).astype(np.float32)
+        t0 = time.perf_counter()
+        for c in cands:
+            O.row_errors_bf16(TYPE_IDS[c], bits, None if name == "token_embd" else im, n_threads=cores)
+        dt = time.perf_counter() - t0
+        sampled = min(128, n_rows)
+        measure_s += dt * sampled / rows * count
+        exact_s += dt * n_rows / rows * count
+        sample.append(f"{name}: {rows} rows x {len(cands)} candidates")
+    encode_s = 0.0
+    bits = workloads.to_bf16(rng.standard_normal((rows * 4, 4096), dtype=np.float32) * np.float32(0.02))
+    im = np.exp(rng.normal(0.0, 1.0, size=4096)).astype(np.float32)
+    for ty, elems in mix_elements.items():
+        if ty not in TYPE_IDS or ty == "F16":
+            continue
+        t0 = time.perf_counter()
+        O.encode_tensor_bf16(TYPE_IDS[ty], bits, im, n_threads=cores)
+        dt = time.perf_counter() - t0
+        encode_s += dt * elems / bits.size
+        sample.append(f"encode {ty}: {bits.shape[0]} rows x 4096")
+    return {"measure_s": round(measure_s, 3), "measure_exact_s": round(exact_s, 2), "encode_s": round(encode_s, 2),
+            "wall_s": round(measure_s + encode_s, 2), "wall_exact_s": round(exact_s + encode_s, 2), "cores": cores,
+            "kind": "port", "sample": "; ".join(sample) + " (extrapolated by rows and elements per type)"}
+
+
+# ---------------------------------------------------------------------------
+# GPU sections
+# ---------------------------------------------------------------------------
+class Timer:
+    def __init__(self, torch, stream):
+        self.torch, self.stream = torch, stream
+
+    def __call__(self, fn):
+        s = self.torch.cuda.Event(enable_timing=True)
+        e = self.torch.cuda.Event(enable_timing=True)
+        s.record(self.stream)
+        fn()
+        e.record(self.stream)
+        return s, e
+
+
+def run_encode_section(sh, torch, ctx, dev, stream, tensors, types, steps, warmup, rank, world, flush):
+    """Device-resident encode of this rank's rows of every tensor to every type,
+    then the same through the host-buffer entry point.  Returns per-rank
+    timings (ms per step, per type)."""
+    dtens = []
+    for tname, bits, im in tensors:
+        lo, hi = shard_rows(bits.shape[0], rank, world)
+        src = torch.from_numpy(bits[lo:hi].view(np.int16)).to(dev)
+        imt = torch.from_numpy(im).to(dev)
+        outs = {t: torch.empty((hi - lo, sh.row_bytes(TYPE_IDS[t], bits.shape[1])), dtype=torch.uint8, device=dev)
+                for t in types}
+        dtens.append((tname, src, imt, outs, lo))
+
+    def encode(t, d):
+        ctx.encode_rows(TYPE_IDS[t], d[1], d[2], row0=d[4], out=d[3][t], stream=stream)
+
+    def evict():
+        # evict the inputs from L2 by reading 512 MB (a write would leave dirty
+        # lines whose write-back lands inside the next timed encode)
+        flush.max()
+
+    timer = Timer(torch, stream)
+    for _ in range(warmup):
+        for t in types:
+            for d in dtens:
+                evict()
+                encode(t, d)
+    ctx.sync(stream)
+    torch.cuda.synchronize()
+    ev = {(t, i): [] for t in types for i in range(len(dtens))}
+    launches0 = ctx.launch_count()
+    for _ in range(steps):
+        for t in types:
+            for i, d in enumerate(dtens):
+                evict()
+                ev[(t, i)].append(timer(lambda: encode(t, d)))
+    torch.cuda.synchronize()
+    launches = ctx.launch_count() - launches0
+    ctx.sync(stream)
+    per_type_ms, per_type_min = {}, {}
+    for t in types:
+        steps_ms = [sum(ev[(t, i)][k][0].elapsed_time(ev[(t, i)][k][1]) for i in range(len(dtens)))
+                    for k in range(steps)]
+        per_type_ms[t] = statistics.median(steps_ms)
+        per_type_min[t] = min(steps_ms)
+    # end to end: this rank's rows from pinned host memory through the C ABI
+    htens = []
+    for (tname, bits, im), d in zip(tensors, dtens):
+        lo, hi = shard_rows(bits.shape[0], rank, world)
+        src_h = torch.from_numpy(bits[lo:hi].view(np.int16)).pin_memory()
+        outs_h = {t: torch.empty(tuple(d[3][t].shape), dtype=torch.uint8).pin_memory() for t in types}
+        htens.append((src_h, im, outs_h, lo))
+    for t in types:
+        for src_h, im, outs_h, lo in htens:
+            ctx.encode_tensor_host(TYPE_IDS[t], src_h, im, row0=lo, out=outs_h[t])
+    e2e_t = {t: [] for t in types}
+    for _ in range(max(1, min(steps, 3))):
+        for t in types:
+            t0 = time.perf_counter()
+            for src_h, im, outs_h, lo in htens:
+                ctx.encode_tensor_host(TYPE_IDS[t], src_h, im, row0=lo, out=outs_h[t])
+            e2e_t[t].append(time.perf_counter() - t0)
+    e2e_per_type = {t: statistics.median(v) for t, v in e2e_t.items()}
+    rank_elts = sum(int(d[1].numel()) for d in dtens)
+    out_bytes = sum(int(d[3][t].numel()) for d in dtens for t in types)
+    return {"per_type_ms": per_type_ms, "per_type_min": per_type_min, "e2e_per_type_s": e2e_per_type,
+            "launches": launches, "rank_elts": rank_elts, "rank_out_bytes": out_bytes}
+
+
+def roofline_for(t, elts, ms, sm_mhz, n_sms, peaks):
+    """Roofline of one type's encode call (one launch over `elts` elements in
+    `ms`): HBM for Q8_0, separate f32 add/mul issue for the rest."""
+    if t == "Q8_0":
+        alg = elts * (2 + OUT_BYTES_PER_ELT[t])
+        hbm = peaks.get("hbm_gbs", 6650.0)
+        r = {"bound": "hbm", "achieved": round(alg / (ms * 1e-3) / 1e9, 2), "peak": hbm, "unit": "GB/s",
+             "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if "hbm_gbs" in peaks else "fallback 6650"}
+    else:
+        alg = elts * FLOPS_PER_ELT[t]
+        peak = n_sms * FP32_OPS_PER_CLK_PER_SM * sm_mhz * 1e6 / 1e12
+        r = {"bound": "fp32", "achieved": round(alg / (ms * 1e-3) / 1e12, 3), "peak": round(peak, 3),
+             "unit": "TFLOP/s",
+             "peak_source": f"{n_sms} SMs x {FP32_OPS_PER_CLK_PER_SM} separate f32 add/mul per clock x median SM "
+                            f"clock {sm_mhz:.0f} MHz (MEASURED_PEAKS.json has no FP32 figure)",
+             "flops_per_elt": FLOPS_PER_ELT[t], "flops_source": "oracle op-count build, as-written algorithm"}
+    r["frac"] = round(r["achieved"] / r["peak"], 4)
+    return r
+
+
+def captured_traffic(type_name, elts):
+    """DRAM bytes per launch of a type's encoder from the committed ncu capture
+    (profiles/traffic_encoder_sweep.txt, one launch over the whole 4096 x
+    14336 tensor), scaled to `elts` elements."""
+    path = os.path.join(ROOT, "profiles", "traffic_encoder_sweep.txt")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        f = line.split()
+        if len(f) >= 4 and not line.startswith("#") and f[1] == type_name:
+            return int((int(f[2]) + int(f[3])) * elts / (4096 * 14336))
+    return None
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    import shoehorn_b200 as sh
+
+    rank, local_rank, world = dist_env()
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    dev = torch.device("cuda", local_rank)
+    ctx = sh.Context(local_rank)
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+    flush.zero_()
+    sections = args.sections.split(",")
+    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peaks = json.load(open(peaks_path)) if os.path.exists(peaks_path) else {}
+    props = torch.cuda.get_device_properties(dev)
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
+    smi_index = int(vis[local_rank]) if len(vis) > local_rank and vis[local_rank].isdigit() else local_rank
+
+    line = {"metric": METRIC, "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic"}
+    sampler = ClockSampler(smi_index)
+    sampler.start()
+
+    # ---- sweep (headline) ----
+    types = [t for t in args.types.split(",") if sh.type_supported(TYPE_IDS[t])]
+    sweep_tensors = [(f"{workloads.SWEEP_SHAPE[0]}x{workloads.SWEEP_SHAPE[1]}", *workloads.sweep_tensor())]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    r = run_encode_section(sh, torch, ctx, dev, stream, sweep_tensors, types, args.steps, args.warmup, rank, world,
+                           flush)
+    in_bytes = sum(b.size * 2 for _, b, _ in sweep_tensors)
+    step_ms = max_over_ranks(sum(r["per_type_ms"].values()), dev)
+    e2e_s = max_over_ranks(sum(r["e2e_per_type_s"].values()), dev)
+    per_type_ms_max = {t: max_over_ranks(r["per_type_ms"][t], dev) for t in types}
+    value = aggregate_gbs(in_bytes, len(types), step_ms * 1e-3)
+    line.update({"value": round(value, 3), "unit": "GB/s", "ms_per_step": round(step_ms, 4)})
+    line["config"] = {"workload": f"encoder sweep {sweep_tensors[0][0]} BF16 ({','.join(types)}), imatrix-weighted",
+                      "types": types, "tensors": [t[0] for t in sweep_tensors],
+                      "l2": "evicted (512 MB read) before every timed encode",
+                      "parallelism": f"rows sharded over {world} rank(s), no collective on the data path"}
+    line["per_type_gbs"] = {t: round(in_bytes / (per_type_ms_max[t] * 1e-3) / 1e9, 3) for t in types}
+    line["per_type_ms"] = {t: round(v, 4) for t, v in per_type_ms_max.items()}
+    line["e2e"] = {"value": round(aggregate_gbs(in_bytes, len(types), e2e_s), 3), "unit": "GB/s",
+                   "h2d_bytes_per_step": len(types) * in_bytes,
+                   "d2h_bytes_per_step": int(sum(OUT_BYTES_PER_ELT[t] for t in types) * in_bytes / 2)}
+    line["gpu_launches"] = r["launches"]
+    sweep_rank = r
+
+    # ---- IQ configuration ----
+    iq = None
+    if "iq" in sections:
+        iq_types = [t for t in IQ_TYPES if sh.type_supported(TYPE_IDS[t])]
+        iq_tensors = workloads.iq_tensors()
+        ri = run_encode_section(sh, torch, ctx, dev, stream, iq_tensors, iq_types, max(1, args.steps // 4),
+                                min(args.warmup, 3), rank, world, flush)
+        iq_bytes = sum(b.size * 2 for _, b, _ in iq_tensors)
+        iq_ms = {t: max_over_ranks(ri["per_type_ms"][t], dev) for t in iq_types}
+        iq_step = sum(iq_ms.values())
+        iq_e2e = max_over_ranks(sum(ri["e2e_per_type_s"].values()), dev)
+        iq = {"workload": "IQ codebook " + " + ".join(t[0] for t in iq_tensors) + " BF16 Student-t, imatrix-weighted",
+              "value": round(aggregate_gbs(iq_bytes, len(iq_types), iq_step * 1e-3), 3), "unit": "GB/s",
+              "per_type_gbs": {t: round(iq_bytes / (iq_ms[t] * 1e-3) / 1e9, 3) for t in iq_types},
+              "per_type_ms": {t: round(v, 4) for t, v in iq_ms.items()},
+              "e2e": {"value": round(aggregate_gbs(iq_bytes, len(iq_types), iq_e2e), 3), "unit": "GB/s"},
+              "gpu_launches": ri["launches"], "_rank": ri, "_tensors": iq_tensors, "_types": iq_types}
+
+    # ---- Llama-3-8B shape: error table + solve + encode ----
+    model = None
+    if "model" in sections:
+        from shoehorn_b200 import host
+        comm = host.Comm(rank, world)
+        recs = host.bench_model(MODEL, device=local_rank, modes=("sampled", "exact"), budget=MODEL_BUDGET,
+                                reserve="0", ctx=MODEL_CTX, comm=comm)
+        model = {"workload": "Llama-3-8B shape (32 layers, hidden 4096, GQA 32/8, FFN 14336, vocab 128256 untied), "
+                             "synthetic BF16 N(0, 0.02), log-normal imatrix; weight budget 5.5 GiB",
+                 "elements": recs[0]["elements"]}
+        for rec in recs:
+            key = "exact" if rec["exact_errors"] else "sampled"
+            m = {k: round(max_over_ranks(rec[k], dev), 4)
+                 for k in ("measure_s", "gather_s", "solve_s", "setup_s", "encode_s", "wall_s")}
+            m["plan_bytes"] = rec["plan_bytes"]
+            m["mix_elements"] = rec["mix_elements"]
+            model[key] = m
+        model["generate_s"] = round(max_over_ranks(recs[0]["generate_s"], dev), 2)
+
+    clocks = sampler.stop()
+    line["clocks"] = clocks
+
+    # roofline of the dominant kernel of the sweep, on rank 0's launch
+    sm_mhz = clocks.get("sm_mhz") or peaks.get("sm_max_mhz", 1965.0)
+    dom = max(types, key=lambda t: sweep_rank["per_type_ms"][t])
+    roof = roofline_for(dom, sweep_rank["rank_elts"], sweep_rank["per_type_ms"][dom], sm_mhz,
+                        props.multi_processor_count, peaks)
+    roof["kernel"] = f"{dom} encode call (row sigma^2 pre-pass + encoder)" if dom != "Q8_0" else "Q8_0 encoder"
+    roof["traffic"] = captured_traffic(dom, sweep_rank["rank_elts"])
+    roof["per_type_frac"] = {t: roofline_for(t, sweep_rank["rank_elts"], sweep_rank["per_type_ms"][t], sm_mhz,
+                                             props.multi_processor_count, peaks)["frac"] for t in types}
+    line["roofline"] = roof
+    if iq:
+        ri = iq.pop("_rank")
+        iq_tensors = iq.pop("_tensors")
+        iq_types = iq.pop("_types")
+        iq["roofline_frac"] = {t: roofline_for(t, ri["rank_elts"], ri["per_type_ms"][t], sm_mhz,
+                                               props.multi_processor_count, peaks)["frac"] for t in iq_types}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(sweep_tensors, types, budget_s=args.ref_budget)
+        if iq:
+            iq["cpu_baseline"] = cpu_baseline(iq_tensors, iq_types, budget_s=args.ref_budget)
+        if model:
+            model["cpu_baseline"] = cpu_model_baseline(model["sampled"]["mix_elements"])
+    line["cpu_baseline"] = cpu
+    if iq:
+        line["iq"] = iq
+    if model:
+        line["model"] = model
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
 
 
 def run_reference(args):
+    """The reference algorithm on the host cores (the C restatement in
+    oracle/; the reference itself is a Rust crate, not buildable here), on
+    the sweep's config and metric; rank 0 only."""
     rank, _, world = dist_env()
     if rank != 0:
         return 0
-    tensors = workload_tensors(args.workload)
+    tensors = [(f"{workloads.SWEEP_SHAPE[0]}x{workloads.SWEEP_SHAPE[1]}", *workloads.sweep_tensor())]
     types = args.types.split(",")
     for _ in range(args.warmup):
         cpu_baseline(tensors, types, budget_s=2.0)
@@ -238,160 +515,15 @@ def run_reference(args):
     value = statistics.median(vals)
     line = {"metric": METRIC, "value": round(value, 5), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(wall / args.steps * 1e3, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": workload_label(args, tensors, types), "types": types, "l2": "n/a (host CPU)"},
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": f"encoder sweep {tensors[0][0]} BF16 ({','.join(types)}), imatrix-weighted",
+                       "types": types, "tensors": [t[0] for t in tensors], "l2": "n/a (host CPU)",
+                       "parallelism": f"host threads of one process ({os.cpu_count()} cores)"},
             "cpu_baseline": {"value": round(value, 5), "unit": "GB/s", "cores": cb["cores"], "kind": "port",
                              "sample": cb["sample"]},
             "e2e": {"value": round(value, 5), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "per_type_gbs": cb["per_type"]}
     print(json.dumps(line), flush=True)
-    return 0
-
-
-def run_ours(args):
-    import torch
-    import torch.distributed as dist
-    import shoehorn_b200 as sh
-
-    rank, local_rank, world = dist_env()
-    torch.cuda.set_device(local_rank)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
-    dev = torch.device("cuda", local_rank)
-    ctx = sh.Context(local_rank)
-    types = [t for t in args.types.split(",") if sh.type_supported(TYPE_IDS[t])]
-    tensors = workload_tensors(args.workload)
-    dtens = []
-    for tname, bits, im in tensors:
-        src = torch.from_numpy(bits.view(np.int16)).to(dev)
-        imt = torch.from_numpy(im).to(dev)
-        outs = {t: torch.empty((bits.shape[0], sh.row_bytes(TYPE_IDS[t], bits.shape[1])), dtype=torch.uint8,
-                               device=dev) for t in types}
-        dtens.append((tname, src, imt, outs))
-    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
-    stream = torch.cuda.current_stream(dev)
-
-    def encode(t, d):
-        ctx.encode_rows(TYPE_IDS[t], d[1], d[2], out=d[3][t], stream=stream)
-
-    for _ in range(args.warmup):
-        for t in types:
-            for d in dtens:
-                flush.zero_()
-                encode(t, d)
-    ctx.sync(stream)
-    torch.cuda.synchronize()
-
-    ev = {(t, i): [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                   for _ in range(args.steps)] for t in types for i in range(len(dtens))}
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
-    smi_index = int(vis[local_rank]) if len(vis) > local_rank and vis[local_rank].isdigit() else local_rank
-    sampler = ClockSampler(smi_index)
-    sampler.start()
-    launches0 = ctx.launch_count()
-    for k in range(args.steps):
-        for t in types:
-            for i, d in enumerate(dtens):
-                flush.zero_()  # evict the input from L2 before every timed encode
-                s, e = ev[(t, i)][k]
-                s.record(stream)
-                encode(t, d)
-                e.record(stream)
-    torch.cuda.synchronize()
-    launches = ctx.launch_count() - launches0
-    ctx.sync(stream)
-    # per type: median over steps of the summed tensor times
-    per_type_ms, per_type_min = {}, {}
-    for t in types:
-        steps_ms = [sum(ev[(t, i)][k][0].elapsed_time(ev[(t, i)][k][1]) for i in range(len(dtens)))
-                    for k in range(args.steps)]
-        per_type_ms[t] = statistics.median(steps_ms)
-        per_type_min[t] = min(steps_ms)
-    step_ms = max_over_ranks(sum(per_type_ms.values()), dev)
-
-    # end to end: host (pinned) buffers through the C-ABI host entry point
-    htens = []
-    for (tname, bits, im), d in zip(tensors, dtens):
-        src_h = torch.from_numpy(bits.view(np.int16)).pin_memory()
-        outs_h = {t: torch.empty(tuple(d[3][t].shape), dtype=torch.uint8).pin_memory() for t in types}
-        htens.append((src_h, im, outs_h))
-    for t in types:
-        for src_h, im, outs_h in htens:
-            ctx.encode_tensor_host(TYPE_IDS[t], src_h, im, out=outs_h[t])
-    if world > 1:
-        dist.barrier()
-    e2e_t = {t: [] for t in types}
-    for _ in range(max(1, min(args.steps, 3))):
-        for t in types:
-            t0 = time.perf_counter()
-            for src_h, im, outs_h in htens:
-                ctx.encode_tensor_host(TYPE_IDS[t], src_h, im, out=outs_h[t])
-            e2e_t[t].append(time.perf_counter() - t0)
-    e2e_step = max_over_ranks(sum(statistics.median(v) for v in e2e_t.values()), dev)
-    clocks = sampler.stop()
-
-    in_bytes = sum(int(d[1].numel()) * 2 for d in dtens)
-    elts = in_bytes // 2
-    value = aggregate_gbs(world, len(types), in_bytes, step_ms * 1e-3)
-    e2e_value = aggregate_gbs(world, len(types), in_bytes, e2e_step)
-    per_type = {t: round(in_bytes / (per_type_ms[t] * 1e-3) / 1e9, 3) for t in types}
-
-    # roofline of the dominant kernel (largest share of the step)
-    dom = max(types, key=lambda t: per_type_ms[t])
-    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    peaks = json.load(open(peaks_path)) if os.path.exists(peaks_path) else {}
-    props = torch.cuda.get_device_properties(dev)
-    sm_mhz = clocks.get("sm_mhz") or peaks.get("sm_max_mhz", 1965.0)
-    if dom == "Q8_0":
-        alg = elts * (2 + OUT_BYTES_PER_ELT[dom])
-        hbm = peaks.get("hbm_gbs", 6650.0)
-        roof = {"bound": "hbm", "achieved": round(alg / (per_type_ms[dom] * 1e-3) / 1e9, 2), "peak": hbm,
-                "unit": "GB/s",
-                "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if "hbm_gbs" in peaks else "fallback"}
-    else:
-        alg = elts * FLOPS_PER_ELT[dom]
-        # no multiply-add contraction is allowed (parity), so the ceiling is
-        # separate f32 adds/multiplies
-        peak = props.multi_processor_count * FP32_OPS_PER_CLK_PER_SM * sm_mhz * 1e6 / 1e12
-        roof = {"bound": "fp32", "achieved": round(alg / (per_type_ms[dom] * 1e-3) / 1e12, 3),
-                "peak": round(peak, 3), "unit": "TFLOP/s",
-                "peak_source": f"{props.multi_processor_count} SMs x {FP32_OPS_PER_CLK_PER_SM} separate f32 add/mul "
-                               f"per clock (no FMA by the parity contract; 121-126 measured by fp32-rate) x median "
-                               f"SM clock {sm_mhz:.0f} MHz (MEASURED_PEAKS.json has no FP32 figure)",
-                "flops_per_elt": FLOPS_PER_ELT[dom], "flops_source": "oracle op-count build, as-written algorithm"}
-    roof["frac"] = round(roof["achieved"] / roof["peak"], 4)
-    roof["kernel"] = f"{dom} encoder"
-    roof["traffic"] = captured_traffic(dom, in_bytes)
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_baseline(tensors, types, budget_s=args.ref_budget)
-
-    if rank == 0:
-        line = {"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                "config": {"workload": workload_label(args, tensors, types), "types": types,
-                           "tensors": [t[0] for t in tensors],
-                           "l2": "flushed (512 MB write) before every timed encode",
-                           "parallelism": f"weak: each of {world} ranks encodes its own copy"},
-                "per_type_gbs": per_type,
-                "per_type_ms": {t: round(v, 4) for t, v in per_type_ms.items()},
-                "per_type_ms_min": {t: round(v, 4) for t, v in per_type_min.items()},
-                "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
-                        "h2d_bytes_per_step": len(types) * in_bytes,
-                        "d2h_bytes_per_step": sum(int(d[3][t].numel()) for d in dtens for t in types)},
-                "roofline": roof, "clocks": clocks, "gpu_launches": launches,
-                "cpu_baseline": cpu}
-        print(json.dumps(line), flush=True)
-    ctx.close()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
     return 0
 
 
@@ -401,13 +533,11 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="kquant", choices=["kquant", "iq"])
-    ap.add_argument("--types", default=None, help="comma-separated types (default: the workload's)")
+    ap.add_argument("--sections", default="sweep,iq,model", help="comma-separated: sweep (always), iq, model")
+    ap.add_argument("--types", default=",".join(SWEEP), help="comma-separated types of the sweep")
     ap.add_argument("--ref-budget", type=float, default=12.0, help="seconds of CPU work per reference sample")
-    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
     args = ap.parse_args()
-    if args.types is None:
-        args.types = ",".join(IQ_TYPES if args.workload == "iq" else SWEEP)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -54,25 +54,18 @@ class Comm:
         def allgather(_user, mine, n, out, cap, sizes):
             try:
                 if not out:
-                    data = ctypes.string_at(mine, n) if n else b""
-                    if self.world == 1:
-                        self._blobs = [data]
-                    else:
-                        import torch.distributed as dist
-                        blobs = [None] * self.world
-                        dist.all_gather_object(blobs, data)
-                        self._blobs = blobs
-                    return sum(len(b) for b in self._blobs)
-                total = sum(len(b) for b in self._blobs)
+                    self._blobs = self._gather(mine, n)
+                    return int(sum(b.size for b in self._blobs))
+                total = int(sum(b.size for b in self._blobs))
                 if total > cap:
                     return -1
-                buf = (ctypes.c_uint8 * cap).from_address(out)
                 sz = (ctypes.c_int64 * self.world).from_address(sizes)
                 at = 0
                 for r, b in enumerate(self._blobs):
-                    buf[at:at + len(b)] = b
-                    sz[r] = len(b)
-                    at += len(b)
+                    if b.size:
+                        ctypes.memmove(out + at, b.ctypes.data, b.size)
+                    sz[r] = b.size
+                    at += b.size
                 self._blobs = None
                 return total
             except Exception:
@@ -90,6 +83,28 @@ class Comm:
         self.allgather = ALLGATHER_FN(allgather)
         self.barrier = BARRIER_FN(barrier)
 
+    def _gather(self, mine, n):
+        """Every rank's bytes (numpy uint8 arrays, rank order): sizes first,
+        then one all-gather of the blobs padded to the largest (on the GPU
+        under NCCL, in host memory under gloo)."""
+        data = np.frombuffer(ctypes.string_at(mine, n), dtype=np.uint8) if n else np.zeros(0, np.uint8)
+        if self.world == 1:
+            return [data]
+        import torch
+        import torch.distributed as dist
+        dev = torch.device("cuda", torch.cuda.current_device()) if dist.get_backend() == "nccl" else torch.device("cpu")
+        size = torch.tensor([data.size], dtype=torch.int64, device=dev)
+        sizes = [torch.zeros_like(size) for _ in range(self.world)]
+        dist.all_gather(sizes, size)
+        sizes = [int(x.item()) for x in sizes]
+        mx = max(sizes)
+        buf = torch.zeros(mx, dtype=torch.uint8, device=dev)
+        if data.size:
+            buf[:data.size] = torch.from_numpy(data.copy()).to(dev)
+        outs = [torch.empty(mx, dtype=torch.uint8, device=dev) for _ in range(self.world)]
+        dist.all_gather(outs, buf)
+        return [o[:sz].cpu().numpy() for o, sz in zip(outs, sizes)]
+
 
 def shard_exchange_check(n_rows, n_cands, sample_rows=128, comm=None):
     """Error-table exchange on made-up errors (no GPU): [n_tensors, max_cands]
@@ -105,13 +120,15 @@ def shard_exchange_check(n_rows, n_cands, sample_rows=128, comm=None):
     return sums
 
 
-def bench_model(name, device=0, exact_errors=False, budget=None, reserve="0", ctx=8192, uniform="",
+def bench_model(name, device=0, modes=("sampled",), budget=None, reserve="0", ctx=8192, uniform="",
                 workers_per_gpu=3, seed=20261201, out_path="", comm=None):
-    """Error table + solve + encode of a synthetic model on this rank's rows.
-    Returns the timing record (dict)."""
+    """Error table + solve + encode of a synthetic model on this rank's rows,
+    once per mode ("sampled": the reference's 128-row error table, "exact":
+    every row).  Returns the timing records (list of dicts)."""
     comm = comm or Comm()
+    bits = (1 if "sampled" in modes else 0) | (2 if "exact" in modes else 0)
     buf = ctypes.create_string_buffer(1 << 16)
-    rc = lib().shh_bench_model(name.encode(), seed, int(exact_errors), (budget or "").encode() or None,
+    rc = lib().shh_bench_model(name.encode(), seed, bits, (budget or "").encode() or None,
                                reserve.encode() if reserve is not None else None, ctx, uniform.encode(),
                                workers_per_gpu, device, comm.rank, comm.world, comm.allgather, comm.barrier, None,
                                out_path.encode(), buf, len(buf))

@@ -163,18 +163,19 @@ int shh_shard_exchange_check(int64_t n_tensors, const uint64_t *n_rows, const in
 }
 
 // Plan (error table + solve) and encode of a synthetic model configuration
-// ("qwen3-0.6b", "llama3-8b", "llama3-70b", "tiny") on this rank's rows,
-// on CUDA device `device`.  budget / reserve / uniform follow the CLI flags
-// (uniform non-empty: a fixed mix, no solve).  out_path empty: output in host
-// memory.  Writes one JSON line of timings into json.  0 on success, -1 with
+// ("qwen3-0.6b", "llama3-8b", "llama3-70b", "tiny") on this rank's rows, on
+// CUDA device `device`.  The model is generated once; then one run per bit
+// of `modes` (1: the reference's 128-row sampled error table, 2: every row,
+// --exact-errors), each a barrier then measure, exchange, solve and encode.
+// budget / reserve / uniform follow the CLI flags (uniform non-empty: a
+// fixed mix, no solve, one run).  out_path empty: output in host memory.
+// Writes a JSON array of timing records into json.  0 on success, -1 with
 // the message in json on failure.
-int shh_bench_model(const char *name, uint64_t seed, int exact_errors, const char *budget, const char *reserve,
-                    uint64_t ctx, const char *uniform, int workers_per_gpu, int device, int rank, int world,
-                    shh_allgather_fn ag, shh_barrier_fn bar, void *user, const char *out_path, char *json,
-                    int64_t cap) {
+int shh_bench_model(const char *name, uint64_t seed, int modes, const char *budget, const char *reserve, uint64_t ctx,
+                    const char *uniform, int workers_per_gpu, int device, int rank, int world, shh_allgather_fn ag,
+                    shh_barrier_fn bar, void *user, const char *out_path, char *json, int64_t cap) {
     try {
         shh::FitArgs a;
-        a.exact_errors = exact_errors != 0;
         if (budget) a.budget = budget;
         if (reserve) a.reserve = reserve;
         if (uniform) a.uniform = uniform;
@@ -186,12 +187,6 @@ int shh_bench_model(const char *name, uint64_t seed, int exact_errors, const cha
         auto sm = shh::synthetic_model(name, seed, threads, rank, world);
         const double gen_s = std::chrono::duration<double>(std::chrono::steady_clock::now() - c0).count();
         shh::GpuPool pool(1, a.timeout_ms, a.workers_per_gpu, device);
-        if (shard.active()) shard.barrier();
-        shh::Timing tm;
-        const auto t0 = std::chrono::steady_clock::now();
-        const shh::Plan plan = shh::build_plan(a, sm->view, sm->imatrix, pool, tm, shard);
-        shh::write_quantized(out_path ? out_path : "", plan, sm->view, sm->imatrix, pool, tm, shard);
-        const double wall = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
         uint64_t elems = 0, mine = 0;
         for (size_t i = 0; i < sm->view.tensors.size(); i++) {
             const auto &t = sm->view.tensors[i];
@@ -200,18 +195,36 @@ int shh_bench_model(const char *name, uint64_t seed, int exact_errors, const cha
             elems += t.n_elements();
             mine += (hi - lo) * t.ne0();
         }
-        std::map<std::string, uint64_t> by_type;
-        for (auto &e : plan.entries) by_type[shh::type_name(e.ty)] += sm->view.tensors[e.tensor_idx].n_elements();
-        std::string mix;
-        for (auto &kv : by_type) mix += (mix.empty() ? "" : ", ") + ("\"" + kv.first + "\": " + std::to_string(kv.second));
-        snprintf(json, (size_t)cap,
-                 "{\"model\": \"%s\", \"rank\": %d, \"world\": %d, \"exact_errors\": %s, \"elements\": %llu, "
-                 "\"rank_elements\": %llu, \"generate_s\": %.3f, \"measure_s\": %.4f, \"gather_s\": %.4f, "
-                 "\"solve_s\": %.4f, \"setup_s\": %.4f, \"encode_s\": %.4f, \"wall_s\": %.4f, \"plan_bytes\": %llu, "
-                 "\"budget_bytes\": %llu, \"mix_elements\": {%s}}",
-                 name, rank, world, a.exact_errors ? "true" : "false", (unsigned long long)elems,
-                 (unsigned long long)mine, gen_s, tm.measure_s, tm.gather_s, tm.solve_s, tm.setup_s, tm.encode_s, wall,
-                 (unsigned long long)plan.total_bytes, (unsigned long long)plan.budget.model_budget, mix.c_str());
+        std::string out = "[";
+        for (int mode = 1; mode <= 2; mode++) {
+            if (!(modes & mode)) continue;
+            a.exact_errors = mode == 2;
+            if (shard.active()) shard.barrier();
+            shh::Timing tm;
+            const auto t0 = std::chrono::steady_clock::now();
+            const shh::Plan plan = shh::build_plan(a, sm->view, sm->imatrix, pool, tm, shard);
+            shh::write_quantized(out_path ? out_path : "", plan, sm->view, sm->imatrix, pool, tm, shard);
+            const double wall = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+            std::map<std::string, uint64_t> by_type;
+            for (auto &e : plan.entries) by_type[shh::type_name(e.ty)] += sm->view.tensors[e.tensor_idx].n_elements();
+            std::string mix;
+            for (auto &kv : by_type) mix += (mix.empty() ? "" : ", ") + ("\"" + kv.first + "\": " + std::to_string(kv.second));
+            char rec[4096];
+            snprintf(rec, sizeof rec,
+                     "{\"model\": \"%s\", \"rank\": %d, \"world\": %d, \"exact_errors\": %s, \"elements\": %llu, "
+                     "\"rank_elements\": %llu, \"generate_s\": %.3f, \"measure_s\": %.4f, \"gather_s\": %.4f, "
+                     "\"solve_s\": %.4f, \"setup_s\": %.4f, \"encode_s\": %.4f, \"wall_s\": %.4f, "
+                     "\"plan_bytes\": %llu, \"budget_bytes\": %llu, \"mix_elements\": {%s}}",
+                     name, rank, world, a.exact_errors ? "true" : "false", (unsigned long long)elems,
+                     (unsigned long long)mine, gen_s, tm.measure_s, tm.gather_s, tm.solve_s, tm.setup_s, tm.encode_s,
+                     wall, (unsigned long long)plan.total_bytes, (unsigned long long)plan.budget.model_budget,
+                     mix.c_str());
+            out += (out.size() > 1 ? ", " : "") + std::string(rec);
+            if (!a.uniform.empty()) break;
+        }
+        out += "]";
+        if ((int64_t)out.size() >= cap) throw shh::Error("timing record too long");
+        snprintf(json, (size_t)cap, "%s", out.c_str());
         return 0;
     } catch (const std::exception &e) {
         snprintf(json, (size_t)cap, "%s", e.what());

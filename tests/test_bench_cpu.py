@@ -10,10 +10,26 @@ import bench
 
 
 def test_workloads_have_the_named_shapes():
-    bits, im = bench.make_workload()
+    bits, im = bench.workloads.sweep_tensor()
     assert bits.shape == (4096, 14336) and bits.dtype == np.uint16 and im.shape == (14336,)
-    iq = bench.make_iq_workload()
+    iq = bench.workloads.iq_tensors()
     assert [t[1].shape for t in iq] == [(4096, 4096), (14336, 4096)]
+
+
+def test_row_shards_partition_every_tensor():
+    for n in (1, 7, 1024, 4096, 14336, 128256):
+        for world in (1, 2, 3, 4, 8):
+            ranges = [bench.shard_rows(n, r, world) for r in range(world)]
+            assert ranges[0][0] == 0 and ranges[-1][1] == n
+            assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
+
+
+def test_model_cpu_baseline_extrapolates_from_a_sample():
+    """The CPU restatement timed on a small sample of the Llama-3-8B shape's
+    error table and encode, extrapolated by rows and elements per type."""
+    cb = bench.cpu_model_baseline({"Q4_K": 4096 * 4096, "F16": 100})
+    assert cb["measure_s"] > 0 and cb["encode_s"] > 0 and cb["measure_exact_s"] > cb["measure_s"]
+    assert cb["kind"] == "port" and "extrapolated" in cb["sample"]
 
 
 def test_reference_arm_prints_one_contract_line():

@@ -28,14 +28,14 @@ def _rank_main(rank, world, port, q):
         r, lr, w = bench.dist_env()
         step_ms = 10.0 + 5.0 * rank  # the slower rank sets the job's time
         got = bench.max_over_ranks(step_ms, torch.device("cpu"))
-        value = bench.aggregate_gbs(w, 4, 1_000_000_000, got * 1e-3)
+        value = bench.aggregate_gbs(1_000_000_000, 4, got * 1e-3)
         dist.barrier()
         q.put((r, lr, w, got, value))
     finally:
         dist.destroy_process_group()
 
 
-def test_two_rank_max_and_weak_scaling_aggregate():
+def test_two_rank_max_and_strong_scaling_aggregate():
     world, port = 2, _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -49,7 +49,7 @@ def test_two_rank_max_and_weak_scaling_aggregate():
     for r, (rank, lrank, w, got, value) in enumerate(res):
         assert (rank, lrank, w) == (r, r, 2)
         assert got == 15.0  # max over ranks, identical on every rank
-        assert abs(value - 2 * 4 * 1.0 / 0.015) < 1e-9  # GB/s over both ranks' work
+        assert abs(value - 4 * 1.0 / 0.015) < 1e-9  # GB/s of the whole tensor, shared by the ranks
 
 
 def test_max_over_ranks_without_a_process_group():
