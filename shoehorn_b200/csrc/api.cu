@@ -169,15 +169,14 @@ int encode_view(shc_ctx *ctx, uint32_t type, EncArgs a, cudaStream_t st, int sms
 }
 
 // Re-encode the host lists (quant_iq.rs neighbour order kept) into the layout
-// the device encoder of variant w reads, with kmap offsets remapped.
-//   IQ2 (w 0..2, scanned cooperatively in groups of four): the count sits in
-//   the entry slot just before a four-entry boundary and the entries follow,
-//   padded to a multiple of four with copies of the list's last entry (a
-//   later copy never wins: the scan keeps the first of equal distances).
-//   IQ2_XXS entries are 8-bit grid indices (lists of at most 255), IQ2_XS
-//   and IQ2_S entries 16-bit packed coordinates.
-//   IQ3 (w 3, 4, scanned per lane from shared memory): 16-bit count, then
-//   the 16-bit packed coordinates.
+// the device encoders read.  Every list is scanned in groups of four
+// entries: its entries start on a four-entry boundary and are padded to a
+// multiple of four with copies of the list's last entry (a later copy never
+// wins: the scans keep the first of equal distances).  IQ2_XXS entries are
+// 8-bit grid indices (lists of at most 255), the others 16-bit packed
+// coordinates.  An off-grid kmap entry carries both the list's first entry
+// and its length: kmap = -(1 + offset + (count << kListCountShift)).
+constexpr int kListCountShift = 19;
 void device_lists(int w, const IqHostTable &t, std::vector<int32_t> &kmap, std::vector<uint8_t> &bytes) {
     kmap = t.kmap;
     bytes.clear();
@@ -196,17 +195,14 @@ void device_lists(int w, const IqHostTable &t, std::vector<int32_t> &kmap, std::
             const uint32_t e = t.neighbours[off + k];
             return w == 0 ? (e & 0xFFFF) : (e >> 16);
         };
-        size_t slot = bytes.size() / esz;
-        if (w <= 2) {
-            while ((slot + 1) % 4 != 0) slot++;
-            put(slot, n);
-            const uint32_t padded = (n + 3) / 4 * 4;
-            for (uint32_t k = 1; k <= padded; k++) put(slot + k, entry(k <= n ? k : n));
-        } else {
-            put(slot, n);
-            for (uint32_t k = 1; k <= n; k++) put(slot + k, entry(k));
+        const size_t slot = (bytes.size() / esz + 3) / 4 * 4;
+        const uint32_t padded = (n + 3) / 4 * 4;
+        for (uint32_t k = 1; k <= padded; k++) put(slot + k - 1, entry(k <= n ? k : n));
+        if (n == 0 || n >= (1u << (31 - kListCountShift)) || slot >= (1u << kListCountShift)) {
+            kmap.clear();  // the encoding cannot hold it (never at the shipped grids)
+            return;
         }
-        kmap[c] = -(int32_t)(slot + 1);
+        kmap[c] = -(int32_t)(1 + slot + ((size_t)n << kListCountShift));
     }
     while (bytes.size() % 16) bytes.push_back(0);
 }
@@ -219,6 +215,7 @@ int upload_iq_tables(shc_ctx *ctx) {
     for (int w = 0; w < 5; w++) {
         build_iq_tables(w, t[w]);
         device_lists(w, t[w], dk[w], lists[w]);
+        if (dk[w].empty()) return SHC_EINVAL;
         total += (t[w].kmap.size() * 2 + t[w].neighbours.size() + t[w].grid_coords.size()) * 4 + lists[w].size() + 1024;
     }
     SHC_TRY(cudaMalloc(&ctx->d_tables, total));

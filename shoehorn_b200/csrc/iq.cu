@@ -517,6 +517,8 @@ __device__ float make_qp_quants32_x4(const float *x, const float *w, uint8_t *ls
     if (!dead && u == 0) {
         float sumlx = 0.0f, suml2 = 0.0f;
         for (int i = 0; i < n; i++) {
+            // l may be negative (the parity-flipped element): the sums take the
+            // i32 value, the level buffer its u8 wrap, as the reference does
             const int l = min(nearest_int_qp(iscale * x[i]), nmax);
             ls[i] = (uint8_t)l;
             sumlx += w[i] * x[i] * (float)l;
@@ -550,17 +552,22 @@ __device__ float make_qp_quants32_x4(const float *x, const float *w, uint8_t *ls
     return res;
 }
 
+// An off-grid kmap entry m < 0 holds -(1 + first entry + (count << kListCountShift)).
+constexpr int kListCountShift = 19;
+
 // Neighbour search layout per variant.  IQ2 lists (8 dimensions, ~10-60
 // entries) are scanned cooperatively: a chunk of CJ jobs queues its off-grid
-// groups as tasks, and rounds of 32 tasks share the warp (term tables, equal
-// candidate ranges per lane).  IQ3 lists (4 dimensions, ~10 entries) are
-// scanned by the lane that owns the job, from lists staged in shared memory,
-// with 16 warps per block to hide the scans' latency.
+// groups as tasks, and rounds of 32 tasks share the warp with equal
+// candidate ranges per lane, scored from per-task term tables.  IQ3 lists (4
+// dimensions, ~10 entries) are scanned by the lane that owns the job, from
+// lists staged in shared memory, four candidates per step, with 16 warps per
+// block (measured: a cooperative scan issued fewer instructions for IQ3 but
+// stalled more and ran slower).
 template <int V>
 struct IqSearch {
     static constexpr bool COOP = V < 3;
     static constexpr int CJ = 32;                  // jobs per chunk (COOP)
-    static constexpr bool LISTS_SMEM = !COOP;      // IQ3: 46-57 KB of lists
+    static constexpr bool LISTS_SMEM = !COOP;      // IQ3: 40-50 KB of lists
     static constexpr int WARPS = COOP ? 8 : 16;    // warps per block
 };
 
@@ -572,21 +579,20 @@ struct IqWarpSmem {
     static constexpr bool COOP = IqSearch<V>::COOP;
     static constexpr int BP = C::BS + 1;
     static constexpr int MAXT = COOP ? IqSearch<V>::CJ * C::NG : 1;  // search tasks per chunk of jobs
-    static constexpr int TS = C::G * C::KM;      // terms per round slot
-    unsigned long long key[MAXT];                // task: winning packed levels, or ~0u
-    unsigned long long rkey[COOP ? 32 : 1];      // round slot: best (d2 bits, list position)
+    static constexpr int TS = C::G * C::KM;      // terms waux_i*diff*diff per round slot
+    uint32_t key[MAXT];                          // task: winning packed levels, or ~0u
+    unsigned long long rkey[COOP ? 32 : 1];      // round slot: best (d2 bits, (position, levels))
     union {
         float x[256];                            // the super-block (weights and sigma^2 only)
-        // waux_i*diff*diff of round slot t for (dimension i, level l) at
-        // [(i*KM + l)*32 + t]: a slot's terms share one bank, so lanes
-        // scanning different lists never collide
+        // term (i, l) of round slot t at [(i*KM + l)*32 + t]: a slot's terms
+        // share one bank, so lanes scanning different lists never collide
         float tab[COOP ? 32 * TS : 1];
     };
     float xv[C::NB * BP];
     float w[C::NB * BP];
     float wa[C::NB * BP];
     float2 jres[C::NB * C::NT];                  // (sumqx, sumq2) of every (block, trial) job
-    int pre[COOP ? 33 : 1];                      // round slot: first candidate in the flattened lists
+    int pre[COOP ? 33 : 1];                      // round slot: first group of four in the flattened lists
     int rbase[COOP ? 32 : 1];                    // round slot: list offset
     int tq_m[MAXT];                              // task: kmap entry (< 0: neighbour list offset)
     float tq_s[MAXT];                            // task: scale the candidates are scored at
@@ -623,14 +629,19 @@ __device__ __forceinline__ int warp_exclusive_scan(int cnt, int lane, int &total
 // (bits << 32 | position) is one 64-bit key.
 
 // Per-lane scan of one list (IQ3): returns the winner's packed levels, or ~0u.
-// Kept out of line: its callers are unrolled over the groups.
+// m is the group's kmap entry (first entry and length of its list); the
+// entries start on a four-entry boundary and are padded to a multiple of
+// four with copies of the last entry, so each 64-bit load brings four
+// candidates whose distances are independent chains.  Kept out of line: its
+// callers are unrolled over the groups.
 template <int V>
 __device__ __noinline__ uint32_t lane_search(const uint16_t *l16, int m, const float *xg, const float *wg,
                                                 float scale) {
     using C = IqCfg<V>;
     constexpr uint32_t MASK = (1u << C::BITS) - 1;
-    const uint16_t *p = l16 + (-m - 1);
-    const int n = p[0];
+    const uint32_t v = (uint32_t)(-m - 1);
+    const int n = (int)(v >> kListCountShift);
+    const uint2 *q4 = reinterpret_cast<const uint2 *>(l16 + (v & ((1u << kListCountShift) - 1)));
     float xi[C::G], wi[C::G];
 #pragma unroll
     for (int i = 0; i < C::G; i++) {
@@ -639,33 +650,38 @@ __device__ __noinline__ uint32_t lane_search(const uint16_t *l16, int m, const f
     }
     float best = FLT_MAX;
     uint32_t bc = ~0u;
-    for (int c = 0; c < n; c++) {
-        const uint32_t cc = p[1 + c];
-        float d2 = 0.0f;
+    for (int g = 0; g < (n + 3) >> 2; g++) {
+        const uint2 w4 = q4[g];
+        const uint32_t cc[4] = {w4.x & 0xFFFFu, w4.x >> 16, w4.y & 0xFFFFu, w4.y >> 16};
+        float d2[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int i = 0; i < C::G; i++) {
-            const float diff = scale * odd_level((cc >> (C::BITS * i)) & MASK) - xi[i];
-            d2 += wi[i] * diff * diff;
-        }
-        if (d2 < best) {
-            best = d2;
-            bc = cc;
-        }
+        for (int i = 0; i < C::G; i++)
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const float diff = scale * odd_level((cc[u] >> (C::BITS * i)) & MASK) - xi[i];
+                d2[u] += wi[i] * diff * diff;
+            }
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+            if (d2[u] < best) {  // in list order: strict keeps the first
+                best = d2[u];
+                bc = cc[u];
+            }
     }
     return bc;
 }
 
 // Cooperative scan of the queued tasks [0, T) (IQ2), 32 per round: each lane
-// tabulates one task's terms per (dimension, level); the round's lists are
-// then laid end to end in groups of four entries (each list padded with
-// copies of its last entry) and cut into 32 equal contiguous ranges of
-// groups, one per lane, so every lane scores the same number of candidates
-// whatever the lists' lengths.  A group is one 32- or 64-bit load and four
-// independent distance chains, so the loads and the serial sums of several
-// candidates are in flight together.  A lane keeps the first minimum of its
-// part of each list and merges it into that list's key (shared-memory
+// tabulates one task's terms per (dimension, level); the round's lists are then laid end to end in groups of four entries (each list
+// padded with copies of its last entry) and cut into 32 equal contiguous
+// ranges of groups, one per lane, so every lane scores the same number of
+// candidates whatever the lists' lengths.  A group is one 32- or 64-bit load
+// and four independent distance chains.  A lane keeps the first minimum of
+// its part of each list and merges it into that list's key (shared-memory
 // atomicMin on (d2 bits, position)); only neighbouring lanes ever share a
 // list.  On return key[q] holds task q's winning packed levels, or ~0u.
+// d2 = sum_i waux_i*(scale*g_i - x_i)^2 in the reference's order
+// (quant_iq.rs:152-156), from 0, one dimension after another.
 template <int V>
 __device__ __noinline__ void search_tasks(IqWarpSmem<V> &S, int T, const void *lists, const uint16_t *gco, int lane) {
     using C = IqCfg<V>;
@@ -677,10 +693,10 @@ __device__ __noinline__ void search_tasks(IqWarpSmem<V> &S, int T, const void *l
         const int q = r0 + lane;
         int ng = 0;
         if (q < T) {
-            const int base = -S.tq_m[q] - 1;  // the count; entries start at base + 1, a multiple of 4
-            const int n = V == 0 ? (int)__ldg(l8 + base) : (int)__ldg(l16 + base);
-            ng = (n + 3) >> 2;
-            S.rbase[lane] = base + 1;
+            // the kmap entry holds the list's first entry (a multiple of 4) and length
+            const uint32_t v = (uint32_t)(-S.tq_m[q] - 1);
+            ng = (int)((v >> kListCountShift) + 3) >> 2;
+            S.rbase[lane] = (int)(v & ((1u << kListCountShift) - 1));
             const float scale = S.tq_s[q];
             const int xo = S.tq_x[q];
             float *tb = S.tab + lane;
@@ -707,27 +723,11 @@ __device__ __noinline__ void search_tasks(IqWarpSmem<V> &S, int T, const void *l
                 if (S.pre[mid + 1] > g0) hi = mid;
                 else t = mid + 1;
             }
-            // Loads run two groups ahead of the scoring: (lt, lend, lent) is the
-            // slot of the next group to load, whose entries sit at lent + 4*g.
-            int lt = t, lend = S.pre[t + 1], lent = S.rbase[t] - 4 * S.pre[t];
-            auto load = [&](int g) -> uint2 {
-                while (g >= lend) {
-                    lt++;
-                    lend = S.pre[lt + 1];
-                    lent = S.rbase[lt] - 4 * S.pre[lt];
-                }
-                if (V == 0) return make_uint2(__ldg(reinterpret_cast<const uint32_t *>(l8 + lent + 4 * g)), 0u);
-                return __ldg(reinterpret_cast<const uint2 *>(l16 + lent + 4 * g));
-            };
-            uint2 w1 = load(g0), w2 = make_uint2(0u, 0u);
-            if (g0 + 1 < g1) w2 = load(g0 + 1);
             int end = S.pre[t + 1];
+            int ent = S.rbase[t] - 4 * S.pre[t];  // slot t's group g sits at entry ent + 4*g
             const float *tb = S.tab + t;
             uint32_t bh = 0xFFFFFFFFu, bl = 0xFFFFFFFFu;
             for (int g = g0; g < g1; g++) {
-                const uint2 w4 = w1;
-                w1 = w2;
-                if (g + 2 < g1) w2 = load(g + 2);
                 if (g == end) {  // this lane's part of slot t is done: merge, move to the next nonempty slot
                     if (bh != 0xFFFFFFFFu) atomicMin(&S.rkey[t], ((unsigned long long)bh << 32) | bl);
                     bh = bl = 0xFFFFFFFFu;
@@ -735,13 +735,16 @@ __device__ __noinline__ void search_tasks(IqWarpSmem<V> &S, int T, const void *l
                         t++;
                     } while (S.pre[t + 1] <= g);
                     end = S.pre[t + 1];
+                    ent = S.rbase[t] - 4 * S.pre[t];
                     tb = S.tab + t;
                 }
                 uint32_t cc[4];
                 if (V == 0) {
+                    const uint32_t w4 = __ldg(reinterpret_cast<const uint32_t *>(l8 + ent + 4 * g));
 #pragma unroll
-                    for (int u = 0; u < 4; u++) cc[u] = gco[(w4.x >> (8 * u)) & 255u];
+                    for (int u = 0; u < 4; u++) cc[u] = gco[(w4 >> (8 * u)) & 255u];
                 } else {
+                    const uint2 w4 = __ldg(reinterpret_cast<const uint2 *>(l16 + ent + 4 * g));
                     cc[0] = w4.x & 0xFFFFu;
                     cc[1] = w4.x >> 16;
                     cc[2] = w4.y & 0xFFFFu;
@@ -757,7 +760,7 @@ __device__ __noinline__ void search_tasks(IqWarpSmem<V> &S, int T, const void *l
                     const uint32_t kh = __float_as_uint(d2[u]);
                     if (d2[u] < FLT_MAX && kh < bh) {  // positions rise within the lane: strict keeps the first
                         bh = kh;
-                        bl = (uint32_t)(4 * g + u);
+                        bl = ((uint32_t)(4 * g + u) << 16) | cc[u];  // (position, the candidate's levels)
                     }
                 }
             }
@@ -766,12 +769,7 @@ __device__ __noinline__ void search_tasks(IqWarpSmem<V> &S, int T, const void *l
         __syncwarp();
         if (q < T) {
             const unsigned long long kk = S.rkey[lane];
-            uint32_t win = 0xFFFFFFFFu;
-            if (kk != ~0ull) {
-                const int at = S.rbase[lane] + (int)(uint32_t)kk - 4 * S.pre[lane];
-                win = V == 0 ? (uint32_t)gco[__ldg(l8 + at)] : (uint32_t)__ldg(l16 + at);
-            }
-            S.key[q] = win;
+            S.key[q] = kk == ~0ull ? 0xFFFFFFFFu : (uint32_t)kk & 0xFFFFu;
         }
         __syncwarp();
     }
@@ -860,7 +858,8 @@ __global__ void __launch_bounds__(IqSearch<V>::WARPS * 32, IqSearch<V>::COOP ? 2
     constexpr int NW = IqSearch<V>::WARPS;
     constexpr bool COOP = IqSearch<V>::COOP;
     extern __shared__ __align__(16) uint8_t smem_raw[];
-    // shared memory: compact kmap | per-warp state | grid coords (IQ2_XXS)
+    // shared memory: compact kmap | per-warp state | grid coords (IQ2_XXS) |
+    // neighbour lists (IQ3; IQ2 reads its lists through L1/L2)
     int *kmap = reinterpret_cast<int *>(smem_raw);
     IqWarpSmem<V> *wsm_all = reinterpret_cast<IqWarpSmem<V> *>(smem_raw + ((C::KMAP * 4 + 15) & ~15));
     uint16_t *gco = reinterpret_cast<uint16_t *>(reinterpret_cast<uint8_t *>(wsm_all + NW));

@@ -31,11 +31,11 @@ struct IqTables {
     const int32_t *kmap[5];        // compact kmap: >=0 grid index, <0 -(offset+1) into neighbours
     const uint32_t *neighbours[5]; // [count, entry...]; entry = grid index | packed coords << 16
     const uint32_t *grid_coords[5];// per grid point: packed lattice coordinates (2 or 3 bits each)
-    // Device copy of the lists in the layout each encoder reads:
-    //   IQ2_XXS: 8-bit [count, grid index...], staged in shared memory
-    //   IQ2_XS : 16-bit [count, coords...] in global memory, each list's
-    //            entries starting on a 16-byte boundary (count in the slot before)
-    //   others : 16-bit [count, coords...], staged in shared memory
+    // Device copy of the lists in the layout the encoders scan: each list's
+    // entries (IQ2_XXS 8-bit grid indices, the others 16-bit packed
+    // coordinates) start on a four-entry boundary, padded to a multiple of
+    // four with copies of the last entry; dkmap's off-grid entries hold
+    // -(1 + first entry + (count << 19)).
     const int32_t *dkmap[5];  // kmap with offsets into `lists`
     const void *lists[5];
     int lists_bytes[5];
