@@ -69,12 +69,31 @@ FLOPS_PER_ELT = {"Q4_K": 745.4, "Q5_K": 745.4, "Q6_K": 151.0, "Q8_0": 5.1, "Q2_K
 # add-only or mul-only operations per clock per SM); fused multiply-adds would
 # reach 256 flops/clk/SM but are excluded by the parity contract.
 FP32_OPS_PER_CLK_PER_SM = 128
-# Llama-3-8B shape: weight budget 5.5 GiB = --budget (weights + KV + compute
-# at ctx 8192) with --reserve 0, as the reference's budget model computes it
-# (main.rs:294-337).
-MODEL = "llama3-8b"
-MODEL_BUDGET = "7309099008"
+# Model-level configurations: shape (layers, hidden, KV width, FFN, vocab),
+# weight budget, and whether the weights are held in host memory or
+# generated as the pipeline streams them (the 70B shape's 141 GB of BF16 is
+# never held).  --budget = weight budget + f16 KV at ctx 8192 + the
+# compute estimate, with --reserve 0 (main.rs:294-337).
 MODEL_CTX = 8192
+MODELS = {
+    "llama3-8b": {"layers": 32, "hidden": 4096, "kv": 1024, "ffn": 14336, "vocab": 128256, "budget_gib": 5.5,
+                  "streaming": False,
+                  "workload": "Llama-3-8B shape (32 layers, hidden 4096, GQA 32/8, FFN 14336, vocab 128256 untied), "
+                              "synthetic BF16 N(0, 0.02), log-normal imatrix; weight budget 5.5 GiB"},
+    "llama3-70b": {"layers": 80, "hidden": 8192, "kv": 1024, "ffn": 28672, "vocab": 128256, "budget_gib": 40.0,
+                   "streaming": True,
+                   "workload": "Llama-3-70B shape (80 layers, hidden 8192, GQA 64/8, FFN 28672, vocab 128256 untied), "
+                               "synthetic BF16 N(0, 0.015) generated as it streams, log-normal imatrix with 1% of "
+                               "columns x100; weight budget 40 GiB; encoded bytes copied to the host and discarded"},
+}
+
+
+def model_budget_arg(name):
+    """The --budget that leaves exactly the configuration's weight budget."""
+    m = MODELS[name]
+    kv = m["layers"] * MODEL_CTX * 8 * (128 + 128) * 2
+    compute = 512 * m["vocab"] * 4 + 512 * m["hidden"] * 4 * 8
+    return str(int(m["budget_gib"] * (1 << 30)) + kv + compute)
 
 
 def shard_rows(n, rank, world):
@@ -191,11 +210,12 @@ def cpu_baseline(tensors, types, budget_s=12.0):
             "per_type": {k: round(v, 5) for k, v in per_type.items()}, "sample": "; ".join(samples)}
 
 
-def model_shapes():
-    """(name, ne0, n_rows, candidates) of the Llama-3-8B shape's solvable
-    tensors, one entry per distinct shape with its count (main.rs:347-380
-    ladder: 11 candidates, 6 for token_embd/output)."""
-    L, E, KV, FF, V = 32, 4096, 1024, 14336, 128256
+def model_shapes(name="llama3-8b"):
+    """(name, ne0, n_rows, candidates, count) of a model configuration's
+    solvable tensors, one entry per distinct shape (main.rs:347-380 ladder:
+    11 candidates, 6 for token_embd/output)."""
+    m = MODELS[name]
+    L, E, KV, FF, V = m["layers"], m["hidden"], m["kv"], m["ffn"], m["vocab"]
     big = ["IQ2_XXS", "IQ2_XS", "IQ2_S", "IQ3_XXS", "IQ3_S", "IQ4_XS", "Q4_K", "Q5_K", "Q6_K", "Q8_0", "F16"]
     small = ["IQ4_XS", "Q4_K", "Q5_K", "Q6_K", "Q8_0", "F16"]
     return [("attn_q", E, E, big, L), ("attn_k", E, KV, big, L), ("attn_v", E, KV, big, L),
@@ -203,12 +223,12 @@ def model_shapes():
             ("ffn_down", FF, E, big, L), ("token_embd", E, V, small, 1), ("output", E, V, small, 1)]
 
 
-def cpu_model_baseline(mix_elements, budget_s=10.0):
-    """The reference's error table and encode for the Llama-3-8B shape on the
-    host cores, extrapolated from a sample: per tensor shape, the error of
-    `rows` rows (of the 128 the reference samples) for every candidate; per
-    type of the chosen mix, the encode of a 4096-wide slab.  Synthetic rows
-    with the configuration's distribution (N(0, 0.02) BF16, log-normal
+def cpu_model_baseline(mix_elements, name="llama3-8b"):
+    """The reference's error table and encode for a model configuration on
+    the host cores, extrapolated from a sample: per tensor shape, the error
+    of `rows` rows (of the 128 the reference samples) for every candidate;
+    per type of the chosen mix, the encode of a 4096-wide slab.  Synthetic
+    rows with the configuration's distribution (N(0, 0.02) BF16, log-normal
     imatrix)."""
     from oracle import oracle as O
     cores = os.cpu_count() or 1
@@ -217,17 +237,17 @@ def cpu_model_baseline(mix_elements, budget_s=10.0):
     sample = []
     measure_s = 0.0
     exact_s = 0.0
-    for name, ne0, n_rows, cands, count in model_shapes():
+    for tname, ne0, n_rows, cands, count in model_shapes(name):
         bits = workloads.to_bf16((rng.standard_normal((rows, ne0), dtype=np.float32) * np.float32(0.02)))
         im = np.exp(rng.normal(0.0, 1.0, size=ne0)).astype(np.float32)
         t0 = time.perf_counter()
         for c in cands:
-            O.row_errors_bf16(TYPE_IDS[c], bits, None if name == "token_embd" else im, n_threads=cores)
+            O.row_errors_bf16(TYPE_IDS[c], bits, None if tname == "token_embd" else im, n_threads=cores)
         dt = time.perf_counter() - t0
         sampled = min(128, n_rows)
         measure_s += dt * sampled / rows * count
         exact_s += dt * n_rows / rows * count
-        sample.append(f"{name}: {rows} rows x {len(cands)} candidates")
+        sample.append(f"{tname}: {rows} rows x {len(cands)} candidates")
     encode_s = 0.0
     bits = workloads.to_bf16(rng.standard_normal((rows * 4, 4096), dtype=np.float32) * np.float32(0.02))
     im = np.exp(rng.normal(0.0, 1.0, size=4096)).astype(np.float32)
@@ -434,22 +454,26 @@ def run_ours(args):
               "e2e": {"value": round(aggregate_gbs(iq_bytes, len(iq_types), iq_e2e), 3), "unit": "GB/s"},
               "gpu_launches": ri["launches"], "_rank": ri, "_tensors": iq_tensors, "_types": iq_types}
 
-    # ---- Llama-3-8B shape: error table + solve + encode ----
+    # ---- model configuration: error table + solve + encode ----
     model = None
     if "model" in sections:
         from shoehorn_b200 import host
         comm = host.Comm(rank, world)
-        recs = host.bench_model(MODEL, device=local_rank, modes=("sampled", "exact"), budget=MODEL_BUDGET,
-                                reserve="0", ctx=MODEL_CTX, comm=comm)
-        model = {"workload": "Llama-3-8B shape (32 layers, hidden 4096, GQA 32/8, FFN 14336, vocab 128256 untied), "
-                             "synthetic BF16 N(0, 0.02), log-normal imatrix; weight budget 5.5 GiB",
-                 "elements": recs[0]["elements"]}
+        mc = MODELS[args.model]
+        modes = tuple(args.model_modes.split(","))
+        recs = host.bench_model(args.model, device=local_rank, modes=modes, budget=model_budget_arg(args.model),
+                                reserve="0", ctx=MODEL_CTX, streaming=mc["streaming"],
+                                out_path="-" if mc["streaming"] else "", comm=comm)
+        model = {"model": args.model, "workload": mc["workload"], "elements": recs[0]["elements"],
+                 "weights_in_host_memory": not mc["streaming"]}
         for rec in recs:
             key = "exact" if rec["exact_errors"] else "sampled"
             m = {k: round(max_over_ranks(rec[k], dev), 4)
                  for k in ("measure_s", "gather_s", "solve_s", "setup_s", "encode_s", "wall_s")}
             m["plan_bytes"] = rec["plan_bytes"]
+            m["budget_bytes"] = rec["budget_bytes"]
             m["mix_elements"] = rec["mix_elements"]
+            m["peak_rss_gb_max_rank"] = round(max_over_ranks(rec["peak_rss_bytes"], dev) / 1e9, 2)
             model[key] = m
         model["generate_s"] = round(max_over_ranks(recs[0]["generate_s"], dev), 2)
 
@@ -479,7 +503,8 @@ def run_ours(args):
         if iq:
             iq["cpu_baseline"] = cpu_baseline(iq_tensors, iq_types, budget_s=args.ref_budget)
         if model:
-            model["cpu_baseline"] = cpu_model_baseline(model["sampled"]["mix_elements"])
+            first = model.get("sampled") or model.get("exact")
+            model["cpu_baseline"] = cpu_model_baseline(first["mix_elements"], args.model)
     line["cpu_baseline"] = cpu
     if iq:
         line["iq"] = iq
@@ -535,6 +560,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--sections", default="sweep,iq,model", help="comma-separated: sweep (always), iq, model")
     ap.add_argument("--types", default=",".join(SWEEP), help="comma-separated types of the sweep")
+    ap.add_argument("--model", default="llama3-8b", choices=sorted(MODELS), help="configuration of the model section")
+    ap.add_argument("--model-modes", default="sampled,exact",
+                    help="error tables of the model section: sampled (the reference's 128 rows), exact (every row)")
     ap.add_argument("--ref-budget", type=float, default=12.0, help="seconds of CPU work per reference sample")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
     args = ap.parse_args()

@@ -34,7 +34,8 @@ def lib():
                                                ctypes.c_int, ctypes.c_int, ALLGATHER_FN, ctypes.c_void_p,
                                                ctypes.c_void_p]
         L.shh_bench_model.restype = ctypes.c_int
-        L.shh_bench_model.argtypes = [ctypes.c_char_p, ctypes.c_uint64, ctypes.c_int, ctypes.c_char_p, ctypes.c_char_p,
+        L.shh_bench_model.argtypes = [ctypes.c_char_p, ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_char_p,
+                                      ctypes.c_char_p,
                                       ctypes.c_uint64, ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                       ctypes.c_int, ALLGATHER_FN, BARRIER_FN, ctypes.c_void_p, ctypes.c_char_p,
                                       ctypes.c_char_p, ctypes.c_int64]
@@ -121,14 +122,16 @@ def shard_exchange_check(n_rows, n_cands, sample_rows=128, comm=None):
 
 
 def bench_model(name, device=0, modes=("sampled",), budget=None, reserve="0", ctx=8192, uniform="",
-                workers_per_gpu=3, seed=20261201, out_path="", comm=None):
+                workers_per_gpu=3, seed=20261201, out_path="", streaming=False, comm=None):
     """Error table + solve + encode of a synthetic model on this rank's rows,
     once per mode ("sampled": the reference's 128-row error table, "exact":
-    every row).  Returns the timing records (list of dicts)."""
+    every row).  streaming: rows are generated as the pipeline asks for them
+    (no weight storage); out_path "-" discards the encoded bytes after their
+    copy to the host.  Returns the timing records (list of dicts)."""
     comm = comm or Comm()
     bits = (1 if "sampled" in modes else 0) | (2 if "exact" in modes else 0)
     buf = ctypes.create_string_buffer(1 << 16)
-    rc = lib().shh_bench_model(name.encode(), seed, bits, (budget or "").encode() or None,
+    rc = lib().shh_bench_model(name.encode(), seed, bits, int(streaming), (budget or "").encode() or None,
                                reserve.encode() if reserve is not None else None, ctx, uniform.encode(),
                                workers_per_gpu, device, comm.rank, comm.world, comm.allgather, comm.barrier, None,
                                out_path.encode(), buf, len(buf))

@@ -4,6 +4,7 @@
 #include <chrono>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <thread>
@@ -91,6 +92,21 @@ typedef int64_t (*shh_allgather_fn)(void *user, const uint8_t *mine, int64_t n_m
                                     int64_t *sizes);
 typedef int (*shh_barrier_fn)(void *user);
 
+// The process's peak resident set (VmHWM), 0 if unknown.
+static uint64_t peak_rss_bytes() {
+    FILE *f = fopen("/proc/self/status", "r");
+    if (!f) return 0;
+    char line[256];
+    uint64_t kb = 0;
+    while (fgets(line, sizeof line, f))
+        if (strncmp(line, "VmHWM:", 6) == 0) {
+            kb = strtoull(line + 6, nullptr, 10);
+            break;
+        }
+    fclose(f);
+    return kb * 1024;
+}
+
 static shh::Shard make_shard(int rank, int world, shh_allgather_fn ag, shh_barrier_fn bar, void *user) {
     shh::Shard s;
     s.rank = rank;
@@ -168,12 +184,16 @@ int shh_shard_exchange_check(int64_t n_tensors, const uint64_t *n_rows, const in
 // of `modes` (1: the reference's 128-row sampled error table, 2: every row,
 // --exact-errors), each a barrier then measure, exchange, solve and encode.
 // budget / reserve / uniform follow the CLI flags (uniform non-empty: a
-// fixed mix, no solve, one run).  out_path empty: output in host memory.
-// Writes a JSON array of timing records into json.  0 on success, -1 with
-// the message in json on failure.
-int shh_bench_model(const char *name, uint64_t seed, int modes, const char *budget, const char *reserve, uint64_t ctx,
-                    const char *uniform, int workers_per_gpu, int device, int rank, int world, shh_allgather_fn ag,
-                    shh_barrier_fn bar, void *user, const char *out_path, char *json, int64_t cap) {
+// fixed mix, no solve, one run).  streaming != 0: no weight storage, every
+// row is generated when the pipeline asks for it (host memory bounded by the
+// staging buffers).  out_path empty: output in host memory; "-": copied to
+// the host and discarded.  Writes a JSON array of timing records into json
+// (with the process's peak resident set so far).  0 on success, -1 with the
+// message in json on failure.
+int shh_bench_model(const char *name, uint64_t seed, int modes, int streaming, const char *budget, const char *reserve,
+                    uint64_t ctx, const char *uniform, int workers_per_gpu, int device, int rank, int world,
+                    shh_allgather_fn ag, shh_barrier_fn bar, void *user, const char *out_path, char *json,
+                    int64_t cap) {
     try {
         shh::FitArgs a;
         if (budget) a.budget = budget;
@@ -184,7 +204,8 @@ int shh_bench_model(const char *name, uint64_t seed, int modes, const char *budg
         const shh::Shard shard = make_shard(rank, world, ag, bar, user);
         const int threads = (int)std::max(1u, std::thread::hardware_concurrency() / (unsigned)std::max(world, 1));
         auto c0 = std::chrono::steady_clock::now();
-        auto sm = shh::synthetic_model(name, seed, threads, rank, world);
+        auto sm = streaming ? shh::synthetic_model_streaming(name, seed)
+                            : shh::synthetic_model(name, seed, threads, rank, world);
         const double gen_s = std::chrono::duration<double>(std::chrono::steady_clock::now() - c0).count();
         shh::GpuPool pool(1, a.timeout_ms, a.workers_per_gpu, device);
         uint64_t elems = 0, mine = 0;
@@ -211,14 +232,15 @@ int shh_bench_model(const char *name, uint64_t seed, int modes, const char *budg
             for (auto &kv : by_type) mix += (mix.empty() ? "" : ", ") + ("\"" + kv.first + "\": " + std::to_string(kv.second));
             char rec[4096];
             snprintf(rec, sizeof rec,
-                     "{\"model\": \"%s\", \"rank\": %d, \"world\": %d, \"exact_errors\": %s, \"elements\": %llu, "
-                     "\"rank_elements\": %llu, \"generate_s\": %.3f, \"measure_s\": %.4f, \"gather_s\": %.4f, "
-                     "\"solve_s\": %.4f, \"setup_s\": %.4f, \"encode_s\": %.4f, \"wall_s\": %.4f, "
-                     "\"plan_bytes\": %llu, \"budget_bytes\": %llu, \"mix_elements\": {%s}}",
-                     name, rank, world, a.exact_errors ? "true" : "false", (unsigned long long)elems,
-                     (unsigned long long)mine, gen_s, tm.measure_s, tm.gather_s, tm.solve_s, tm.setup_s, tm.encode_s,
-                     wall, (unsigned long long)plan.total_bytes, (unsigned long long)plan.budget.model_budget,
-                     mix.c_str());
+                     "{\"model\": \"%s\", \"rank\": %d, \"world\": %d, \"exact_errors\": %s, \"streaming\": %s, "
+                     "\"elements\": %llu, \"rank_elements\": %llu, \"generate_s\": %.3f, \"measure_s\": %.4f, "
+                     "\"gather_s\": %.4f, \"solve_s\": %.4f, \"setup_s\": %.4f, \"encode_s\": %.4f, "
+                     "\"wall_s\": %.4f, \"plan_bytes\": %llu, \"budget_bytes\": %llu, \"peak_rss_bytes\": %llu, "
+                     "\"mix_elements\": {%s}}",
+                     name, rank, world, a.exact_errors ? "true" : "false", streaming ? "true" : "false",
+                     (unsigned long long)elems, (unsigned long long)mine, gen_s, tm.measure_s, tm.gather_s, tm.solve_s,
+                     tm.setup_s, tm.encode_s, wall, (unsigned long long)plan.total_bytes,
+                     (unsigned long long)plan.budget.model_budget, (unsigned long long)peak_rss_bytes(), mix.c_str());
             out += (out.size() > 1 ? ", " : "") + std::string(rec);
             if (!a.uniform.empty()) break;
         }
@@ -228,6 +250,27 @@ int shh_bench_model(const char *name, uint64_t seed, int modes, const char *budg
         return 0;
     } catch (const std::exception &e) {
         snprintf(json, (size_t)cap, "%s", e.what());
+        return -1;
+    }
+}
+
+// Rows r0 .. r0 + n - 1 of tensor `tensor` of a synthetic model, as the
+// pipeline sees them: mode 0 from the whole model held in memory, 1 from
+// rank `rank` of `world` row-sharded copies (the rows must be that rank's),
+// 2 from the streaming source.  0 on success.
+int shh_synthetic_rows(const char *name, uint64_t seed, int64_t tensor, uint64_t r0, uint64_t n, int mode, int rank,
+                       int world, uint8_t *dst) {
+    try {
+        if (mode == 2) {
+            auto sm = shh::synthetic_model_streaming(name, seed);
+            sm->view.fill((size_t)tensor, r0, n, 1, dst);
+            return 0;
+        }
+        auto sm = mode == 1 ? shh::synthetic_model(name, seed, 2, rank, world) : shh::synthetic_model(name, seed, 2);
+        const auto &t = sm->view.tensors[(size_t)tensor];
+        std::memcpy(dst, sm->view.row((size_t)tensor, r0), (size_t)(n * shh::row_bytes(t.ty, t.ne0())));
+        return 0;
+    } catch (...) {
         return -1;
     }
 }

@@ -309,13 +309,23 @@ struct DevRows {
     const void *ptr;
     uint32_t src_type;
 };
-// first: host address of the first row; consecutive rows `step` rows apart.
-static DevRows rows_to_device(GpuPool::Worker &wk, const TensorInfo &t, const uint8_t *first, uint64_t n,
+// Rows r0, r0 + step, ... (n of them) of tensor ti: copied from the view's
+// resident bytes, or generated by its streaming source into the worker's
+// pinned staging buffer first.  The caller synchronises the worker's stream
+// before its next job, so the staging buffer is free again by then.
+static DevRows rows_to_device(GpuPool::Worker &wk, const ModelView &m, size_t ti, uint64_t r0, uint64_t n,
                               uint64_t step) {
+    const TensorInfo &t = m.tensors[ti];
     const uint64_t ne0 = t.ne0(), srb = row_bytes(t.ty, ne0);
     void *raw = wk.d(0, (size_t)(n * srb + 16));
-    cuda_check(cudaMemcpy2DAsync(raw, srb, first, srb * step, srb, n, cudaMemcpyHostToDevice, wk.st),
-               "row upload");
+    if (m.streaming()) {
+        uint8_t *stage = static_cast<uint8_t *>(wk.h(2, (size_t)(n * srb)));
+        m.fill(ti, r0, n, step, stage);
+        cuda_check(cudaMemcpyAsync(raw, stage, (size_t)(n * srb), cudaMemcpyHostToDevice, wk.st), "row upload");
+    } else {
+        cuda_check(cudaMemcpy2DAsync(raw, srb, m.row(ti, r0), srb * step, srb, n, cudaMemcpyHostToDevice, wk.st),
+                   "row upload");
+    }
     if (t.ty == T_F32 || t.ty == T_F16 || t.ty == T_BF16) return {raw, t.ty};
     void *f = wk.d(1, (size_t)(n * ne0 * 4 + 16));
     shc_check(shc_decode_rows(wk.ctx, t.ty, static_cast<const uint8_t *>(raw), (int64_t)n, (int64_t)ne0,
@@ -493,7 +503,7 @@ Plan build_plan(const FitArgs &args, const ModelView &m, const Imatrix &im, GpuP
         const auto &t = m.tensors[ti];
         const auto &types = to_solve[jb.k].second;
         const uint64_t ne0 = t.ne0(), step = meas[jb.k].step, ni = jb.i1 - jb.i0;
-        const DevRows src = rows_to_device(wk, t, m.row(ti, jb.i0 * step), ni, step);
+        const DevRows src = rows_to_device(wk, m, ti, jb.i0 * step, ni, step);
         const std::vector<float> *tim = lookup(im, t.name);
         const float *ims = row_slice(tim, ne0, rows_per_mat_of(t), jb.i0 * step);
         float *dim = nullptr;
@@ -644,7 +654,8 @@ void write_quantized(const std::string &out_path, const Plan &plan, const ModelV
     // next to the output, renamed when complete; every rank writes its rows
     // with positional writes from the workers' pinned buffers at their final
     // offsets, so no page of the output is faulted in through a mapping.
-    const bool to_file = !out_path.empty();
+    const bool discard = out_path == "-";
+    const bool to_file = !out_path.empty() && !discard;
     const std::string tmp = out_path + ".tmp";
     uint8_t *map = nullptr;
     uint64_t map_len = 0;
@@ -666,7 +677,7 @@ void write_quantized(const std::string &out_path, const Plan &plan, const ModelV
                 if (fd < 0) throw Error("opening " + tmp);
             }
         }
-    } else {
+    } else if (!discard) {
         map_len = lead ? L.data_start : 0;
         for (size_t ei = 0; ei < plan.entries.size(); ei++) {
             local_base[ei] = map_len;
@@ -701,6 +712,7 @@ void write_quantized(const std::string &out_path, const Plan &plan, const ModelV
     };
     // rows starting at row r0 of entry ei
     auto put_rows = [&](size_t ei, uint64_t r0, const void *p, size_t n) {
+        if (discard) return;
         if (to_file) pwrite_all(L.data_start + L.offsets[ei] + r0 * drb[ei], p, n);
         else std::memcpy(map + local_base[ei] + (r0 - lo[ei]) * drb[ei], p, n);
     };
@@ -751,6 +763,7 @@ void write_quantized(const std::string &out_path, const Plan &plan, const ModelV
             wk.d(2, need_im);
             wk.d(4, need_out);
             wk.h(1, need_out);
+            if (m.streaming()) wk.h(2, need_raw);
         });
     tm.setup_s = secs_since(s0);
     const auto t0 = Clock::now();
@@ -761,8 +774,15 @@ void write_quantized(const std::string &out_path, const Plan &plan, const ModelV
     }
     for (size_t ei = 0; ei < plan.entries.size(); ei++) {  // tensors copied untouched (main.rs:735-737)
         const auto &e = plan.entries[ei];
-        if (e.ty == m.tensors[e.tensor_idx].ty && hi[ei] > lo[ei])
-            put_rows(ei, lo[ei], m.row(e.tensor_idx, lo[ei]), (size_t)((hi[ei] - lo[ei]) * drb[ei]));
+        if (e.ty != m.tensors[e.tensor_idx].ty || hi[ei] <= lo[ei]) continue;
+        const size_t nb = (size_t)((hi[ei] - lo[ei]) * drb[ei]);
+        if (m.streaming()) {
+            std::vector<uint8_t> tmpb(nb);
+            m.fill(e.tensor_idx, lo[ei], hi[ei] - lo[ei], 1, tmpb.data());
+            put_rows(ei, lo[ei], tmpb.data(), nb);
+        } else {
+            put_rows(ei, lo[ei], m.row(e.tensor_idx, lo[ei]), nb);
+        }
     }
     pool.run(jobs.size(), [&](int w, size_t j) {
         auto &wk = pool.worker(w);
@@ -770,7 +790,7 @@ void write_quantized(const std::string &out_path, const Plan &plan, const ModelV
         const auto &e = plan.entries[jb.e];
         const auto &t = m.tensors[e.tensor_idx];
         const uint64_t ne0 = t.ne0(), n = jb.r1 - jb.r0, rb = drb[jb.e];
-        const DevRows src = rows_to_device(wk, t, m.row(e.tensor_idx, jb.r0), n, 1);
+        const DevRows src = rows_to_device(wk, m, e.tensor_idx, jb.r0, n, 1);
         const std::vector<float> *tim = lookup(im, t.name);
         const float *ims = row_slice(tim, ne0, rows_per_mat_of(t), jb.r0);
         float *dim = nullptr;
@@ -793,8 +813,8 @@ void write_quantized(const std::string &out_path, const Plan &plan, const ModelV
     if (to_file && lead && rename(tmp.c_str(), out_path.c_str()) != 0)
         throw Error("renaming " + tmp + " -> " + out_path);
     tm.encode_s = secs_since(t0);
-    fprintf(stderr, "wrote %s (%s)\n", to_file ? out_path.c_str() : "(memory)",
-            fmt_size(to_file ? L.total : map_len).c_str());
+    fprintf(stderr, "wrote %s (%s)\n", to_file ? out_path.c_str() : discard ? "(discarded)" : "(memory)",
+            fmt_size(to_file || discard ? L.total : map_len).c_str());
 }
 
 }  // namespace shh

@@ -79,8 +79,11 @@ struct Plan {
     uint64_t fixed_bytes = 0;
 };
 
-// Tensor storage seen by the pipeline: infos plus a host pointer to each
-// tensor's raw bytes (an mmap'd GGUF, or synthetic data in host memory).
+// Tensor storage seen by the pipeline: infos plus either a host pointer to
+// each tensor's raw bytes (an mmap'd GGUF, or synthetic data in host
+// memory), or a streaming source that writes requested rows into a caller's
+// buffer (synthetic models too large to hold: their rows are generated on
+// demand into the workers' pinned staging buffers).
 // A rank of a sharded run may hold only rows [row_lo[i], ...) of tensor i:
 // data(i) then points at row row_lo[i] (row_lo empty: whole tensors).
 struct ModelView {
@@ -88,9 +91,13 @@ struct ModelView {
     std::vector<TensorInfo> tensors;
     uint64_t alignment = 32;
     std::function<const uint8_t *(size_t)> data;
+    // streaming source: rows r0, r0 + step, ... (n of them) of tensor i,
+    // written back to back into dst
+    std::function<void(size_t i, uint64_t r0, uint64_t n, uint64_t step, uint8_t *dst)> fill;
     uint64_t total_bytes = 0;
     std::vector<uint64_t> row_lo;
-    // host address of row r of tensor i
+    bool streaming() const { return (bool)fill; }
+    // host address of row r of tensor i (resident tensors only)
     const uint8_t *row(size_t i, uint64_t r) const {
         const auto &t = tensors[i];
         const uint64_t lo = row_lo.empty() ? 0 : row_lo[i];
@@ -133,7 +140,8 @@ void print_plan(const Plan &plan, const ModelView &m);
 uint32_t file_type_code(const std::vector<PlanEntry> &entries);  // main.rs:628-659
 // main.rs:691-751 write_quantized (without the calibration reuse path):
 // writes out_path via a temporary file and a rename.  An empty out_path
-// encodes into host memory.  With an active shard every rank encodes the
+// encodes into host memory; "-" copies every encoded range to the host and
+// discards it (a sink for models whose output would not fit in memory).  With an active shard every rank encodes the
 // rows it owns and writes them at their final offsets of the same file
 // (rank 0 writes the header; the barrier orders creation and the rename).
 void write_quantized(const std::string &out_path, const Plan &plan, const ModelView &m, const Imatrix &im,
@@ -160,5 +168,8 @@ struct SyntheticModel {
 // the split.
 std::unique_ptr<SyntheticModel> synthetic_model(const std::string &name, uint64_t seed, int threads, int rank = 0,
                                                 int world = 1);
+// The same models with no weight storage: view.fill generates any rows on
+// demand (host memory stays bounded by the pipeline's staging buffers).
+std::unique_ptr<SyntheticModel> synthetic_model_streaming(const std::string &name, uint64_t seed);
 
 }  // namespace shh

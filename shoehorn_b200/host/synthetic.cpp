@@ -7,6 +7,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <thread>
+#include <vector>
 
 #include "pipeline.hpp"
 
@@ -33,15 +34,45 @@ inline uint64_t splitmix64(uint64_t x) {
     x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
     return x ^ (x >> 31);
 }
-// Two standard normals for counter p of stream `key` (Box-Muller).
+// Standard normal quantiles z_k = Phi^-1(p_k) at p_k = (k + 1/2) / kIcdfBins
+// for k = -1 .. kIcdfBins (the two outer points extrapolate the first and
+// last bins), found by bisection on Phi(z) = erfc(-z / sqrt 2) / 2.  A
+// uniform u in [0, 1) maps to z by linear interpolation between the two
+// quantiles around it: a table sampler of N(0, 1) to within ~1e-4 in z,
+// several times faster than Box-Muller, so synthetic models of 70 B
+// weights can be generated as they stream.
+constexpr int kIcdfBins = 4096;
+struct IcdfTable {
+    float z[kIcdfBins + 2];
+    IcdfTable() {
+        for (int k = -1; k <= kIcdfBins; k++) {
+            const double p = ((double)k + 0.5) / kIcdfBins;
+            double lo = -10.0, hi = 10.0;
+            for (int it = 0; it < 100; it++) {
+                const double mid = 0.5 * (lo + hi);
+                if (0.5 * std::erfc(-mid / std::sqrt(2.0)) < p) lo = mid;
+                else hi = mid;
+            }
+            z[k + 1] = (float)(0.5 * (lo + hi));
+        }
+    }
+};
+const IcdfTable &icdf() {
+    static const IcdfTable t;
+    return t;
+}
+inline float normal_of(const IcdfTable &t, uint32_t u24) {  // u24: 24 uniform bits
+    const float f = (float)u24 * ((float)kIcdfBins / 16777216.0f) + 0.5f;  // in [0.5, kIcdfBins + 0.5)
+    const int k = (int)f;                                                   // f >= 0: truncation is floor
+    const float a = t.z[k], b = t.z[k + 1];
+    return a + (f - (float)k) * (b - a);
+}
+// Two standard normals for counter p of stream `key`.
 inline void normal2(uint64_t key, uint64_t p, float &z0, float &z1) {
+    const IcdfTable &t = icdf();
     const uint64_t r = splitmix64(key ^ (p * 0xD1B54A32D192ED03ull));
-    const float u1 = ((float)(uint32_t)(r >> 40) + 1.0f) * (1.0f / 16777217.0f);  // (0, 1]
-    const float u2 = (float)(uint32_t)(r & 0xFFFFFFu) * (1.0f / 16777216.0f);
-    const float rad = std::sqrt(-2.0f * std::log(u1));
-    const float th = 6.2831853f * u2;
-    z0 = rad * std::cos(th);
-    z1 = rad * std::sin(th);
+    z0 = normal_of(t, (uint32_t)(r >> 40));
+    z1 = normal_of(t, (uint32_t)(r & 0xFFFFFFu));
 }
 inline uint16_t to_bf16(float f) {
     uint32_t u;
@@ -55,24 +86,35 @@ struct Spec {
     uint32_t ty;
 };
 
+// The weights of a spec tensor: N(0, stdv) BF16 from stream seed + index.
+struct ModelSpec {
+    std::vector<KV> kvs;
+    std::vector<Spec> specs;
+    float stdv = 0.02f;
+    bool boost = false;  // 1% of imatrix columns x100
+};
+
 // Elements [e0, e0 + n) of a tensor whose element pair p is normal2(key, p):
 // any range of rows can be generated alone and equals the same rows of the
 // whole tensor (e0 even).
 void fill_normal_bf16(uint8_t *dst, uint64_t e0, uint64_t n, uint64_t key, float stdv, int threads) {
     uint16_t *o = reinterpret_cast<uint16_t *>(dst);
     const uint64_t p0 = e0 / 2, pairs = (n + 1) / 2;
-    std::vector<std::thread> th;
-    for (int t = 0; t < threads; t++) {
-        th.emplace_back([=]() {
-            const uint64_t a = pairs * (uint64_t)t / (uint64_t)threads, b = pairs * (uint64_t)(t + 1) / (uint64_t)threads;
-            for (uint64_t p = a; p < b; p++) {
-                float z0, z1;
-                normal2(key, p0 + p, z0, z1);
-                o[2 * p] = to_bf16(z0 * stdv);
-                if (2 * p + 1 < n) o[2 * p + 1] = to_bf16(z1 * stdv);
-            }
-        });
+    auto part = [=](int t, int nt) {
+        const uint64_t a = pairs * (uint64_t)t / (uint64_t)nt, b = pairs * (uint64_t)(t + 1) / (uint64_t)nt;
+        for (uint64_t p = a; p < b; p++) {
+            float z0, z1;
+            normal2(key, p0 + p, z0, z1);
+            o[2 * p] = to_bf16(z0 * stdv);
+            if (2 * p + 1 < n) o[2 * p + 1] = to_bf16(z1 * stdv);
+        }
+    };
+    if (threads <= 1) {
+        part(0, 1);
+        return;
     }
+    std::vector<std::thread> th;
+    for (int t = 0; t < threads; t++) th.emplace_back(part, t, threads);
     for (auto &x : th) x.join();
 }
 }  // namespace
@@ -122,19 +164,12 @@ static std::unique_ptr<SyntheticModel> e2e_model() {
     return sm;
 }
 
-std::unique_ptr<SyntheticModel> synthetic_model(const std::string &name, uint64_t seed, int threads, int rank,
-                                                int world) {
-    if (name == "e2e") {
-        if (world > 1) throw Error("the e2e fixture is not generated in shards");
-        return e2e_model();
-    }
-    auto sm = std::make_unique<SyntheticModel>();
-    std::vector<Spec> specs;
+static ModelSpec model_spec(const std::string &name) {
+    ModelSpec ms;
+    auto &specs = ms.specs;
     std::string arch;
     uint64_t n_layer, n_embd, n_head, n_kv, head_dim, n_ff, n_vocab, ctx_len;
     bool tied, qk_norm;
-    float stdv = 0.02f;
-    bool boost = false;
     if (name == "qwen3-0.6b") {
         arch = "qwen3"; n_layer = 28; n_embd = 1024; n_head = 16; n_kv = 8; head_dim = 128; n_ff = 3072;
         n_vocab = 151936; ctx_len = 40960; tied = true; qk_norm = true;
@@ -143,7 +178,7 @@ std::unique_ptr<SyntheticModel> synthetic_model(const std::string &name, uint64_
         n_vocab = 128256; ctx_len = 8192; tied = false; qk_norm = false;
     } else if (name == "llama3-70b") {
         arch = "llama"; n_layer = 80; n_embd = 8192; n_head = 64; n_kv = 8; head_dim = 128; n_ff = 28672;
-        n_vocab = 128256; ctx_len = 8192; tied = false; qk_norm = false; stdv = 0.015f; boost = true;
+        n_vocab = 128256; ctx_len = 8192; tied = false; qk_norm = false; ms.stdv = 0.015f; ms.boost = true;
     } else if (name == "tiny") {  // e2e_tests.rs:28-67 shapes
         arch = "llama"; n_layer = 2; n_embd = 256; n_head = 4; n_kv = 2; head_dim = 64; n_ff = 64;
         n_vocab = 256; ctx_len = 2048; tied = false; qk_norm = false;
@@ -171,25 +206,56 @@ std::unique_ptr<SyntheticModel> synthetic_model(const std::string &name, uint64_
     specs.push_back({"output_norm.weight", {n_embd}, T_F32});
     if (!tied) specs.push_back({"output.weight", {n_embd, n_vocab}, T_BF16});
 
+    auto &kv = ms.kvs;
+    kv.emplace_back("general.architecture", Value::Str(arch));
+    kv.emplace_back("general.name", Value::Str("synthetic " + name));
+    kv.emplace_back(arch + ".block_count", Value::U32((uint32_t)n_layer));
+    kv.emplace_back(arch + ".context_length", Value::U32((uint32_t)ctx_len));
+    kv.emplace_back(arch + ".embedding_length", Value::U32((uint32_t)n_embd));
+    kv.emplace_back(arch + ".feed_forward_length", Value::U32((uint32_t)n_ff));
+    kv.emplace_back(arch + ".attention.head_count", Value::U32((uint32_t)n_head));
+    kv.emplace_back(arch + ".attention.head_count_kv", Value::U32((uint32_t)n_kv));
+    kv.emplace_back(arch + ".attention.key_length", Value::U32((uint32_t)head_dim));
+    kv.emplace_back(arch + ".attention.value_length", Value::U32((uint32_t)head_dim));
+    kv.emplace_back(arch + ".vocab_size", Value::U32((uint32_t)n_vocab));
+    kv.emplace_back("general.file_type", Value::U32(32));  // MOSTLY_BF16
+    return ms;
+}
+
+// Per-column importance exp(N(0,1)) of a 2-D tensor (1% of columns x100
+// with boost); token_embd gets none (real imatrices never cover it).
+static void add_imatrix(SyntheticModel &sm, const TensorInfo &t, size_t i, uint64_t seed, bool boost) {
+    if (t.ty == T_F32 || t.name == "token_embd.weight" || t.dims.size() != 2) return;
+    std::vector<float> im((size_t)t.ne0());
+    const uint64_t key = splitmix64(seed ^ 0x1A7B1C00ull ^ i);
+    for (uint64_t c = 0; c < t.ne0(); c += 2) {
+        float z0, z1;
+        normal2(key, c / 2, z0, z1);
+        im[(size_t)c] = std::exp(z0);
+        if (c + 1 < t.ne0()) im[(size_t)c + 1] = std::exp(z1);
+    }
+    if (boost)
+        for (uint64_t c = 0; c < t.ne0(); c++)
+            if (splitmix64(key + 7919 * c) % 100 == 0) im[(size_t)c] *= 100.0f;
+    sm.imatrix[t.name.substr(0, t.name.size() - 7)] = std::move(im);  // imatrix entries drop ".weight"
+}
+
+std::unique_ptr<SyntheticModel> synthetic_model(const std::string &name, uint64_t seed, int threads, int rank,
+                                                int world) {
+    if (name == "e2e") {
+        if (world > 1) throw Error("the e2e fixture is not generated in shards");
+        return e2e_model();
+    }
+    const ModelSpec ms = model_spec(name);
+    auto sm = std::make_unique<SyntheticModel>();
     auto &v = sm->view;
-    v.kvs.emplace_back("general.architecture", Value::Str(arch));
-    v.kvs.emplace_back("general.name", Value::Str("synthetic " + name));
-    v.kvs.emplace_back(arch + ".block_count", Value::U32((uint32_t)n_layer));
-    v.kvs.emplace_back(arch + ".context_length", Value::U32((uint32_t)ctx_len));
-    v.kvs.emplace_back(arch + ".embedding_length", Value::U32((uint32_t)n_embd));
-    v.kvs.emplace_back(arch + ".feed_forward_length", Value::U32((uint32_t)n_ff));
-    v.kvs.emplace_back(arch + ".attention.head_count", Value::U32((uint32_t)n_head));
-    v.kvs.emplace_back(arch + ".attention.head_count_kv", Value::U32((uint32_t)n_kv));
-    v.kvs.emplace_back(arch + ".attention.key_length", Value::U32((uint32_t)head_dim));
-    v.kvs.emplace_back(arch + ".attention.value_length", Value::U32((uint32_t)head_dim));
-    v.kvs.emplace_back(arch + ".vocab_size", Value::U32((uint32_t)n_vocab));
-    v.kvs.emplace_back("general.file_type", Value::U32(32));  // MOSTLY_BF16
+    v.kvs = ms.kvs;
     v.alignment = 32;
-    for (size_t i = 0; i < specs.size(); i++) {
+    for (size_t i = 0; i < ms.specs.size(); i++) {
         TensorInfo t;
-        t.name = specs[i].name;
-        t.dims = specs[i].dims;
-        t.ty = specs[i].ty;
+        t.name = ms.specs[i].name;
+        t.dims = ms.specs[i].dims;
+        t.ty = ms.specs[i].ty;
         uint64_t lo, hi;  // the rows this rank holds
         shard_rows(t.n_rows(), rank, world, lo, hi);
         v.row_lo.push_back(lo);
@@ -199,30 +265,57 @@ std::unique_ptr<SyntheticModel> synthetic_model(const std::string &name, uint64_
             float *f = reinterpret_cast<float *>(buf->ptr);
             for (uint64_t e = 0; e < (hi - lo) * t.ne0(); e++) f[e] = 1.0f;
         } else {
-            fill_normal_bf16(buf->ptr, lo * t.ne0(), (hi - lo) * t.ne0(), seed + i, stdv, threads);
-            if (t.name != "token_embd.weight" && t.dims.size() == 2) {
-                // per-column importance exp(N(0,1)) (1% of columns x100 for the 70B config)
-                std::vector<float> im((size_t)t.ne0());
-                const uint64_t key = splitmix64(seed ^ 0x1A7B1C00ull ^ i);
-                for (uint64_t c = 0; c < t.ne0(); c += 2) {
-                    float z0, z1;
-                    normal2(key, c / 2, z0, z1);
-                    im[(size_t)c] = std::exp(z0);
-                    if (c + 1 < t.ne0()) im[(size_t)c + 1] = std::exp(z1);
-                }
-                if (boost)
-                    for (uint64_t c = 0; c < t.ne0(); c++)
-                        if (splitmix64(key + 7919 * c) % 100 == 0) im[(size_t)c] *= 100.0f;
-                std::string base = t.name.substr(0, t.name.size() - 7);  // imatrix entries drop ".weight"
-                sm->imatrix[base] = std::move(im);
-            }
+            fill_normal_bf16(buf->ptr, lo * t.ne0(), (hi - lo) * t.ne0(), seed + i, ms.stdv, threads);
         }
+        add_imatrix(*sm, t, i, seed, ms.boost);
         v.tensors.push_back(t);
         v.total_bytes += t.byte_size();
         sm->storage.push_back(std::move(buf));
     }
     SyntheticModel *raw = sm.get();
     v.data = [raw](size_t i) { return (const uint8_t *)raw->storage[i]->ptr; };
+    return sm;
+}
+
+std::unique_ptr<SyntheticModel> synthetic_model_streaming(const std::string &name, uint64_t seed) {
+    if (name == "e2e") throw Error("the e2e fixture is not streamed");
+    const ModelSpec ms = model_spec(name);
+    auto sm = std::make_unique<SyntheticModel>();
+    auto &v = sm->view;
+    v.kvs = ms.kvs;
+    v.alignment = 32;
+    for (size_t i = 0; i < ms.specs.size(); i++) {
+        TensorInfo t;
+        t.name = ms.specs[i].name;
+        t.dims = ms.specs[i].dims;
+        t.ty = ms.specs[i].ty;
+        add_imatrix(*sm, t, i, seed, ms.boost);
+        v.tensors.push_back(t);
+        v.total_bytes += t.byte_size();
+    }
+    const float stdv = ms.stdv;
+    SyntheticModel *raw = sm.get();
+    v.fill = [raw, seed, stdv](size_t i, uint64_t r0, uint64_t n, uint64_t step, uint8_t *dst) {
+        const TensorInfo &t = raw->view.tensors[i];
+        const uint64_t ne0 = t.ne0(), rb = row_bytes(t.ty, ne0);
+        if (t.ty == T_F32) {
+            for (uint64_t k = 0; k < n; k++) {
+                float *f = reinterpret_cast<float *>(dst + k * rb);
+                for (uint64_t e = 0; e < ne0; e++) f[e] = 1.0f;
+            }
+            return;
+        }
+        // large requests are split over a few threads (the pipeline's
+        // workers already run one request each)
+        const int nt = n * ne0 >= (4u << 20) ? 4 : 1;
+        std::vector<std::thread> th;
+        for (int tt = 0; tt < nt; tt++)
+            th.emplace_back([=]() {
+                for (uint64_t k = n * (uint64_t)tt / (uint64_t)nt; k < n * (uint64_t)(tt + 1) / (uint64_t)nt; k++)
+                    fill_normal_bf16(dst + k * rb, (r0 + k * step) * ne0, ne0, seed + i, stdv, 1);
+            });
+        for (auto &x : th) x.join();
+    };
     return sm;
 }
 

@@ -172,3 +172,21 @@ def test_two_gpu_sharding_gives_identical_output(tmp_path):
             "--exact-errors", "--gpus", str(g))
         outs.append(open(out, "rb").read())
     assert outs[0] == outs[1]
+
+
+def test_streamed_model_writes_the_same_file(tmp_path):
+    """A model whose rows are generated as the pipeline asks for them (how
+    the 70B shape runs without holding its weights) plans and writes the
+    same GGUF, byte for byte, as the same model held in memory."""
+    from shoehorn_b200 import host
+    budget = str(64 * 1024 + 576 * 1024 + 400 * 1024)  # KV + compute at ctx 64, then 400 KiB of weights
+    files = []
+    for streaming in (False, True):
+        out = str(tmp_path / f"tiny-{int(streaming)}.gguf")
+        recs = host.bench_model("tiny", modes=("sampled", "exact"), budget=budget, reserve="0", ctx=64,
+                                out_path=out, streaming=streaming)
+        assert [r["streaming"] for r in recs] == [streaming, streaming]
+        files.append(open(out, "rb").read())
+    assert files[0] == files[1]
+    fit = gguf.GGUFReader(str(tmp_path / "tiny-1.gguf"))
+    assert any(t.tensor_type.name not in ("F16", "F32") for t in fit.tensors)

@@ -67,3 +67,27 @@ def test_every_sampled_row_is_owned_by_exactly_one_rank():
     once: without the exchange a rank's sums cover only its own rows."""
     ones = host.shard_exchange_check(N_ROWS, N_CANDS)
     assert np.all(ones[np.arange(len(N_ROWS)), 0] > 0)
+
+
+def _rows(name, tensor, r0, n, mode, rank=0, world=1, ne0=256):
+    import ctypes
+    L = host.lib()
+    L.shh_synthetic_rows.argtypes = [ctypes.c_char_p, ctypes.c_uint64, ctypes.c_int64, ctypes.c_uint64, ctypes.c_uint64,
+                                     ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+    out = np.zeros(n * ne0, dtype=np.uint16)
+    assert L.shh_synthetic_rows(name.encode(), 20261201, tensor, r0, n, mode, rank, world, out.ctypes.data) == 0
+    return out
+
+
+def test_streamed_and_sharded_synthetic_rows_equal_the_whole_model():
+    """The synthetic weights are a function of (tensor, element), so a rank's
+    shard and the streaming source (rows generated on demand, the 70B
+    shape's way) give the same bytes as the model held whole."""
+    # tiny: tensor 1 is token_embd-adjacent attn_q [256 x 256]; tensor 0 token_embd [256 x 256]
+    for tensor in (0, 2):
+        whole = _rows("tiny", tensor, 0, 256, 0)
+        assert np.array_equal(_rows("tiny", tensor, 0, 256, 2), whole)
+        assert np.array_equal(_rows("tiny", tensor, 128, 128, 1, rank=1, world=2), whole[128 * 256:])
+        assert np.array_equal(_rows("tiny", tensor, 37, 5, 2), whole[37 * 256:42 * 256])
+    x = (whole.astype(np.uint32) << 16).view(np.float32)
+    assert abs(float(x.std()) - 0.02) < 0.002 and abs(float(x.mean())) < 0.002
