@@ -45,3 +45,37 @@ def iq_tensors(seed=SEED):
         im = np.exp(rng.normal(0.0, 1.0, size=ne0)).astype(np.float32)
         out.append((f"{rows}x{ne0}", to_bf16(w), im))
     return out
+
+
+def main(argv=None):
+    """Encode a sample of a benchmark workload on cuda:0 a few times (a small,
+    repeatable launch for profilers):
+
+      python -m shoehorn_b200.workloads --type 14 --rows 512 [--dist iq] [--repeat 2]
+    """
+    import argparse
+    ap = argparse.ArgumentParser(prog="python -m shoehorn_b200.workloads")
+    ap.add_argument("--type", type=int, required=True, help="ggml type id")
+    ap.add_argument("--rows", type=int, default=512)
+    ap.add_argument("--dist", choices=["sweep", "iq"], default="sweep",
+                    help="sweep: N(0, 0.02) + outliers, 14336 wide; iq: Student-t, 4096 wide")
+    ap.add_argument("--repeat", type=int, default=2)
+    args = ap.parse_args(argv)
+    import torch
+    import shoehorn_b200 as sh
+    if args.dist == "sweep":
+        bits, im = sweep_tensor(n_rows=args.rows)
+    else:
+        rng = np.random.default_rng(5)
+        w = (rng.standard_t(5.0, size=(args.rows, 4096)) * (0.02 / np.sqrt(5.0 / 3.0))).astype(np.float32)
+        bits, im = to_bf16(w), np.exp(rng.normal(0.0, 1.0, size=4096)).astype(np.float32)
+    with sh.Context(0) as ctx:
+        src = torch.from_numpy(bits.view(np.int16)).cuda()
+        imt = torch.from_numpy(im).cuda()
+        for _ in range(args.repeat):
+            ctx.encode_rows(args.type, src, imt, sync=True)
+    print(f"encoded {args.rows} x {bits.shape[1]} to type {args.type} x{args.repeat}")
+
+
+if __name__ == "__main__":
+    main()
