@@ -25,18 +25,26 @@ namespace shc {
 // Row sigma^2 (quant.rs:153-155): sequential f32 fold of x^2 over the whole
 // row, then / ne0.  The fold is order-dependent, so one thread owns one row
 // and its adds form one dependent chain (4 cycles each: 29 us for a 14336
-// row).  A block owns 32 rows and has two warps: the loader streams tiles of
-// 32 rows x 128 bytes into a kSigStages-deep shared-memory ring with
-// cp.async (16-byte chunks, 4 rows x 128 B per instruction, coalesced); the
-// folder (lane r = row r) only reads its row from the ring, unpacks, squares
-// (packed) and adds, so its instruction stream stays inside the chain's
-// latency.  The two warps hand stages over through named barriers: FULL(s)
-// after the loader's copies into stage s landed, EMPTY(s) after the folder
-// read it; both warps walk the same tiles, so every barrier is met.  Chunk
-// (row r, j) sits in slot j*32 + r so that lane r reads its row 16 bytes at
-// a time without bank conflicts.
+// row, measured 4.1 cycles per dependent add).  A block owns 32 rows and has
+// kSigLoaders + 1 warps: the loaders stream tiles of 32 rows x 512 bytes into
+// a kSigStages-deep shared-memory ring with cp.async (16-byte chunks, one
+// row's 512 B per instruction, coalesced; each loader copies 8 of the tile's
+// 32 rows, so four warps keep four times the copies in flight that one
+// would); the folder (lane r = row r) only reads its row from the ring,
+// unpacks, squares (packed) and adds, so its instruction stream stays inside
+// the chain's latency.  The warps hand stages over through named barriers
+// counting all of them: FULL(s) after the loaders' copies into stage s
+// landed, EMPTY(s) after the folder read it; every warp walks the same
+// tiles, so every barrier is met.  Chunk (row r, j) sits in slot j*32 + r so
+// that lane r reads its row 16 bytes at a time without bank conflicts.
+// Measured on the 4096 x 14336 sweep tensor: 86 us with one loader and
+// 128-byte tiles, 78 us with four loaders, against the 30 us chain.
 // ---------------------------------------------------------------------------
 constexpr int kSigStages = 6;
+constexpr int kSigLoaders = 4;
+constexpr int kSigThreads = 32 * (kSigLoaders + 1);
+constexpr int kSigChunks = 32;  // 16-byte chunks of each row per tile
+constexpr size_t kSigSmem = (size_t)kSigStages * kSigChunks * 32 * 16;  // 96 KB
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
     const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
@@ -45,9 +53,13 @@ __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
-// Named barrier `id` over the block's two warps (64 threads).
-__device__ __forceinline__ void bar_sync64(int id) { asm volatile("bar.sync %0, 64;\n" ::"r"(id) : "memory"); }
-__device__ __forceinline__ void bar_arrive64(int id) { asm volatile("bar.arrive %0, 64;\n" ::"r"(id) : "memory"); }
+// Named barrier `id` over all the block's warps.
+__device__ __forceinline__ void bar_sync_all(int id) {
+    asm volatile("bar.sync %0, %1;\n" ::"r"(id), "n"(kSigThreads) : "memory");
+}
+__device__ __forceinline__ void bar_arrive_all(int id) {
+    asm volatile("bar.arrive %0, %1;\n" ::"r"(id), "n"(kSigThreads) : "memory");
+}
 __device__ __forceinline__ int sig_full(int s) { return 1 + s; }
 __device__ __forceinline__ int sig_empty(int s) { return 1 + kSigStages + s; }
 
@@ -79,40 +91,43 @@ __device__ __forceinline__ void sigma_fold(const uint4 q, float &s) {
 }
 
 template <int SRC>
-__global__ void __launch_bounds__(64) row_sigma2_kernel(RowSrc src, int64_t n_rows, float *out) {
-    __shared__ __align__(16) uint4 ring[kSigStages][256];
+__global__ void __launch_bounds__(kSigThreads) row_sigma2_kernel(RowSrc src, int64_t n_rows, float *out) {
+    extern __shared__ __align__(16) uint4 sig_ring[];  // [kSigStages][kSigChunks * 32]
+    auto ring = [&](int64_t t) { return sig_ring + (t % kSigStages) * (kSigChunks * 32); };
     const int lane = threadIdx.x & 31;
-    const bool loader = threadIdx.x < 32;
+    const int lw = threadIdx.x >> 5;  // loaders 0 .. kSigLoaders-1, then the folder
+    const bool loader = lw < kSigLoaders;
     const int64_t rbase = (int64_t)blockIdx.x * 32;
     const int64_t ne0 = src.ne0;
     constexpr int esz = SRC == SHC_SRC_F32 ? 4 : 2;
     constexpr int per_chunk = 16 / esz;            // elements per 16-byte chunk
-    constexpr int64_t tile_cols = 8 * per_chunk;   // 128 bytes of every row per tile
+    constexpr int64_t tile_cols = kSigChunks * per_chunk;  // 512 bytes of every row per tile
     const int64_t ntiles = (ne0 + tile_cols - 1) / tile_cols;
     const int64_t full_tiles = ne0 / tile_cols;
     if (loader) {
         const char *base = static_cast<const char *>(src.ptr);
         const int64_t row_bytes = src.row_stride * esz;
-        // this lane's chunks of a tile: rows i*4 + lane/8, 16-byte column lane%8
-        const int j = lane & 7;
+        // this lane's chunks of a tile: 16-byte column `lane` of rows 8*lw .. 8*lw + 7
+        const int j = lane;
         auto issue = [&](int64_t t) {
-            uint4 *slot = ring[t % kSigStages];
+            uint4 *slot = ring(t);
             const int64_t col = t * tile_cols + (int64_t)j * per_chunk;
+            if (col < ne0) {
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const int r = i * 4 + (lane >> 3);
-                if (rbase + r < n_rows && col < ne0)
-                    cp_async16(&slot[j * 32 + r], base + (rbase + r) * row_bytes + col * esz);
+                for (int i = 0; i < 8; i++) {
+                    const int r = lw * 8 + i;
+                    if (rbase + r < n_rows) cp_async16(&slot[j * 32 + r], base + (rbase + r) * row_bytes + col * esz);
+                }
             }
             cp_async_commit();
         };
         for (int64_t t = 0; t < ntiles; t++) {
-            if (t >= kSigStages) bar_sync64(sig_empty((int)(t % kSigStages)));  // the folder released the stage
+            if (t >= kSigStages) bar_sync_all(sig_empty((int)(t % kSigStages)));  // the folder released the stage
             issue(t);
             if (t >= kSigStages - 1) {
                 cp_async_wait<kSigStages - 1>();  // tile t - (kSigStages - 1) landed
                 __syncwarp();
-                bar_arrive64(sig_full((int)((t - (kSigStages - 1)) % kSigStages)));
+                bar_arrive_all(sig_full((int)((t - (kSigStages - 1)) % kSigStages)));
             }
         }
         // hand over the tiles still in flight, oldest first
@@ -120,26 +135,34 @@ __global__ void __launch_bounds__(64) row_sigma2_kernel(RowSrc src, int64_t n_ro
         for (int64_t t = first; t < ntiles; t++) {
             cp_async_wait<0>();
             __syncwarp();
-            bar_arrive64(sig_full((int)(t % kSigStages)));
+            bar_arrive_all(sig_full((int)(t % kSigStages)));
         }
     } else {
         float s = 0.0f;
         const bool mine = rbase + lane < n_rows;
         for (int64_t t = 0; t < ntiles; t++) {
             const int st = (int)(t % kSigStages);
-            bar_sync64(sig_full(st));
-            const uint4 *slot = ring[st];
+            bar_sync_all(sig_full(st));
+            const uint4 *slot = ring(t);
             if (mine) {
                 if (t < full_tiles) {
+                    // eight chunks at a time, loaded before their adds, so no
+                    // load latency sits on the add chain
+#pragma unroll 1
+                    for (int j0 = 0; j0 < kSigChunks; j0 += 8) {
+                        uint4 q[8];
 #pragma unroll
-                    for (int jj = 0; jj < 8; jj++) sigma_fold<SRC>(slot[jj * 32 + lane], s);
+                        for (int jj = 0; jj < 8; jj++) q[jj] = slot[(j0 + jj) * 32 + lane];
+#pragma unroll
+                        for (int jj = 0; jj < 8; jj++) sigma_fold<SRC>(q[jj], s);
+                    }
                 } else {  // the row's ragged end: whole chunks only (ne0 is a multiple of 8)
                     const int nchunks = (int)((ne0 - t * tile_cols + per_chunk - 1) / per_chunk);
                     for (int jj = 0; jj < nchunks; jj++) sigma_fold<SRC>(slot[jj * 32 + lane], s);
                 }
             }
             // the loader waits on this stage only once it has kSigStages tiles ahead
-            if (t + kSigStages < ntiles) bar_arrive64(sig_empty(st));
+            if (t + kSigStages < ntiles) bar_arrive_all(sig_empty(st));
         }
         if (mine) out[rbase + lane] = s / (float)ne0;
     }
@@ -148,9 +171,13 @@ __global__ void __launch_bounds__(64) row_sigma2_kernel(RowSrc src, int64_t n_ro
 cudaError_t launch_row_sigma2(const RowSrc &src, int64_t n_rows, float *out, cudaStream_t st) {
     if (n_rows <= 0) return cudaSuccess;
     const int64_t blocks = (n_rows + 31) / 32;
-    if (src.src_type == SHC_SRC_BF16) row_sigma2_kernel<SHC_SRC_BF16><<<(unsigned)blocks, 64, 0, st>>>(src, n_rows, out);
-    else if (src.src_type == SHC_SRC_F16) row_sigma2_kernel<SHC_SRC_F16><<<(unsigned)blocks, 64, 0, st>>>(src, n_rows, out);
-    else row_sigma2_kernel<SHC_SRC_F32><<<(unsigned)blocks, 64, 0, st>>>(src, n_rows, out);
+    auto fn = src.src_type == SHC_SRC_BF16 ? row_sigma2_kernel<SHC_SRC_BF16>
+              : src.src_type == SHC_SRC_F16 ? row_sigma2_kernel<SHC_SRC_F16>
+                                            : row_sigma2_kernel<SHC_SRC_F32>;
+    int per_sm = 1;
+    cudaError_t e = resident_blocks((const void *)fn, kSigThreads, kSigSmem, &per_sm);  // raises the smem limit
+    if (e != cudaSuccess) return e;
+    fn<<<(unsigned)blocks, kSigThreads, kSigSmem, st>>>(src, n_rows, out);
     return cudaGetLastError();
 }
 
