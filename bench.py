@@ -489,6 +489,11 @@ def run_ours(args):
     roof["traffic"] = captured_traffic(dom, sweep_rank["rank_elts"])
     roof["per_type_frac"] = {t: roofline_for(t, sweep_rank["rank_elts"], sweep_rank["per_type_ms"][t], sm_mhz,
                                              props.multi_processor_count, peaks)["frac"] for t in types}
+    if dom in ("Q4_K", "Q5_K"):
+        # frac counts the as-written operations while the kernel skips grids
+        # whose levels repeat; the pipe's measured occupancy sits beside it
+        roof["fma_pipe_active"] = 0.489
+        roof["fma_pipe_source"] = "ncu sm__pipe_fma_cycles_active of enc_qk45_kernel<15>, profiles/enc_qk45_q4k_4096x14336.md"
     line["roofline"] = roof
     if iq:
         ri = iq.pop("_rank")

@@ -42,3 +42,17 @@ def test_reference_arm_prints_one_contract_line():
         assert k in line, k
     assert line["impl"] == "reference" and line["value"] > 0
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["cpu_baseline"]["kind"] == "port"
+
+
+def test_model_budgets_leave_the_configured_weight_budget():
+    """--budget = weights + f16 KV at ctx 8192 + the compute estimate
+    (main.rs:294-337 with --reserve 0): 5.5 GiB for the 8B shape, 40 GiB for
+    the 70B shape."""
+    for name, gib in (("llama3-8b", 5.5), ("llama3-70b", 40.0)):
+        m = bench.MODELS[name]
+        kv = m["layers"] * 8192 * 8 * 256 * 2
+        compute = 512 * m["vocab"] * 4 + 512 * m["hidden"] * 32
+        assert int(bench.model_budget_arg(name)) - kv - compute == int(gib * (1 << 30))
+    assert bench.model_budget_arg("llama3-8b") == "7309099008"
+    names = [s[0] for s in bench.model_shapes("llama3-70b")]
+    assert names[-2:] == ["token_embd", "output"] and sum(s[4] for s in bench.model_shapes("llama3-70b")) == 562
