@@ -15,7 +15,7 @@ CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libshoehorn_cuda.so")
 BUILD_DIR = os.path.join(HERE, "_build")
 SOURCES = ["api.cu", "kquant.cu", "decode.cu", "iq.cu", "iq_host.cpp", "noalloc.cu"]
-HEADERS = ["common.cuh", "kernels.cuh", "iq_host.h", "iq_tables.h"]
+HEADERS = ["common.cuh", "kernels.cuh", "decode.cuh", "fuse.cuh", "iq_host.h", "iq_tables.h"]
 HOST = os.path.join(HERE, "host")
 HOST_SOURCES = ["gguf.cpp", "imatrix.cpp", "solver.cpp", "pipeline.cpp", "synthetic.cpp", "host_api.cpp"]
 HOST_HEADERS = ["gguf.hpp", "imatrix.hpp", "solver.hpp", "pipeline.hpp", "shard.hpp"]

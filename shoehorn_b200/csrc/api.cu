@@ -393,46 +393,44 @@ int shc_row_errors(shc_ctx *ctx, const uint32_t *types, int n_types, uint32_t sr
     bool any_sig = false;
     for (int t = 0; t < n_types; t++) any_sig |= needs_sigma2(types[t]);
     float *sig = nullptr;
-    std::vector<uint8_t *> codes((size_t)n_types, nullptr);
-    auto cleanup = [&]() {
-        for (auto p : codes)
-            if (p) cudaFreeAsync(p, st);
-        if (sig) cudaFreeAsync(sig, st);
-    };
     if (any_sig) {
         if (scratch_alloc(ctx, (void **)&sig, sizeof(float) * (size_t)n_s, st) != cudaSuccess) return SHC_ENOMEM;
         cudaError_t e = launch_row_sigma2(a.src, n_s, sig, st);
         ctx->launches++;
         if (e != cudaSuccess) {
-            cleanup();
+            cudaFreeAsync(sig, st);
             return cuda_status(e);
         }
     }
-    for (int t = 0; t < n_types; t++) {
+    // One fused launch per block-quantized candidate: encode, decode and the
+    // weighted squared error in one kernel, the codes kept in shared memory.
+    // An elementwise candidate (F32/F16/BF16) round-trips inside one plain
+    // error pass.
+    std::vector<uint32_t> plain_types;
+    std::vector<int> plain_slot;
+    cudaError_t e = cudaSuccess;
+    for (int t = 0; t < n_types && e == cudaSuccess; t++) {
         const uint32_t ty = types[t];
-        if (block_elems(ty) == 1) continue;  // elementwise types are round-tripped inside the error pass
-        const int64_t rb = shc_row_bytes(ty, ne0);
-        if (scratch_alloc(ctx, (void **)&codes[(size_t)t], (size_t)(rb * n_s), st) != cudaSuccess) {
-            cleanup();
-            return SHC_ENOMEM;
+        if (block_elems(ty) == 1) {
+            plain_types.push_back(ty);
+            plain_slot.push_back(t);
+            continue;
         }
         EncArgs at = a;
-        at.dst = codes[(size_t)t];
-        at.dst_row_bytes = rb;
-        at.dst_aligned16 = ((rb & 15) == 0) ? 1 : 0;
         at.sigma2 = sig;
-        cudaError_t e;
-        if (is_iq(ty)) e = launch_iq(ty, at, ctx->iq, ctx->num_sms, st);
-        else e = launch_kquant(ty, at, ctx->num_sms, st);
+        at.err = err + (size_t)t * (size_t)n_s;
+        if (is_iq(ty)) e = launch_iq_fused(ty, at, ctx->iq, ctx->num_sms, st);
+        else e = launch_kquant_fused(ty, at, ctx->num_sms, st);
         ctx->launches++;
-        if (e != cudaSuccess) {
-            cleanup();
-            return cuda_status(e);
+    }
+    if (e == cudaSuccess && !plain_types.empty()) {
+        for (size_t p = 0; p < plain_types.size() && e == cudaSuccess; p++) {
+            const uint8_t *none = nullptr;
+            e = launch_row_sse(&plain_types[p], 1, &none, a, err + (size_t)plain_slot[p] * (size_t)n_s, st);
+            ctx->launches++;
         }
     }
-    cudaError_t e = launch_row_sse(types, n_types, codes.data(), a, err, st);
-    ctx->launches++;
-    cleanup();
+    if (sig) cudaFreeAsync(sig, st);
     return cuda_status(e);
 }
 

@@ -13,6 +13,7 @@
 #include <cfloat>
 
 #include "iq_tables.h"
+#include "fuse.cuh"
 #include "kernels.cuh"
 
 namespace shc {
@@ -79,7 +80,10 @@ __device__ __forceinline__ int iq4_ceil(float t) {
 // elements for XS, 32 per block for NL) run one unit per lane first, so each
 // serial chain is issued once instead of on all 32 lanes; the batch's units
 // are then encoded one after another.
-template <bool XS>
+//
+// FUSE: the fused error table (fuse.cuh): warps 0-6 encode one unit each per
+// stage (a batch of one), warp 7 folds.
+template <bool XS, bool FUSE>
 __global__ void __launch_bounds__(256) enc_iq4_kernel(EncArgs a) {
     __shared__ Iq4Lut lut;
     __shared__ float s_x[8][8 * 33];
@@ -101,8 +105,29 @@ __global__ void __launch_bounds__(256) enc_iq4_kernel(EncArgs a) {
     const int64_t nblk = a.n_rows * bpr;
     const int64_t nwarps = (int64_t)gridDim.x * 8, wg = (int64_t)blockIdx.x * 8 + wid;
     const int64_t u_lo = nunits * wg / nwarps, u_hi = nunits * (wg + 1) / nwarps;
-    for (int64_t b0 = u_lo; b0 < u_hi; b0 += 32) {
-    const int batch = (int)(u_hi - b0 < 32 ? u_hi - b0 : 32);
+    constexpr int NWE = 7;
+    extern __shared__ __align__(16) uint8_t iq4_fuse_smem[];
+    FuseSmem<NWE> *F = reinterpret_cast<FuseSmem<NWE> *>(iq4_fuse_smem);
+    // IQ4_NL units: eight blocks, flat over the tensor (direct) or the eight
+    // blocks from 256 u of row r at unit r * upr + u (fused, rows aligned)
+    const int64_t upr = (bpr + 7) >> 3;
+    auto unit_blk0 = [&](int64_t g) -> int64_t {
+        if (!FUSE) return g * 8;
+        const int64_t r = g / upr;
+        return r * bpr + (g - r * upr) * 8;
+    };
+    auto unit_nb = [&](int64_t g) -> int {
+        const int64_t left = FUSE ? bpr - (g - (g / upr) * upr) * 8 : nblk - g * 8;
+        return (int)(left < 8 ? left : 8);
+    };
+    if constexpr (FUSE) {
+        fuse_setup(*F);
+        if (wid == NWE) {
+            fuse_fold(*F, a, XS ? (ne0 >> 8) : upr, lane);
+            return;
+        }
+    }
+    auto units = [&](int64_t b0, int batch) {
     // sigma2 = 2 * (sequential sum of x^2 over the super-block) / size, one unit per lane
     {
         const int64_t gu = b0 + lane;
@@ -120,10 +145,11 @@ __global__ void __launch_bounds__(256) enc_iq4_kernel(EncArgs a) {
                 }
                 s_sig[wid][lane][0] = 2.0f * s / 256.0f;
             } else {
+                const int64_t ub0 = unit_blk0(gu);
+                const int unb = unit_nb(gu);
 #pragma unroll 1
-                for (int bb = 0; bb < 8; bb++) {
-                    const int64_t blk = gu * 8 + bb;
-                    if (blk >= nblk) break;
+                for (int bb = 0; bb < unb; bb++) {
+                    const int64_t blk = ub0 + bb;
                     const int64_t row = blk / bpr, col = (blk - row * bpr) * 32;
                     float s = 0.0f;
 #pragma unroll
@@ -149,8 +175,8 @@ __global__ void __launch_bounds__(256) enc_iq4_kernel(EncArgs a) {
             row = g / nsb;
             col = (g - row * nsb) * 256 + b * 32;
         } else {
-            const int64_t blk = g * 8 + b;
-            valid = blk < nblk;
+            const int64_t blk = unit_blk0(g) + b;
+            valid = b < unit_nb(g);
             row = valid ? blk / bpr : 0;
             col = valid ? (blk - row * bpr) * 32 : 0;
         }
@@ -342,7 +368,8 @@ __global__ void __launch_bounds__(256) enc_iq4_kernel(EncArgs a) {
             }
         }
         __syncwarp();
-        if (XS) {
+        if (FUSE) {
+        } else if (XS) {
             const int64_t nsb = ne0 >> 8;
             const int64_t sbi = g - (g / nsb) * nsb;
             store_block(a.dst + (g / nsb) * a.dst_row_bytes + sbi * 136, o, 136, a.dst_aligned16 != 0, lane);
@@ -353,6 +380,18 @@ __global__ void __launch_bounds__(256) enc_iq4_kernel(EncArgs a) {
         }
         __syncwarp();
     }
+    };
+    if constexpr (!FUSE) {
+        for (int64_t b0 = u_lo; b0 < u_hi; b0 += 32) units(b0, (int)(u_hi - b0 < 32 ? u_hi - b0 : 32));
+    } else {
+        const int64_t upr_f = XS ? (ne0 >> 8) : upr;
+        FuseIter<NWE> it(a, upr_f, wid);
+        uint32_t fk = 0;
+        while (it.next()) {
+            if (it.valid) units(it.row * upr_f + it.unit, 1);
+            fuse_emit<XS ? SHC_TYPE_IQ4_XS : SHC_TYPE_IQ4_NL, XS ? 0 : 18>(*F, wid, fk, it.valid, a, it.row, it.unit,
+                                                                          s_out[wid], lane);
+        }
     }
 }
 
@@ -848,7 +887,15 @@ __device__ __forceinline__ void take_results(IqWarpSmem<V> &S, int pos, uint32_t
     }
 }
 
+// FUSE: the fused error table (fuse.cuh): the last warp folds, the others
+// encode; its slots take the fold warp's workspace when they fit there, else
+// they follow the lists.
 template <int V>
+struct FuseInWs {
+    static constexpr bool value = sizeof(FuseSmem<IqSearch<V>::WARPS - 1>) <= sizeof(IqWarpSmem<V>);
+};
+
+template <int V, bool FUSE>
 __global__ void __launch_bounds__(IqSearch<V>::WARPS * 32, IqSearch<V>::COOP ? 2 : 1)
     enc_iq_lattice_kernel(EncArgs a, const int32_t *__restrict__ g_kmap, const void *__restrict__ g_lists,
                           int lists_bytes, const uint32_t *__restrict__ g_coords) {
@@ -878,7 +925,18 @@ __global__ void __launch_bounds__(IqSearch<V>::WARPS * 32, IqSearch<V>::COOP ? 2
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     IqWarpSmem<V> &S = wsm_all[wid];
     const int64_t ne0 = a.src.ne0, nsb = ne0 >> 8, total = a.n_rows * nsb;
-    for (int64_t g = (int64_t)blockIdx.x * NW + wid; g < total; g += (int64_t)gridDim.x * NW) {
+    constexpr int NWE = NW - 1;
+    FuseSmem<NWE> *F = reinterpret_cast<FuseSmem<NWE> *>(
+        FuseInWs<V>::value ? reinterpret_cast<uint8_t *>(wsm_all + NWE)
+                        : s_lists + (IqSearch<V>::LISTS_SMEM ? ((lists_bytes + 15) & ~15) : 0));
+    if constexpr (FUSE) {
+        fuse_setup(*F);
+        if (wid == NWE) {
+            fuse_fold(*F, a, nsb, lane);
+            return;
+        }
+    }
+    auto unit = [&](int64_t g) {
         const int64_t row = g / nsb;
         const int64_t sbi = g - row * nsb;
         const int64_t col0 = sbi << 8;
@@ -1213,42 +1271,69 @@ __global__ void __launch_bounds__(IqSearch<V>::WARPS * 32, IqSearch<V>::COOP ? 2
             }
         }
         __syncwarp();
-        store_block(a.dst + row * a.dst_row_bytes + sbi * C::OUT, S.out, C::OUT, a.dst_aligned16 != 0, lane);
+        if constexpr (!FUSE)
+            store_block(a.dst + row * a.dst_row_bytes + sbi * C::OUT, S.out, C::OUT, a.dst_aligned16 != 0, lane);
         __syncwarp();
+    };
+    if constexpr (!FUSE) {
+        for (int64_t g = (int64_t)blockIdx.x * NW + wid; g < total; g += (int64_t)gridDim.x * NW) unit(g);
+    } else {
+        constexpr uint32_t TYPE = V == 0 ? SHC_TYPE_IQ2_XXS : V == 1 ? SHC_TYPE_IQ2_XS : V == 2 ? SHC_TYPE_IQ2_S
+                                  : V == 3 ? SHC_TYPE_IQ3_XXS : SHC_TYPE_IQ3_S;
+        FuseIter<NWE> it(a, nsb, wid);
+        uint32_t fk = 0;
+        while (it.next()) {
+            if (it.valid) unit(it.row * nsb + it.unit);
+            fuse_emit<TYPE, 0>(*F, wid, fk, it.valid, a, it.row, it.unit, S.out, lane);
+        }
     }
 }
 
-template <int V>
-static cudaError_t launch_lattice(const EncArgs &a, const IqTables &iq, int num_sms, cudaStream_t st) {
+template <int V, bool FUSE>
+static cudaError_t launch_lattice(EncArgs a, const IqTables &iq, int num_sms, cudaStream_t st) {
     using C = IqCfg<V>;
     constexpr int NW = IqSearch<V>::WARPS;
-    const size_t smem = ((C::KMAP * 4 + 15) & ~(size_t)15) + NW * sizeof(IqWarpSmem<V>) + 512 +
-                        (IqSearch<V>::LISTS_SMEM ? (size_t)iq.lists_bytes[V] : 0);
-    auto fn = enc_iq_lattice_kernel<V>;
+    size_t smem = ((C::KMAP * 4 + 15) & ~(size_t)15) + NW * sizeof(IqWarpSmem<V>) + 512 +
+                  (IqSearch<V>::LISTS_SMEM ? (((size_t)iq.lists_bytes[V] + 15) & ~(size_t)15) : 0);
+    if (FUSE && !FuseInWs<V>::value) smem += sizeof(FuseSmem<NW - 1>);
+    auto fn = enc_iq_lattice_kernel<V, FUSE>;
     int per_sm = 1;
     cudaError_t e = resident_blocks((const void *)fn, NW * 32, smem, &per_sm);
     if (e != cudaSuccess) return e;
-    const int64_t work = a.n_rows * (a.src.ne0 / 256);
-    int64_t grid = (work + NW - 1) / NW;
+    const int64_t upr = a.src.ne0 / 256;
     const int64_t cap = (int64_t)num_sms * per_sm;
+    int64_t grid;
+    if (FUSE) {
+        a.fuse_rows = fuse_rows_per_group(a.n_rows, upr, NW - 1, cap);
+        grid = (a.n_rows + a.fuse_rows - 1) / a.fuse_rows;
+    } else {
+        grid = (a.n_rows * upr + NW - 1) / NW;
+    }
     if (grid > cap) grid = cap;
     if (grid < 1) grid = 1;
     fn<<<(unsigned)grid, NW * 32, smem, st>>>(a, iq.dkmap[V], iq.lists[V], iq.lists_bytes[V], iq.grid_coords[V]);
     return cudaGetLastError();
 }
 
-template <bool XS>
-static cudaError_t launch_iq4(const EncArgs &a, int num_sms, cudaStream_t st) {
-    auto fn = enc_iq4_kernel<XS>;
+template <bool XS, bool FUSE>
+static cudaError_t launch_iq4(EncArgs a, int num_sms, cudaStream_t st) {
+    auto fn = enc_iq4_kernel<XS, FUSE>;
+    const size_t smem = FUSE ? sizeof(FuseSmem<7>) : 0;
     int per_sm = 1;
-    cudaError_t e = resident_blocks((const void *)fn, 256, 0, &per_sm);
+    cudaError_t e = resident_blocks((const void *)fn, 256, smem, &per_sm);
     if (e != cudaSuccess) return e;
-    const int64_t units = XS ? a.n_rows * (a.src.ne0 / 256) : (a.n_rows * (a.src.ne0 / 32) + 7) / 8;
     const int64_t cap = (int64_t)num_sms * per_sm;
-    int64_t grid = (units + 7) / 8;
+    int64_t grid;
+    if (FUSE) {
+        a.fuse_rows = fuse_rows_per_group(a.n_rows, (a.src.ne0 + 255) / 256, 7, cap);
+        grid = (a.n_rows + a.fuse_rows - 1) / a.fuse_rows;
+    } else {
+        const int64_t units = XS ? a.n_rows * (a.src.ne0 / 256) : (a.n_rows * (a.src.ne0 / 32) + 7) / 8;
+        grid = (units + 7) / 8;
+    }
     if (grid > cap) grid = cap;
     if (grid < 1) grid = 1;
-    fn<<<(unsigned)grid, 256, 0, st>>>(a);
+    fn<<<(unsigned)grid, 256, smem, st>>>(a);
     return cudaGetLastError();
 }
 
@@ -1264,13 +1349,27 @@ bool iq_supported(uint32_t type) {
 
 cudaError_t launch_iq(uint32_t type, const EncArgs &a, const IqTables &iq, int num_sms, cudaStream_t st) {
     switch (type) {
-    case SHC_TYPE_IQ4_NL: return launch_iq4<false>(a, num_sms, st);
-    case SHC_TYPE_IQ4_XS: return launch_iq4<true>(a, num_sms, st);
-    case SHC_TYPE_IQ2_XXS: return launch_lattice<0>(a, iq, num_sms, st);
-    case SHC_TYPE_IQ2_XS: return launch_lattice<1>(a, iq, num_sms, st);
-    case SHC_TYPE_IQ2_S: return launch_lattice<2>(a, iq, num_sms, st);
-    case SHC_TYPE_IQ3_XXS: return launch_lattice<3>(a, iq, num_sms, st);
-    case SHC_TYPE_IQ3_S: return launch_lattice<4>(a, iq, num_sms, st);
+    case SHC_TYPE_IQ4_NL: return launch_iq4<false, false>(a, num_sms, st);
+    case SHC_TYPE_IQ4_XS: return launch_iq4<true, false>(a, num_sms, st);
+    case SHC_TYPE_IQ2_XXS: return launch_lattice<0, false>(a, iq, num_sms, st);
+    case SHC_TYPE_IQ2_XS: return launch_lattice<1, false>(a, iq, num_sms, st);
+    case SHC_TYPE_IQ2_S: return launch_lattice<2, false>(a, iq, num_sms, st);
+    case SHC_TYPE_IQ3_XXS: return launch_lattice<3, false>(a, iq, num_sms, st);
+    case SHC_TYPE_IQ3_S: return launch_lattice<4, false>(a, iq, num_sms, st);
+    default: return cudaErrorNotSupported;
+    }
+}
+
+cudaError_t launch_iq_fused(uint32_t type, const EncArgs &a, const IqTables &iq, int num_sms, cudaStream_t st) {
+    if (!a.err || a.n_rows < 1) return cudaErrorInvalidValue;
+    switch (type) {
+    case SHC_TYPE_IQ4_NL: return launch_iq4<false, true>(a, num_sms, st);
+    case SHC_TYPE_IQ4_XS: return launch_iq4<true, true>(a, num_sms, st);
+    case SHC_TYPE_IQ2_XXS: return launch_lattice<0, true>(a, iq, num_sms, st);
+    case SHC_TYPE_IQ2_XS: return launch_lattice<1, true>(a, iq, num_sms, st);
+    case SHC_TYPE_IQ2_S: return launch_lattice<2, true>(a, iq, num_sms, st);
+    case SHC_TYPE_IQ3_XXS: return launch_lattice<3, true>(a, iq, num_sms, st);
+    case SHC_TYPE_IQ3_S: return launch_lattice<4, true>(a, iq, num_sms, st);
     default: return cudaErrorNotSupported;
     }
 }

@@ -21,6 +21,10 @@ struct EncArgs {
     int64_t dst_row_bytes;
     int *status;
     int dst_aligned16;
+    // Fused error table (the *_fused launchers): err[i] receives row i's
+    // weighted squared error; rows are handed out in groups of fuse_rows.
+    double *err;
+    int64_t fuse_rows;
 };
 
 // IQ lattice tables resident on the device (built on the host as
@@ -110,6 +114,11 @@ cudaError_t launch_decode(uint32_t type, const uint8_t *src, int64_t n_rows, int
                           cudaStream_t st);
 // err[t*n + i] for t < n_types, i < n: weighted SSE of codes[t] (n rows of
 // row_bytes(types[t])) against the source rows.
+// Fused quantize -> dequantize -> weighted SSE of one candidate type: one
+// launch, a.err[i] for every row i of the view, no codes written (a.dst
+// unused).  The K-quant types read a.sigma2 like the plain encoders.
+cudaError_t launch_kquant_fused(uint32_t type, const EncArgs &a, int num_sms, cudaStream_t st);
+cudaError_t launch_iq_fused(uint32_t type, const EncArgs &a, const IqTables &iq, int num_sms, cudaStream_t st);
 cudaError_t launch_row_sse(const uint32_t *types_host, int n_types, const uint8_t *const *codes_host, const EncArgs &a,
                            double *err, cudaStream_t st);
 

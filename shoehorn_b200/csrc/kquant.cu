@@ -17,6 +17,7 @@
 #include <mutex>
 #include <tuple>
 
+#include "fuse.cuh"
 #include "kernels.cuh"
 
 namespace shc {
@@ -197,7 +198,12 @@ __device__ __forceinline__ float max_nan(float a, float b) {
     return r;
 }
 
+//
+// FUSE: the fused error table (fuse.cuh): warps 0-6 encode a row's 256-element
+// unit each (lanes 0-7, one block per lane), warp 7 folds.
+template <bool FUSE>
 __global__ void __launch_bounds__(256, 4) enc_q8_0_kernel(EncArgs a) {
+    constexpr int NWE = 7;
     __shared__ __align__(16) uint8_t s_out[8][32 * 34];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int64_t bpr = a.src.ne0 >> 5;
@@ -205,10 +211,21 @@ __global__ void __launch_bounds__(256, 4) enc_q8_0_kernel(EncArgs a) {
     const int64_t nwi = (nblk + 31) >> 5;
     const bool contiguous = a.src.row_stride == a.src.ne0;
     uint8_t *so = s_out[wid];
-    for (int64_t it = (int64_t)blockIdx.x * 8 + wid; it < nwi; it += (int64_t)gridDim.x * 8) {
-        const int64_t blk = (it << 5) + lane;
+    extern __shared__ __align__(16) uint8_t q8_fuse_smem[];
+    FuseSmem<NWE> *F = reinterpret_cast<FuseSmem<NWE> *>(q8_fuse_smem);
+    const int64_t upr = (bpr + 7) >> 3;
+    if constexpr (FUSE) {
+        fuse_setup(*F);
+        if (wid == NWE) {
+            fuse_fold(*F, a, upr, lane);
+            return;
+        }
+    }
+    // blocks [blk0, blk0 + nb) of the tensor, one per lane
+    auto unit = [&](int64_t blk0, int nb) {
+        const int64_t blk = blk0 + lane;
         float v[32];
-        if (blk < nblk) {
+        if (lane < nb) {
             int64_t row = 0, col = blk * 32;  // rows back to back: the block index is the element offset / 32
             if (!contiguous) {
                 row = blk / bpr;
@@ -267,10 +284,22 @@ __global__ void __launch_bounds__(256, 4) enc_q8_0_kernel(EncArgs a) {
             o16[2 + 2 * m] = (uint16_t)(w[m] >> 16);
         }
         __syncwarp();
-        const int64_t left = nblk - (it << 5);
-        const int nb = (int)(left < 32 ? left : 32);
-        store_block(a.dst + (it << 5) * 34, so, nb * 34, a.dst_aligned16 && nb == 32, lane);
+        if constexpr (!FUSE) store_block(a.dst + blk0 * 34, so, nb * 34, a.dst_aligned16 && nb == 32, lane);
         __syncwarp();
+    };
+    if constexpr (!FUSE) {
+        for (int64_t it = (int64_t)blockIdx.x * 8 + wid; it < nwi; it += (int64_t)gridDim.x * 8) {
+            const int64_t left = nblk - (it << 5);
+            unit(it << 5, (int)(left < 32 ? left : 32));
+        }
+    } else {
+        FuseIter<NWE> it(a, upr, wid);
+        uint32_t fk = 0;
+        while (it.next()) {
+            const int64_t left = bpr - it.unit * 8;
+            if (it.valid) unit(it.row * bpr + it.unit * 8, (int)(left < 8 ? left : 8));
+            fuse_emit<SHC_TYPE_Q8_0, 34>(*F, wid, fk, it.valid, a, it.row, it.unit, so, lane);
+        }
     }
 }
 
@@ -315,16 +344,28 @@ struct __align__(16) Qx16Warp {
 // the exact levels at grids 0 and 18 count the crossings and the estimate
 // t ~ 10 (thr |max|/|x| - nmax) + 9, good to well within 0.01 of a grid,
 // places each one. The (sub-block, grid) jobs are dealt over the 32 lanes.
-template <int NMAX>
+//
+// FUSE: the fused error table (fuse.cuh): warps 0-6 encode, warp 7 folds.
+template <int NMAX, bool FUSE>
 __global__ void __launch_bounds__(256, 3) enc_qx16_kernel(EncArgs a) {
     constexpr float FN = (float)NMAX;
     constexpr int OUT = NMAX == 32 ? 210 : 110;
+    constexpr int NWE = 7;
     extern __shared__ __align__(16) uint8_t qx16_smem[];
-    Qx16Warp *W = reinterpret_cast<Qx16Warp *>(qx16_smem) + (threadIdx.x >> 5);
+    const int wid = threadIdx.x >> 5;
+    Qx16Warp *W = reinterpret_cast<Qx16Warp *>(qx16_smem) + wid;
     const int lane = threadIdx.x & 31;
     const int s = lane >> 1, q = lane & 1;
     const int64_t ne0 = a.src.ne0, nsb = ne0 >> 8, total = a.n_rows * nsb;
-    for (int64_t g = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); g < total; g += (int64_t)gridDim.x * 8) {
+    FuseSmem<NWE> *F = reinterpret_cast<FuseSmem<NWE> *>(qx16_smem + NWE * sizeof(Qx16Warp));
+    if constexpr (FUSE) {
+        fuse_setup(*F);
+        if (wid == NWE) {
+            fuse_fold(*F, a, nsb, lane);
+            return;
+        }
+    }
+    auto unit = [&](int64_t g) {
         const int64_t row = g / nsb;
         const int64_t sbi = g - row * nsb;
         const int64_t col0 = sbi << 8;
@@ -563,8 +604,19 @@ __global__ void __launch_bounds__(256, 3) enc_qx16_kernel(EncArgs a) {
             }
         }
         __syncwarp();
-        store_block(a.dst + row * a.dst_row_bytes + sbi * OUT, o, OUT, false, lane);
+        if constexpr (!FUSE) store_block(a.dst + row * a.dst_row_bytes + sbi * OUT, o, OUT, false, lane);
         __syncwarp();
+    };
+    if constexpr (!FUSE) {
+        for (int64_t g = (int64_t)blockIdx.x * 8 + wid; g < total; g += (int64_t)gridDim.x * 8) unit(g);
+    } else {
+        FuseIter<NWE> it(a, nsb, wid);
+        uint32_t fk = 0;
+        while (it.next()) {
+            if (it.valid) unit(it.row * nsb + it.unit);
+            fuse_emit<NMAX == 32 ? SHC_TYPE_Q6_K : SHC_TYPE_Q3_K, 0>(*F, wid, fk, it.valid, a, it.row, it.unit, W->out,
+                                                                    lane);
+        }
     }
 }
 
@@ -704,21 +756,33 @@ __device__ __forceinline__ float err_from_key(unsigned int k) {
 }
 
 
-template <int N, int NMAX>
-__device__ __forceinline__ void qkx3_super_blocks(const EncArgs &a, Qkx3Warp<N> *W) {
+// FUSE: the fused error table (fuse.cuh): warps 0-6 encode, warp 7 folds.
+constexpr int kQkx3Warps = 8;
+template <int N, int NMAX, bool FUSE>
+__device__ __forceinline__ void qkx3_super_blocks(const EncArgs &a, uint8_t *smem) {
     using Wp = Qkx3Warp<N>;
     constexpr int LPS = Wp::LPS, PAD = Wp::PAD;
     constexpr float FN = (float)NMAX;
     constexpr bool Q2 = N == 16;
     constexpr int BB = Q2 ? 84 : (NMAX == 31 ? 176 : 144);
-    const int lane = threadIdx.x & 31;
+    constexpr int NWE = kQkx3Warps - 1;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    Wp *W = reinterpret_cast<Wp *>(smem) + wid;
     const int s = lane / LPS, q = lane % LPS;
     const int64_t ne0 = a.src.ne0, nsb = ne0 >> 8, total = a.n_rows * nsb;
-    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t nwarps = (int64_t)gridDim.x * kQkx3Warps;
+    FuseSmem<NWE> *F = reinterpret_cast<FuseSmem<NWE> *>(smem + NWE * sizeof(Wp));
+    if constexpr (FUSE) {
+        fuse_setup(*F);
+        if (wid == NWE) {
+            fuse_fold(*F, a, nsb, lane);
+            return;
+        }
+    }
     float *snx = &W->nx[s * PAD];
     float *sw = &W->w[s * PAD];
     float *su = &W->u[s * PAD];
-    for (int64_t g = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); g < total; g += nwarps) {
+    auto unit = [&](int64_t g) {
         const int64_t row = g / nsb;
         const int64_t sbi = g - row * nsb;
         const int64_t col0 = sbi << 8;
@@ -1010,26 +1074,35 @@ __device__ __forceinline__ void qkx3_super_blocks(const EncArgs &a, Qkx3Warp<N> 
             }
         }
         __syncwarp();
-        store_block(a.dst + row * a.dst_row_bytes + sbi * BB, o, BB, !Q2 && a.dst_aligned16 != 0, lane);
+        if constexpr (!FUSE) store_block(a.dst + row * a.dst_row_bytes + sbi * BB, o, BB, !Q2 && a.dst_aligned16 != 0, lane);
         __syncwarp();
+    };
+    if constexpr (!FUSE) {
+        for (int64_t g = (int64_t)blockIdx.x * kQkx3Warps + wid; g < total; g += nwarps) unit(g);
+    } else {
+        constexpr uint32_t TYPE = Q2 ? SHC_TYPE_Q2_K : NMAX == 31 ? SHC_TYPE_Q5_K : SHC_TYPE_Q4_K;
+        FuseIter<NWE> it(a, nsb, wid);
+        uint32_t fk = 0;
+        while (it.next()) {
+            if (it.valid) unit(it.row * nsb + it.unit);
+            fuse_emit<TYPE, 0>(*F, wid, fk, it.valid, a, it.row, it.unit, W->out, lane);
+        }
     }
 }
 
-constexpr int kQkx3Warps = 8;
-template <int NMAX>
+template <int NMAX, bool FUSE>
 __global__ void __launch_bounds__(256, 2) enc_qk45_kernel(EncArgs a) {
     extern __shared__ __align__(16) uint8_t qkx3_smem[];
-    qkx3_super_blocks<32, NMAX>(a, reinterpret_cast<Qkx3Warp<32> *>(qkx3_smem) + (threadIdx.x >> 5));
+    qkx3_super_blocks<32, NMAX, FUSE>(a, qkx3_smem);
 }
-template __global__ void enc_qk45_kernel<15>(EncArgs);
-template __global__ void enc_qk45_kernel<31>(EncArgs);
 
 // Q2_K (ggml block_q2_K layout): make_qkx3_quants (quant.rs:77-141, nmax 3,
 // rmin -0.9, rdelta 0.05, 37 grids) per 16-element sub-block, 4-bit scale and
 // min codes against the super-block's largest scale and min, 2-bit levels.
+template <bool FUSE>
 __global__ void __launch_bounds__(256, 2) enc_q2_k_kernel(EncArgs a) {
     extern __shared__ __align__(16) uint8_t qkx3_smem[];
-    qkx3_super_blocks<16, 3>(a, reinterpret_cast<Qkx3Warp<16> *>(qkx3_smem) + (threadIdx.x >> 5));
+    qkx3_super_blocks<16, 3, FUSE>(a, qkx3_smem);
 }
 
 // ---------------------------------------------------------------------------
@@ -1092,7 +1165,9 @@ __device__ bool legacy_sym_levels(const EncArgs &a, int64_t row, int64_t col, ui
     return true;
 }
 
-template <int KIND>
+// FUSE: the fused error table (fuse.cuh): warps 0-6 encode a row's
+// 256-element unit each, warp 7 folds.
+template <int KIND, bool FUSE>
 __global__ void __launch_bounds__(256) enc_legacy_kernel(EncArgs a) {
     constexpr bool SYM = KIND < 2;
     constexpr int NMAX = KIND == 0 ? 8 : KIND == 1 ? 16 : KIND == 2 ? 15 : 31;
@@ -1107,9 +1182,21 @@ __global__ void __launch_bounds__(256) enc_legacy_kernel(EncArgs a) {
     const int b = lane >> 2, q = lane & 3;
     const int64_t ne0 = a.src.ne0, bpr = ne0 >> 5, nblk = a.n_rows * bpr;
     const int64_t ngrp = (nblk + 7) >> 3;
-    for (int64_t g = (int64_t)blockIdx.x * 8 + wid; g < ngrp; g += (int64_t)gridDim.x * 8) {
-        const int64_t blk = g * 8 + b;
-        const bool valid = blk < nblk;
+    constexpr int NWE = 7;
+    extern __shared__ __align__(16) uint8_t legacy_fuse_smem[];
+    FuseSmem<NWE> *F = reinterpret_cast<FuseSmem<NWE> *>(legacy_fuse_smem);
+    const int64_t upr = (bpr + 7) >> 3;
+    if constexpr (FUSE) {
+        fuse_setup(*F);
+        if (wid == NWE) {
+            fuse_fold(*F, a, upr, lane);
+            return;
+        }
+    }
+    // blocks [blk0, blk0 + nb) of the tensor, 4 lanes per block
+    auto unit = [&](int64_t blk0, int nb) {
+        const int64_t blk = blk0 + b;
+        const bool valid = b < nb;
         const int64_t row = valid ? blk / bpr : 0;
         const int64_t col = valid ? (blk - row * bpr) * 32 : 0;
         float v[8], base[8];
@@ -1335,10 +1422,24 @@ __global__ void __launch_bounds__(256) enc_legacy_kernel(EncArgs a) {
             }
         }
         __syncwarp();
-        const int64_t blk0 = g * 8;
-        const int nb = (int)(nblk - blk0 < 8 ? nblk - blk0 : 8);
-        store_block(a.dst + blk0 * BB, s_out[wid], nb * BB, a.dst_aligned16 && nb == 8, lane);
+        if constexpr (!FUSE) store_block(a.dst + blk0 * BB, s_out[wid], nb * BB, a.dst_aligned16 && nb == 8, lane);
         __syncwarp();
+    };
+    if constexpr (!FUSE) {
+        for (int64_t g = (int64_t)blockIdx.x * 8 + wid; g < ngrp; g += (int64_t)gridDim.x * 8) {
+            const int64_t blk0 = g * 8;
+            unit(blk0, (int)(nblk - blk0 < 8 ? nblk - blk0 : 8));
+        }
+    } else {
+        constexpr uint32_t TYPE = KIND == 0 ? SHC_TYPE_Q4_0 : KIND == 1 ? SHC_TYPE_Q5_0 : KIND == 2 ? SHC_TYPE_Q4_1
+                                                                                                 : SHC_TYPE_Q5_1;
+        FuseIter<NWE> it(a, upr, wid);
+        uint32_t fk = 0;
+        while (it.next()) {
+            const int64_t left = bpr - it.unit * 8;
+            if (it.valid) unit(it.row * bpr + it.unit * 8, (int)(left < 8 ? left : 8));
+            fuse_emit<TYPE, BB>(*F, wid, fk, it.valid, a, it.row, it.unit, s_out[wid], lane);
+        }
     }
 }
 
@@ -1443,32 +1544,73 @@ static cudaError_t launch_qx16(void (*fn)(EncArgs), const EncArgs &a, int num_sm
 cudaError_t launch_kquant(uint32_t type, const EncArgs &a, int num_sms, cudaStream_t st) {
     switch (type) {
     case SHC_TYPE_Q8_0: {
-        unsigned grid = persistent_grid((const void *)enc_q8_0_kernel, 256, num_sms, (a.n_rows * (a.src.ne0 / 32) + 31) / 32);
-        enc_q8_0_kernel<<<grid, 256, 0, st>>>(a);
+        unsigned grid = persistent_grid((const void *)enc_q8_0_kernel<false>, 256, num_sms,
+                                        (a.n_rows * (a.src.ne0 / 32) + 31) / 32);
+        enc_q8_0_kernel<false><<<grid, 256, 0, st>>>(a);
         break;
     }
-    case SHC_TYPE_Q6_K: return launch_qx16(enc_qx16_kernel<32>, a, num_sms, st);
-    case SHC_TYPE_Q3_K: return launch_qx16(enc_qx16_kernel<4>, a, num_sms, st);
-    case SHC_TYPE_Q2_K: return launch_qkx3<16>(enc_q2_k_kernel, a, num_sms, st);
-    case SHC_TYPE_Q4_K: return launch_qkx3<32>(enc_qk45_kernel<15>, a, num_sms, st);
-    case SHC_TYPE_Q5_K: return launch_qkx3<32>(enc_qk45_kernel<31>, a, num_sms, st);
+    case SHC_TYPE_Q6_K: return launch_qx16(enc_qx16_kernel<32, false>, a, num_sms, st);
+    case SHC_TYPE_Q3_K: return launch_qx16(enc_qx16_kernel<4, false>, a, num_sms, st);
+    case SHC_TYPE_Q2_K: return launch_qkx3<16>(enc_q2_k_kernel<false>, a, num_sms, st);
+    case SHC_TYPE_Q4_K: return launch_qkx3<32>(enc_qk45_kernel<15, false>, a, num_sms, st);
+    case SHC_TYPE_Q5_K: return launch_qkx3<32>(enc_qk45_kernel<31, false>, a, num_sms, st);
     case SHC_TYPE_Q4_0: case SHC_TYPE_Q5_0: case SHC_TYPE_Q4_1: case SHC_TYPE_Q5_1: {
         const int64_t ngrp = (a.n_rows * (a.src.ne0 / 32) + 7) / 8;
-        const void *fn = type == SHC_TYPE_Q4_0 ? (const void *)enc_legacy_kernel<0>
-                         : type == SHC_TYPE_Q5_0 ? (const void *)enc_legacy_kernel<1>
-                         : type == SHC_TYPE_Q4_1 ? (const void *)enc_legacy_kernel<2>
-                                                 : (const void *)enc_legacy_kernel<3>;
+        const void *fn = type == SHC_TYPE_Q4_0 ? (const void *)enc_legacy_kernel<0, false>
+                         : type == SHC_TYPE_Q5_0 ? (const void *)enc_legacy_kernel<1, false>
+                         : type == SHC_TYPE_Q4_1 ? (const void *)enc_legacy_kernel<2, false>
+                                                 : (const void *)enc_legacy_kernel<3, false>;
         unsigned grid = persistent_grid(fn, 256, num_sms, ngrp);
-        if (type == SHC_TYPE_Q4_0) enc_legacy_kernel<0><<<grid, 256, 0, st>>>(a);
-        else if (type == SHC_TYPE_Q5_0) enc_legacy_kernel<1><<<grid, 256, 0, st>>>(a);
-        else if (type == SHC_TYPE_Q4_1) enc_legacy_kernel<2><<<grid, 256, 0, st>>>(a);
-        else enc_legacy_kernel<3><<<grid, 256, 0, st>>>(a);
+        if (type == SHC_TYPE_Q4_0) enc_legacy_kernel<0, false><<<grid, 256, 0, st>>>(a);
+        else if (type == SHC_TYPE_Q5_0) enc_legacy_kernel<1, false><<<grid, 256, 0, st>>>(a);
+        else if (type == SHC_TYPE_Q4_1) enc_legacy_kernel<2, false><<<grid, 256, 0, st>>>(a);
+        else enc_legacy_kernel<3, false><<<grid, 256, 0, st>>>(a);
         break;
     }
     default:
         return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
+}
+
+// Fused launch: 8 warps per CTA (7 encoders + the fold warp), dynamic shared
+// memory = the encoders' workspaces (ws_bytes) + the fold slots, groups of
+// rows sized for the resident CTAs, one CTA per group up to the resident
+// count.
+static cudaError_t launch_fused(void (*fn)(EncArgs), EncArgs a, size_t ws_bytes, int64_t upr, int num_sms,
+                                cudaStream_t st) {
+    constexpr int NWE = 7;
+    const size_t smem = ws_bytes + sizeof(FuseSmem<NWE>);
+    int per_sm = 1;
+    cudaError_t e = resident_blocks((const void *)fn, 256, smem, &per_sm);
+    if (e != cudaSuccess) return e;
+    const int64_t cap = (int64_t)num_sms * per_sm;
+    a.fuse_rows = fuse_rows_per_group(a.n_rows, upr, NWE, cap);
+    int64_t grid = (a.n_rows + a.fuse_rows - 1) / a.fuse_rows;
+    if (grid > cap) grid = cap;
+    if (grid < 1) grid = 1;
+    fn<<<(unsigned)grid, 256, smem, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_kquant_fused(uint32_t type, const EncArgs &a, int num_sms, cudaStream_t st) {
+    if (!a.err || a.n_rows < 1) return cudaErrorInvalidValue;
+    const int64_t ne0 = a.src.ne0, upr = (ne0 + 255) / 256;
+    switch (type) {
+    case SHC_TYPE_Q8_0: return launch_fused(enc_q8_0_kernel<true>, a, 0, upr, num_sms, st);
+    case SHC_TYPE_Q6_K: return launch_fused(enc_qx16_kernel<32, true>, a, 7 * sizeof(Qx16Warp), upr, num_sms, st);
+    case SHC_TYPE_Q3_K: return launch_fused(enc_qx16_kernel<4, true>, a, 7 * sizeof(Qx16Warp), upr, num_sms, st);
+    case SHC_TYPE_Q2_K: return launch_fused(enc_q2_k_kernel<true>, a, 7 * sizeof(Qkx3Warp<16>), upr, num_sms, st);
+    case SHC_TYPE_Q4_K:
+        return launch_fused(enc_qk45_kernel<15, true>, a, 7 * sizeof(Qkx3Warp<32>), upr, num_sms, st);
+    case SHC_TYPE_Q5_K:
+        return launch_fused(enc_qk45_kernel<31, true>, a, 7 * sizeof(Qkx3Warp<32>), upr, num_sms, st);
+    case SHC_TYPE_Q4_0: return launch_fused(enc_legacy_kernel<0, true>, a, 0, upr, num_sms, st);
+    case SHC_TYPE_Q5_0: return launch_fused(enc_legacy_kernel<1, true>, a, 0, upr, num_sms, st);
+    case SHC_TYPE_Q4_1: return launch_fused(enc_legacy_kernel<2, true>, a, 0, upr, num_sms, st);
+    case SHC_TYPE_Q5_1: return launch_fused(enc_legacy_kernel<3, true>, a, 0, upr, num_sms, st);
+    default: return cudaErrorInvalidValue;
+    }
 }
 
 }  // namespace shc

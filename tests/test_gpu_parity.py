@@ -209,6 +209,67 @@ def test_row_errors_match_oracle(ctx, row_step):
         assert np.array_equal(got[t].view(np.uint64), want.view(np.uint64)), NAMES[ty]
 
 
+# The error table is one fused launch per candidate: rows are handed out in
+# groups (1 to 32 rows, one fold lane per row), a group's 256-element units in
+# column order over its rows, groups grid-strided over the resident CTAs.
+# These shapes give groups of one row (few rows, long rows), groups with a
+# short last group, many groups per CTA, and a sampled view of a 3-D tensor
+# whose imatrix slice changes with the matrix.
+@pytest.mark.parametrize("n_rows,ne0,row_step,rows_per_mat", [
+    (1, 4096, 1, 0), (3, 2048, 1, 0), (45, 512, 1, 0), (2400, 256, 1, 0), (9000, 256, 1, 0), (600, 512, 7, 100)])
+def test_row_errors_fused_groups(ctx, n_rows, ne0, row_step, rows_per_mat):
+    bits, im1 = sweep_rows(n_rows, ne0, seed=n_rows + ne0)
+    im = im1
+    if rows_per_mat:
+        n_mats = (n_rows + rows_per_mat - 1) // rows_per_mat
+        im = np.exp(np.random.default_rng(3).normal(0, 1.0, size=n_mats * ne0)).astype(np.float32)
+    types = supported(KQ + IQ) + [F16, BF16, F32]
+    got = ctx.row_errors(types, dev(bits.view(np.int16)), dev(im), row_step=row_step,
+                         rows_per_mat=rows_per_mat).cpu().numpy()
+    for t, ty in enumerate(types):
+        want = O.row_errors_bf16(ty, bits, im, row_step=row_step, rows_per_mat=rows_per_mat)
+        assert np.array_equal(got[t].view(np.uint64), want.view(np.uint64)), NAMES[ty]
+
+
+# Rows whose last 256-element unit is short (32-element block types only).
+@pytest.mark.parametrize("n_rows,ne0", [(1, 96), (9, 800), (300, 288)])
+def test_row_errors_fused_short_units(ctx, n_rows, ne0):
+    bits, im = sweep_rows(n_rows, ne0, seed=ne0)
+    types = [t for t in supported(KQ + IQ) if sh.GgmlType(t).block_layout()[0] == 32]
+    assert len(types) >= 6
+    got = ctx.row_errors(types, dev(bits.view(np.int16)), dev(im)).cpu().numpy()
+    for t, ty in enumerate(types):
+        want = O.row_errors_bf16(ty, bits, im)
+        assert np.array_equal(got[t].view(np.uint64), want.view(np.uint64)), NAMES[ty]
+
+
+def test_row_errors_fused_legacy_carried_levels(ctx):
+    """The fused table on legacy blocks that re-emit an earlier block's levels
+    (quant.rs:171-198) and on NaN rows."""
+    bits, im = sweep_rows(40, 1024, seed=78)
+    im = im.copy()
+    im[64:128] = 0.0
+    x = bf16_bits_to_f32(bits)
+    x[3, 200] = np.nan
+    bits = f32_to_bf16_bits(x)
+    types = [2, 6, 3, 7]
+    for imv in (im, None):
+        got = ctx.row_errors(types, dev(bits.view(np.int16)), None if imv is None else dev(imv)).cpu().numpy()
+        for t, ty in enumerate(types):
+            want = O.row_errors_bf16(ty, bits, imv)
+            assert np.array_equal(got[t].view(np.uint64), want.view(np.uint64)), NAMES[ty]
+
+
+def test_row_errors_fused_iq_configuration(ctx):
+    """The IQ configuration's distribution (Student-t, log-normal imatrix)."""
+    bits, im = student_rows(160, 4096, seed=77)
+    types = supported(IQ) + supported(KQ)
+    got = ctx.row_errors(types, dev(bits.view(np.int16)), dev(im), row_step=1).cpu().numpy()
+    for t, ty in enumerate(types):
+        want = O.row_errors_bf16(ty, bits, im)
+        assert np.array_equal(got[t].view(np.uint64), want.view(np.uint64)), NAMES[ty]
+
+
 def test_row_errors_without_imatrix_and_edges(ctx):
     x = edge_rows(512)
     bits = f32_to_bf16_bits(x)
