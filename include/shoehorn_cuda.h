@@ -115,8 +115,11 @@ int shc_decode_rows(shc_ctx *ctx, uint32_t ggml_type, const uint8_t *src, int64_
  * types (device pointers).  err[t * n_sampled + i] receives
  * quant.rs:618 row_error(types[t], row(i*row_step), im) as the reference
  * computes it (f64 sum in element order); n_sampled = ceil(n_rows/row_step).
- * The codes never leave the device.  The caller sums rows in row order and
- * scales by n_rows / n_sampled (main.rs:546-560). */
+ * One kernel launch per block-quantized candidate encodes, decodes and folds
+ * the error with the codes held in shared memory (plus one row sigma^2 pass
+ * shared by the K-quant candidates); a NaN error is stored as the default
+ * quiet NaN.  The caller sums rows in row order and scales by
+ * n_rows / n_sampled (main.rs:546-560). */
 int shc_row_errors(shc_ctx *ctx, const uint32_t *types, int n_types, uint32_t src_type, const void *src,
                    int64_t n_rows, int64_t ne0, const float *imatrix, int64_t imatrix_len, int64_t rows_per_mat,
                    int64_t row0, int64_t row_step, double *err, void *stream);

@@ -8,10 +8,11 @@
 // column-major, item i = unit i / R' of row i % R' (R' = the group's row
 // count), so the group's rows advance together.  Stage j gives item
 // j * NWE + w to encoder warp w; the CTA's last warp folds.  Encoder warp w
-// writes its item's differences d (f32, exact) into its slot and arrives on
-// full[w]; the fold warp waits for the stage's slots, lane r folds the slots
-// of row r in item order (so each row is folded in column order, one serial
-// f64 chain per row, as the reference does), then arrives on empty[w].  A
+// writes its item's terms f64(w_i) * d_i * d_i (exact per element, 32 lanes
+// at once) into its slot and arrives on full[w]; the fold warp waits for the
+// stage's slots, lane r adds up the slots of row r in item order (so each row
+// is one serial f64 chain in column order, as the reference folds it), then
+// arrives on empty[w].  A
 // slot is rewritten only after its previous contents were folded, which the
 // encoder waits for after encoding its next item: the fold of stage j runs
 // while stage j + 1 encodes.
@@ -25,12 +26,12 @@
 
 namespace shc {
 
-constexpr int kFuseStride = 260;  // floats per slot: 256 + 4, so slots start on different banks
+constexpr int kFuseStride = 258;  // doubles per slot: 256 + 2, so slots start on different banks
 constexpr unsigned long long kFuseWaitNs = 2000000000ull;
 
 template <int NWE>
 struct __align__(16) FuseSmem {
-    float d[NWE][kFuseStride];
+    double t[NWE][kFuseStride];
     unsigned long long full[NWE];   // encoder warp w -> fold warp, 32 arrivals per phase
     unsigned long long empty[NWE];  // fold warp -> encoder warp w, 32 arrivals per phase
     int abort;
@@ -129,8 +130,8 @@ struct FuseIter {
     }
 };
 
-// Encoder side: the differences x - decode(codes) of this warp's item into
-// its slot.  TYPE is the encoded ggml type; BB the bytes of one 32-element
+// Encoder side: the terms f64(w) * d * d, d = x - decode(codes), of this
+// warp's item into its slot (w = the imatrix weight, 1 without one).  TYPE is the encoded ggml type; BB the bytes of one 32-element
 // block for the 32-element block types (a unit is then up to eight blocks
 // back to back in `codes`), 0 when `codes` holds one 256-element block.
 // Lane l takes elements 32 (l / 4) + 8 (l % 4) + [0, 8).
@@ -146,17 +147,21 @@ __device__ __forceinline__ void fuse_emit(FuseSmem<NWE> &F, int w, uint32_t &k, 
             float y[32];
             if (BB) decode_sub32(TYPE, codes + sub * BB, 0, y);
             else decode_sub32(TYPE, codes, sub, y);
-            float xv[8];
+            float xv[8], wv[8];
             load8(a.src, row, c0 + e0, xv);
-            float dv[8];
+            const float *imr = im_row(a.im, a.src.ne0, a.row0 + row * a.row_step);
+            load_im8(imr, c0 + e0, wv);
+            double tv[8];
 #pragma unroll
             for (int t = 0; t < 8; t++) {
                 const float yv = qq == 0 ? y[t] : qq == 1 ? y[8 + t] : qq == 2 ? y[16 + t] : y[24 + t];
-                dv[t] = xv[t] - yv;
+                const double dd = (double)(xv[t] - yv);
+                const double wd = imr ? (double)wv[t] : 1.0;
+                tv[t] = wd * dd * dd;
             }
-            float4 *dst = reinterpret_cast<float4 *>(&F.d[w][e0]);
-            dst[0] = make_float4(dv[0], dv[1], dv[2], dv[3]);
-            dst[1] = make_float4(dv[4], dv[5], dv[6], dv[7]);
+            double2 *dst = reinterpret_cast<double2 *>(&F.t[w][e0]);
+#pragma unroll
+            for (int t = 0; t < 4; t++) dst[t] = make_double2(tv[2 * t], tv[2 * t + 1]);
         }
     }
     __syncwarp();
@@ -182,7 +187,6 @@ __device__ void fuse_fold(FuseSmem<NWE> &F, const EncArgs &a, int64_t upr, int l
         G.group(grp, r0, reff, items);
         const int64_t nst = (items + NWE - 1) / NWE;
         const bool mine = lane < reff;
-        const float *imr = mine ? im_row(a.im, ne0, a.row0 + (r0 + lane) * a.row_step) : nullptr;
         double s = 0.0;
         for (int64_t j = 0; j < nst; j++, k++) {
             for (int w = 0; w < NWE; w++) mbar_wait(&F.full[w], (uint32_t)(k & 1), &F.abort, a.status);
@@ -193,19 +197,18 @@ __device__ void fuse_fold(FuseSmem<NWE> &F, const EncArgs &a, int64_t upr, int l
                     if (idx >= items) break;
                     const int64_t c0 = (idx / reff) * 256;
                     const int n = (int)(ne0 - c0 < 256 ? ne0 - c0 : 256);
-                    const float *dp = F.d[w];
-                    for (int e = 0; e < n; e += 8) {
-                        const float4 d0 = *reinterpret_cast<const float4 *>(dp + e);
-                        const float4 d1 = *reinterpret_cast<const float4 *>(dp + e + 4);
-                        const float dv[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
-                        float wv[8];
-                        load_im8(imr, c0 + e, wv);
-#pragma unroll
-                        for (int t = 0; t < 8; t++) {
-                            const double wd = imr ? (double)wv[t] : 1.0;
-                            const double dd = (double)dv[t];
-                            s += wd * dd * dd;
-                        }
+                    const double2 *tp = reinterpret_cast<const double2 *>(F.t[w]);
+#pragma unroll 4
+                    for (int e = 0; e < n / 2; e += 4) {
+                        const double2 t0 = tp[e], t1 = tp[e + 1], t2 = tp[e + 2], t3 = tp[e + 3];
+                        s += t0.x;
+                        s += t0.y;
+                        s += t1.x;
+                        s += t1.y;
+                        s += t2.x;
+                        s += t2.y;
+                        s += t3.x;
+                        s += t3.y;
                     }
                 }
             }

@@ -10,6 +10,7 @@
 // replayed by one lane per block.  Lattice lookups use the compact kmap
 // staged in shared memory; neighbour lists are read through the read-only
 // cache.
+#include <algorithm>
 #include <cfloat>
 
 #include "iq_tables.h"
@@ -565,6 +566,7 @@ __device__ float make_qp_quants32_x4(const float *x, const float *w, uint8_t *ls
         }
         for (int it = 0; it < 5; it++) {
             int n_changed = 0;
+#pragma unroll 1
             for (int i = 0; i < n; i++) {
                 const float wi = w[i];
                 const float li = (float)ls[i];
@@ -644,6 +646,12 @@ struct IqWarpSmem {
     uint8_t qpl[C::QP ? 256 : 1];                // make_qp_quants levels per block (IQ2_XXS)
     float qps[C::QP ? C::NB : 1];                // make_qp_quants result per block (IQ2_XXS)
     uint16_t gidx[64];                           // grid index per lattice group
+    // IQ3: per-block rounding requests served one (block, group) per lane
+    float rid[COOP ? 1 : C::NB];                 // id the block's groups round at
+    float rsc[COOP ? 1 : C::NB];                 // scale their neighbours are scored at
+    uint32_t rtodo[COOP ? 1 : C::NB];            // groups to round (0: none)
+    uint16_t rg[COOP ? 1 : C::NB * C::NG];       // result: the group's packed levels
+    uint8_t roff[COOP ? 1 : C::NB * C::NG];      // result: 1 if it was off the grid
     __align__(16) uint8_t out[112];
 };
 
@@ -858,6 +866,55 @@ __device__ __forceinline__ uint32_t round_block(IqWarpSmem<V> &S, const int *kma
     return offm;
 }
 
+// IQ2_XXS takes round_block out of line: its kernel is large enough that
+// the three inlined copies cost more in instruction fetch than the calls.
+template <int V>
+__device__ __noinline__ uint32_t round_block_call(IqWarpSmem<V> &S, const int *kmap, const uint16_t *l16, int xb,
+                                                  float id, float scale, uint32_t todo, Levels<V> &lv,
+                                                  int (&mk)[IqCfg<V>::NG], int *status) {
+    return round_block<V>(S, kmap, l16, xb, id, scale, todo, lv, mk, status);
+}
+template <int V>
+__device__ __forceinline__ uint32_t round_block_sel(IqWarpSmem<V> &S, const int *kmap, const uint16_t *l16, int xb,
+                                                    float id, float scale, uint32_t todo, Levels<V> &lv,
+                                                    int (&mk)[IqCfg<V>::NG], int *status) {
+    if constexpr (V == 0) return round_block_call<V>(S, kmap, l16, xb, id, scale, todo, lv, mk, status);
+    else return round_block<V>(S, kmap, l16, xb, id, scale, todo, lv, mk, status);
+}
+
+// IQ3: round the groups S.rtodo[b] of every block b at S.rid[b], one
+// (block, group) per lane, searching off-grid groups' neighbour lists at
+// S.rsc[b]; results in S.rg / S.roff.  The same per-group steps as
+// round_block, which walks a block's groups on one lane.  Every lane of the
+// warp must call it.
+template <int V>
+__device__ __forceinline__ void round_groups_lanes(IqWarpSmem<V> &S, const int *kmap, const uint16_t *l16, int lane,
+                                                   int *status) {
+    using C = IqCfg<V>;
+    constexpr int BP = C::BS + 1;
+    __syncwarp();
+#pragma unroll 1
+    for (int task = lane; task < C::NB * C::NG; task += 32) {
+        const int b = task / C::NG, k = task - b * C::NG;
+        if (!((S.rtodo[b] >> k) & 1u)) continue;
+        const int xo = b * BP + k * C::G;
+        uint32_t g = round_group<V>(S.xv + xo, S.rid[b]);
+        const int m = kmap[kmap_index<V>(g)];
+        uint8_t off = 0;
+        if (m < 0) {
+            off = 1;
+            g = lane_search<V>(l16, m, S.xv + xo, S.wa + xo, S.rsc[b]);
+            if (g == ~0u) {
+                set_status(status, SHC_ENONEIGHBOUR);
+                g = 0;
+            }
+        }
+        S.rg[task] = (uint16_t)g;
+        S.roff[task] = off;
+    }
+    __syncwarp();
+}
+
 template <int V>
 __device__ __forceinline__ void queue_tasks(IqWarpSmem<V> &S, int pos, uint32_t offm, const int (&mk)[IqCfg<V>::NG],
                                             int xb, float scale) {
@@ -890,27 +947,29 @@ __device__ __forceinline__ void take_results(IqWarpSmem<V> &S, int pos, uint32_t
 // FUSE: the fused error table (fuse.cuh): the last warp folds, the others
 // encode; its slots take the fold warp's workspace when they fit there, else
 // they follow the lists.
-template <int V>
-struct FuseInWs {
-    static constexpr bool value = sizeof(FuseSmem<IqSearch<V>::WARPS - 1>) <= sizeof(IqWarpSmem<V>);
+// Fused launches use 16 warps for every variant (one resident block per SM).
+template <int V, bool FUSE>
+struct IqWarps {
+    static constexpr int value = FUSE ? 16 : IqSearch<V>::WARPS;
 };
 
 template <int V, bool FUSE>
-__global__ void __launch_bounds__(IqSearch<V>::WARPS * 32, IqSearch<V>::COOP ? 2 : 1)
+__global__ void __launch_bounds__(IqWarps<V, FUSE>::value * 32, (IqSearch<V>::COOP && !FUSE) ? 2 : 1)
     enc_iq_lattice_kernel(EncArgs a, const int32_t *__restrict__ g_kmap, const void *__restrict__ g_lists,
                           int lists_bytes, const uint32_t *__restrict__ g_coords) {
     using C = IqCfg<V>;
     constexpr int BP = C::BS + 1;
     constexpr int NJ = C::NB * C::NT;
-    constexpr int NW = IqSearch<V>::WARPS;
+    constexpr int NW = IqWarps<V, FUSE>::value;
     constexpr bool COOP = IqSearch<V>::COOP;
     extern __shared__ __align__(16) uint8_t smem_raw[];
-    // shared memory: compact kmap | per-warp state | grid coords (IQ2_XXS) |
-    // neighbour lists (IQ3; IQ2 reads its lists through L1/L2)
+    // shared memory: compact kmap | grid coords (IQ2_XXS) | per-warp state |
+    // neighbour lists (IQ3; IQ2 reads its lists through L1/L2) | fold slots
+    // (fused IQ3; fused IQ2 lays them over the fold warp's state and on)
     int *kmap = reinterpret_cast<int *>(smem_raw);
-    IqWarpSmem<V> *wsm_all = reinterpret_cast<IqWarpSmem<V> *>(smem_raw + ((C::KMAP * 4 + 15) & ~15));
-    uint16_t *gco = reinterpret_cast<uint16_t *>(reinterpret_cast<uint8_t *>(wsm_all + NW));
-    uint8_t *s_lists = reinterpret_cast<uint8_t *>(gco + 256);
+    uint16_t *gco = reinterpret_cast<uint16_t *>(smem_raw + ((C::KMAP * 4 + 15) & ~15));
+    IqWarpSmem<V> *wsm_all = reinterpret_cast<IqWarpSmem<V> *>(reinterpret_cast<uint8_t *>(gco + 256));
+    uint8_t *s_lists = reinterpret_cast<uint8_t *>(wsm_all + NW);
     for (int i = threadIdx.x; i < C::KMAP; i += blockDim.x) kmap[i] = g_kmap[i];
     if (V == 0)
         for (int i = threadIdx.x; i < 256; i += blockDim.x) gco[i] = (uint16_t)g_coords[i];
@@ -927,8 +986,7 @@ __global__ void __launch_bounds__(IqSearch<V>::WARPS * 32, IqSearch<V>::COOP ? 2
     const int64_t ne0 = a.src.ne0, nsb = ne0 >> 8, total = a.n_rows * nsb;
     constexpr int NWE = NW - 1;
     FuseSmem<NWE> *F = reinterpret_cast<FuseSmem<NWE> *>(
-        FuseInWs<V>::value ? reinterpret_cast<uint8_t *>(wsm_all + NWE)
-                        : s_lists + (IqSearch<V>::LISTS_SMEM ? ((lists_bytes + 15) & ~15) : 0));
+        IqSearch<V>::LISTS_SMEM ? s_lists + ((lists_bytes + 15) & ~15) : reinterpret_cast<uint8_t *>(wsm_all + NWE));
     if constexpr (FUSE) {
         fuse_setup(*F);
         if (wid == NWE) {
@@ -1047,7 +1105,7 @@ __global__ void __launch_bounds__(IqSearch<V>::WARPS * 32, IqSearch<V>::COOP ? 2
                 if (job) {
                     const float id = ((float)(2 * C::KM - 1) + (float)(C::IS_LO + t) * C::STEP) / S.bmax[b];
                     sc = 1.0f / id;
-                    offm = round_block<V>(S, kmap, l16, b * BP, id, sc, (1u << C::NG) - 1, lv, mk, a.status);
+                    offm = round_block_sel<V>(S, kmap, l16, b * BP, id, sc, (1u << C::NG) - 1, lv, mk, a.status);
                 }
                 int T;
                 const int pos = warp_exclusive_scan(__popc(offm), lane, T);
@@ -1096,13 +1154,30 @@ __global__ void __launch_bounds__(IqSearch<V>::WARPS * 32, IqSearch<V>::COOP ? 2
         // blocks that have one
         Levels<V> wl;
         uint32_t woff = 0;
-        {
+        if constexpr (!COOP) {
+            if (lane < C::NB) {
+                S.rtodo[lane] = cwin >= 0 ? (1u << C::NG) - 1 : 0u;
+                if (cwin >= 0) {
+                    const float id = ((float)(2 * C::KM - 1) + (float)(C::IS_LO + cwin) * C::STEP) / S.bmax[lane];
+                    S.rid[lane] = id;
+                    S.rsc[lane] = 1.0f / id;
+                }
+            }
+            round_groups_lanes<V>(S, kmap, l16, lane, a.status);
+            if (cwin >= 0) {
+#pragma unroll
+                for (int k = 0; k < C::NG; k++) {
+                    wl.set_group(k, S.rg[lane * C::NG + k]);
+                    woff |= (uint32_t)S.roff[lane * C::NG + k] << k;
+                }
+            }
+        } else {
             float sc = 0.0f;
             int mk[C::NG];
             if (cwin >= 0) {
                 const float id = ((float)(2 * C::KM - 1) + (float)(C::IS_LO + cwin) * C::STEP) / S.bmax[lane];
                 sc = 1.0f / id;
-                woff = round_block<V>(S, kmap, l16, lane * BP, id, sc, (1u << C::NG) - 1, wl, mk, a.status);
+                woff = round_block_sel<V>(S, kmap, l16, lane * BP, id, sc, (1u << C::NG) - 1, wl, mk, a.status);
             }
             if (COOP) {
                 int T;
@@ -1130,9 +1205,22 @@ __global__ void __launch_bounds__(IqSearch<V>::WARPS * 32, IqSearch<V>::COOP ? 2
             const bool reproject = blk && ((V == 0) ? (scale > 0.0f) : (off != 0 && scale > 0.0f));
             uint32_t offm = 0;
             int mk[C::NG];
-            if (reproject) {
+            if constexpr (!COOP) {
                 const uint32_t todo = (V == 0 || V == 4) ? ((1u << C::NG) - 1) : off;
-                offm = round_block<V>(S, kmap, l16, b * BP, 1.0f / scale, scale, todo, ls, mk, a.status);
+                if (lane < C::NB) {
+                    S.rtodo[b] = reproject ? todo : 0u;
+                    S.rid[b] = 1.0f / scale;
+                    S.rsc[b] = scale;
+                }
+                round_groups_lanes<V>(S, kmap, l16, lane, a.status);
+                if (reproject) {
+#pragma unroll
+                    for (int k = 0; k < C::NG; k++)
+                        if ((todo >> k) & 1u) ls.set_group(k, S.rg[b * C::NG + k]);
+                }
+            } else if (reproject) {
+                const uint32_t todo = (V == 0 || V == 4) ? ((1u << C::NG) - 1) : off;
+                offm = round_block_sel<V>(S, kmap, l16, b * BP, 1.0f / scale, scale, todo, ls, mk, a.status);
             }
             int pos = 0;
             if (COOP) {
@@ -1292,10 +1380,13 @@ __global__ void __launch_bounds__(IqSearch<V>::WARPS * 32, IqSearch<V>::COOP ? 2
 template <int V, bool FUSE>
 static cudaError_t launch_lattice(EncArgs a, const IqTables &iq, int num_sms, cudaStream_t st) {
     using C = IqCfg<V>;
-    constexpr int NW = IqSearch<V>::WARPS;
-    size_t smem = ((C::KMAP * 4 + 15) & ~(size_t)15) + NW * sizeof(IqWarpSmem<V>) + 512 +
-                  (IqSearch<V>::LISTS_SMEM ? (((size_t)iq.lists_bytes[V] + 15) & ~(size_t)15) : 0);
-    if (FUSE && !FuseInWs<V>::value) smem += sizeof(FuseSmem<NW - 1>);
+    constexpr int NW = IqWarps<V, FUSE>::value;
+    const size_t ws_end = ((C::KMAP * 4 + 15) & ~(size_t)15) + 512 + NW * sizeof(IqWarpSmem<V>);
+    size_t smem = ws_end + (IqSearch<V>::LISTS_SMEM ? (((size_t)iq.lists_bytes[V] + 15) & ~(size_t)15) : 0);
+    if (FUSE) {
+        if (IqSearch<V>::LISTS_SMEM) smem += sizeof(FuseSmem<NW - 1>);
+        else smem = std::max(smem, ws_end - sizeof(IqWarpSmem<V>) + sizeof(FuseSmem<NW - 1>));
+    }
     auto fn = enc_iq_lattice_kernel<V, FUSE>;
     int per_sm = 1;
     cudaError_t e = resident_blocks((const void *)fn, NW * 32, smem, &per_sm);

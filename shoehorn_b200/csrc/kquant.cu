@@ -345,12 +345,14 @@ struct __align__(16) Qx16Warp {
 // t ~ 10 (thr |max|/|x| - nmax) + 9, good to well within 0.01 of a grid,
 // places each one. The (sub-block, grid) jobs are dealt over the 32 lanes.
 //
-// FUSE: the fused error table (fuse.cuh): warps 0-6 encode, warp 7 folds.
+// FUSE: the fused error table (fuse.cuh), 16 warps: warps 0-14 encode, warp
+// 15 folds (one resident block per SM keeps the encoders' count while a
+// launch of few rows still spreads over the SMs).
 template <int NMAX, bool FUSE>
-__global__ void __launch_bounds__(256, 3) enc_qx16_kernel(EncArgs a) {
+__global__ void __launch_bounds__(FUSE ? 512 : 256, FUSE ? 1 : 3) enc_qx16_kernel(EncArgs a) {
     constexpr float FN = (float)NMAX;
     constexpr int OUT = NMAX == 32 ? 210 : 110;
-    constexpr int NWE = 7;
+    constexpr int NWE = 15;
     extern __shared__ __align__(16) uint8_t qx16_smem[];
     const int wid = threadIdx.x >> 5;
     Qx16Warp *W = reinterpret_cast<Qx16Warp *>(qx16_smem) + wid;
@@ -756,7 +758,8 @@ __device__ __forceinline__ float err_from_key(unsigned int k) {
 }
 
 
-// FUSE: the fused error table (fuse.cuh): warps 0-6 encode, warp 7 folds.
+// FUSE: the fused error table (fuse.cuh), 16 warps (Q2_K, whose workspace is
+// larger: 8): the last warp folds, the others encode.
 constexpr int kQkx3Warps = 8;
 template <int N, int NMAX, bool FUSE>
 __device__ __forceinline__ void qkx3_super_blocks(const EncArgs &a, uint8_t *smem) {
@@ -765,7 +768,7 @@ __device__ __forceinline__ void qkx3_super_blocks(const EncArgs &a, uint8_t *sme
     constexpr float FN = (float)NMAX;
     constexpr bool Q2 = N == 16;
     constexpr int BB = Q2 ? 84 : (NMAX == 31 ? 176 : 144);
-    constexpr int NWE = kQkx3Warps - 1;
+    constexpr int NWE = Q2 ? 7 : 15;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     Wp *W = reinterpret_cast<Wp *>(smem) + wid;
     const int s = lane / LPS, q = lane % LPS;
@@ -1091,7 +1094,7 @@ __device__ __forceinline__ void qkx3_super_blocks(const EncArgs &a, uint8_t *sme
 }
 
 template <int NMAX, bool FUSE>
-__global__ void __launch_bounds__(256, 2) enc_qk45_kernel(EncArgs a) {
+__global__ void __launch_bounds__(FUSE ? 512 : 256, FUSE ? 1 : 2) enc_qk45_kernel(EncArgs a) {
     extern __shared__ __align__(16) uint8_t qkx3_smem[];
     qkx3_super_blocks<32, NMAX, FUSE>(a, qkx3_smem);
 }
@@ -1573,23 +1576,24 @@ cudaError_t launch_kquant(uint32_t type, const EncArgs &a, int num_sms, cudaStre
     return cudaGetLastError();
 }
 
-// Fused launch: 8 warps per CTA (7 encoders + the fold warp), dynamic shared
+// Fused launch: NWE encoder warps + the fold warp per CTA, dynamic shared
 // memory = the encoders' workspaces (ws_bytes) + the fold slots, groups of
 // rows sized for the resident CTAs, one CTA per group up to the resident
 // count.
+template <int NWE>
 static cudaError_t launch_fused(void (*fn)(EncArgs), EncArgs a, size_t ws_bytes, int64_t upr, int num_sms,
                                 cudaStream_t st) {
-    constexpr int NWE = 7;
     const size_t smem = ws_bytes + sizeof(FuseSmem<NWE>);
+    constexpr int threads = (NWE + 1) * 32;
     int per_sm = 1;
-    cudaError_t e = resident_blocks((const void *)fn, 256, smem, &per_sm);
+    cudaError_t e = resident_blocks((const void *)fn, threads, smem, &per_sm);
     if (e != cudaSuccess) return e;
     const int64_t cap = (int64_t)num_sms * per_sm;
     a.fuse_rows = fuse_rows_per_group(a.n_rows, upr, NWE, cap);
     int64_t grid = (a.n_rows + a.fuse_rows - 1) / a.fuse_rows;
     if (grid > cap) grid = cap;
     if (grid < 1) grid = 1;
-    fn<<<(unsigned)grid, 256, smem, st>>>(a);
+    fn<<<(unsigned)grid, threads, smem, st>>>(a);
     return cudaGetLastError();
 }
 
@@ -1597,18 +1601,21 @@ cudaError_t launch_kquant_fused(uint32_t type, const EncArgs &a, int num_sms, cu
     if (!a.err || a.n_rows < 1) return cudaErrorInvalidValue;
     const int64_t ne0 = a.src.ne0, upr = (ne0 + 255) / 256;
     switch (type) {
-    case SHC_TYPE_Q8_0: return launch_fused(enc_q8_0_kernel<true>, a, 0, upr, num_sms, st);
-    case SHC_TYPE_Q6_K: return launch_fused(enc_qx16_kernel<32, true>, a, 7 * sizeof(Qx16Warp), upr, num_sms, st);
-    case SHC_TYPE_Q3_K: return launch_fused(enc_qx16_kernel<4, true>, a, 7 * sizeof(Qx16Warp), upr, num_sms, st);
-    case SHC_TYPE_Q2_K: return launch_fused(enc_q2_k_kernel<true>, a, 7 * sizeof(Qkx3Warp<16>), upr, num_sms, st);
+    case SHC_TYPE_Q8_0: return launch_fused<7>(enc_q8_0_kernel<true>, a, 0, upr, num_sms, st);
+    case SHC_TYPE_Q6_K:
+        return launch_fused<15>(enc_qx16_kernel<32, true>, a, 15 * sizeof(Qx16Warp), upr, num_sms, st);
+    case SHC_TYPE_Q3_K:
+        return launch_fused<15>(enc_qx16_kernel<4, true>, a, 15 * sizeof(Qx16Warp), upr, num_sms, st);
+    case SHC_TYPE_Q2_K:
+        return launch_fused<7>(enc_q2_k_kernel<true>, a, 7 * sizeof(Qkx3Warp<16>), upr, num_sms, st);
     case SHC_TYPE_Q4_K:
-        return launch_fused(enc_qk45_kernel<15, true>, a, 7 * sizeof(Qkx3Warp<32>), upr, num_sms, st);
+        return launch_fused<15>(enc_qk45_kernel<15, true>, a, 15 * sizeof(Qkx3Warp<32>), upr, num_sms, st);
     case SHC_TYPE_Q5_K:
-        return launch_fused(enc_qk45_kernel<31, true>, a, 7 * sizeof(Qkx3Warp<32>), upr, num_sms, st);
-    case SHC_TYPE_Q4_0: return launch_fused(enc_legacy_kernel<0, true>, a, 0, upr, num_sms, st);
-    case SHC_TYPE_Q5_0: return launch_fused(enc_legacy_kernel<1, true>, a, 0, upr, num_sms, st);
-    case SHC_TYPE_Q4_1: return launch_fused(enc_legacy_kernel<2, true>, a, 0, upr, num_sms, st);
-    case SHC_TYPE_Q5_1: return launch_fused(enc_legacy_kernel<3, true>, a, 0, upr, num_sms, st);
+        return launch_fused<15>(enc_qk45_kernel<31, true>, a, 15 * sizeof(Qkx3Warp<32>), upr, num_sms, st);
+    case SHC_TYPE_Q4_0: return launch_fused<7>(enc_legacy_kernel<0, true>, a, 0, upr, num_sms, st);
+    case SHC_TYPE_Q5_0: return launch_fused<7>(enc_legacy_kernel<1, true>, a, 0, upr, num_sms, st);
+    case SHC_TYPE_Q4_1: return launch_fused<7>(enc_legacy_kernel<2, true>, a, 0, upr, num_sms, st);
+    case SHC_TYPE_Q5_1: return launch_fused<7>(enc_legacy_kernel<3, true>, a, 0, upr, num_sms, st);
     default: return cudaErrorInvalidValue;
     }
 }
