@@ -30,8 +30,9 @@ struct shc_ctx {
     // host-buffer pipeline resources (one host call at a time)
     std::mutex host_mu;
     cudaStream_t hs[4] = {nullptr, nullptr, nullptr, nullptr};  // h2d, compute, d2h, row sigma^2
-    void *pin[4] = {nullptr, nullptr, nullptr, nullptr};  // in0, in1, out0, out1 (pageable staging)
-    size_t pin_bytes[4] = {0, 0, 0, 0};
+    static constexpr int kPinSlots = 6;  // pageable staging: in 0-2, out 3-5
+    void *pin[kPinSlots] = {};
+    size_t pin_bytes[kPinSlots] = {};
 };
 
 namespace {
@@ -336,7 +337,7 @@ int shc_free(shc_ctx *ctx) {
         cudaDeviceSynchronize();
         for (int i = 0; i < 4; i++)
             if (ctx->hs[i]) cudaStreamDestroy(ctx->hs[i]);
-        for (int i = 0; i < 4; i++)
+        for (int i = 0; i < shc_ctx::kPinSlots; i++)
             if (ctx->pin[i]) cudaFreeHost(ctx->pin[i]);
         if (ctx->d_tables) cudaFree(ctx->d_tables);
         if (ctx->pool) cudaMemPoolDestroy(ctx->pool);
@@ -462,12 +463,24 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
     const bool bounded = timeout_ms >= 0;
     const size_t eb = src_elem_bytes(src_type);
     const size_t in_row = (size_t)ne0 * eb;
-    // equal chunks of at most ~16 MiB of source: copies of one chunk overlap
-    // the encode of the previous one, and no short tail chunk pays a whole
-    // row sigma^2 pass (a fixed serial-chain latency) for a few rows
+    // Chunks: equal chunks of at most ~16 MiB of source (a short tail chunk
+    // would pay a whole row sigma^2 pass, a fixed serial-chain latency, for a
+    // few rows), the last one cut in two so that less work is left once the
+    // final host-to-device copy lands.  Three buffer slots: the copy of chunk
+    // k+2 never waits for the encode of chunk k.
+    constexpr int NS = 3;
     const int64_t max_chunk = std::max<int64_t>(1, (int64_t)((16u << 20) / in_row));
-    const int64_t n_chunks = (n_rows + max_chunk - 1) / max_chunk;
-    const int64_t chunk = (n_rows + n_chunks - 1) / n_chunks;
+    const int64_t n_eq = (n_rows + max_chunk - 1) / max_chunk;
+    const int64_t chunk = (n_rows + n_eq - 1) / n_eq;
+    std::vector<std::pair<int64_t, int64_t>> chunks;  // (first row, rows)
+    for (int64_t r = 0; r < n_rows; r += chunk) chunks.emplace_back(r, std::min(chunk, n_rows - r));
+    if (n_eq > 1 && chunks.back().second >= 64) {
+        const auto last = chunks.back();
+        const int64_t h = last.second / 2;
+        chunks.back().second = last.second - h;
+        chunks.emplace_back(last.first + last.second - h, h);
+    }
+    const int64_t n_chunks = (int64_t)chunks.size();
     const bool pin_src = is_pinned(host_src), pin_dst = is_pinned(host_dst);
     cudaStream_t s_in = ctx->hs[0], s_cmp = ctx->hs[1], s_out = ctx->hs[2], s_sig = ctx->hs[3];
     // The row sigma^2 pre-pass (one thread per row, bound by its serial sums)
@@ -478,12 +491,12 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
     const bool pre_sig = needs_sigma2(type) && n_rows > 1;
     const int enc_sms = pre_sig ? std::max(1, ctx->num_sms - kSigmaSms) : 0;
     int rc = SHC_OK;
-    void *d_in[2] = {nullptr, nullptr};
-    uint8_t *d_out[2] = {nullptr, nullptr};
-    float *d_sig[2] = {nullptr, nullptr};
+    void *d_in[NS] = {};
+    uint8_t *d_out[NS] = {};
+    float *d_sig[NS] = {};
     float *d_im = nullptr;
-    cudaEvent_t ev_in[2], ev_cmp[2], ev_out[2], ev_sig[2];
-    for (int b = 0; b < 2; b++) {
+    cudaEvent_t ev_in[NS], ev_cmp[NS], ev_out[NS], ev_sig[NS];
+    for (int b = 0; b < NS; b++) {
         cudaEventCreateWithFlags(&ev_in[b], cudaEventDisableTiming);
         cudaEventCreateWithFlags(&ev_cmp[b], cudaEventDisableTiming);
         cudaEventCreateWithFlags(&ev_out[b], cudaEventDisableTiming);
@@ -492,14 +505,15 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
     auto fail = [&](int code) {
         if (rc == SHC_OK) rc = code;
     };
-    for (int b = 0; b < 2 && rc == SHC_OK; b++) {
+    const int nslots = (int)std::min<int64_t>(NS, n_chunks);
+    for (int b = 0; b < nslots && rc == SHC_OK; b++) {
         if (scratch_alloc(ctx, &d_in[b], in_row * (size_t)chunk, s_cmp) != cudaSuccess) fail(SHC_ENOMEM);
         if (scratch_alloc(ctx, (void **)&d_out[b], (size_t)rb * (size_t)chunk, s_cmp) != cudaSuccess) fail(SHC_ENOMEM);
         if (pre_sig && rc == SHC_OK &&
             scratch_alloc(ctx, (void **)&d_sig[b], sizeof(float) * (size_t)chunk, s_cmp) != cudaSuccess)
             fail(SHC_ENOMEM);
         if (!pin_src && rc == SHC_OK) fail(ensure_pinned(ctx, b, in_row * (size_t)chunk));
-        if (!pin_dst && rc == SHC_OK) fail(ensure_pinned(ctx, 2 + b, (size_t)rb * (size_t)chunk));
+        if (!pin_dst && rc == SHC_OK) fail(ensure_pinned(ctx, NS + b, (size_t)rb * (size_t)chunk));
     }
     if (rc == SHC_OK && host_im && im_len > 0) {
         if (scratch_alloc(ctx, (void **)&d_im, sizeof(float) * (size_t)im_len, s_cmp) != cudaSuccess) fail(SHC_ENOMEM);
@@ -507,18 +521,19 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
             fail(SHC_ECUDA);
     }
     if (rc == SHC_OK) {
-        // the allocations above are ordered on s_cmp; make the copy streams wait
+        // the allocations above are ordered on s_cmp; make the other streams wait
         cudaEventRecord(ev_cmp[0], s_cmp);
         cudaStreamWaitEvent(s_in, ev_cmp[0], 0);
         cudaStreamWaitEvent(s_out, ev_cmp[0], 0);
         cudaStreamWaitEvent(s_sig, ev_cmp[0], 0);
-        cudaEventRecord(ev_cmp[1], s_cmp);
-        for (int b = 0; b < 2; b++) {
+        for (int b = 0; b < NS; b++) {
+            cudaEventRecord(ev_cmp[b], s_cmp);
             cudaEventRecord(ev_out[b], s_out);
             cudaEventRecord(ev_in[b], s_in);
         }
     }
-    std::vector<int64_t> pending_out(2, -1);  // chunk whose pageable output sits in pin[2+b]
+    int64_t pending_out[NS];  // chunk whose pageable output sits in pin[NS + b]
+    for (int b = 0; b < NS; b++) pending_out[b] = -1;
     auto drain_out = [&](int b) {
         if (pending_out[b] < 0) return;
         int w = wait_event(ev_out[b], deadline, bounded);
@@ -526,17 +541,16 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
             fail(w);
             return;
         }
-        const int64_t k = pending_out[b];
-        const int64_t r0 = k * chunk, nr = std::min(chunk, n_rows - r0);
-        std::memcpy(host_dst + r0 * rb, ctx->pin[2 + b], (size_t)(nr * rb));
+        const auto &c = chunks[(size_t)pending_out[b]];
+        std::memcpy(host_dst + c.first * rb, ctx->pin[NS + b], (size_t)(c.second * rb));
         pending_out[b] = -1;
     };
     for (int64_t k = 0; k < n_chunks && rc == SHC_OK; k++) {
-        const int b = (int)(k & 1);
-        const int64_t r0 = k * chunk, nr = std::min(chunk, n_rows - r0);
+        const int b = (int)(k % NS);
+        const int64_t r0 = chunks[(size_t)k].first, nr = chunks[(size_t)k].second;
         const size_t in_bytes = in_row * (size_t)nr;
         const uint8_t *src_k = static_cast<const uint8_t *>(host_src) + (size_t)r0 * in_row;
-        // H2D of chunk k into d_in[b] once the encode of chunk k-2 released it
+        // H2D of chunk k into d_in[b] once the encode of chunk k-NS released it
         cudaStreamWaitEvent(s_in, ev_cmp[b], 0);
         if (pin_src) {
             if (cudaMemcpyAsync(d_in[b], src_k, in_bytes, cudaMemcpyHostToDevice, s_in) != cudaSuccess) fail(SHC_ECUDA);
@@ -549,7 +563,7 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
         cudaEventRecord(ev_in[b], s_in);
         EncArgs a = make_args(ctx, src_type, d_in[b], nr, ne0, ne0, d_im, im_len, rows_per_mat, row0 + r0, 1, d_out[b], rb);
         // sigma^2 of chunk k once its input landed (d_sig[b] is free: the
-        // chunk's H2D already waited for the encode of chunk k-2)
+        // chunk's H2D already waited for the encode of chunk k-NS)
         cudaEvent_t ready = ev_in[b];
         if (pre_sig) {
             cudaStreamWaitEvent(s_sig, ev_in[b], 0);
@@ -572,13 +586,13 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
                 fail(SHC_ECUDA);
         } else {
             drain_out(b);
-            if (cudaMemcpyAsync(ctx->pin[2 + b], d_out[b], (size_t)(nr * rb), cudaMemcpyDeviceToHost, s_out) != cudaSuccess)
+            if (cudaMemcpyAsync(ctx->pin[NS + b], d_out[b], (size_t)(nr * rb), cudaMemcpyDeviceToHost, s_out) != cudaSuccess)
                 fail(SHC_ECUDA);
             pending_out[b] = k;
         }
         cudaEventRecord(ev_out[b], s_out);
     }
-    for (int b = 0; b < 2; b++) drain_out(b);
+    for (int b = 0; b < NS; b++) drain_out(b);
     // release buffers after all queued work; wait (bounded) for completion
     cudaEvent_t done;
     cudaEventCreateWithFlags(&done, cudaEventDisableTiming);
@@ -588,7 +602,7 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
     cudaStreamWaitEvent(s_cmp, done, 0);
     cudaEventRecord(done, s_sig);
     cudaStreamWaitEvent(s_cmp, done, 0);
-    for (int b = 0; b < 2; b++) {
+    for (int b = 0; b < NS; b++) {
         if (d_in[b]) cudaFreeAsync(d_in[b], s_cmp);
         if (d_out[b]) cudaFreeAsync(d_out[b], s_cmp);
         if (d_sig[b]) cudaFreeAsync(d_sig[b], s_cmp);
@@ -598,7 +612,7 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
     int w = wait_event(done, deadline, bounded);
     if (rc == SHC_OK) rc = w;
     cudaEventDestroy(done);
-    for (int b = 0; b < 2; b++) {
+    for (int b = 0; b < NS; b++) {
         cudaEventDestroy(ev_in[b]);
         cudaEventDestroy(ev_cmp[b]);
         cudaEventDestroy(ev_out[b]);
