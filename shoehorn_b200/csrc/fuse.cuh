@@ -45,12 +45,15 @@ __device__ __forceinline__ void mbar_init(unsigned long long *b, unsigned count)
 __device__ __forceinline__ void mbar_arrive(unsigned long long *b) {
     asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.shared::cta.b64 st, [%0];\n}" ::"r"(smem_u32(b)) : "memory");
 }
+// One bounded try: the thread sleeps in hardware until the phase completes or
+// about kFuseSuspendNs pass (so a waiting warp takes no issue slots).
+constexpr uint32_t kFuseSuspendNs = 1000000;
 __device__ __forceinline__ bool mbar_test(unsigned long long *b, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
         : "=r"(ok)
-        : "r"(smem_u32(b)), "r"(parity)
+        : "r"(smem_u32(b)), "r"(parity), "r"(kFuseSuspendNs)
         : "memory");
     return ok != 0;
 }

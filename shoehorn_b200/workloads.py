@@ -52,6 +52,9 @@ def main(argv=None):
     repeatable launch for profilers):
 
       python -m shoehorn_b200.workloads --type 14 --rows 512 [--dist iq] [--repeat 2]
+
+    --table STEP computes the fused error table (row_errors) of every STEP-th
+    row instead of encoding.
     """
     import argparse
     ap = argparse.ArgumentParser(prog="python -m shoehorn_b200.workloads")
@@ -60,6 +63,8 @@ def main(argv=None):
     ap.add_argument("--dist", choices=["sweep", "iq"], default="sweep",
                     help="sweep: N(0, 0.02) + outliers, 14336 wide; iq: Student-t, 4096 wide")
     ap.add_argument("--repeat", type=int, default=2)
+    ap.add_argument("--table", type=int, default=0, metavar="STEP",
+                    help="fused error table of every STEP-th row instead of the encode")
     args = ap.parse_args(argv)
     import torch
     import shoehorn_b200 as sh
@@ -73,8 +78,12 @@ def main(argv=None):
         src = torch.from_numpy(bits.view(np.int16)).cuda()
         imt = torch.from_numpy(im).cuda()
         for _ in range(args.repeat):
-            ctx.encode_rows(args.type, src, imt, sync=True)
-    print(f"encoded {args.rows} x {bits.shape[1]} to type {args.type} x{args.repeat}")
+            if args.table:
+                ctx.row_errors([args.type], src, imt, row_step=args.table, sync=True)
+            else:
+                ctx.encode_rows(args.type, src, imt, sync=True)
+    what = f"error table (row step {args.table})" if args.table else "encoded"
+    print(f"{what} {args.rows} x {bits.shape[1]} to type {args.type} x{args.repeat}")
 
 
 if __name__ == "__main__":
