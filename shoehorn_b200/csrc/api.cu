@@ -403,33 +403,18 @@ int shc_row_errors(shc_ctx *ctx, const uint32_t *types, int n_types, uint32_t sr
             return cuda_status(e);
         }
     }
-    // One fused launch per block-quantized candidate: encode, decode and the
-    // weighted squared error in one kernel, the codes kept in shared memory.
-    // An elementwise candidate (F32/F16/BF16) round-trips inside one plain
-    // error pass.
-    std::vector<uint32_t> plain_types;
-    std::vector<int> plain_slot;
+    // One fused launch per candidate: encode, decode and the weighted
+    // squared error in one kernel, the codes kept in shared memory (an
+    // elementwise candidate round-trips each element in place of a code).
     cudaError_t e = cudaSuccess;
     for (int t = 0; t < n_types && e == cudaSuccess; t++) {
         const uint32_t ty = types[t];
-        if (block_elems(ty) == 1) {
-            plain_types.push_back(ty);
-            plain_slot.push_back(t);
-            continue;
-        }
         EncArgs at = a;
         at.sigma2 = sig;
         at.err = err + (size_t)t * (size_t)n_s;
         if (is_iq(ty)) e = launch_iq_fused(ty, at, ctx->iq, ctx->num_sms, st);
         else e = launch_kquant_fused(ty, at, ctx->num_sms, st);
         ctx->launches++;
-    }
-    if (e == cudaSuccess && !plain_types.empty()) {
-        for (size_t p = 0; p < plain_types.size() && e == cudaSuccess; p++) {
-            const uint8_t *none = nullptr;
-            e = launch_row_sse(&plain_types[p], 1, &none, a, err + (size_t)plain_slot[p] * (size_t)n_s, st);
-            ctx->launches++;
-        }
     }
     if (sig) cudaFreeAsync(sig, st);
     return cuda_status(e);

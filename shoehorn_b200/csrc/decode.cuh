@@ -269,4 +269,11 @@ __device__ __forceinline__ void decode_sub32(uint32_t type, const uint8_t *blk, 
     }
 }
 
+// Elementwise "encodings" (quant.rs:546-560) round-tripped to f32.
+__device__ __forceinline__ float roundtrip_plain(uint32_t type, float x) {
+    if (type == SHC_TYPE_F16) return f16_val(f16_bits(x));
+    if (type == SHC_TYPE_BF16) return __uint_as_float(__float_as_uint(x) & 0xFFFF0000u);
+    return x;
+}
+
 }  // namespace shc

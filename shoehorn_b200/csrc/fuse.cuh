@@ -172,6 +172,37 @@ __device__ __forceinline__ void fuse_emit(FuseSmem<NWE> &F, int w, uint32_t &k, 
     k++;
 }
 
+// Encoder side for the elementwise types (F32, F16, BF16): the "codes" are
+// the row itself, round-tripped through TYPE (quant.rs:546-560).
+template <uint32_t TYPE, int NWE>
+__device__ __forceinline__ void fuse_emit_plain(FuseSmem<NWE> &F, int w, uint32_t &k, bool valid, const EncArgs &a,
+                                                int64_t row, int64_t unit, int lane) {
+    if (k >= 1) mbar_wait(&F.empty[w], (k - 1) & 1u, &F.abort, a.status);
+    if (valid) {
+        const int64_t c0 = unit * 256;
+        const int e0 = lane * 8;
+        if (c0 + e0 < a.src.ne0) {
+            float xv[8], wv[8];
+            load8(a.src, row, c0 + e0, xv);
+            const float *imr = im_row(a.im, a.src.ne0, a.row0 + row * a.row_step);
+            load_im8(imr, c0 + e0, wv);
+            double tv[8];
+#pragma unroll
+            for (int t = 0; t < 8; t++) {
+                const double dd = (double)(xv[t] - roundtrip_plain(TYPE, xv[t]));
+                const double wd = imr ? (double)wv[t] : 1.0;
+                tv[t] = wd * dd * dd;
+            }
+            double2 *dst = reinterpret_cast<double2 *>(&F.t[w][e0]);
+#pragma unroll
+            for (int t = 0; t < 4; t++) dst[t] = make_double2(tv[2 * t], tv[2 * t + 1]);
+        }
+    }
+    __syncwarp();
+    mbar_arrive(&F.full[w]);
+    k++;
+}
+
 // Fold warp: per row of each group, sum f64(w) * d * d over the row's
 // elements in order, one lane per row; err[row] for every row of the view.
 template <int NWE>

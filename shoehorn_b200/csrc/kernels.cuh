@@ -112,14 +112,11 @@ bool iq_supported(uint32_t type);
 cudaError_t launch_iq(uint32_t type, const EncArgs &a, const IqTables &iq, int num_sms, cudaStream_t st);
 cudaError_t launch_decode(uint32_t type, const uint8_t *src, int64_t n_rows, int64_t ne0, float *dst, int num_sms,
                           cudaStream_t st);
-// err[t*n + i] for t < n_types, i < n: weighted SSE of codes[t] (n rows of
-// row_bytes(types[t])) against the source rows.
 // Fused quantize -> dequantize -> weighted SSE of one candidate type: one
 // launch, a.err[i] for every row i of the view, no codes written (a.dst
-// unused).  The K-quant types read a.sigma2 like the plain encoders.
+// unused).  The K-quant types read a.sigma2 like the plain encoders;
+// launch_kquant_fused also takes the elementwise types (F32, F16, BF16).
 cudaError_t launch_kquant_fused(uint32_t type, const EncArgs &a, int num_sms, cudaStream_t st);
 cudaError_t launch_iq_fused(uint32_t type, const EncArgs &a, const IqTables &iq, int num_sms, cudaStream_t st);
-cudaError_t launch_row_sse(const uint32_t *types_host, int n_types, const uint8_t *const *codes_host, const EncArgs &a,
-                           double *err, cudaStream_t st);
 
 }  // namespace shc

@@ -1464,6 +1464,26 @@ __global__ void enc_plain_kernel(uint32_t type, EncArgs a) {
     }
 }
 
+// Error table of an elementwise candidate (F32, F16, BF16): the fused
+// layout of fuse.cuh with the round trip in place of an encoder; 7 warps
+// compute terms, warp 7 folds.
+template <uint32_t TYPE>
+__global__ void __launch_bounds__(256) plain_fused_kernel(EncArgs a) {
+    constexpr int NWE = 7;
+    extern __shared__ __align__(16) uint8_t plain_fuse_smem[];
+    FuseSmem<NWE> *F = reinterpret_cast<FuseSmem<NWE> *>(plain_fuse_smem);
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int64_t upr = (a.src.ne0 + 255) / 256;
+    fuse_setup(*F);
+    if (wid == NWE) {
+        fuse_fold(*F, a, upr, lane);
+        return;
+    }
+    FuseIter<NWE> it(a, upr, wid);
+    uint32_t fk = 0;
+    while (it.next()) fuse_emit_plain<TYPE>(*F, wid, fk, it.valid, a, it.row, it.unit, lane);
+}
+
 cudaError_t launch_plain(uint32_t type, const EncArgs &a, int num_sms, cudaStream_t st) {
     const int64_t n = a.n_rows * a.src.ne0;
     int64_t blocks = (n + 255) / 256;
@@ -1616,6 +1636,9 @@ cudaError_t launch_kquant_fused(uint32_t type, const EncArgs &a, int num_sms, cu
     case SHC_TYPE_Q5_0: return launch_fused<7>(enc_legacy_kernel<1, true>, a, 0, upr, num_sms, st);
     case SHC_TYPE_Q4_1: return launch_fused<7>(enc_legacy_kernel<2, true>, a, 0, upr, num_sms, st);
     case SHC_TYPE_Q5_1: return launch_fused<7>(enc_legacy_kernel<3, true>, a, 0, upr, num_sms, st);
+    case SHC_TYPE_F32: return launch_fused<7>(plain_fused_kernel<SHC_TYPE_F32>, a, 0, upr, num_sms, st);
+    case SHC_TYPE_F16: return launch_fused<7>(plain_fused_kernel<SHC_TYPE_F16>, a, 0, upr, num_sms, st);
+    case SHC_TYPE_BF16: return launch_fused<7>(plain_fused_kernel<SHC_TYPE_BF16>, a, 0, upr, num_sms, st);
     default: return cudaErrorInvalidValue;
     }
 }

@@ -243,6 +243,19 @@ def test_row_errors_fused_short_units(ctx, n_rows, ne0):
         assert np.array_equal(got[t].view(np.uint64), want.view(np.uint64)), NAMES[ty]
 
 
+@pytest.mark.parametrize("n_rows,ne0", [(3, 8), (40, 200), (130, 1032)])
+def test_row_errors_fused_elementwise(ctx, n_rows, ne0):
+    """F32/F16/BF16 candidates: the round trip in place of an encoder, rows of
+    any multiple-of-8 width (the last 256-element unit short)."""
+    bits, im = sweep_rows(n_rows, ne0, seed=ne0 + 1)
+    types = [F32, F16, BF16]
+    for imv in (im, None):
+        got = ctx.row_errors(types, dev(bits.view(np.int16)), None if imv is None else dev(imv)).cpu().numpy()
+        for t, ty in enumerate(types):
+            want = O.row_errors_bf16(ty, bits, imv)
+            assert np.array_equal(got[t].view(np.uint64), want.view(np.uint64)), NAMES[ty]
+
+
 def test_row_errors_fused_legacy_carried_levels(ctx):
     """The fused table on legacy blocks that re-emit an earlier block's levels
     (quant.rs:171-198) and on NaN rows."""
