@@ -643,6 +643,7 @@ struct IqWarpSmem {
     float bscale[C::NB];                         // final block scale
     uint8_t live[C::NB];
     uint8_t signs[32];                           // per 8-element sign group
+    float sigb[32];                              // sigma^2 of the warp's next 32 super-blocks
     uint8_t qpl[C::QP ? 256 : 1];                // make_qp_quants levels per block (IQ2_XXS)
     float qps[C::QP ? C::NB : 1];                // make_qp_quants result per block (IQ2_XXS)
     uint16_t gidx[64];                           // grid index per lattice group
@@ -994,7 +995,8 @@ __global__ void __launch_bounds__(IqWarps<V, FUSE>::value * 32, (IqSearch<V>::CO
             return;
         }
     }
-    auto unit = [&](int64_t g) {
+    // sig_in >= 0: the super-block's sigma^2, computed ahead for a batch
+    auto unit = [&](int64_t g, float sig_in) {
         const int64_t row = g / nsb;
         const int64_t sbi = g - row * nsb;
         const int64_t col0 = sbi << 8;
@@ -1002,12 +1004,15 @@ __global__ void __launch_bounds__(IqWarps<V, FUSE>::value * 32, (IqSearch<V>::CO
         // ---- P0: load, super-block sigma^2, weights, signs ----
         float v[8];
         load8(a.src, row, col0 + lane * 8, v);
+        float sig = sig_in;
+        if (sig_in < 0.0f) {
 #pragma unroll
-        for (int k = 0; k < 8; k++) S.x[lane * 8 + k] = v[k];
-        __syncwarp();
-        float ssum = 0.0f;
-        for (int i = 0; i < 256; i++) ssum += S.x[i] * S.x[i];
-        const float sig = C::SIG2X ? 2.0f * ssum / 256.0f : ssum / 256.0f;
+            for (int k = 0; k < 8; k++) S.x[lane * 8 + k] = v[k];
+            __syncwarp();
+            float ssum = 0.0f;
+            for (int i = 0; i < 256; i++) ssum += S.x[i] * S.x[i];
+            sig = C::SIG2X ? 2.0f * ssum / 256.0f : ssum / 256.0f;
+        }
         float base[8];
         load_im8(imr, col0 + lane * 8, base);
         float wv[8];
@@ -1364,14 +1369,36 @@ __global__ void __launch_bounds__(IqWarps<V, FUSE>::value * 32, (IqSearch<V>::CO
         __syncwarp();
     };
     if constexpr (!FUSE) {
-        for (int64_t g = (int64_t)blockIdx.x * NW + wid; g < total; g += (int64_t)gridDim.x * NW) unit(g);
+        // the warp's super-blocks g0, g0 + st, ... in batches of 32: lane k
+        // first folds the sigma^2 of the batch's k-th super-block (the
+        // serial sum over its 256 elements, one super-block per lane)
+        const int64_t st = (int64_t)gridDim.x * NW;
+        for (int64_t g0 = (int64_t)blockIdx.x * NW + wid; g0 < total; g0 += 32 * st) {
+            {
+                const int64_t gk = g0 + lane * st;
+                float ssum = 0.0f;
+                if (gk < total) {
+                    const int64_t row = gk / nsb, col0 = (gk - row * nsb) << 8;
+#pragma unroll 4
+                    for (int m = 0; m < 32; m++) {
+                        float v[8];
+                        load8(a.src, row, col0 + m * 8, v);
+#pragma unroll
+                        for (int k = 0; k < 8; k++) ssum += v[k] * v[k];
+                    }
+                }
+                S.sigb[lane] = C::SIG2X ? 2.0f * ssum / 256.0f : ssum / 256.0f;
+            }
+            __syncwarp();
+            for (int k = 0; k < 32 && g0 + k * st < total; k++) unit(g0 + k * st, S.sigb[k]);
+        }
     } else {
         constexpr uint32_t TYPE = V == 0 ? SHC_TYPE_IQ2_XXS : V == 1 ? SHC_TYPE_IQ2_XS : V == 2 ? SHC_TYPE_IQ2_S
                                   : V == 3 ? SHC_TYPE_IQ3_XXS : SHC_TYPE_IQ3_S;
         FuseIter<NWE> it(a, nsb, wid);
         uint32_t fk = 0;
         while (it.next()) {
-            if (it.valid) unit(it.row * nsb + it.unit);
+            if (it.valid) unit(it.row * nsb + it.unit, -1.0f);
             fuse_emit<TYPE, 0>(*F, wid, fk, it.valid, a, it.row, it.unit, S.out, lane);
         }
     }
