@@ -237,30 +237,43 @@ __global__ void __launch_bounds__(256, 4) enc_q8_0_kernel(EncArgs a) {
 #pragma unroll
             for (int k = 0; k < 32; k++) v[k] = 0.0f;
         }
-        // amax over |x| ignoring NaN as the reference's max fold does; the
-        // NaN-propagating fold flags the blocks that need the general path
-        float amax = 0.0f, amaxn = 0.0f;
+        // the NaN-propagating max of |x| flags the blocks that need the
+        // general path; without NaN it is the reference's NaN-ignoring max
+        float amaxn = 0.0f;
 #pragma unroll
-        for (int k = 0; k < 32; k++) {
-            amax = fmaxf(amax, fabsf(v[k]));
-            amaxn = max_nan(amaxn, fabsf(v[k]));
+        for (int k = 0; k < 32; k++) amaxn = max_nan(amaxn, fabsf(v[k]));
+        float amax = amaxn;
+        if (!(amaxn < INFINITY)) {
+            amax = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 32; k++) amax = fmaxf(amax, fabsf(v[k]));
         }
         const float d = amax / 127.0f;
         const float id = d > 0.0f ? 1.0f / d : 0.0f;
         uint32_t w[8];
         if (amaxn < INFINITY && id < INFINITY) {
+            // two elements per instruction: |y| = |x| id; 2^23 + round-half-up(|y|)
+            // by an RZ and an RD add (identities of floor_half_up), the
+            // magnitude back out exactly, the sign of x put on it, and the
+            // int8 code read as the low byte of m + 1.5 * 2^23
+            const float2 id2 = make_float2(id, id);
 #pragma unroll
             for (int m = 0; m < 8; m++) {
-                uint32_t word = 0;
+                uint32_t q[4];
 #pragma unroll
-                for (int t = 0; t < 4; t++) {
-                    const float y = v[m * 4 + t] * id;
-                    // 2^23 + round-half-up(|y|) (identities of floor_half_up)
-                    const uint32_t r = __float_as_uint(__fadd_rd(__fadd_rz(fabsf(y), 0.5f), 8388608.0f)) & 0xFFu;
-                    const uint32_t sg = (uint32_t)((int32_t)__float_as_uint(y) >> 31);
-                    word |= (((r ^ sg) - sg) & 0xFFu) << (8 * t);
+                for (int h = 0; h < 2; h++) {
+                    const float x0 = v[m * 4 + 2 * h], x1 = v[m * 4 + 2 * h + 1];
+                    const float2 y = __fmul2_rn(make_float2(fabsf(x0), fabsf(x1)), id2);
+                    const float2 u = __fadd2_rd(__fadd2_rz(y, make_float2(0.5f, 0.5f)), make_float2(8388608.0f, 8388608.0f));
+                    const float2 r = __fadd2_rn(u, make_float2(-8388608.0f, -8388608.0f));
+                    const float2 sgn = make_float2(
+                        __uint_as_float(__float_as_uint(r.x) | (__float_as_uint(x0) & 0x80000000u)),
+                        __uint_as_float(__float_as_uint(r.y) | (__float_as_uint(x1) & 0x80000000u)));
+                    const float2 c = __fadd2_rn(sgn, make_float2(12582912.0f, 12582912.0f));
+                    q[2 * h] = __float_as_uint(c.x);
+                    q[2 * h + 1] = __float_as_uint(c.y);
                 }
-                w[m] = word;
+                w[m] = __byte_perm(__byte_perm(q[0], q[1], 0x0040), __byte_perm(q[2], q[3], 0x0040), 0x5410);
             }
         } else {
 #pragma unroll
