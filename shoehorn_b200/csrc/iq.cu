@@ -1263,16 +1263,26 @@ __global__ void __launch_bounds__(IqWarps<V, FUSE>::value * 32, (IqSearch<V>::CO
             }
         }
         __syncwarp();
-        // ---- P4: super-block scale and packing (lane 0) ----
-        if (lane == 0) {
+        // ---- P4: super-block scale and packing, lane b packs block b ----
+        {
             uint8_t *o = S.out;
-            for (int i = 0; i < C::OUT; i++) o[i] = 0;
-            float max_scale = 0.0f;
-            for (int b = 0; b < C::NB; b++) max_scale = rmaxf(max_scale, S.bscale[b]);
+            for (int i = lane; i < C::OUT; i += 32) o[i] = 0;
+            // the max of the block scales (NaN-ignoring, -0 < +0: associative,
+            // so the butterfly gives the reference's sequential fold)
+            float max_scale = lane < C::NB ? S.bscale[lane] : 0.0f;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) max_scale = rmaxf(max_scale, __shfl_xor_sync(0xffffffffu, max_scale, off));
+            max_scale = rmaxf(0.0f, max_scale);
             const bool has = max_scale != 0.0f;
             const float d = max_scale / 31.0f;
             const float id = 1.0f / d;
-            auto nib = [&](int b) { return clampi(nearest_int(0.5f * (id * S.bscale[b] - 1.0f)), 0, 15); };
+            const int b = lane;
+            const bool mine = b < C::NB;
+            const int nb_l = mine ? clampi(nearest_int(0.5f * (id * S.bscale[b] - 1.0f)), 0, 15) : 0;
+            // block b's scale nibble paired with block b + 1's (even b writes the byte)
+            const int nb_pair = nb_l | (__shfl_down_sync(0xffffffffu, nb_l, 1) << 4);
+            const bool live = mine && S.live[b];
+            __syncwarp();
             auto put16 = [&](int at, uint16_t h) {
                 o[at] = (uint8_t)(h & 0xFF);
                 o[at + 1] = (uint8_t)(h >> 8);
@@ -1285,81 +1295,72 @@ __global__ void __launch_bounds__(IqWarps<V, FUSE>::value * 32, (IqSearch<V>::CO
             };
             if (V == 0) {  // IQ2_XXS: the q2 words only reach the output with a nonzero scale
                 if (has) {
-                    put16(0, f16_bits(d));
-                    for (int b = 0; b < 8; b++) {
+                    if (lane == 0) put16(0, f16_bits(d));
+                    if (mine) {
                         uint32_t q0 = 0, q1 = 0;
                         for (int k = 0; k < 4; k++) {
                             q0 |= (uint32_t)S.gidx[b * 4 + k] << (8 * k);
                             q1 |= (uint32_t)S.signs[b * 4 + k] << (7 * k);
                         }
-                        q1 |= (uint32_t)nib(b) << 28;
+                        q1 |= (uint32_t)nb_l << 28;
                         put32(2 + 8 * b, q0);
                         put32(6 + 8 * b, q1);
                     }
                 }
             } else if (V == 1) {  // IQ2_XS
                 if (has) {
-                    put16(0, f16_bits(d));
-                    for (int b = 0; b < 16; b++)
+                    if (lane == 0) put16(0, f16_bits(d));
+                    if (mine) {
                         for (int k = 0; k < 2; k++)
                             put16(2 + 2 * (2 * b + k), (uint16_t)(S.gidx[b * 2 + k] | (S.signs[b * 2 + k] << 9)));
-                    for (int b = 0; b < 16; b++) {
-                        const uint8_t l = (uint8_t)nib(b);
-                        if (b % 2 == 0) o[66 + b / 2] = l;
-                        else o[66 + b / 2] |= (uint8_t)(l << 4);
+                        if (b % 2 == 0) o[66 + b / 2] = (uint8_t)nb_pair;
                     }
                 }
             } else if (V == 2) {  // IQ2_S: grid and sign bytes are written per block
-                for (int b = 0; b < 16; b++) {
-                    if (!S.live[b]) continue;
+                // high grid bits of blocks b, b + 1 share one byte (two bits per group)
+                uint32_t qh = 0;
+                if (live) {
                     for (int k = 0; k < 2; k++) {
                         const int i8v = 2 * b + k, gi = S.gidx[b * 2 + k];
                         o[2 + i8v] = (uint8_t)(gi & 255);
-                        o[2 + 64 + i8v / 4] |= (uint8_t)((gi >> 8) << (2 * (i8v % 4)));
+                        qh |= (uint32_t)((gi >> 8) << (2 * (i8v % 4)));
                         o[2 + 32 + i8v] = S.signs[b * 2 + k];
                     }
                 }
+                const uint32_t qh_pair = qh | __shfl_down_sync(0xffffffffu, qh, 1);
+                if (mine && b % 2 == 0) o[2 + 64 + b / 2] = (uint8_t)qh_pair;
                 if (has) {
-                    put16(0, f16_bits(d * 0.9875f));
-                    for (int b = 0; b < 16; b++) {
-                        const uint8_t l = (uint8_t)nib(b);
-                        const int so = 2 + 64 + 8 + b / 2;
-                        if (b % 2 == 0) o[so] = l;
-                        else o[so] |= (uint8_t)(l << 4);
-                    }
+                    if (lane == 0) put16(0, f16_bits(d * 0.9875f));
+                    if (mine && b % 2 == 0) o[2 + 64 + 8 + b / 2] = (uint8_t)nb_pair;
                 }
             } else if (V == 3) {  // IQ3_XXS
-                for (int b = 0; b < 8; b++) {
-                    if (!S.live[b]) continue;
+                if (live)
                     for (int k = 0; k < 8; k++) o[2 + 8 * b + k] = (uint8_t)S.gidx[b * 8 + k];
-                }
                 if (has) {
-                    put16(0, f16_bits(d * 1.0125f));
-                    for (int b = 0; b < 8; b++) {
+                    if (lane == 0) put16(0, f16_bits(d * 1.0125f));
+                    if (mine) {
                         uint32_t sas = 0;
-                        if (S.live[b])
+                        if (live)
                             sas = (uint32_t)S.signs[b * 4] | ((uint32_t)S.signs[b * 4 + 1] << 7) |
                                   ((uint32_t)S.signs[b * 4 + 2] << 14) | ((uint32_t)S.signs[b * 4 + 3] << 21);
-                        sas |= (uint32_t)nib(b) << 28;
+                        sas |= (uint32_t)nb_l << 28;
                         put32(2 + 64 + 4 * b, sas);
                     }
                 }
             } else {  // IQ3_S
-                for (int b = 0; b < 8; b++) {
-                    if (!S.live[b]) continue;
+                if (live) {
+                    uint8_t hi = 0;
                     for (int k = 0; k < 8; k++) {
                         const int gi = S.gidx[b * 8 + k];
                         o[2 + 8 * b + k] = (uint8_t)(gi & 255);
-                        o[2 + 64 + b] |= (uint8_t)((gi >> 8) << k);
+                        hi |= (uint8_t)((gi >> 8) << k);
                     }
+                    o[2 + 64 + b] = hi;
                     for (int k = 0; k < 4; k++) o[2 + 64 + 8 + 4 * b + k] = S.signs[b * 4 + k];
                 }
                 if (has) {
-                    put16(0, f16_bits(d * 1.033f));
-                    for (int b = 0; b < 8; b += 2) {
-                        const uint8_t l1 = (uint8_t)nib(b), l2 = (uint8_t)nib(b + 1);
-                        o[2 + 64 + 8 + 32 + b / 2] = (uint8_t)(l1 | (l2 << 4));
-                    }
+                    if (lane == 0) put16(0, f16_bits(d * 1.033f));
+                    if (mine && b % 2 == 0) o[2 + 64 + 8 + 32 + b / 2] = (uint8_t)nb_pair;
                 }
             }
         }
