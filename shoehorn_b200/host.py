@@ -122,7 +122,7 @@ def shard_exchange_check(n_rows, n_cands, sample_rows=128, comm=None):
 
 
 def bench_model(name, device=0, modes=("sampled",), budget=None, reserve="0", ctx=8192, uniform="",
-                workers_per_gpu=3, seed=20261201, out_path="", streaming=False, comm=None):
+                workers_per_gpu=4, seed=20261201, out_path="", streaming=False, comm=None):
     """Error table + solve + encode of a synthetic model on this rank's rows,
     once per mode ("sampled": the reference's 128-row error table, "exact":
     every row).  streaming: rows are generated as the pipeline asks for them

@@ -27,7 +27,7 @@ struct FitArgs {  // main.rs:43-85, plus the GPU harness options
     bool calibrate = false;
     bool exact_errors = false;
     int gpus = 1;
-    int workers_per_gpu = 3;  // concurrent jobs (own stream and context) per GPU
+    int workers_per_gpu = 4;  // concurrent jobs (own stream and context) per GPU (4 measured best of 2/3/4/6)
     std::string uniform;  // "TYPE[,tensor=TYPE...]": fixed mix instead of a solve
     int64_t timeout_ms = 3600 * 1000;
 };
@@ -111,7 +111,7 @@ ModelView view_of(const Model &m);
 class GpuPool {
   public:
     // devices first_device .. first_device + n_gpus - 1
-    GpuPool(int n_gpus, int64_t timeout_ms, int per_gpu = 3, int first_device = 0);
+    GpuPool(int n_gpus, int64_t timeout_ms, int per_gpu = 4, int first_device = 0);
     ~GpuPool();
     int size() const { return (int)workers_.size(); }
     int gpus() const { return n_gpus_; }
