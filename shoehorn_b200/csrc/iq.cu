@@ -185,10 +185,7 @@ __global__ void __launch_bounds__(256, (!XS && !FUSE) ? 4 : 0) enc_iq4_kernel(En
         float v[8], base[8];
         if (valid) {
             load8(a.src, row, col + q * 8, v);
-            if (imr) {
-#pragma unroll
-                for (int k = 0; k < 8; k++) base[k] = __ldg(imr + col + q * 8 + k);
-            }
+            if (imr) load_im8(imr, col + q * 8, base);
         } else {
 #pragma unroll
             for (int k = 0; k < 8; k++) v[k] = 0.0f;
@@ -202,11 +199,20 @@ __global__ void __launch_bounds__(256, (!XS && !FUSE) ? 4 : 0) enc_iq4_kernel(En
 #pragma unroll
         for (int k = 0; k < 8; k++) ws[q * 8 + k] = imr ? base[k] * sqrtf(sig + v[k] * v[k]) : v[k] * v[k];
         __syncwarp();
+        // max |x| of the block, first strict maximum (quant_iq.rs:1053-1059):
+        // each of the block's four lanes scans its own eight elements, then
+        // a butterfly keeps the lower lane's value unless the higher lane's is
+        // strictly larger, which is the serial scan's first-maximum rule.
         float amax = 0.0f, mx = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 32; i++) {
-            const float av = fabsf(xs[i]);
-            if (av > amax) { amax = av; mx = xs[i]; }
+        for (int k = 0; k < 8; k++) {
+            const float av = fabsf(v[k]);
+            if (av > amax) { amax = av; mx = v[k]; }
+        }
+#pragma unroll
+        for (int off = 1; off <= 2; off <<= 1) {
+            const float oa = __shfl_xor_sync(0xffffffffu, amax, off), om = __shfl_xor_sync(0xffffffffu, mx, off);
+            if ((q & off) == 0 ? oa > amax : !(amax > oa)) { amax = oa; mx = om; }
         }
         const bool live = !(amax < kGroupMaxEps);
         // Trials whose code vector repeats the previous trial's are skipped.

@@ -541,12 +541,17 @@ __global__ void __launch_bounds__(FUSE ? 512 : 256, FUSE ? 1 : 3) enc_qx16_kerne
             W->scale[s] = best_scale;
         }
         __syncwarp();
+        // largest |scale| over the 16 sub-blocks, first strict maximum
+        // (quant.rs:243-246): lanes 2s and 2s+1 hold sub-block s; a butterfly
+        // keeps the lower sub-block's value unless the higher one's is
+        // strictly larger (NaN and zero never replace the initial 0)
         const float best_scale = W->scale[s];
         float max_abs = 0.0f, max_scale = 0.0f;
+        if (fabsf(best_scale) > 0.0f) { max_abs = fabsf(best_scale); max_scale = best_scale; }
 #pragma unroll
-        for (int sb = 0; sb < 16; sb++) {
-            const float sv = W->scale[sb];
-            if (fabsf(sv) > max_abs) { max_abs = fabsf(sv); max_scale = sv; }
+        for (int off = 2; off <= 16; off <<= 1) {
+            const float oa = __shfl_xor_sync(0xffffffffu, max_abs, off), om = __shfl_xor_sync(0xffffffffu, max_scale, off);
+            if ((lane & off) == 0 ? oa > max_abs : !(max_abs > oa)) { max_abs = oa; max_scale = om; }
         }
         uint8_t *o = W->out;
         if (max_abs < kGroupMaxEps) {
