@@ -29,20 +29,31 @@ __device__ const float d_kv_f[16] = {-127.f, -104.f, -83.f, -65.f, -49.f, -35.f,
 // (v0, v15) the binary search ends at the unique mu with v[mu-1] <= x < v[mu];
 // the codebook values are integers, so v[k] <= x <=> v[k] <= floor(x) and
 // mu = 1 + cnt[floor(x)], with cnt[f] = #{k in 1..14 : v[k] <= f}.
-// Outside, clamping x to [-128, 127] keeps the answer: for x <= -127 the
-// pair (v0, v1) picks v0, for x >= 113 the pair (v14, v15) picks v15, and
-// fminf before fmaxf sends NaN to 127, hence v15, where the reference's
-// search ends for NaN.  floor() of the clamped value is read from the
-// mantissa of RD(x + 1.5*2^23): no conversion instruction.
+// Outside, the end pairs keep the answer: for x <= -127 the pair (v0, v1)
+// picks v0, for x >= 113 the pair (v14, v15) picks v15.  The table covers
+// floor(x) in [-136, 135]; floor() is read from the mantissa of
+// RD(x + 1.5*2^23) (no conversion instruction), slot = floor(x) + 136.
+//
+// Two entry forms:
+//  - clamped (any x): fminf before fmaxf clamps to [-128, 127] and sends NaN
+//    to 127, hence v15, where the reference's search ends for NaN;
+//  - bounded (x in [-136, 136) or NaN, as the trial products id*x are: |id|
+//    <= 134/|max| and |x| <= |max|): the slot is clamped as an unsigned
+//    integer instead, which maps every NaN bit pattern (exponent all ones,
+//    either sign) above 271, hence to the last pair, and the comparison
+//    with NaN is false, so NaN again picks v15.
 struct Iq4Lut {
     float v[16];
-    float2 pair[256];  // (v[mu-1], v[mu]) by floor(x) + 128
-    uint8_t cnt[256];  // mu - 1 by floor(x) + 128
+    float2 pair[272];  // (v[mu-1], v[mu]) by floor(x) + 136
+    uint8_t cnt[272];  // mu - 1 by floor(x) + 136
 };
 
 __device__ __forceinline__ float iq4_clamp(float x) { return fmaxf(fminf(x, 127.0f), -128.0f); }
-__device__ __forceinline__ int iq4_slot(float xc) {  // floor(xc) + 128 for xc in [-128, 127]
-    return (int)__float_as_uint(__fadd_rd(xc, 12582912.0f)) - 0x4B400000 + 128;
+__device__ __forceinline__ int iq4_slot(float xc) {  // floor(xc) + 136 for xc in [-136, 136)
+    return (int)__float_as_uint(__fadd_rd(xc, 12582912.0f)) - 0x4B400000 + 136;
+}
+__device__ __forceinline__ int iq4_slot_bounded(float x) {  // x in [-136, 136) or NaN
+    return (int)min(__float_as_uint(__fadd_rd(x, 12582912.0f)) - (0x4B400000u - 136u), 271u);
 }
 __device__ __forceinline__ int best_index_iq4(const Iq4Lut &L, float x) {
     const float xc = iq4_clamp(x);
@@ -51,18 +62,23 @@ __device__ __forceinline__ int best_index_iq4(const Iq4Lut &L, float x) {
     const int mu = 1 + L.cnt[f];
     return (xc - p.x < p.y - xc) ? mu - 1 : mu;
 }
-// The codebook value best_index_iq4 selects.
-__device__ __forceinline__ float best_value_iq4(const Iq4Lut &L, float x) {
-    const float xc = iq4_clamp(x);
-    const float2 p = L.pair[iq4_slot(xc)];
-    return (xc - p.x < p.y - xc) ? p.x : p.y;
+__device__ __forceinline__ int best_index_iq4_bounded(const Iq4Lut &L, float x) {
+    const int f = iq4_slot_bounded(x);
+    const float2 p = L.pair[f];
+    const int mu = 1 + L.cnt[f];
+    return (x - p.x < p.y - x) ? mu - 1 : mu;
+}
+// The codebook value best_index_iq4 selects, for x in [-136, 136) or NaN.
+__device__ __forceinline__ float best_value_iq4_bounded(const Iq4Lut &L, float x) {
+    const float2 p = L.pair[iq4_slot_bounded(x)];
+    return (x - p.x < p.y - x) ? p.x : p.y;
 }
 
 __device__ void init_iq4_lut(Iq4Lut &L) {
     for (int i = threadIdx.x; i < 16; i += blockDim.x) L.v[i] = d_kv_f[i];
-    for (int f = threadIdx.x; f < 256; f += blockDim.x) {
+    for (int f = threadIdx.x; f < 272; f += blockDim.x) {
         int c = 0;
-        for (int k = 1; k <= 14; k++) c += (d_kv_f[k] <= (float)(f - 128)) ? 1 : 0;
+        for (int k = 1; k <= 14; k++) c += (d_kv_f[k] <= (float)(f - 136)) ? 1 : 0;
         L.cnt[f] = (uint8_t)c;
         L.pair[f] = make_float2(d_kv_f[c], d_kv_f[c + 1]);
     }
@@ -87,8 +103,10 @@ __device__ __forceinline__ int iq4_ceil(float t) {
 template <bool XS, bool FUSE>
 __global__ void __launch_bounds__(256, (!XS && !FUSE) ? 4 : 0) enc_iq4_kernel(EncArgs a) {  // plain NL: 4 blocks/SM measured 4 % faster
     __shared__ Iq4Lut lut;
-    __shared__ float s_x[8][8 * 33];
-    __shared__ float s_w[8][8 * 33];
+    // block b's element pair p as (x[2p], x[2p+1], w[2p], w[2p+1]) at
+    // s_xw[wid][b * 17 + p]: one 16-byte load per pair in the trial loop, the
+    // blocks 17 slots apart so that lanes on different blocks use other banks
+    __shared__ float4 s_xw[8][8 * 17];
     __shared__ float2 s_res[8][8][16];
     __shared__ float s_scale[8][8];
     __shared__ float s_sig[8][32][8];
@@ -190,14 +208,15 @@ __global__ void __launch_bounds__(256, (!XS && !FUSE) ? 4 : 0) enc_iq4_kernel(En
 #pragma unroll
             for (int k = 0; k < 8; k++) v[k] = 0.0f;
         }
-        float *xs = &s_x[wid][b * 33];
-#pragma unroll
-        for (int k = 0; k < 8; k++) xs[q * 8 + k] = v[k];
-        __syncwarp();
         const float sig = s_sig[wid][u][XS ? 0 : b];
-        float *ws = &s_w[wid][b * 33];
+        {
+            float wk[8];
 #pragma unroll
-        for (int k = 0; k < 8; k++) ws[q * 8 + k] = imr ? base[k] * sqrtf(sig + v[k] * v[k]) : v[k] * v[k];
+            for (int k = 0; k < 8; k++) wk[k] = imr ? base[k] * sqrtf(sig + v[k] * v[k]) : v[k] * v[k];
+            float4 *xw = &s_xw[wid][b * 17 + q * 4];
+#pragma unroll
+            for (int p = 0; p < 4; p++) xw[p] = make_float4(v[2 * p], v[2 * p + 1], wk[2 * p], wk[2 * p + 1]);
+        }
         __syncwarp();
         // max |x| of the block, first strict maximum (quant_iq.rs:1053-1059):
         // each of the block's four lanes scans its own eight elements, then
@@ -233,7 +252,7 @@ __global__ void __launch_bounds__(256, (!XS && !FUSE) ? 4 : 0) enc_iq4_kernel(En
                 const float id1 = (-7.0f + -127.0f) / mx, id15 = (7.0f + -127.0f) / mx;
 #pragma unroll
                 for (int k = 0; k < 8; k++) {
-                    const int i1 = best_index_iq4(lut, id1 * v[k]), i15 = best_index_iq4(lut, id15 * v[k]);
+                    const int i1 = best_index_iq4_bounded(lut, id1 * v[k]), i15 = best_index_iq4_bounded(lut, id15 * v[k]);
                     if (i1 != i15) {
                         const float r = mx / v[k];
                         const int lo = min(i1, i15), hi = max(i1, i15);
@@ -279,15 +298,16 @@ __global__ void __launch_bounds__(256, (!XS && !FUSE) ? 4 : 0) enc_iq4_kernel(En
                 const int code = s_job[wid][t];
                 const int jb = code >> 4, j = code & 15;
                 const float jmx = s_mx[wid][jb];
-                const float *jx = &s_x[wid][jb * 33], *jw = &s_w[wid][jb * 33];
+                const float4 *jxw = &s_xw[wid][jb * 17];
                 const float id = j == 0 ? 1.0f / (-jmx / -127.0f) : ((float)(j - 8) + -127.0f) / jmx;
                 float sumqx = 0.0f, sumq2 = 0.0f;
 #pragma unroll
-                for (int i = 0; i < 32; i += 2) {  // element pairs; products feed scalar sums only
-                    const float2 xi = make_float2(jx[i], jx[i + 1]);
+                for (int p = 0; p < 16; p++) {  // element pairs; products feed scalar sums only
+                    const float4 f = jxw[p];
+                    const float2 xi = make_float2(f.x, f.y);
                     const float2 y = __fmul2_rn(make_float2(id, id), xi);
-                    const float2 qv = make_float2(best_value_iq4(lut, y.x), best_value_iq4(lut, y.y));
-                    const float2 wq = __fmul2_rn(make_float2(jw[i], jw[i + 1]), qv);
+                    const float2 qv = make_float2(best_value_iq4_bounded(lut, y.x), best_value_iq4_bounded(lut, y.y));
+                    const float2 wq = __fmul2_rn(make_float2(f.z, f.w), qv);
                     const float2 sx = __fmul2_rn(wq, xi);
                     const float2 s2 = __fmul2_rn(wq, qv);
                     sumqx = __fadd_rn(sumqx, sx.x);
@@ -322,11 +342,17 @@ __global__ void __launch_bounds__(256, (!XS && !FUSE) ? 4 : 0) enc_iq4_kernel(En
         uint8_t *o = s_out[wid];
         float idl;
         if (XS) {
+            // largest |scale| of the eight blocks, first strict maximum
+            // (quant_iq.rs:1094-1097), by a butterfly over the blocks' lanes
             float amax_s = 0.0f, max_s = 0.0f;
+            {
+                const float dv = s_scale[wid][b];
+                if (fabsf(dv) > 0.0f) { amax_s = fabsf(dv); max_s = dv; }
+            }
 #pragma unroll
-            for (int bb = 0; bb < 8; bb++) {
-                const float dv = s_scale[wid][bb];
-                if (fabsf(dv) > amax_s) { amax_s = fabsf(dv); max_s = dv; }
+            for (int off = 4; off <= 16; off <<= 1) {
+                const float oa = __shfl_xor_sync(0xffffffffu, amax_s, off), om = __shfl_xor_sync(0xffffffffu, max_s, off);
+                if ((lane & off) == 0 ? oa > amax_s : !(amax_s > oa)) { amax_s = oa; max_s = om; }
             }
             const float d = -max_s / 32.0f;
             const float id = d != 0.0f ? 1.0f / d : 0.0f;

@@ -123,13 +123,16 @@ __global__ void __launch_bounds__(kSigThreads) row_sigma2_kernel(RowSrc src, int
             cp_async_commit();
         };
         for (int64_t t = 0; t < ntiles; t++) {
-            if (t >= kSigStages) bar_sync_all(sig_empty((int)(t % kSigStages)));  // the folder released the stage
-            issue(t);
+            // announce tile t - (kSigStages - 1) before waiting for a free
+            // stage: the folder waits for the next tile before it releases
+            // the current one
             if (t >= kSigStages - 1) {
-                cp_async_wait<kSigStages - 1>();  // tile t - (kSigStages - 1) landed
+                cp_async_wait<kSigStages - 2>();  // tiles 0 .. t - 1 issued: tile t - (kSigStages - 1) landed
                 __syncwarp();
                 bar_arrive_all(sig_full((int)((t - (kSigStages - 1)) % kSigStages)));
             }
+            if (t >= kSigStages) bar_sync_all(sig_empty((int)(t % kSigStages)));  // the folder released the stage
+            issue(t);
         }
         // hand over the tiles still in flight, oldest first
         const int64_t first = ntiles > kSigStages - 1 ? ntiles - (kSigStages - 1) : 0;
@@ -139,31 +142,52 @@ __global__ void __launch_bounds__(kSigThreads) row_sigma2_kernel(RowSrc src, int
             bar_arrive_all(sig_full((int)(t % kSigStages)));
         }
     } else {
+        // Full tiles are folded in groups of eight chunks; the next group
+        // (the next tile's first, at a tile's last group, after its FULL
+        // barrier) is read into registers before the current group's adds,
+        // so the shared-memory latency, long while the loaders' copies land,
+        // stays off the add chain.  Lanes past n_rows fold stale slots and
+        // store nothing.
         float s = 0.0f;
         const bool mine = rbase + lane < n_rows;
-        for (int64_t t = 0; t < ntiles; t++) {
-            const int st = (int)(t % kSigStages);
-            bar_sync_all(sig_full(st));
+        uint4 cur[8];
+        if (full_tiles > 0) {
+            bar_sync_all(sig_full(0));
+            const uint4 *slot = ring(0);
+#pragma unroll
+            for (int jj = 0; jj < 8; jj++) cur[jj] = slot[jj * 32 + lane];
+        }
+        for (int64_t t = 0; t < full_tiles; t++) {
             const uint4 *slot = ring(t);
-            if (mine) {
-                if (t < full_tiles) {
-                    // eight chunks at a time, loaded before their adds, so no
-                    // load latency sits on the add chain
-#pragma unroll 1
-                    for (int j0 = 0; j0 < kSigChunks; j0 += 8) {
-                        uint4 q[8];
 #pragma unroll
-                        for (int jj = 0; jj < 8; jj++) q[jj] = slot[(j0 + jj) * 32 + lane];
+            for (int g = 0; g < kSigChunks / 8; g++) {
+                uint4 nxt[8];
+                if (g + 1 < kSigChunks / 8) {
 #pragma unroll
-                        for (int jj = 0; jj < 8; jj++) sigma_fold<SRC>(q[jj], s);
+                    for (int jj = 0; jj < 8; jj++) nxt[jj] = slot[((g + 1) * 8 + jj) * 32 + lane];
+                } else if (t + 1 < ntiles) {
+                    bar_sync_all(sig_full((int)((t + 1) % kSigStages)));
+                    if (t + 1 < full_tiles) {
+                        const uint4 *ns = ring(t + 1);
+#pragma unroll
+                        for (int jj = 0; jj < 8; jj++) nxt[jj] = ns[jj * 32 + lane];
                     }
-                } else {  // the row's ragged end: whole chunks only (ne0 is a multiple of 8)
-                    const int nchunks = (int)((ne0 - t * tile_cols + per_chunk - 1) / per_chunk);
-                    for (int jj = 0; jj < nchunks; jj++) sigma_fold<SRC>(slot[jj * 32 + lane], s);
                 }
+#pragma unroll
+                for (int jj = 0; jj < 8; jj++) sigma_fold<SRC>(cur[jj], s);
+#pragma unroll
+                for (int jj = 0; jj < 8; jj++) cur[jj] = nxt[jj];
             }
-            // the loader waits on this stage only once it has kSigStages tiles ahead
-            if (t + kSigStages < ntiles) bar_arrive_all(sig_empty(st));
+            // the loaders wait on this stage only once they are kSigStages tiles ahead
+            if (t + kSigStages < ntiles) bar_arrive_all(sig_empty((int)(t % kSigStages)));
+        }
+        if (full_tiles < ntiles) {  // the row's ragged end: whole chunks only (ne0 is a multiple of 8)
+            const int64_t t = full_tiles;
+            if (t == 0) bar_sync_all(sig_full(0));  // else synced during the last full tile
+            const uint4 *slot = ring(t);
+            const int nchunks = (int)((ne0 - t * tile_cols + per_chunk - 1) / per_chunk);
+            for (int jj = 0; jj < nchunks; jj++) sigma_fold<SRC>(slot[jj * 32 + lane], s);
+            if (t + kSigStages < ntiles) bar_arrive_all(sig_empty((int)(t % kSigStages)));
         }
         if (mine) out[rbase + lane] = s / (float)ne0;
     }
