@@ -29,20 +29,27 @@ namespace shc {
 // row, measured 4.1 cycles per dependent add).  A block owns 32 rows and has
 // kSigLoaders + 1 warps: the loaders stream tiles of 32 rows x 512 bytes into
 // a kSigStages-deep shared-memory ring with cp.async (16-byte chunks, one
-// row's 512 B per instruction, coalesced; each loader copies 8 of the tile's
-// 32 rows, so four warps keep four times the copies in flight that one
-// would); the folder (lane r = row r) only reads its row from the ring,
-// unpacks, squares (packed) and adds, so its instruction stream stays inside
-// the chain's latency.  The warps hand stages over through named barriers
-// counting all of them: FULL(s) after the loaders' copies into stage s
-// landed, EMPTY(s) after the folder read it; every warp walks the same
-// tiles, so every barrier is met.  Chunk (row r, j) sits in slot j*32 + r so
+// row's 512 B per instruction, coalesced; the three loaders copy 11, 11 and
+// 10 of the tile's 32 rows, keeping that many times the copies in flight
+// that one warp would); the folder (warp 0, lane r = row r) only reads its
+// row from the ring, unpacks, squares (packed) and adds.  It reads the next
+// group of eight chunks into registers before adding the current group, so
+// the shared-memory latency (long while the loaders' copies land) stays off
+// the add chain.  The warps hand stages over through named barriers counting
+// all of them: FULL(s) after the loaders' copies into stage s landed, EMPTY(s)
+// after the folder read it.  The folder waits for the next tile's FULL before
+// it releases the current tile's EMPTY, so the loaders announce their oldest
+// landed tile before they wait for a free stage; every warp walks the same
+// tiles, so every barrier is met (the call order is replayed on the CPU by
+// tests/test_sigma_protocol.py).  Chunk (row r, j) sits in slot j*32 + r so
 // that lane r reads its row 16 bytes at a time without bank conflicts.
 // Measured on the 4096 x 14336 sweep tensor: 86 us with one loader and
-// 128-byte tiles, 78 us with four loaders, against the 30 us chain.
+// 128-byte tiles, 78 us with four loaders, 60 us with the register-prefetched
+// groups, 56 us with the folder alone on its sub-partition, against the
+// 30 us chain.
 // ---------------------------------------------------------------------------
 constexpr int kSigStages = 6;
-constexpr int kSigLoaders = 4;
+constexpr int kSigLoaders = 3;
 constexpr int kSigThreads = 32 * (kSigLoaders + 1);
 constexpr int kSigChunks = 32;  // 16-byte chunks of each row per tile
 constexpr size_t kSigSmem = (size_t)kSigStages * kSigChunks * 32 * 16;  // 96 KB
@@ -96,8 +103,11 @@ __global__ void __launch_bounds__(kSigThreads) row_sigma2_kernel(RowSrc src, int
     extern __shared__ __align__(16) uint4 sig_ring[];  // [kSigStages][kSigChunks * 32]
     auto ring = [&](int64_t t) { return sig_ring + (t % kSigStages) * (kSigChunks * 32); };
     const int lane = threadIdx.x & 31;
-    const int lw = threadIdx.x >> 5;  // loaders 0 .. kSigLoaders-1, then the folder
-    const bool loader = lw < kSigLoaders;
+    // warp 0 folds, alone on its scheduler sub-partition (warps are spread
+    // over the four by warp index; a loader beside it cost 4 us), warps 1..
+    // kSigLoaders load
+    const int lw = (int)(threadIdx.x >> 5) - 1;
+    const bool loader = lw >= 0;
     const int64_t rbase = (int64_t)blockIdx.x * 32;
     const int64_t ne0 = src.ne0;
     constexpr int esz = SRC == SHC_SRC_F32 ? 4 : 2;
@@ -108,16 +118,16 @@ __global__ void __launch_bounds__(kSigThreads) row_sigma2_kernel(RowSrc src, int
     if (loader) {
         const char *base = static_cast<const char *>(src.ptr);
         const int64_t row_bytes = src.row_stride * esz;
-        // this lane's chunks of a tile: 16-byte column `lane` of rows 8*lw .. 8*lw + 7
+        // this lane's chunks of a tile: 16-byte column `lane` of rows lw, lw + kSigLoaders, ...
         const int j = lane;
         auto issue = [&](int64_t t) {
             uint4 *slot = ring(t);
             const int64_t col = t * tile_cols + (int64_t)j * per_chunk;
             if (col < ne0) {
 #pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    const int r = lw * 8 + i;
-                    if (rbase + r < n_rows) cp_async16(&slot[j * 32 + r], base + (rbase + r) * row_bytes + col * esz);
+                for (int i = 0; i < (32 + kSigLoaders - 1) / kSigLoaders; i++) {
+                    const int r = lw + kSigLoaders * i;
+                    if (r < 32 && rbase + r < n_rows) cp_async16(&slot[j * 32 + r], base + (rbase + r) * row_bytes + col * esz);
                 }
             }
             cp_async_commit();

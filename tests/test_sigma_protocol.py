@@ -1,9 +1,9 @@
 """The row sigma^2 kernel's stage hand-off, replayed on the CPU.
 
-row_sigma2_kernel (shoehorn_b200/csrc/kquant.cu) has four loader warps and a
+row_sigma2_kernel (shoehorn_b200/csrc/kquant.cu) has three loader warps and a
 folding warp that pass ring stages to each other through hardware named
 barriers: FULL(s) (loaders arrive, folder syncs) and EMPTY(s) (folder arrives,
-loaders sync), each completing once all five warps reached it.  A mistake in
+loaders sync), each completing once all four warps reached it.  A mistake in
 the order of these calls hangs the kernel (a barrier that never completes) or
 lets two tiles' arrivals meet in one barrier instance.  These tests replay the
 exact sequence of barrier calls each warp makes, under many interleavings, for
@@ -16,7 +16,7 @@ import random
 import pytest
 
 STAGES = 6   # kSigStages
-LOADERS = 4  # kSigLoaders
+LOADERS = 3  # kSigLoaders
 
 
 def loader_calls(ntiles):
