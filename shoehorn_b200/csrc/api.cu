@@ -30,6 +30,8 @@ struct shc_ctx {
     // host-buffer pipeline resources (one host call at a time)
     std::mutex host_mu;
     cudaStream_t hs[4] = {nullptr, nullptr, nullptr, nullptr};  // h2d, compute, d2h, row sigma^2
+    static constexpr int kHostEvents = 13;                       // the host-buffer encode's events, kept
+    cudaEvent_t hev[kHostEvents] = {};
     static constexpr int kPinSlots = 6;  // pageable staging: in 0-2, out 3-5
     void *pin[kPinSlots] = {};
     size_t pin_bytes[kPinSlots] = {};
@@ -77,14 +79,20 @@ bool encodable(uint32_t t) {
     }
 }
 
-// Wait for an event with a deadline; never blocks past it.
+// Wait for an event with a deadline; never blocks past it.  The first
+// 200 us poll between yields (a 20 us sleep lasts ~70 us with Linux's
+// default timer slack, which short waits such as a status read would pay in
+// full); longer waits then poll every 20 us asleep.
 int wait_event(cudaEvent_t ev, std::chrono::steady_clock::time_point deadline, bool bounded) {
+    const auto spin_until = std::chrono::steady_clock::now() + std::chrono::microseconds(200);
     for (;;) {
         cudaError_t e = cudaEventQuery(ev);
         if (e == cudaSuccess) return SHC_OK;
         if (e != cudaErrorNotReady) return cuda_status(e);
-        if (bounded && std::chrono::steady_clock::now() > deadline) return SHC_ETIMEOUT;
-        std::this_thread::sleep_for(std::chrono::microseconds(20));
+        const auto now = std::chrono::steady_clock::now();
+        if (bounded && now > deadline) return SHC_ETIMEOUT;
+        if (now < spin_until) std::this_thread::yield();
+        else std::this_thread::sleep_for(std::chrono::microseconds(20));
     }
 }
 
@@ -322,6 +330,8 @@ int shc_init(int device, shc_ctx **out) {
     if (rc == SHC_OK) rc = upload_iq_tables(ctx);
     for (int i = 0; rc == SHC_OK && i < 4; i++)
         if (cudaStreamCreateWithFlags(&ctx->hs[i], cudaStreamNonBlocking) != cudaSuccess) rc = SHC_ECUDA;
+    for (int i = 0; rc == SHC_OK && i < shc_ctx::kHostEvents; i++)
+        if (cudaEventCreateWithFlags(&ctx->hev[i], cudaEventDisableTiming) != cudaSuccess) rc = SHC_ECUDA;
     if (rc != SHC_OK) {
         shc_free(ctx);
         return rc;
@@ -337,6 +347,8 @@ int shc_free(shc_ctx *ctx) {
         cudaDeviceSynchronize();
         for (int i = 0; i < 4; i++)
             if (ctx->hs[i]) cudaStreamDestroy(ctx->hs[i]);
+        for (int i = 0; i < shc_ctx::kHostEvents; i++)
+            if (ctx->hev[i]) cudaEventDestroy(ctx->hev[i]);
         for (int i = 0; i < shc_ctx::kPinSlots; i++)
             if (ctx->pin[i]) cudaFreeHost(ctx->pin[i]);
         if (ctx->d_tables) cudaFree(ctx->d_tables);
@@ -480,13 +492,9 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
     uint8_t *d_out[NS] = {};
     float *d_sig[NS] = {};
     float *d_im = nullptr;
-    cudaEvent_t ev_in[NS], ev_cmp[NS], ev_out[NS], ev_sig[NS];
-    for (int b = 0; b < NS; b++) {
-        cudaEventCreateWithFlags(&ev_in[b], cudaEventDisableTiming);
-        cudaEventCreateWithFlags(&ev_cmp[b], cudaEventDisableTiming);
-        cudaEventCreateWithFlags(&ev_out[b], cudaEventDisableTiming);
-        cudaEventCreateWithFlags(&ev_sig[b], cudaEventDisableTiming);
-    }
+    // the context's events (one host-buffer call at a time holds host_mu)
+    static_assert(4 * NS + 1 <= shc_ctx::kHostEvents, "host events");
+    cudaEvent_t *ev_in = ctx->hev, *ev_cmp = ctx->hev + NS, *ev_out = ctx->hev + 2 * NS, *ev_sig = ctx->hev + 3 * NS;
     auto fail = [&](int code) {
         if (rc == SHC_OK) rc = code;
     };
@@ -579,8 +587,7 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
     }
     for (int b = 0; b < NS; b++) drain_out(b);
     // release buffers after all queued work; wait (bounded) for completion
-    cudaEvent_t done;
-    cudaEventCreateWithFlags(&done, cudaEventDisableTiming);
+    cudaEvent_t done = ctx->hev[4 * NS];
     cudaEventRecord(done, s_in);
     cudaStreamWaitEvent(s_cmp, done, 0);
     cudaEventRecord(done, s_out);
@@ -593,20 +600,18 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
         if (d_sig[b]) cudaFreeAsync(d_sig[b], s_cmp);
     }
     if (d_im) cudaFreeAsync(d_im, s_cmp);
+    // the device status word of this call's kernels, read and cleared behind
+    // them (as shc_sync does), so that one wait covers both
+    int *slot = ctx->h_status_pool + (ctx->status_slot.fetch_add(1) % kStatusSlots);
+    *slot = 0;
+    const bool status_read = rc == SHC_OK &&
+                             cudaMemcpyAsync(slot, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost, s_cmp) == cudaSuccess &&
+                             cudaMemsetAsync(ctx->d_status, 0, sizeof(int), s_cmp) == cudaSuccess;
+    if (rc == SHC_OK && !status_read) rc = SHC_ECUDA;
     cudaEventRecord(done, s_cmp);
     int w = wait_event(done, deadline, bounded);
     if (rc == SHC_OK) rc = w;
-    cudaEventDestroy(done);
-    for (int b = 0; b < NS; b++) {
-        cudaEventDestroy(ev_in[b]);
-        cudaEventDestroy(ev_cmp[b]);
-        cudaEventDestroy(ev_out[b]);
-        cudaEventDestroy(ev_sig[b]);
-    }
-    if (rc == SHC_OK) {
-        int st = shc_sync(ctx, s_cmp, timeout_ms);
-        if (st != SHC_OK) rc = st;
-    }
+    if (rc == SHC_OK && *slot != SHC_OK) rc = *slot;
     return rc;
 }
 
