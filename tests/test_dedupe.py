@@ -75,14 +75,58 @@ _CNT = np.array([sum(1 for k in range(1, 15) if KV[k] <= f - 128) for f in range
 
 
 def iq4_index(y):
-    """best_index_int8 (quant_iq.rs:1002-1024) as the kernel evaluates it:
-    clamp to [-128, 127] (NaN to the top), neighbouring pair from floor(x),
-    rounded distances compared."""
+    """best_index_int8 (quant_iq.rs:1002-1024) as the kernel's final pass
+    evaluates it: clamp to [-128, 127] (NaN to the top), neighbouring pair
+    from floor(x), rounded distances compared."""
     xc = np.maximum(np.minimum(y, f32(127)), f32(-128)).astype(f32)
     xc = np.where(np.isnan(y), f32(127), xc)
     mu = 1 + _CNT[np.floor(xc.astype(np.float64)).astype(int) + 128]
     lower = (xc - KV[mu - 1]).astype(f32) < (KV[mu] - xc).astype(f32)
     return np.where(lower, mu - 1, mu)
+
+
+# The trial loop's form (iq.cu best_value_iq4_bounded / best_index_iq4_bounded):
+# no float clamp, a table over floor(y) in [-136, 135], the slot read from the
+# bits of RD(y + 1.5 * 2^23) and clamped as an unsigned integer at 271.
+_CNT272 = np.array([sum(1 for k in range(1, 15) if KV[k] <= f - 136) for f in range(272)])
+
+
+def iq4_slot_bounded(y):
+    """Slot of the clamp-free lookup for f32 y (finite in [-136, 136), or NaN
+    as the device add produces it: the canonical 0x7FFFFFFF)."""
+    y = np.asarray(y, f32)
+    fin = np.isfinite(y)
+    bits = np.where(fin, np.uint32(0x4B400000) + np.floor(np.where(fin, y, 0).astype(np.float64)).astype(np.int64)
+                    .astype(np.uint32), np.uint32(0x7FFFFFFF)).astype(np.uint32)
+    return np.minimum(bits - np.uint32(0x4B400000 - 136), np.uint32(271)).astype(np.int64)
+
+
+def iq4_index_bounded(y):
+    y = np.asarray(y, f32)
+    mu = 1 + _CNT272[iq4_slot_bounded(y)]
+    with np.errstate(invalid="ignore"):
+        lower = (y - KV[mu - 1]).astype(f32) < (KV[mu] - y).astype(f32)
+    return np.where(lower, mu - 1, mu)
+
+
+def test_iq4_clamp_free_lookup_matches_the_clamped_search():
+    """Trial products are bounded by 134 (1 + 2^-22) in magnitude (|id| <=
+    134/|max|, |x| <= |max|), or NaN: over that domain the clamp-free lookup
+    picks the codebook index the clamped binary-search form picks."""
+    mids = (KV[:-1] + KV[1:]) / 2
+    near = [mids[:, None] + np.arange(-64, 65)[None, :] * np.spacing(np.abs(mids))[:, None]]
+    grid = np.arange(-136.0, 136.0, 1 / 64)
+    rng = np.random.default_rng(31)
+    y = np.concatenate([np.concatenate(near).ravel(), grid, KV, KV - np.spacing(np.abs(KV)), KV + np.spacing(np.abs(KV)),
+                        rng.uniform(-136, 136, 200_000), rng.standard_normal(100_000) * 20,
+                        np.array([-135.99998, 135.99998, -0.0, 0.0, 1e-30, -1e-30, np.nan])]).astype(f32)
+    y = y[(np.abs(y) < 136) | np.isnan(y)]
+    np.testing.assert_array_equal(iq4_index_bounded(y), iq4_index(y))
+    # every NaN bit pattern, either sign, lands above the table and is clamped
+    # onto the last pair, where the false comparison picks v15 as the clamped
+    # form (NaN sent to 127) does
+    for b in (0x7F800001, 0x7FC00000, 0x7FFFFFFF, 0xFF800001, 0xFFC00000, 0xFFFFFFFF):
+        assert (b - (0x4B400000 - 136)) % 2**32 > 271
 
 
 def iq4_changes_and_marks(x):
