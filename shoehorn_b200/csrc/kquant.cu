@@ -45,8 +45,8 @@ namespace shc {
 // that lane r reads its row 16 bytes at a time without bank conflicts.
 // Measured on the 4096 x 14336 sweep tensor: 86 us with one loader and
 // 128-byte tiles, 78 us with four loaders, 60 us with the register-prefetched
-// groups, 56 us with the folder alone on its sub-partition, against the
-// 30 us chain.
+// groups, 57.6 us (launch-list mean) with the folder alone on its
+// sub-partition, against the 30 us chain.
 // ---------------------------------------------------------------------------
 constexpr int kSigStages = 6;
 constexpr int kSigLoaders = 3;
@@ -171,7 +171,7 @@ __global__ void __launch_bounds__(kSigThreads) row_sigma2_kernel(RowSrc src, int
             const uint4 *slot = ring(t);
 #pragma unroll
             for (int g = 0; g < kSigChunks / 8; g++) {
-                uint4 nxt[8];
+                uint4 nxt[8];  // left unset when no full tile follows: cur is not read again then
                 if (g + 1 < kSigChunks / 8) {
 #pragma unroll
                     for (int jj = 0; jj < 8; jj++) nxt[jj] = slot[((g + 1) * 8 + jj) * 32 + lane];
