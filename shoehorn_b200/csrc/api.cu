@@ -29,7 +29,8 @@ struct shc_ctx {
     std::atomic<int64_t> launches{0};
     // host-buffer pipeline resources (one host call at a time)
     std::mutex host_mu;
-    cudaStream_t hs[4] = {nullptr, nullptr, nullptr, nullptr};  // h2d, compute, d2h, row sigma^2
+    static constexpr int kHostStreams = 5;
+    cudaStream_t hs[kHostStreams] = {};  // h2d, compute, d2h, row sigma^2, second compute
     static constexpr int kHostEvents = 13;                       // the host-buffer encode's events, kept
     cudaEvent_t hev[kHostEvents] = {};
     static constexpr int kPinSlots = 6;  // pageable staging: in 0-2, out 3-5
@@ -328,7 +329,7 @@ int shc_init(int device, shc_ctx **out) {
             rc = SHC_ECUDA;
     }
     if (rc == SHC_OK) rc = upload_iq_tables(ctx);
-    for (int i = 0; rc == SHC_OK && i < 4; i++)
+    for (int i = 0; rc == SHC_OK && i < shc_ctx::kHostStreams; i++)
         if (cudaStreamCreateWithFlags(&ctx->hs[i], cudaStreamNonBlocking) != cudaSuccess) rc = SHC_ECUDA;
     for (int i = 0; rc == SHC_OK && i < shc_ctx::kHostEvents; i++)
         if (cudaEventCreateWithFlags(&ctx->hev[i], cudaEventDisableTiming) != cudaSuccess) rc = SHC_ECUDA;
@@ -345,7 +346,7 @@ int shc_free(shc_ctx *ctx) {
     {
         DevGuard g(ctx->device);
         cudaDeviceSynchronize();
-        for (int i = 0; i < 4; i++)
+        for (int i = 0; i < shc_ctx::kHostStreams; i++)
             if (ctx->hs[i]) cudaStreamDestroy(ctx->hs[i]);
         for (int i = 0; i < shc_ctx::kHostEvents; i++)
             if (ctx->hev[i]) cudaEventDestroy(ctx->hev[i]);
@@ -479,7 +480,7 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
     }
     const int64_t n_chunks = (int64_t)chunks.size();
     const bool pin_src = is_pinned(host_src), pin_dst = is_pinned(host_dst);
-    cudaStream_t s_in = ctx->hs[0], s_cmp = ctx->hs[1], s_out = ctx->hs[2], s_sig = ctx->hs[3];
+    cudaStream_t s_in = ctx->hs[0], s_cmp = ctx->hs[1], s_out = ctx->hs[2], s_sig = ctx->hs[3], s_cmp2 = ctx->hs[4];
     // The row sigma^2 pre-pass (one thread per row, bound by its serial sums)
     // runs on its own stream for chunk k+1 while chunk k encodes; the
     // encoder's persistent grid leaves kSigmaSms SMs' worth of blocks free so
@@ -487,6 +488,13 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
     constexpr int kSigmaSms = 4;
     const bool pre_sig = needs_sigma2(type) && n_rows > 1;
     const int enc_sms = pre_sig ? std::max(1, ctx->num_sms - kSigmaSms) : 0;
+    // Without the pre-pass, consecutive chunks encode on two streams in
+    // turn: each encoder's persistent grid ends with its slowest warps'
+    // last units (about one unit's time, 0.2 ms for the IQ2 encoders), and
+    // the next chunk's blocks take the SMs as they free up.  (The pre-pass
+    // types keep one stream: a second encoder would take the SMs the
+    // pre-pass of the next chunk runs on.)
+    const bool two_cmp = !pre_sig;
     int rc = SHC_OK;
     void *d_in[NS] = {};
     uint8_t *d_out[NS] = {};
@@ -519,6 +527,7 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
         cudaStreamWaitEvent(s_in, ev_cmp[0], 0);
         cudaStreamWaitEvent(s_out, ev_cmp[0], 0);
         cudaStreamWaitEvent(s_sig, ev_cmp[0], 0);
+        cudaStreamWaitEvent(s_cmp2, ev_cmp[0], 0);
         for (int b = 0; b < NS; b++) {
             cudaEventRecord(ev_cmp[b], s_cmp);
             cudaEventRecord(ev_out[b], s_out);
@@ -567,11 +576,12 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
             a.sigma2 = d_sig[b];
         }
         // encode chunk k once its input (and sigma^2) landed and d_out[b] was drained
-        cudaStreamWaitEvent(s_cmp, ready, 0);
-        cudaStreamWaitEvent(s_cmp, ev_out[b], 0);
-        int e = encode_view(ctx, type, a, s_cmp, enc_sms);
+        cudaStream_t sc = (two_cmp && (k & 1)) ? s_cmp2 : s_cmp;
+        cudaStreamWaitEvent(sc, ready, 0);
+        cudaStreamWaitEvent(sc, ev_out[b], 0);
+        int e = encode_view(ctx, type, a, sc, enc_sms);
         if (e != SHC_OK) { fail(e); break; }
-        cudaEventRecord(ev_cmp[b], s_cmp);
+        cudaEventRecord(ev_cmp[b], sc);
         // D2H of chunk k
         cudaStreamWaitEvent(s_out, ev_cmp[b], 0);
         if (pin_dst) {
@@ -593,6 +603,8 @@ int shc_encode_tensor_host(shc_ctx *ctx, uint32_t type, uint32_t src_type, const
     cudaEventRecord(done, s_out);
     cudaStreamWaitEvent(s_cmp, done, 0);
     cudaEventRecord(done, s_sig);
+    cudaStreamWaitEvent(s_cmp, done, 0);
+    cudaEventRecord(done, s_cmp2);
     cudaStreamWaitEvent(s_cmp, done, 0);
     for (int b = 0; b < NS; b++) {
         if (d_in[b]) cudaFreeAsync(d_in[b], s_cmp);
